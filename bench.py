@@ -1,0 +1,413 @@
+"""Benchmark of the B200 GGUF K-quant dequant x fp32 matvec (libtb_cuda_sm100.so).
+
+Metric: K-quant matvec HBM GB/s (algorithmic bytes / time).
+
+Workload ("step") — BASELINE config 2, the per-type sweep at Qwen3-4B shapes:
+q 4096x2560, k 1024x2560, v 1024x2560, gate 9728x2560, up 9728x2560,
+down 2560x9728, lm_head 151936x2560, for each of Q2_K, Q3_K, Q4_K, Q5_K, Q6_K,
+Q8_0 (Q4_K added to the config's five types so the headline type is in the
+line): 42 matvecs, 1.99 GB of weights resident in HBM, seeded synthetic data
+(trailblaze_b200.synth).  Algorithmic bytes per matvec = weights + 4K + 4M.
+One step reads every tensor once, so consecutive reads of a tensor are
+separated by ~2 GB of other traffic (> 126 MB L2): no L2 flush is needed.
+
+`value`      device time of K steps replayed from one CUDA graph, CUDA events on
+             the launching stream, barrier + synchronize on both sides, max over
+             ranks; whole-job GB/s.
+`e2e`        the same sweep through the blocking reference ABI
+             tb_cuda_matvec_device(W_dev, qtype, M, K, x_host, out_host): every
+             call copies x host->device and y device->host (wall clock).
+`roofline`   the kernel with the largest share of step time, timed per launch
+             with CUDA events inside the timed pass; peak = MEASURED_PEAKS.json.
+`cpu_baseline` the reference's own CPU path (oracle/_ref, built from its
+             sources: tb_dispatch_matvec AVX-512/AVX2 tier for Q4_K/Q3_K/Q8_0,
+             tb_gguf_dequant_matvec for Q2_K/Q5_K/Q6_K), all host threads, on a
+             bounded row sample of the same tensors.
+
+N > 1 (torchrun, one process per GPU, NCCL): weak scaling.  Every matrix is a
+row shard of an N-times-taller matrix (rank r owns rows [r*M, (r+1)*M), drawn
+from its own seed stream); rows are independent, so there is no collective in
+the data path; the only collectives are the timing barriers and the
+max-reduction of the elapsed time.
+
+--impl reference: the reference's CPU implementation alone (rank 0; other ranks
+exit 0), same config and metric, each step a bounded row sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from trailblaze_b200 import qtypes as Q  # noqa: E402
+from trailblaze_b200 import synth  # noqa: E402
+
+SHAPES = [("q_proj", 4096, 2560), ("k_proj", 1024, 2560), ("v_proj", 1024, 2560),
+          ("gate", 9728, 2560), ("up", 9728, 2560), ("down", 2560, 9728), ("lm_head", 151936, 2560)]
+TYPES = [Q.Q2_K, Q.Q3_K, Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q8_0]
+SEED = 20261201
+METRIC = "K-quant matvec HBM GB/s (% of 8 TB/s)"
+# reference CPU routine per type: 1 = tb_dispatch_matvec AVX-512 tier,
+# 2 = AVX2 tier, 0 = tb_gguf_dequant_matvec (the dispatch tiers do no work for these types)
+REF_PATH = {Q.Q4_K: 1, Q.Q3_K: 1, Q.Q8_0: 1, Q.Q2_K: 0, Q.Q5_K: 0, Q.Q6_K: 0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def workload(rank: int, world: int):
+    """[(name, qtype, M, K, W bytes (rank's rows), x)] — rank-sharded rows of N*M-row matrices."""
+    out = []
+    for ti, qt in enumerate(TYPES):
+        for si, (nm, M, K) in enumerate(SHAPES):
+            tensor = 100 * ti + si
+            rb = Q.row_bytes(qt, K)
+            full = synth.weights(qt, M, K, seed=SEED + 7919 * rank, tensor=tensor) if world > 1 else \
+                synth.weights(qt, M, K, seed=SEED, tensor=tensor)
+            assert full.size == M * rb
+            out.append((f"{Q.NAMES[qt]}:{nm}", qt, M, K, full))
+    xs = {K: synth.activations(K, seed=SEED + K) for _, _, K in SHAPES}
+    return out, xs
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (200 ms period)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        try:
+            import torch
+            u = str(getattr(torch.cuda.get_device_properties(index), "uuid", "") or "")
+            if u:
+                self.index = u if u.startswith("GPU-") else f"GPU-{u}"
+        except Exception:  # noqa: BLE001
+            pass
+        self.proc = None
+        self.path = os.path.join(REPO, "gpurun_out", f"clocks_dev{index}.csv") \
+            if os.path.isdir(os.path.join(REPO, "gpurun_out")) else f"/tmp/tb_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.f.close()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for ln in open(self.path):
+                p = [v.strip() for v in ln.split(",")]
+                if len(p) < 9:
+                    continue
+                try:
+                    sm.append(float(p[1]))
+                    mx = float(p[2])
+                except ValueError:
+                    continue
+                for nme, v in zip(names, p[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(nme)
+        except OSError:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        load = [v for v in sm if mx and v >= 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample(items, budget_s: float, nthreads: int, repeat: int = 1):
+    """Time the reference CPU path on a row sample of every matrix; returns (GB/s, info)."""
+    from oracle.oracle import Reference
+    ref = Reference()
+    # calibrate: 1% of rows of the largest matrix of each type
+    xs = {}
+    rate = {}
+    for name, qt, M, K, W in items:
+        if qt in rate:
+            continue
+        x = synth.activations(K, seed=SEED + K)
+        xs[K] = x
+        rows = max(nthreads, M // 200)
+        rb = Q.row_bytes(qt, K)
+        t, _ = ref.time_matvec(REF_PATH[qt], qt, W[:rows * rb], rows, K, rb, x, nthreads, 1)
+        rate[qt] = rows * rb / max(t, 1e-9)
+    total_bytes = sum(M * Q.row_bytes(qt, K) for _, qt, M, K, _ in items)
+    est_full = sum(M * Q.row_bytes(qt, K) / rate[qt] for _, qt, M, K, _ in items)
+    frac = min(1.0, budget_s / max(est_full, 1e-9))
+    tot_b, tot_t = 0, 0.0
+    for name, qt, M, K, W in items:
+        rb = Q.row_bytes(qt, K)
+        rows = max(min(M, nthreads), int(M * frac))
+        x = xs.get(K)
+        if x is None:
+            x = xs[K] = synth.activations(K, seed=SEED + K)
+        t, _ = ref.time_matvec(REF_PATH[qt], qt, W[:rows * rb], rows, K, rb, x, nthreads, repeat)
+        tot_b += rows * rb + 4 * K + 4 * rows
+        tot_t += t
+    info = {"rows_fraction": round(frac, 5), "bytes": tot_b, "seconds": round(tot_t, 3),
+            "variant": ref.variant, "of_total_bytes": total_bytes}
+    return tot_b / tot_t / 1e9, info
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    items, _ = workload(0, 1)
+    nthreads = os.cpu_count() or 1
+    budget = float(os.environ.get("TB_REF_STEP_SECONDS", "4"))
+    for _ in range(args.warmup):
+        cpu_sample(items, budget / 4, nthreads)
+    rates, info = [], {}
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r, info = cpu_sample(items, budget, nthreads)
+        rates.append(r)
+    wall = time.perf_counter() - t0
+    value = statistics.median(rates)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * wall / max(args.steps, 1), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "qwen3-4b-shape per-type matvec sweep (BASELINE config 2 + Q4_K)",
+                   "types": [Q.NAMES[t] for t in TYPES], "shapes": SHAPES},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nthreads, "kind": "reference",
+                         "sample": f"{info.get('rows_fraction')} of every matrix's rows per step "
+                                   f"({info.get('bytes')} B), reference routines per BASELINE.md s3, "
+                                   f"{info.get('variant')} build"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    from trailblaze_b200 import load
+    k = load()
+    assert k.tb_cuda_init() == 1
+
+    t_gen = time.perf_counter()
+    items, xs_host = workload(rank, world)
+    log(f"[bench] rank {rank}: generated {sum(w.nbytes for *_, w in items) / 1e9:.2f} GB in "
+        f"{time.perf_counter() - t_gen:.1f}s")
+    stream = torch.cuda.Stream()
+    dW = [torch.from_numpy(w).cuda() for *_, w in items]
+    dx = {K: torch.from_numpy(x).cuda() for K, x in xs_host.items()}
+    dy = [torch.empty(M, dtype=torch.float32, device="cuda") for _, _, M, _, _ in items]
+    torch.cuda.synchronize()
+    alg = [Q.alg_bytes(qt, M, K) for _, qt, M, K, _ in items]
+    step_bytes = sum(alg)
+
+    def step(s):
+        for i, (_, qt, M, K, _) in enumerate(items):
+            r = k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), s)
+            assert r == 1
+
+    sh = stream.cuda_stream
+    with torch.cuda.stream(stream):
+        step(sh)   # sets kernel attributes before capture
+    torch.cuda.synchronize()
+    assert k.tb_cuda_last_error() == 0
+    n0 = k.tb_cuda_launch_count()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step(stream.cuda_stream)
+    launches_per_step = k.tb_cuda_launch_count() - n0
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    assert k.tb_cuda_last_error() == 0
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        time.sleep(0.3)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                g.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = ev0.elapsed_time(ev1)
+    assert k.tb_cuda_last_error() == 0
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * step_bytes / (ms_step * 1e-3) / 1e9
+
+    # ---- per-launch timing of the same launches (events on the launching stream) ----
+    per = np.zeros(len(items))
+    reps = max(3, min(args.steps, 10))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            for i, (_, qt, M, K, _) in enumerate(items):
+                evs[i][0].record(stream)
+                k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), sh)
+                evs[i][1].record(stream)
+            torch.cuda.synchronize()
+            for i in range(len(items)):
+                per[i] += evs[i][0].elapsed_time(evs[i][1])
+    per /= reps
+    # dominant kernel: a (type) instantiation, ranked by its share of the step
+    by_type = {}
+    for i, (name, qt, M, K, _) in enumerate(items):
+        by_type.setdefault(qt, []).append(i)
+    top_qt = max(by_type, key=lambda q: sum(per[i] for i in by_type[q]))
+    top_i = max(by_type[top_qt], key=lambda i: per[i])
+    hbm, hbm_kind = peaks()
+    ach = alg[top_i] / (per[top_i] * 1e-3) / 1e9
+    traffic = None
+    tf = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        try:
+            traffic = json.load(open(tf)).get(items[top_i][0])
+        except ValueError:
+            traffic = None
+    per_mv = {items[i][0]: {"us": round(per[i] * 1e3, 2), "GBps": round(alg[i] / (per[i] * 1e-3) / 1e9, 1),
+                            "frac_hbm": round(alg[i] / (per[i] * 1e-3) / 1e9 / hbm, 3)} for i in range(len(items))}
+
+    # ---- end to end through the blocking reference ABI ----
+    e2e = None
+    if not args.no_e2e:
+        outs = [np.empty(M, dtype=np.float32) for _, _, M, _, _ in items]
+        xh = {K: np.ascontiguousarray(x) for K, x in xs_host.items()}
+        for _ in range(2):
+            for i, (_, qt, M, K, _) in enumerate(items):
+                assert k.tb_cuda_matvec_device(dW[i].data_ptr(), qt, M, K, xh[K], outs[i]) == 1
+        e_steps = max(3, args.steps // 2)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e_steps):
+            for i, (_, qt, M, K, _) in enumerate(items):
+                k.tb_cuda_matvec_device(dW[i].data_ptr(), qt, M, K, xh[K], outs[i])
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([dt], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        e2e = {"value": round(world * step_bytes * e_steps / dt / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": sum(4 * K for _, _, _, K, _ in items),
+               "d2h_bytes_per_step": sum(4 * M for _, _, M, _, _ in items),
+               "api": "tb_cuda_matvec_device (blocking, host x in / host y out)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            hosts = [(n, qt, M, K, w) for n, qt, M, K, w in items]
+            rate, info = cpu_sample(hosts, float(os.environ.get("TB_CPU_SECONDS", "12")), os.cpu_count() or 1)
+            cpu = {"value": round(rate, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"first {info['rows_fraction']} of every matrix's rows ({info['bytes']} B, "
+                             f"{info['seconds']} s), reference routines per BASELINE.md s3, {info['variant']} build"}
+        except Exception as e:  # noqa: BLE001 - the baseline must not sink the GPU line
+            cpu = {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"unavailable: {type(e).__name__}: {e}"}
+
+    clocks = clk.summary()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded; trailblaze_b200.synth)",
+        "config": {"workload": "qwen3-4b-shape per-type matvec sweep (BASELINE config 2 + Q4_K)",
+                   "types": [Q.NAMES[t] for t in TYPES], "shapes": SHAPES,
+                   "bytes_per_step_per_gpu": step_bytes,
+                   "l2": "no flush: each step streams 1.99 GB > 126 MB L2 before a tensor is re-read",
+                   "parallelism": f"row-sharded x{world}, no data-path collective",
+                   "timing": "CUDA graph of one step, CUDA events, max over ranks"},
+        "frac_of_8TBps": round(value / world / 8000.0, 4),
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "kernel": f"k_matvec<{Q.NAMES[top_qt]}> on {items[top_i][0]}",
+                     "achieved": round(ach, 1), "peak": hbm, "peak_kind": hbm_kind, "unit": "GB/s",
+                     "frac": round(ach / hbm, 4), "traffic": traffic,
+                     "alg_bytes_per_launch": alg[top_i]},
+        "per_matvec": per_mv,
+        "clocks": clocks,
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,115 @@
+/*
+ * include/tb_gguf_dequant.h — C ABI of libtb_cuda_sm100.so, the B200 (sm_100a)
+ * GGUF K-quant dequant x fp32 matrix-vector library.
+ *
+ * Part 1 is a drop-in for Trailblaze's layer4/tb_gguf_dequant.h:19-43: the
+ * same eight symbols with the same argument meaning, return codes and
+ * ownership, so layer4/tb_gguf.c and layer4/tb_infer.c built with -DTB_CUDA
+ * link against this library unchanged.  Part 2 adds stream-ordered
+ * device-pointer entry points that have no reference counterpart.
+ *
+ * Conventions (shared with the reference):
+ *   - int returns are 1 = success, 0 = failure (the caller may fall back);
+ *     pointer returns are NULL on failure.  Nothing in the library aborts.
+ *   - qtype ids are ggml's: 0 F32, 1 F16, 2 Q4_0, 8 Q8_0, 10 Q2_K, 11 Q3_K,
+ *     12 Q4_K, 13 Q5_K, 14 Q6_K, 15 Q8_K, 21 IQ3_S (decoded as Q3_K, as the
+ *     reference does), 30 BF16.
+ *   - W is M rows of K weights, each row exactly K/block_weights blocks of
+ *     raw GGUF bytes, rows contiguous.  K must be a multiple of the
+ *     block size (256 for K-quants, 32 for Q4_0/Q8_0, 1 for F32/F16/BF16);
+ *     other K are rejected with 0 (the reference truncates silently).
+ *   - Results: y[m] = sum_k dequant(W)[m,k] * x[k] with fp32 x and fp32
+ *     accumulation; dequantisation follows the reference CUDA kernels bit for
+ *     bit (tb_gguf_dequant.cu:89-332), and Q2_K follows tb_gguf.c:210-225.
+ *   - The library computes on the GPU only.  There is no CPU fallback inside
+ *     it: the caller's own fallback (tb_gguf.c:449-451) stays where it is.
+ */
+#ifndef TB_GGUF_DEQUANT_B200_H
+#define TB_GGUF_DEQUANT_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ───────────── Part 1: the reference ABI (tb_gguf_dequant.h:19-43) ───────── */
+
+/* Replaces tb_gguf_dequant.h:19 / tb_gguf_dequant.cu:388-400.  Binds the
+ * calling thread's current CUDA device (device 0 unless the host selected
+ * another), creates the library stream and staging buffers.  1 = ok. */
+int   tb_cuda_init(void);
+
+/* Replaces tb_gguf_dequant.h:22 / .cu:411-416.  Allocates byte_count bytes of
+ * HBM and copies host_data into it synchronously; the host keeps ownership of
+ * host_data.  Returns the device pointer or NULL. */
+void *tb_cuda_upload_tensor(const void *host_data, size_t byte_count);
+
+/* Replaces tb_gguf_dequant.h:23 / .cu:418.  NULL-safe. */
+void  tb_cuda_free_tensor(void *d_ptr);
+
+/* Replaces tb_gguf_dequant.h:27 / .cu:403-409.  Copies x into the library's
+ * device-resident activation buffer.  A following tb_cuda_matvec_device call
+ * with x_host == NULL uses it, so one upload serves every matvec of a step
+ * (the reference declares this but never reads the buffer).  1 = ok. */
+int   tb_cuda_upload_x(const float *x_host, int K);
+
+/* Replaces tb_gguf_dequant.h:31 / .cu:420.  The argument is the reference's
+ * `const TBOscSnapshot *` (a pointer, so the ABI is identical); it is accepted
+ * and ignored.  Launch geometry never depends on it (the reference's
+ * oscillator-driven grid skips rows, tb_gguf_dequant.cu:378-384). */
+void  tb_cuda_set_snap(const void *snap);
+
+/* Replaces tb_gguf_dequant.h:36-37 / .cu:422-472.  Blocking: copies x_host
+ * (K floats; NULL = the buffer from tb_cuda_upload_x) to the device, runs the
+ * matvec on W_device (device pointer, any byte alignment, e.g. an expert's
+ * row offset into a packed tensor), and copies M floats into out_host.
+ * 1 = out_host filled; 0 = unsupported qtype/shape or a CUDA error. */
+int   tb_cuda_matvec_device(const void *W_device, int qtype, int M, int K,
+                            const float *x_host, float *out_host);
+
+/* Replaces tb_gguf_dequant.h:40 / .cu:474-476.  Waits for all library work. */
+void  tb_cuda_sync_all(void);
+
+/* Replaces tb_gguf_dequant.h:43 / .cu:478-486.  Frees staging buffers and the
+ * stream; safe to call twice; tb_cuda_init may be called again afterwards. */
+void  tb_cuda_cleanup(void);
+
+/* ───────────── Part 2: additive entry points (no reference counterpart) ─── */
+
+/* Stream-ordered matvec on device pointers: d_y[M] = dequant(W_dev) @ d_x[K].
+ * No host synchronisation; `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  Returns 1 if the launch was issued, 0 on bad arguments or a launch
+ * error.  Device-side failures (a bounded wait that ran out) are reported by
+ * tb_cuda_last_error().  The tb_gguf_tensor_matvec call site
+ * (tb_gguf.c:444-451) and the MoE expert call sites (tb_infer.c:810-816) map
+ * onto this with d_data (+ a byte offset) as W_dev. */
+int   tb_cuda_matvec_dev(const void *W_dev, int qtype, int M, int K,
+                         const float *d_x, float *d_y, void *stream);
+
+/* Bit-exact dequantisation of M rows of K weights into d_out[M*K] (fp32),
+ * stream-ordered.  sem = 0 gives the reference CUDA-kernel semantics (the
+ * parity contract); sem = 1 gives layer4/tb_gguf.c's shipped decoders, which
+ * differ for Q4_K (tb_gguf.c:163-168) and Q5_K (tb_gguf.c:139).  1 = issued. */
+int   tb_cuda_dequant_dev(const void *W_dev, int qtype, int M, int K,
+                          float *d_out, int sem, void *stream);
+
+/* Block geometry of a qtype: weights and bytes per block.  1 = known qtype. */
+int   tb_cuda_qtype_info(int qtype, int *block_weights, int *block_bytes);
+
+/* Synchronises the device, then returns and clears the library's device error
+ * word: 0 = none, 1 = a pipeline wait ran out of its iteration limit,
+ * 2 = a CUDA runtime error was seen by a blocking call. */
+int   tb_cuda_last_error(void);
+
+/* Number of matvec / dequant kernel launches the library has issued since
+ * load (a host-side counter, for launch accounting in benchmarks). */
+unsigned long long tb_cuda_launch_count(void);
+
+/* Library build identifier, e.g. "tb_cuda_sm100 1.0 sm_100a". */
+const char *tb_cuda_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TB_GGUF_DEQUANT_B200_H */

@@ -1,0 +1,108 @@
+"""Python mirror of the Trailblaze dequant ABI (layer4/tb_gguf_dequant.h).
+
+Method names and argument meaning follow the C entry points one for one
+(tb_cuda_init, tb_cuda_upload_tensor, tb_cuda_matvec_device, ...), and so does
+error behaviour: calls return the C return code (1 / 0, pointer / 0) instead of
+raising, exactly like the reference's callers see them, except where a Python
+caller would have no way to see a failure (a ctypes argument error raises).
+Every compute call goes to libtb_cuda_sm100.so.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import qtypes as Q
+from ._lib import lib
+
+_fp = ctypes.POINTER(ctypes.c_float)
+
+
+def _fptr(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_fp)
+
+
+class KQuantLib:
+    """Thin wrapper over the C ABI (one per process; the library is process-global)."""
+
+    def __init__(self):
+        self.L = lib()
+
+    # ---- part 1: the reference ABI ------------------------------------------------
+    def tb_cuda_init(self) -> int:
+        return self.L.tb_cuda_init()
+
+    def tb_cuda_upload_tensor(self, host: np.ndarray) -> int:
+        host = np.ascontiguousarray(host)
+        p = self.L.tb_cuda_upload_tensor(host.ctypes.data_as(ctypes.c_void_p), host.nbytes)
+        return int(p or 0)
+
+    def tb_cuda_free_tensor(self, d_ptr: int) -> None:
+        self.L.tb_cuda_free_tensor(ctypes.c_void_p(d_ptr) if d_ptr else None)
+
+    def tb_cuda_upload_x(self, x: np.ndarray) -> int:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        return self.L.tb_cuda_upload_x(_fptr(x), x.size)
+
+    def tb_cuda_set_snap(self, snap_ptr: int | None) -> None:
+        self.L.tb_cuda_set_snap(ctypes.c_void_p(snap_ptr) if snap_ptr else None)
+
+    def tb_cuda_matvec_device(self, W_dev: int, qtype: int, M: int, K: int,
+                              x: np.ndarray | None, out: np.ndarray) -> int:
+        if x is not None:
+            x = np.ascontiguousarray(x, dtype=np.float32)
+        return self.L.tb_cuda_matvec_device(ctypes.c_void_p(W_dev), qtype, M, K, _fptr(x), _fptr(out))
+
+    def tb_cuda_sync_all(self) -> None:
+        self.L.tb_cuda_sync_all()
+
+    def tb_cuda_cleanup(self) -> None:
+        self.L.tb_cuda_cleanup()
+
+    # ---- part 2: device-pointer entry points ------------------------------------------
+    def tb_cuda_matvec_dev(self, W_dev: int, qtype: int, M: int, K: int, d_x: int, d_y: int,
+                           stream: int = 0) -> int:
+        return self.L.tb_cuda_matvec_dev(ctypes.c_void_p(W_dev), qtype, M, K, ctypes.c_void_p(d_x),
+                                         ctypes.c_void_p(d_y), ctypes.c_void_p(stream or None))
+
+    def tb_cuda_dequant_dev(self, W_dev: int, qtype: int, M: int, K: int, d_out: int, sem: int = 0,
+                            stream: int = 0) -> int:
+        return self.L.tb_cuda_dequant_dev(ctypes.c_void_p(W_dev), qtype, M, K, ctypes.c_void_p(d_out),
+                                          sem, ctypes.c_void_p(stream or None))
+
+    def tb_cuda_qtype_info(self, qtype: int) -> tuple[int, int] | None:
+        bw, bb = ctypes.c_int(), ctypes.c_int()
+        if not self.L.tb_cuda_qtype_info(qtype, ctypes.byref(bw), ctypes.byref(bb)):
+            return None
+        return bw.value, bb.value
+
+    def tb_cuda_last_error(self) -> int:
+        return self.L.tb_cuda_last_error()
+
+    def tb_cuda_launch_count(self) -> int:
+        return int(self.L.tb_cuda_launch_count())
+
+    def tb_cuda_version(self) -> str:
+        return self.L.tb_cuda_version().decode()
+
+    # ---- convenience ------------------------------------------------------------------
+    def matvec(self, W_dev: int, qtype: int, M: int, K: int, x: np.ndarray) -> np.ndarray:
+        """Blocking y = dequant(W) @ x through tb_cuda_matvec_device; raises on a 0 return."""
+        out = np.empty(M, dtype=np.float32)
+        if not self.tb_cuda_matvec_device(W_dev, qtype, M, K, x, out):
+            raise RuntimeError(f"tb_cuda_matvec_device failed ({Q.NAMES.get(qtype, qtype)} {M}x{K})")
+        return out
+
+
+_singleton: KQuantLib | None = None
+
+
+def load() -> KQuantLib:
+    global _singleton
+    if _singleton is None:
+        _singleton = KQuantLib()
+    return _singleton
