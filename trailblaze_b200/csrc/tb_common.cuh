@@ -3,10 +3,12 @@
 // Block geometry follows the reference (layer4/tb_gguf_dequant.cu:37-47,
 // layer4/tb_gguf.c:380-393).  A "unit" is the piece of a row that one lane of
 // the matvec kernel decodes: one 256-weight super-block for the K-quants, eight
-// 32-weight blocks for Q4_0/Q8_0, and 256 elements for F32/F16/BF16.
+// 32-weight blocks for Q4_0/Q8_0, and 64 elements for F32/F16/BF16 (so a stage
+// of 32 units stays a few KB for every type).
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace tb {
@@ -21,14 +23,14 @@ enum DevErr : int { ERR_NONE = 0, ERR_WAIT_TIMEOUT = 1, ERR_RUNTIME = 2 };
 struct Geom {
     int block_weights;   // weights per block
     int block_bytes;     // bytes per block
-    int unit_blocks;     // blocks per matvec unit (256 weights)
+    int unit_blocks;     // blocks per matvec unit (256 weights; 64 for F32/F16/BF16)
 };
 
 __host__ __device__ constexpr Geom geom_of(int qt)
 {
-    return qt == QT_F32   ? Geom{1, 4, 256}
-         : qt == QT_F16   ? Geom{1, 2, 256}
-         : qt == QT_BF16  ? Geom{1, 2, 256}
+    return qt == QT_F32   ? Geom{1, 4, 64}
+         : qt == QT_F16   ? Geom{1, 2, 64}
+         : qt == QT_BF16  ? Geom{1, 2, 64}
          : qt == QT_Q4_0  ? Geom{32, 18, 8}
          : qt == QT_Q8_0  ? Geom{32, 34, 8}
          : qt == QT_Q2_K  ? Geom{256, 84, 1}
@@ -55,6 +57,20 @@ __device__ __forceinline__ float h2f_ref(uint32_t h)
 }
 
 __device__ __forceinline__ float bf2f(uint32_t b) { return __uint_as_float(b << 16); }
+
+// The two fp16 halves of w through the same reference converter, for the matvec
+// path: the hardware conversion, then the exponent-0 rule (m*2^-136 where IEEE
+// gives m*2^-24, i.e. a factor 2^-112, exact as an fp32 subnormal).  Finite
+// values and infinities are bit-identical to h2f_ref; a NaN stays a NaN (its
+// payload can differ, which no product with it can show).
+__device__ __forceinline__ float2 h2f2_ref(uint32_t w)
+{
+    float2 f = __half22float2(__halves2half2(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)),
+                                             __ushort_as_half(static_cast<unsigned short>(w >> 16))));
+    f.x *= (w & 0x00007C00u) ? 1.0f : 0x1p-112f;
+    f.y *= (w & 0x7C000000u) ? 1.0f : 0x1p-112f;
+    return f;
+}
 
 // ── 32-bit fast division by a runtime-constant divisor (Granlund–Montgomery,
 //    "round-up" form).  Exact for every 32-bit numerator.                   ──

@@ -1,461 +1,615 @@
-// tb_decoders.cuh — per-type unit decoders of the sm_100a matvec.
+// tb_decoders.cuh — per-type row decoders of the sm_100a matvec.
 //
-// Each decoder returns sum_i w_i * x_i over one unit (256 weights) whose raw
-// bytes sit in shared memory, for the reference decode semantics of
+// The matvec kernel gives every thread ("lane") a fixed run of GPL consecutive
+// 32-weight groups of a row (a column slot) for the whole launch.  The lane's
+// activations for that slot live in registers (struct Lane, filled once by
+// load()), and row_dot() returns sum_i w_i * x_i over the slot for one row whose
+// raw GGUF bytes are staged in shared memory.  Decode semantics are those of
 // layer4/tb_gguf_dequant.cu:89-332 (Q2_K: layer4/tb_gguf.c:210-225).
 //
-// Integer fields become floats without any int->float conversion.  A field of
-// value q masked in place at bit position P (P + width <= 24) of a 32-bit word
-// is, read as an fp32 bit pattern, exactly q * 2^(P-149): a subnormal, or for
-// P + width = 24 the first normal binade, which has the same spacing.  The
-// activation is stored prescaled by 2^(149-P-C) for the P at which its weight's
-// field is extracted, so every product is q*x*2^-C exactly as fp32 rounds q*x,
-// and one power-of-two factor 2^C per group undoes the scale.  Per weight that
-// is one LOP3 plus half of an FFMA2 (the sm_100 paired fp32 FMA).  The kernels
-// are built without -ftz, so subnormal operands keep their value.
+// Two arithmetic paths:
 //
-// Position patterns (field index m inside its 32-bit word; fields at bits 24+
-// are first moved down by 8 with one shift per word):
-//   P4(m) = m<6 ? 4m : 4m-8    nibbles  (8 per word)
-//   P2(m) = m<12 ? 2m : 2m-8   2-bit    (16 per word)
-//   P1(m) = m<24 ? m : m-8     1-bit    (32 per word)
-//   P8(m) = m<3 ? 8m : 16      bytes    (4 per word)
+// * Integer path (Q4_K, Q5_K, Q6_K, Q2_K, Q8_0, Q4_0, Q8_K).  Each group's 32
+//   activations are written exactly as X_i * 2^(E-20), E the exponent of the
+//   group's largest |x|, X_i = round(x_i * 2^(20-E)) a 22-bit integer, and X_i
+//   is split into three int8 digits X = H*2^14 + M*2^7 + L (H in [-128,127],
+//   M, L in [0,127]).  The quant fields are masked four at a time into the
+//   bytes of a word and multiplied against packed digits with dp4a (4 int8
+//   MACs per instruction, exact int32 sums); one group's sums are combined in
+//   fp32 and scaled by the block scales.  The only approximation is the
+//   rounding of x to 2^-21 of its group's largest magnitude, below fp32's own
+//   accumulation error for 32-term sums; products and sums are exact.
+//   Digits are packed in the byte order in which a type's fields come out of
+//   their words (see pk_index), so no field is ever moved after masking.
+//
+// * Float path (Q3_K, F32, F16, BF16), one group per lane.  A field of value q
+//   masked in place at bit position P (P + width <= 24) of a 32-bit word is,
+//   read as an fp32 bit pattern, exactly q * 2^(P-149) (a subnormal, or the
+//   first normal binade, which has the same spacing).  Activations are stored
+//   prescaled by 2^(149-P-C) for the position of their field, so every product
+//   is q*x*2^-C with fp32 rounding; one power of two per group undoes the scale.
+//   The library is built without -ftz, so subnormal operands keep their value.
 #pragma once
 
 #include "tb_common.cuh"
 
 namespace tb {
 
-constexpr int XC = 100;                   // common product scale exponent
-constexpr int XSTRIDE = 260;              // floats per unit in a staged x array (256 + bank skew)
+constexpr int XC = 100;   // product scale exponent of the float path
 
-__host__ __device__ constexpr int P4(int m) { return m < 6 ? 4 * m : 4 * m - 8; }
 __host__ __device__ constexpr int P2(int m) { return m < 12 ? 2 * m : 2 * m - 8; }
-__host__ __device__ constexpr int P1(int m) { return m < 24 ? m : m - 8; }
-__host__ __device__ constexpr int P8(int m) { return m < 3 ? 8 * m : 16; }
 
 // 2^e as an fp32 bit pattern, e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __uint_as_float(uint32_t(127 + e) << 23); }
-
 __device__ __forceinline__ float fbits(uint32_t v) { return __uint_as_float(v); }
-
-// small unsigned integer (< 2^23) to float, exact, without I2F
-__device__ __forceinline__ float u2f_small(uint32_t v)
-{
-    return __uint_as_float(0x4B000000u | v) - 8388608.0f;
-}
-
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
-
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-
-// ---- field extraction + paired FMA over one word ---------------------------
-// 8 nibbles of w against x[0..7] (prescaled with P4); two accumulators.
-__device__ __forceinline__ void acc_nib8(uint32_t w, const float *x, float2 &a0, float2 &a1)
-{
-    const float4 xl = *reinterpret_cast<const float4 *>(x);
-    const float4 xh = *reinterpret_cast<const float4 *>(x + 4);
-    const uint32_t w8 = w >> 8;
-    a0 = ffma2(f2(fbits(w & 0xFu), fbits(w & 0xF0u)), f2(xl.x, xl.y), a0);
-    a1 = ffma2(f2(fbits(w & 0xF00u), fbits(w & 0xF000u)), f2(xl.z, xl.w), a1);
-    a0 = ffma2(f2(fbits(w & 0xF0000u), fbits(w & 0xF00000u)), f2(xh.x, xh.y), a0);
-    a1 = ffma2(f2(fbits(w8 & 0xF0000u), fbits(w8 & 0xF00000u)), f2(xh.z, xh.w), a1);
-}
-
-// 16 two-bit fields of w against x[0..15] (prescaled with P2).
-__device__ __forceinline__ void acc_2b16(uint32_t w, const float *x, float2 &a0, float2 &a1)
-{
-    const float4 x0 = *reinterpret_cast<const float4 *>(x);
-    const float4 x1 = *reinterpret_cast<const float4 *>(x + 4);
-    const float4 x2 = *reinterpret_cast<const float4 *>(x + 8);
-    const float4 x3 = *reinterpret_cast<const float4 *>(x + 12);
-    const uint32_t w8 = w >> 8;
-    a0 = ffma2(f2(fbits(w & 0x3u), fbits(w & 0xCu)), f2(x0.x, x0.y), a0);
-    a1 = ffma2(f2(fbits(w & 0x30u), fbits(w & 0xC0u)), f2(x0.z, x0.w), a1);
-    a0 = ffma2(f2(fbits(w & 0x300u), fbits(w & 0xC00u)), f2(x1.x, x1.y), a0);
-    a1 = ffma2(f2(fbits(w & 0x3000u), fbits(w & 0xC000u)), f2(x1.z, x1.w), a1);
-    a0 = ffma2(f2(fbits(w & 0x30000u), fbits(w & 0xC0000u)), f2(x2.x, x2.y), a0);
-    a1 = ffma2(f2(fbits(w & 0x300000u), fbits(w & 0xC00000u)), f2(x2.z, x2.w), a1);
-    a0 = ffma2(f2(fbits(w8 & 0x30000u), fbits(w8 & 0xC0000u)), f2(x3.x, x3.y), a0);
-    a1 = ffma2(f2(fbits(w8 & 0x300000u), fbits(w8 & 0xC00000u)), f2(x3.z, x3.w), a1);
-}
-
-// 16 one-bit fields of w starting at bit `base` (0 or 16) against x[0..15]
-// (prescaled with P1 of the bit index within the word).
-template <int BASE>
-__device__ __forceinline__ void acc_1b16(uint32_t w, const float *x, float2 &a0, float2 &a1)
-{
-    const float4 x0 = *reinterpret_cast<const float4 *>(x);
-    const float4 x1 = *reinterpret_cast<const float4 *>(x + 4);
-    const float4 x2 = *reinterpret_cast<const float4 *>(x + 8);
-    const float4 x3 = *reinterpret_cast<const float4 *>(x + 12);
-    if (BASE == 0) {
-        a0 = ffma2(f2(fbits(w & 0x1u), fbits(w & 0x2u)), f2(x0.x, x0.y), a0);
-        a1 = ffma2(f2(fbits(w & 0x4u), fbits(w & 0x8u)), f2(x0.z, x0.w), a1);
-        a0 = ffma2(f2(fbits(w & 0x10u), fbits(w & 0x20u)), f2(x1.x, x1.y), a0);
-        a1 = ffma2(f2(fbits(w & 0x40u), fbits(w & 0x80u)), f2(x1.z, x1.w), a1);
-        a0 = ffma2(f2(fbits(w & 0x100u), fbits(w & 0x200u)), f2(x2.x, x2.y), a0);
-        a1 = ffma2(f2(fbits(w & 0x400u), fbits(w & 0x800u)), f2(x2.z, x2.w), a1);
-        a0 = ffma2(f2(fbits(w & 0x1000u), fbits(w & 0x2000u)), f2(x3.x, x3.y), a0);
-        a1 = ffma2(f2(fbits(w & 0x4000u), fbits(w & 0x8000u)), f2(x3.z, x3.w), a1);
-    } else {
-        const uint32_t w8 = w >> 8;   // bits 24..31 -> 16..23
-        a0 = ffma2(f2(fbits(w & 0x10000u), fbits(w & 0x20000u)), f2(x0.x, x0.y), a0);
-        a1 = ffma2(f2(fbits(w & 0x40000u), fbits(w & 0x80000u)), f2(x0.z, x0.w), a1);
-        a0 = ffma2(f2(fbits(w & 0x100000u), fbits(w & 0x200000u)), f2(x1.x, x1.y), a0);
-        a1 = ffma2(f2(fbits(w & 0x400000u), fbits(w & 0x800000u)), f2(x1.z, x1.w), a1);
-        a0 = ffma2(f2(fbits(w8 & 0x10000u), fbits(w8 & 0x20000u)), f2(x2.x, x2.y), a0);
-        a1 = ffma2(f2(fbits(w8 & 0x40000u), fbits(w8 & 0x80000u)), f2(x2.z, x2.w), a1);
-        a0 = ffma2(f2(fbits(w8 & 0x100000u), fbits(w8 & 0x200000u)), f2(x3.x, x3.y), a0);
-        a1 = ffma2(f2(fbits(w8 & 0x400000u), fbits(w8 & 0x800000u)), f2(x3.z, x3.w), a1);
-    }
-}
-
-// 4 bytes of w (already biased to unsigned) against x[0..3] (prescaled with P8).
-__device__ __forceinline__ void acc_b4(uint32_t w, const float *x, float2 &a0, float2 &a1)
-{
-    const float4 xv = *reinterpret_cast<const float4 *>(x);
-    a0 = ffma2(f2(fbits(w & 0xFFu), fbits(w & 0xFF00u)), f2(xv.x, xv.y), a0);
-    a1 = ffma2(f2(fbits(w & 0xFF0000u), fbits((w >> 8) & 0xFF0000u)), f2(xv.z, xv.w), a1);
-}
-
 __device__ __forceinline__ float hsum(float2 a0, float2 a1) { return (a0.x + a0.y) + (a1.x + a1.y); }
 
-// 8 six-bit (Q4_K/Q5_K) scales and mins, unpacked four per word.
-// tb_gguf_dequant.cu:103-108: s[j]=sc[j]&63, m[j]=sc[j+4]&63,
-// s[j+4]=(sc[j]>>6)|((sc[j+8]&15)<<2), m[j+4]=(sc[j+4]>>6)|((sc[j+8]>>4)<<2).
-__device__ __forceinline__ void unpack_sm(uint32_t s0, uint32_t s1, uint32_t s2, uint32_t &sl,
-                                          uint32_t &sh, uint32_t &ml, uint32_t &mh)
+// byte b of w placed in the low byte of 0x4B000000 (= 2^23 + byte) minus 2^23:
+// an exact small-integer-to-float conversion with one PRMT and one FADD.
+__device__ __forceinline__ float byte_to_float(uint32_t w, uint32_t b)
 {
-    sl = s0 & 0x3F3F3F3Fu;
-    ml = s1 & 0x3F3F3F3Fu;
-    sh = ((s0 >> 6) & 0x03030303u) | ((s2 << 2) & 0x3C3C3C3Cu);
-    mh = ((s1 >> 6) & 0x03030303u) | ((s2 >> 2) & 0x3C3C3C3Cu);
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + b)) - 8388608.0f;
+}
+__device__ __forceinline__ float sbyte_to_float(uint32_t w, uint32_t b)
+{
+    return static_cast<float>(static_cast<int8_t>((w >> (8 * b)) & 0xFFu));
 }
 
-__device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8 * j)) & 0xFFu; }
+// Where, inside a row, a lane's slot starts.
+struct Pos {
+    uint32_t off;   // byte offset of the block holding the slot's first group
+    uint32_t gi0;   // index of that group inside its block (0..7 for 256-weight blocks)
+    int ng;         // groups of the slot present in the row (GPL, fewer at the row's end)
+    int n;          // weights of the slot's last group present (32, fewer only for floats)
+};
+
+// 32-bit words of a block whose staged copy may start at any byte.
+// A16 = the caller guarantees 16-byte alignment (plain vector loads).
+template <bool A16>
+struct Words {
+    const uint8_t *p;
+    UnitBytes ub;
+    __device__ __forceinline__ explicit Words(const uint8_t *blk) : p(blk), ub(blk) {}
+    __device__ __forceinline__ uint32_t operator()(int i) const
+    {
+        return A16 ? reinterpret_cast<const uint32_t *>(p)[i] : ub.w(i);
+    }
+    __device__ __forceinline__ uint4 q4(int byte_off) const
+    {
+        if (A16) return *reinterpret_cast<const uint4 *>(p + byte_off);
+        const int i = byte_off >> 2;
+        return make_uint4(ub.w(i), ub.w(i + 1), ub.w(i + 2), ub.w(i + 3));
+    }
+};
+
+// Reads the 32 activations of the slot's group `g` from the slot's staged copy
+// `xs` (shared memory); `nv` = activations of the slot that exist (zeros after).
+__device__ __forceinline__ void load_group(const float *xs, int nv, int g, float (&v)[32])
+{
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (32 * g + i < nv) ? xs[32 * g + i] : 0.f;
+}
 
 // ============================================================================
-// Q4_K — 144 B: d,dmin @0, scales @4, qs @16 (tb_gguf_dequant.cu:89-118).
+// Integer path
 // ============================================================================
+
+// Digit packings: the activation index (0..31 in the group) that lands in byte
+// b of packed word w, matching how each field layout is masked:
+//   PK_NIB   nibbles of four 4-byte words: word t<4 low nibbles (w & 0x0F0F0F0F)
+//            = weights 8t+2b, word 4+t high nibbles = weights 8t+2b+1
+//   PK_TWO16 2-bit fields of two 16-weight words: (w >> 2j) & 0x03030303 of
+//            word h = weights 16h + 4b + j, packed at 4h + j
+//   PK_ONE32 bits of one 32-weight word: (w >> j) & 0x01010101 = weights j + 8b
+//   PK_BYTE  bytes in order: weights 4w + b
+enum { PK_NIB = 0, PK_TWO16 = 1, PK_ONE32 = 2, PK_BYTE = 3 };
+
+__host__ __device__ constexpr int pk_index(int pk, int w, int b)
+{
+    return pk == PK_NIB ? 8 * (w & 3) + 2 * b + (w >> 2)
+         : pk == PK_TWO16 ? 16 * (w >> 2) + 4 * b + (w & 3)
+         : pk == PK_ONE32 ? w + 8 * b
+                          : 4 * w + b;
+}
+
+// A lane's activations for GPL groups: NPK digit packings x 3 digits x 8 words.
+template <int GPL, int NPK>
+struct LaneI8 {
+    int dg[GPL][NPK][3][8];
+    float sx[GPL];      // 2^(E-20) per group
+    float X[GPL][2];    // plain fp32 sums of x over each group's two 16-halves
+};
+
+template <int GPL, int PK0, int PK1>
+__device__ __forceinline__ void load_i8(LaneI8<GPL, (PK1 < 0 ? 1 : 2)> &L, const float *xs, int nv)
+{
+#pragma unroll
+    for (int g = 0; g < GPL; ++g) {
+        float v[32];
+        load_group(xs, nv, g, v);
+        float s0 = 0.f, s1 = 0.f, mx = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            s0 += v[i];
+            s1 += v[16 + i];
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+        L.X[g][0] = s0;
+        L.X[g][1] = s1;
+        int E = mx > 0.f ? static_cast<int>((__float_as_uint(mx) >> 23) & 255u) - 127 : 0;
+        E = E < -100 ? -100 : E;
+        const float up = exp2i(20 - E);
+        L.sx[g] = exp2i(E - 20);
+        int H[32], Mi[32], Lo[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            int q = __float2int_rn(v[i] * up);   // |q| <= 2^21
+            q = q > 2097151 ? 2097151 : (q < -2097152 ? -2097152 : q);
+            H[i] = q >> 14;
+            Mi[i] = (q >> 7) & 127;
+            Lo[i] = q & 127;
+        }
+#pragma unroll
+        for (int pk = 0; pk < (PK1 < 0 ? 1 : 2); ++pk) {
+            const int P = pk == 0 ? PK0 : PK1;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                uint32_t a = 0, b = 0, c = 0;
+#pragma unroll
+                for (int byte = 0; byte < 4; ++byte) {
+                    const int i = pk_index(P, w, byte);
+                    a |= (static_cast<uint32_t>(H[i]) & 0xFFu) << (8 * byte);
+                    b |= (static_cast<uint32_t>(Mi[i]) & 0xFFu) << (8 * byte);
+                    c |= (static_cast<uint32_t>(Lo[i]) & 0xFFu) << (8 * byte);
+                }
+                L.dg[g][pk][0][w] = static_cast<int>(a);
+                L.dg[g][pk][1][w] = static_cast<int>(b);
+                L.dg[g][pk][2][w] = static_cast<int>(c);
+            }
+        }
+    }
+}
+
+// Three-digit accumulator: I[d] += fields . digits[d], kept as two independent
+// chains (even / odd adds) so consecutive dp4a do not wait on each other.
+struct Acc3 {
+    int h0 = 0, m0 = 0, l0 = 0, h1 = 0, m1 = 0, l1 = 0;
+    bool odd = false;
+    __device__ __forceinline__ void add(uint32_t f, const int (&d)[3][8], int w)
+    {
+        if (!odd) {
+            h0 = __dp4a(static_cast<int>(f), d[0][w], h0);
+            m0 = __dp4a(static_cast<int>(f), d[1][w], m0);
+            l0 = __dp4a(static_cast<int>(f), d[2][w], l0);
+        } else {
+            h1 = __dp4a(static_cast<int>(f), d[0][w], h1);
+            m1 = __dp4a(static_cast<int>(f), d[1][w], m1);
+            l1 = __dp4a(static_cast<int>(f), d[2][w], l1);
+        }
+        odd = !odd;
+    }
+    // sum_i f_i X_i = H*2^14 + M*2^7 + L as fp32 (exact up to the final rounding)
+    __device__ __forceinline__ float value() const
+    {
+        return fmaf(static_cast<float>(h0 + h1), 16384.f, static_cast<float>((m0 + m1) * 128 + l0 + l1));
+    }
+    // same, combined in int32: valid while |sum f_i H_i| * 2^14 stays below 2^31
+    // (fields below 32 on 32 weights, or below 64 on 16 weights)
+    __device__ __forceinline__ float value_i32() const
+    {
+        return static_cast<float>((h0 + h1) * 16384 + (m0 + m1) * 128 + l0 + l1);
+    }
+};
+
+// Low / high nibbles of a 4-byte word against PK_NIB words t and 4+t.
+__device__ __forceinline__ void nib_word(Acc3 &a, uint32_t w, const int (&d)[3][8], int t)
+{
+    a.add(w & 0x0F0F0F0Fu, d, t);
+    a.add((w >> 4) & 0x0F0F0F0Fu, d, 4 + t);
+}
+
+// The eight 6-bit Q4_K/Q5_K scales (or mins) of one half of a block as 4 bytes.
+// tb_gguf_dequant.cu:103-108: for j<4 s[j] = sc[j]&63; s[j+4] =
+// (sc[j]>>6) | ((sc[j+8]&15)<<2); mins likewise from sc[j+4] and sc[j+8]>>4.
+// Written as one mux so a lane's half needs no branch: with upper = 0 the shift
+// is 0 and the mask keeps all six bits of w_lo; with upper = 1 it keeps the top
+// two bits of w_lo (moved down) and takes four bits of the third word.
+__device__ __forceinline__ uint32_t sm_half(uint32_t w_lo, uint32_t w_hi8, uint32_t upper, bool mins)
+{
+    const uint32_t x = w_lo >> (6u * upper);
+    const uint32_t y = mins ? (w_hi8 >> 2) : (w_hi8 << 2);
+    const uint32_t k = upper ? 0x03030303u : 0x3F3F3F3Fu;
+    return ((x & k) | (y & ~k)) & 0x3F3F3F3Fu;
+}
+
+// ---- Q4_K — 144 B: d,dmin @0, scales @4, qs @16 (tb_gguf_dequant.cu:89-118) ----
+// w = d*s_g*q - dmin*m_g: group sum = d*s_g*sum(q x) - dmin*m_g*sum(x).
 template <bool A16>
 struct DecQ4K {
-    static constexpr int NXA = 1;
-    __device__ static float xmul(int, int i) { return exp2i(149 - P4(i & 7) - XC); }
-
-    __device__ static float dot(const uint8_t *u, int, const float *xa, const float *,
-                                const float *xs16)
+    static constexpr int GPL = 4;
+    using Lane = LaneI8<GPL, 1>;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        uint32_t h0, s0, s1, s2;
-        UnitBytes ub(u);
-        if (A16) {
-            const uint4 h = *reinterpret_cast<const uint4 *>(u);
-            h0 = h.x; s0 = h.y; s1 = h.z; s2 = h.w;
-        } else {
-            h0 = ub.w(0); s0 = ub.w(1); s1 = ub.w(2); s2 = ub.w(3);
-        }
-        const float d = h2f_ref(h0 & 0xFFFFu), dmin = h2f_ref(h0 >> 16);
-        uint32_t sl, sh, ml, mh;
-        unpack_sm(s0, s1, s2, sl, sh, ml, mh);
-        const float dC = d * exp2i(XC);
+        load_i8<GPL, PK_NIB, -1>(L, xs, nv);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    {
+        const Words<A16> W(row + p.off);
+        const uint4 h = W.q4(0);
+        const uint32_t upper = p.gi0 >> 2;
+        const uint32_t sw = sm_half(h.y, h.w, upper, false), mw = sm_half(h.z, h.w, upper, true);
+        const float2 dd = h2f2_ref(h.x);
+        const float d = dd.x, dmin = dd.y;
         float tot = 0.f;
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            uint32_t q[4];
-            if (A16) {
-                const uint4 v = *reinterpret_cast<const uint4 *>(u + 16 + 16 * g);
-                q[0] = v.x; q[1] = v.y; q[2] = v.z; q[3] = v.w;
-            } else {
-#pragma unroll
-                for (int t = 0; t < 4; ++t) q[t] = ub.w(4 + 4 * g + t);
-            }
-            float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) acc_nib8(q[t], xa + 32 * g + 8 * t, a0, a1);
-            const uint32_t sw = g < 4 ? sl : sh, mw = g < 4 ? ml : mh;
-            const float S = dC * u2f_small(byte_of(sw, g & 3));
-            const float Mn = dmin * u2f_small(byte_of(mw, g & 3));
-            const float X = xs16[2 * g] + xs16[2 * g + 1];
-            tot = fmaf(S, hsum(a0, a1), tot);
-            tot = fmaf(-Mn, X, tot);
+        for (int g = 0; g < GPL; ++g) {
+            const uint4 q = W.q4(16 + 16 * (p.gi0 + g));
+            Acc3 a;
+            nib_word(a, q.x, L.dg[g][0], 0);
+            nib_word(a, q.y, L.dg[g][0], 1);
+            nib_word(a, q.z, L.dg[g][0], 2);
+            nib_word(a, q.w, L.dg[g][0], 3);
+            const uint32_t sb = (p.gi0 & 3u) + g;
+            const float S = d * byte_to_float(sw, sb), Mn = dmin * byte_to_float(mw, sb);
+            tot = fmaf(S * L.sx[g], a.value_i32(), tot);
+            tot = fmaf(-Mn, L.X[g][0] + L.X[g][1], tot);
         }
         return tot;
     }
 };
 
-// ============================================================================
-// Q5_K — 176 B: d,dmin @0, scales @4, qh @16, qs @48 (tb_gguf_dequant.cu:158-191).
-// q = nibble | qh_bit<<4; the high bit is accumulated against x*16.
-// ============================================================================
+// ---- Q5_K — 176 B: d,dmin @0, scales @4, qh @16, qs @48 (tb_gguf_dequant.cu:158-191) ----
+// q = nibble | qh_bit<<4; the high bit is masked as 0x10 per byte (already x16).
 template <bool A16>
 struct DecQ5K {
-    static constexpr int NXA = 2;
-    __device__ static float xmul(int a, int i)
+    static constexpr int GPL = 2;
+    using Lane = LaneI8<GPL, 2>;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        return a == 0 ? exp2i(149 - P4(i & 7) - XC) : exp2i(149 + 4 - P1(i & 31) - XC);
+        load_i8<GPL, PK_NIB, PK_ONE32>(L, xs, nv);
     }
-
-    __device__ static float dot(const uint8_t *u, int, const float *xa, const float *xb,
-                                const float *xs16)
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
     {
-        uint32_t h0, s0, s1, s2;
-        UnitBytes ub(u);
-        if (A16) {
-            const uint4 h = *reinterpret_cast<const uint4 *>(u);
-            h0 = h.x; s0 = h.y; s1 = h.z; s2 = h.w;
-        } else {
-            h0 = ub.w(0); s0 = ub.w(1); s1 = ub.w(2); s2 = ub.w(3);
-        }
-        const float d = h2f_ref(h0 & 0xFFFFu), dmin = h2f_ref(h0 >> 16);
-        uint32_t sl, sh, ml, mh;
-        unpack_sm(s0, s1, s2, sl, sh, ml, mh);
-        const float dC = d * exp2i(XC);
+        const Words<A16> W(row + p.off);
+        const uint4 h = W.q4(0);
+        const uint32_t upper = p.gi0 >> 2;
+        const uint32_t sw = sm_half(h.y, h.w, upper, false), mw = sm_half(h.z, h.w, upper, true);
+        const float2 dd = h2f2_ref(h.x);
+        const float d = dd.x, dmin = dd.y;
         float tot = 0.f;
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            uint32_t q[4], hb;
-            if (A16) {
-                const uint4 v = *reinterpret_cast<const uint4 *>(u + 48 + 16 * g);
-                q[0] = v.x; q[1] = v.y; q[2] = v.z; q[3] = v.w;
-                hb = *reinterpret_cast<const uint32_t *>(u + 16 + 4 * g);
-            } else {
-#pragma unroll
-                for (int t = 0; t < 4; ++t) q[t] = ub.w(12 + 4 * g + t);
-                hb = ub.w(4 + g);
-            }
-            float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) acc_nib8(q[t], xa + 32 * g + 8 * t, a0, a1);
-            acc_1b16<0>(hb, xb + 32 * g, a0, a1);
-            acc_1b16<16>(hb, xb + 32 * g + 16, a0, a1);
-            const uint32_t sw = g < 4 ? sl : sh, mw = g < 4 ? ml : mh;
-            const float S = dC * u2f_small(byte_of(sw, g & 3));
-            const float Mn = dmin * u2f_small(byte_of(mw, g & 3));
-            const float X = xs16[2 * g] + xs16[2 * g + 1];
-            tot = fmaf(S, hsum(a0, a1), tot);
-            tot = fmaf(-Mn, X, tot);
+        for (int g = 0; g < GPL; ++g) {
+            const uint32_t gi = p.gi0 + g;
+            const uint4 q = W.q4(48 + 16 * gi);
+            const uint32_t hb = W(4 + gi);
+            Acc3 a;
+            nib_word(a, q.x, L.dg[g][0], 0);
+            nib_word(a, q.y, L.dg[g][0], 1);
+            nib_word(a, q.z, L.dg[g][0], 2);
+            nib_word(a, q.w, L.dg[g][0], 3);
+            a.add((hb << 4) & 0x10101010u, L.dg[g][1], 0);
+            a.add((hb << 3) & 0x10101010u, L.dg[g][1], 1);
+            a.add((hb << 2) & 0x10101010u, L.dg[g][1], 2);
+            a.add((hb << 1) & 0x10101010u, L.dg[g][1], 3);
+            a.add(hb & 0x10101010u, L.dg[g][1], 4);
+            a.add((hb >> 1) & 0x10101010u, L.dg[g][1], 5);
+            a.add((hb >> 2) & 0x10101010u, L.dg[g][1], 6);
+            a.add((hb >> 3) & 0x10101010u, L.dg[g][1], 7);
+            const uint32_t sb = (p.gi0 & 3u) + g;
+            const float S = d * byte_to_float(sw, sb), Mn = dmin * byte_to_float(mw, sb);
+            tot = fmaf(S * L.sx[g], a.value_i32(), tot);
+            tot = fmaf(-Mn, L.X[g][0] + L.X[g][1], tot);
         }
         return tot;
     }
 };
 
-// ============================================================================
-// Q6_K — 210 B: ql @0, qh @128, int8 scales @192, d @208 (tb_gguf_dequant.cu:196-217).
-// w = d*sc[i>>4]*(q-32), q = ql nibble | qh 2 bits<<4.
-// ============================================================================
+// ---- Q6_K — 210 B: ql @0, qh @128, int8 scales @192, d @208 (tb_gguf_dequant.cu:196-217) ----
+// w = d*sc[i>>4]*(q-32), q = ql nibble | (qh 2 bits)<<4; the high bits are
+// masked as 0x30 per byte (already x16); each 16-weight half has its own scale.
 struct DecQ6K {
-    static constexpr int NXA = 2;
-    __device__ static float xmul(int a, int i)
+    static constexpr int GPL = 2;
+    using Lane = LaneI8<GPL, 2>;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        return a == 0 ? exp2i(149 - P4(i & 7) - XC) : exp2i(149 + 4 - P2(i & 15) - XC);
+        load_i8<GPL, PK_NIB, PK_TWO16>(L, xs, nv);
     }
-
-    __device__ static float dot(const uint8_t *u, int, const float *xa, const float *xb,
-                                const float *xs16)
+    __device__ static void hi16(Acc3 &a, uint32_t hq, const int (&d)[3][8], int base)
     {
-        UnitBytes ub(u);
-        const float d = h2f_ref(ub.w(52) & 0xFFFFu);
-        const uint32_t sc4[4] = {ub.w(48), ub.w(49), ub.w(50), ub.w(51)};
-        const float C = exp2i(XC);
+        a.add((hq << 4) & 0x30303030u, d, base + 0);
+        a.add((hq << 2) & 0x30303030u, d, base + 1);
+        a.add(hq & 0x30303030u, d, base + 2);
+        a.add((hq >> 2) & 0x30303030u, d, base + 3);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    {
+        const Words<false> W(row + p.off);
+        const float d = h2f2_ref(W(52)).x;
+        const uint32_t scw = W.ub.at(192 + 2 * p.gi0);   // the slot's 2*GPL int8 scales
         float tot = 0.f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const uint32_t l0 = ub.w(2 * j), l1 = ub.w(2 * j + 1), hq = ub.w(32 + j);
-            float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-            acc_nib8(l0, xa + 16 * j, a0, a1);
-            acc_nib8(l1, xa + 16 * j + 8, a0, a1);
-            acc_2b16(hq, xb + 16 * j, a0, a1);
-            const int sc = static_cast<int8_t>(byte_of(sc4[j >> 2], j & 3));
-            const float ds = d * static_cast<float>(sc);
-            tot = fmaf(ds, fmaf(hsum(a0, a1), C, -32.f * xs16[j]), tot);
+        for (int g = 0; g < GPL; ++g) {
+            const uint32_t gi = p.gi0 + g;
+            const uint4 l = W.q4(16 * gi);
+            const uint32_t h0 = W(32 + 2 * gi), h1 = W(33 + 2 * gi);
+            Acc3 a, b;
+            nib_word(a, l.x, L.dg[g][0], 0);
+            nib_word(a, l.y, L.dg[g][0], 1);
+            hi16(a, h0, L.dg[g][1], 0);
+            nib_word(b, l.z, L.dg[g][0], 2);
+            nib_word(b, l.w, L.dg[g][0], 3);
+            hi16(b, h1, L.dg[g][1], 4);
+            const float s0 = sbyte_to_float(scw, 2 * g), s1 = sbyte_to_float(scw, 2 * g + 1);
+            const float t0 = fmaf(a.value_i32(), L.sx[g], -32.f * L.X[g][0]);
+            const float t1 = fmaf(b.value_i32(), L.sx[g], -32.f * L.X[g][1]);
+            tot = fmaf(d * s0, t0, tot);
+            tot = fmaf(d * s1, t1, tot);
         }
         return tot;
     }
 };
 
-// ============================================================================
-// Q3_K — 110 B: hmask @0, qs @32, scales @96, d @108 (tb_gguf_dequant.cu:124-151).
-// S[j] = d*((lo4|hi2<<4)-32) with is=(j<8?j:j-8); w = S[i>>4]*(low2|hbit<<2 - 4).
-// ============================================================================
-struct DecQ3K {
-    static constexpr int NXA = 2;
-    __device__ static float xmul(int a, int i)
-    {
-        return a == 0 ? exp2i(149 - P2(i & 15) - XC) : exp2i(149 + 2 - P1(i & 31) - XC);
-    }
-
-    __device__ static float dot(const uint8_t *u, int, const float *xa, const float *xb,
-                                const float *xs16)
-    {
-        UnitBytes ub(u);
-        // scale bytes 96..107; sub-scales read sr[0..3] and sr[8..9] only
-        const uint32_t r0 = ub.w(24), r2 = ub.w(26);
-        const float d = h2f_ref(ub.w(27) & 0xFFFFu);
-        const float C = exp2i(XC);
-        float S[8];
-#pragma unroll
-        for (int is = 0; is < 8; ++is) {
-            const uint32_t lo_byte = byte_of(r0, is >> 1);
-            const uint32_t lo4 = (lo_byte >> ((is & 1) * 4)) & 15u;
-            const uint32_t hi2 = (byte_of(r2, is >> 2) >> ((is & 3) * 2)) & 3u;
-            S[is] = d * static_cast<float>(static_cast<int>(lo4 | (hi2 << 4)) - 32);
-        }
-        float tot = 0.f;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const uint32_t lq = ub.w(8 + j), hm = ub.w(j >> 1);
-            float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-            acc_2b16(lq, xa + 16 * j, a0, a1);
-            if (j & 1) acc_1b16<16>(hm, xb + 16 * j, a0, a1);
-            else       acc_1b16<0>(hm, xb + 16 * j, a0, a1);
-            tot = fmaf(S[j & 7], fmaf(hsum(a0, a1), C, -4.f * xs16[j]), tot);
-        }
-        return tot;
-    }
-};
-
-// ============================================================================
-// Q2_K — 84 B: scales @0 (lo4 scale, hi4 min), qs @16, d @80, dmin @82
-// (tb_gguf.c:210-225).  w = d*(sc&15)*q - dmin*(sc>>4) per 16 weights.
-// ============================================================================
+// ---- Q2_K — 84 B: scales @0 (lo4 scale, hi4 min), qs @16, d @80, dmin @82 ----
+// (tb_gguf.c:210-225) w = d*(sc&15)*q - dmin*(sc>>4) per 16-weight scale block.
 struct DecQ2K {
-    static constexpr int NXA = 1;
-    __device__ static float xmul(int, int i) { return exp2i(149 - P2(i & 15) - XC); }
-
-    __device__ static float dot(const uint8_t *u, int, const float *xa, const float *,
-                                const float *xs16)
+    static constexpr int GPL = 2;   // the slot's 2*GPL scale bytes are read as one word
+    using Lane = LaneI8<GPL, 1>;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        UnitBytes ub(u);
-        const uint32_t sc4[4] = {ub.w(0), ub.w(1), ub.w(2), ub.w(3)};
-        const uint32_t dd = ub.w(20);
-        const float d = h2f_ref(dd & 0xFFFFu), dmin = h2f_ref(dd >> 16);
-        const float dC = d * exp2i(XC);
+        load_i8<GPL, PK_TWO16, -1>(L, xs, nv);
+    }
+    __device__ static void two16(Acc3 &a, uint32_t q, const int (&d)[3][8], int base)
+    {
+        a.add(q & 0x03030303u, d, base + 0);
+        a.add((q >> 2) & 0x03030303u, d, base + 1);
+        a.add((q >> 4) & 0x03030303u, d, base + 2);
+        a.add((q >> 6) & 0x03030303u, d, base + 3);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    {
+        const Words<false> W(row + p.off);
+        const uint32_t dd = W(20);
+        const float2 df = h2f2_ref(dd);
+        const float d = df.x, dmin = df.y;
+        const uint32_t s01 = W(p.gi0 >> 1);   // the 2*GPL scale bytes of the slot
         float tot = 0.f;
 #pragma unroll
-        for (int g = 0; g < 16; ++g) {
-            float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-            acc_2b16(ub.w(4 + g), xa + 16 * g, a0, a1);
-            const uint32_t sb = byte_of(sc4[g >> 2], g & 3);
-            const float sc = dC * u2f_small(sb & 15u);
-            const float mn = dmin * u2f_small(sb >> 4);
-            tot = fmaf(sc, hsum(a0, a1), tot);
-            tot = fmaf(-mn, xs16[g], tot);
+        for (int g = 0; g < GPL; ++g) {
+            const uint32_t gi = p.gi0 + g;
+            const uint32_t q0 = W(4 + 2 * gi), q1 = W(5 + 2 * gi);
+            Acc3 a, b;
+            two16(a, q0, L.dg[g][0], 0);
+            two16(b, q1, L.dg[g][0], 4);
+            const uint32_t c0 = (s01 >> (16 * g)) & 0xFFu, c1 = (s01 >> (16 * g + 8)) & 0xFFu;
+            const float sc0 = d * byte_to_float(c0 & 15u, 0), mn0 = dmin * byte_to_float(c0 >> 4, 0);
+            const float sc1 = d * byte_to_float(c1 & 15u, 0), mn1 = dmin * byte_to_float(c1 >> 4, 0);
+            tot = fmaf(sc0 * L.sx[g], a.value_i32(), tot);
+            tot = fmaf(sc1 * L.sx[g], b.value_i32(), tot);
+            tot = fmaf(-mn0, L.X[g][0], tot);
+            tot = fmaf(-mn1, L.X[g][1], tot);
         }
         return tot;
     }
 };
 
-// ============================================================================
-// Q8_0 — 34 B / 32 weights, 8 blocks per unit: d @0, int8 qs @2
-// (tb_gguf_dequant.cu:246-262).  Bytes biased by 128 (xor 0x80), bias removed
-// with the block's x sum.
-// ============================================================================
+// ---- Q8_0 — 34 B / 32 weights: d @0, int8 qs @2 (tb_gguf_dequant.cu:246-262) ----
 struct DecQ80 {
-    static constexpr int NXA = 1;
-    __device__ static float xmul(int, int i) { return exp2i(149 - P8(i & 3) - XC); }
-
-    __device__ static float dot(const uint8_t *u, int nblk, const float *xa, const float *,
-                                const float *xs16)
+    static constexpr int GPL = 4;
+    using Lane = LaneI8<GPL, 1>;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        const float C = exp2i(XC);
+        load_i8<GPL, PK_BYTE, -1>(L, xs, nv);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    {
         float tot = 0.f;
-        for (int b = 0; b < nblk; ++b) {
-            const uint8_t *blk = u + 34 * b;
-            UnitBytes hb(blk);
-            UnitBytes qb(blk + 2);
-            const float d = h2f_ref(hb.w(0) & 0xFFFFu);
-            float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
 #pragma unroll
-            for (int t = 0; t < 8; ++t) acc_b4(qb.w(t) ^ 0x80808080u, xa + 32 * b + 4 * t, a0, a1);
-            const float X = xs16[2 * b] + xs16[2 * b + 1];
-            tot = fmaf(d, fmaf(hsum(a0, a1), C, -128.f * X), tot);
+        for (int g = 0; g < GPL; ++g) {
+            if (g >= p.ng) break;
+            const uint8_t *blk = row + p.off + 34 * g;
+            const UnitBytes hb(blk), qb(blk + 2);
+            const float d = h2f2_ref(hb.w(0)).x;
+            Acc3 a;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) a.add(qb.w(t), L.dg[g][0], t);
+            tot = fmaf(d * L.sx[g], a.value(), tot);
         }
         return tot;
     }
 };
 
-// ============================================================================
-// Q4_0 — 18 B / 32 weights, 8 blocks per unit: d @0, qs @2
-// (tb_gguf_dequant.cu:222-241).  w[2t]=d*(lo-8), w[2t+1]=d*(hi-8).
-// ============================================================================
+// ---- Q4_0 — 18 B / 32 weights: d @0, qs @2 (tb_gguf_dequant.cu:222-241) ----
+// w[2t] = d*(lo-8), w[2t+1] = d*(hi-8).
 struct DecQ40 {
-    static constexpr int NXA = 1;
-    __device__ static float xmul(int, int i) { return exp2i(149 - P4(i & 7) - XC); }
-
-    __device__ static float dot(const uint8_t *u, int nblk, const float *xa, const float *,
-                                const float *xs16)
+    static constexpr int GPL = 4;
+    using Lane = LaneI8<GPL, 1>;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        const float C = exp2i(XC);
+        load_i8<GPL, PK_NIB, -1>(L, xs, nv);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    {
         float tot = 0.f;
-        for (int b = 0; b < nblk; ++b) {
-            const uint8_t *blk = u + 18 * b;
-            UnitBytes hb(blk);
-            UnitBytes qb(blk + 2);
-            const float d = h2f_ref(hb.w(0) & 0xFFFFu);
-            float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) acc_nib8(qb.w(t), xa + 32 * b + 8 * t, a0, a1);
-            const float X = xs16[2 * b] + xs16[2 * b + 1];
-            tot = fmaf(d, fmaf(hsum(a0, a1), C, -8.f * X), tot);
+        for (int g = 0; g < GPL; ++g) {
+            if (g >= p.ng) break;
+            const uint8_t *blk = row + p.off + 18 * g;
+            const UnitBytes hb(blk), qb(blk + 2);
+            const float d = h2f2_ref(hb.w(0)).x;
+            Acc3 a;
+            nib_word(a, qb.w(0), L.dg[g][0], 0);
+            nib_word(a, qb.w(1), L.dg[g][0], 1);
+            nib_word(a, qb.w(2), L.dg[g][0], 2);
+            nib_word(a, qb.w(3), L.dg[g][0], 3);
+            tot = fmaf(d, fmaf(a.value_i32(), L.sx[g], -8.f * (L.X[g][0] + L.X[g][1])), tot);
         }
         return tot;
     }
 };
 
-// ============================================================================
-// Q8_K — 292 B: f32 d @0, int8 qs @4, bsums ignored (tb_gguf_dequant.cu:268-284).
-// ============================================================================
+// ---- Q8_K — 292 B: f32 d @0, int8 qs @4, bsums ignored (tb_gguf_dequant.cu:268-284) ----
 struct DecQ8K {
-    static constexpr int NXA = 1;
-    __device__ static float xmul(int, int i) { return exp2i(149 - P8(i & 3) - XC); }
-
-    __device__ static float dot(const uint8_t *u, int, const float *xa, const float *,
-                                const float *xs16)
+    static constexpr int GPL = 4;
+    using Lane = LaneI8<GPL, 1>;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        UnitBytes ub(u);
-        const float d = __uint_as_float(ub.w(0));
-        float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-#pragma unroll 16
-        for (int t = 0; t < 64; ++t) acc_b4(ub.w(1 + t) ^ 0x80808080u, xa + 4 * t, a0, a1);
-        float X = 0.f;
+        load_i8<GPL, PK_BYTE, -1>(L, xs, nv);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    {
+        const Words<false> W(row + p.off);
+        const float d = __uint_as_float(W(0));
+        float tot = 0.f;
 #pragma unroll
-        for (int g = 0; g < 16; ++g) X += xs16[g];
-        return d * fmaf(hsum(a0, a1), exp2i(XC), -128.f * X);
+        for (int g = 0; g < GPL; ++g) {
+            const int b = 1 + 8 * static_cast<int>(p.gi0 + g);
+            Acc3 a;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) a.add(W(b + t), L.dg[g][0], t);
+            tot = fmaf(L.sx[g], a.value(), tot);
+        }
+        return d * tot;
     }
 };
 
 // ============================================================================
-// F32 / F16 / BF16 — 256 elements per unit, `n` valid (the last unit of a row
-// may be partial).  F16 uses the reference converter (tb_gguf_dequant.cu:54-63).
+// Float path
 // ============================================================================
+
+// The lane's 32 activations as 16 register pairs (two prescaled arrays) plus
+// the plain fp32 sums of each 16-half.
+struct XRegs {
+    float2 a[16];
+    float2 b[16];
+    float X0, X1;
+};
+
+template <class MulA, class MulB>
+__device__ __forceinline__ void load_f32(XRegs &L, const float *xs, int nv, MulA ma, MulB mb)
+{
+    float v[32];
+    load_group(xs, nv, 0, v);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        s0 += v[i];
+        s1 += v[16 + i];
+    }
+    L.X0 = s0;
+    L.X1 = s1;
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+        L.a[p] = f2(v[2 * p] * ma(2 * p), v[2 * p + 1] * ma(2 * p + 1));
+        L.b[p] = f2(v[2 * p] * mb(2 * p), v[2 * p + 1] * mb(2 * p + 1));
+    }
+}
+
+// 16 two-bit fields at P2 positions against x pairs O..O+7.
+template <int O>
+__device__ __forceinline__ void two16f(uint32_t w, const float2 (&x)[16], float2 &a0, float2 &a1)
+{
+    const uint32_t w8 = w >> 8;
+    a0 = ffma2(f2(fbits(w & 0x3u), fbits(w & 0xCu)), x[O + 0], a0);
+    a1 = ffma2(f2(fbits(w & 0x30u), fbits(w & 0xC0u)), x[O + 1], a1);
+    a0 = ffma2(f2(fbits(w & 0x300u), fbits(w & 0xC00u)), x[O + 2], a0);
+    a1 = ffma2(f2(fbits(w & 0x3000u), fbits(w & 0xC000u)), x[O + 3], a1);
+    a0 = ffma2(f2(fbits(w & 0x30000u), fbits(w & 0xC0000u)), x[O + 4], a0);
+    a1 = ffma2(f2(fbits(w & 0x300000u), fbits(w & 0xC00000u)), x[O + 5], a1);
+    a0 = ffma2(f2(fbits(w8 & 0x30000u), fbits(w8 & 0xC0000u)), x[O + 6], a0);
+    a1 = ffma2(f2(fbits(w8 & 0x300000u), fbits(w8 & 0xC00000u)), x[O + 7], a1);
+}
+
+// 8 one-bit fields at bits m (m < 8) against x pairs O..O+3.
+template <int O>
+__device__ __forceinline__ void bit8f(uint32_t w, const float2 (&x)[16], float2 &a0, float2 &a1)
+{
+    a0 = ffma2(f2(fbits(w & 0x1u), fbits(w & 0x2u)), x[O + 0], a0);
+    a1 = ffma2(f2(fbits(w & 0x4u), fbits(w & 0x8u)), x[O + 1], a1);
+    a0 = ffma2(f2(fbits(w & 0x10u), fbits(w & 0x20u)), x[O + 2], a0);
+    a1 = ffma2(f2(fbits(w & 0x40u), fbits(w & 0x80u)), x[O + 3], a1);
+}
+
+// ---- Q3_K — 110 B: hmask @0, qs @32, scales @96, d @108 (tb_gguf_dequant.cu:124-151) ----
+// Scale block j uses is = (j<8 ? j : j-8): lo4 = (sc[is>>1] >> 4(is&1)) & 15 =
+// (word24 >> 4is) & 15, hi2 = (sc[8+(is>>2)] >> 2(is&3)) & 3 = (word26 >> 2is) & 3;
+// w = d*((lo4|hi2<<4)-32) * (low2 | hbit<<2 - 4).  The high bit accumulates
+// against x*4 (second array), read 8 bits at a time at positions 0..7.
+struct DecQ3K {
+    static constexpr int GPL = 1;
+    using Lane = XRegs;
+    __device__ static void load(Lane &L, const float *xs, int nv)
+    {
+        load_f32(L, xs, nv, [](int i) { return exp2i(149 - P2(i & 15) - XC); },
+                 [](int i) { return exp2i(149 + 2 - (i & 7) - XC); });
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    {
+        const Words<false> W(row + p.off);
+        const uint32_t hm = W(p.gi0);
+        const uint32_t q0 = W(8 + 2 * p.gi0), q1 = W(9 + 2 * p.gi0);
+        const uint32_t r0 = W(24), r2 = W(26), dw = W(27);
+        float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f), b0 = f2(0.f, 0.f), b1 = f2(0.f, 0.f);
+        two16f<0>(q0, x.a, a0, a1);
+        bit8f<0>(hm, x.b, a0, a1);
+        bit8f<4>(hm >> 8, x.b, a0, a1);
+        two16f<8>(q1, x.a, b0, b1);
+        bit8f<8>(hm >> 16, x.b, b0, b1);
+        bit8f<12>(hm >> 24, x.b, b0, b1);
+        const float d = h2f2_ref(dw).x;
+        const uint32_t j0 = 2 * p.gi0, is0 = j0 < 8 ? j0 : j0 - 8, is1 = is0 + 1;
+        const int v0 = static_cast<int>(((r0 >> (4 * is0)) & 15u) | (((r2 >> (2 * is0)) & 3u) << 4)) - 32;
+        const int v1 = static_cast<int>(((r0 >> (4 * is1)) & 15u) | (((r2 >> (2 * is1)) & 3u) << 4)) - 32;
+        const float S0 = d * static_cast<float>(v0), S1 = d * static_cast<float>(v1);
+        const float C = exp2i(XC);
+        const float t0 = fmaf(hsum(a0, a1), C, -4.f * x.X0);
+        const float t1 = fmaf(hsum(b0, b1), C, -4.f * x.X1);
+        return fmaf(S0, t0, S1 * t1);
+    }
+};
+
+// ---- F32 / F16 / BF16 — `n` valid elements in the slot's group ----
+// F16 uses the reference converter (tb_gguf_dequant.cu:54-63).
 template <int QT>
 struct DecFloat {
-    static constexpr int NXA = 1;
-    __device__ static float xmul(int, int) { return 1.f; }
-
-    __device__ static float dot(const uint8_t *u, int n, const float *xa, const float *,
-                                const float *)
+    static constexpr int GPL = 1;
+    using Lane = XRegs;
+    __device__ static void load(Lane &L, const float *xs, int nv)
     {
-        UnitBytes ub(u);
+        load_f32(L, xs, nv, [](int) { return 1.f; }, [](int) { return 0.f; });
+    }
+    __device__ static float elem(const UnitBytes &ub, int i)
+    {
+        if (QT == QT_F32) return __uint_as_float(ub.w(i));
+        const uint32_t w = ub.w(i >> 1);
+        const uint32_t h = (i & 1) ? (w >> 16) : (w & 0xFFFFu);
+        return QT == QT_F16 ? h2f_ref(h) : __uint_as_float(h << 16);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    {
+        const UnitBytes ub(row + p.off);
         float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-        if (QT == QT_F32) {
-            int i = 0;
-            for (; i + 2 <= n; i += 2)
-                a0 = ffma2(f2(__uint_as_float(ub.w(i)), __uint_as_float(ub.w(i + 1))),
-                           f2(xa[i], xa[i + 1]), a0);
-            if (i < n) a1.x = fmaf(__uint_as_float(ub.w(i)), xa[i], a1.x);
-        } else {
-            int t = 0;
-            for (; 2 * t + 2 <= n; ++t) {
-                const uint32_t w = ub.w(t);
-                const float lo = QT == QT_F16 ? h2f_ref(w & 0xFFFFu) : __uint_as_float(w << 16);
-                const float hi = QT == QT_F16 ? h2f_ref(w >> 16) : __uint_as_float(w & 0xFFFF0000u);
-                a0 = ffma2(f2(lo, hi), f2(xa[2 * t], xa[2 * t + 1]), a0);
+        if (p.n == 32) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                float2 w;
+                if (QT == QT_F32) {
+                    w = f2(__uint_as_float(ub.w(2 * q)), __uint_as_float(ub.w(2 * q + 1)));
+                } else {
+                    const uint32_t v = ub.w(q);
+                    w = QT == QT_F16 ? f2(h2f_ref(v & 0xFFFFu), h2f_ref(v >> 16))
+                                     : f2(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+                }
+                if (q & 1) a1 = ffma2(w, x.a[q], a1);
+                else       a0 = ffma2(w, x.a[q], a0);
             }
-            if (2 * t < n) {
-                const uint32_t w = ub.w(t);
-                const float lo = QT == QT_F16 ? h2f_ref(w & 0xFFFFu) : __uint_as_float(w << 16);
-                a1.x = fmaf(lo, xa[2 * t], a1.x);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                if (2 * q < p.n) a0.x = fmaf(elem(ub, 2 * q), x.a[q].x, a0.x);
+                if (2 * q + 1 < p.n) a0.y = fmaf(elem(ub, 2 * q + 1), x.a[q].y, a0.y);
             }
         }
         return hsum(a0, a1);

@@ -3,21 +3,29 @@
 // Replaces the ten one-CTA-per-row kernels of layer4/tb_gguf_dequant.cu:89-332
 // (plus Q2_K, which the reference lacks).  Layout and schedule:
 //
-//   * W is read as one flat stream of "units" (256 weights of one row; rows are
-//     contiguous, so the stream is W's memory order).  Each CTA owns a
-//     contiguous range of rows; its units are split evenly over its warps.
-//   * Each warp runs its own ring of NST shared-memory stages.  Lane 0 fills a
-//     stage with one 1-D bulk copy (cp.async.bulk, TMA engine, no multicast) of
-//     the next 32 units, widened to 16-byte boundaries, with an L2 evict-first
-//     hint; completion is an mbarrier transaction count.  Every wait is bounded.
-//   * x is staged once per CTA, prescaled for the decoder's bit-field positions
-//     (see tb_decoders.cuh), with 16-element partial sums for the min/offset
-//     terms.
-//   * Lane l decodes unit (it*32 + l); a segmented shuffle reduction by row
-//     combines the lanes, a register carry joins a row across iterations, and
-//     rows that straddle two warps are combined in warp order at the end, so the
-//     summation order is fixed and results are run-to-run deterministic.
+//   * A row of K weights is ceil(K/32) groups of 32, cut into CS column slots
+//     of GPL consecutive groups (GPL per type, tb_decoders.cuh).  Every thread
+//     of a CTA owns one slot for the whole launch: the slot's activations live
+//     in its registers in the decoder's form.  P = floor(threads / CS) rows are
+//     decoded side by side ("phases").  x is read from global memory once per
+//     CTA, coalesced, into shared memory padded by one float per slot (so the
+//     threads' slot reads hit 32 different banks), and from there into
+//     registers; every weight then costs only its own bytes.
+//   * Each CTA owns a contiguous range of rows and streams it in tiles of TR
+//     rows (TR*row_bytes contiguous bytes) through a ring of NST shared-memory
+//     stages.  A stage is filled by one 1-D bulk copy (cp.async.bulk, TMA
+//     engine, no multicast) widened to 16-byte boundaries, with an L2
+//     evict-first hint; completion is an mbarrier transaction count.  Every
+//     wait is bounded.
+//   * There is no CTA-wide barrier per tile.  A row's per-slot partial sums are
+//     added across the 8 (or fewer) consecutive threads of one block by
+//     shuffles and written to a per-stage partial buffer; each warp then takes
+//     a ticket on the stage.  The warp that takes the last ticket sums every
+//     row of the tile in a fixed order, writes y, and refills the stage with
+//     the tile NST ahead.  The summation order never depends on timing, so
+//     results are run-to-run deterministic.
 #include <cstdio>
+#include <cstdlib>
 
 #include "tb_common.cuh"
 #include "tb_decoders.cuh"
@@ -30,251 +38,286 @@ struct MvArgs {
     const float *x;
     float *y;
     int *err;
-    uint32_t M, K, upr;           // rows, columns, units per row
-    uint32_t unit_bytes;          // bytes of a full unit
-    uint32_t last_unit_bytes;     // bytes of a row's last unit
-    uint32_t unit_n, last_unit_n; // blocks (Q4_0/Q8_0) or elements (F*) in full / last unit
+    uint32_t M, K;
     unsigned long long row_bytes;
-    FastDiv fd_upr;
-    uint32_t nst, cap;            // stages per warp, bytes per stage
+    uint32_t block_weights, block_bytes;
+    uint32_t cs;       // column slots per row
+    uint32_t phases;   // rows decoded side by side
+    uint32_t rpl;      // rows per thread per tile
+    uint32_t tr;       // rows per tile (= phases * rpl)
+    uint32_t rw;       // threads pre-reduced by shuffles (1, 2, 4 or 8; divides cs)
+    uint32_t npart;    // partial sums per row (= cs / rw)
+    uint32_t nst;      // stages in the ring
+    uint32_t cap;      // bytes per stage
     uint32_t wait_limit;
 };
 
 static constexpr uint32_t kFull = 0xFFFFFFFFu;
 static constexpr uint32_t kDrainLimit = 1u << 26;
+static constexpr int kMaxThreads = 384;   // up to 168 registers per thread
 
-template <class D, int NW>
-__global__ void __launch_bounds__(NW * 32, 1) k_matvec(const MvArgs a)
+// shared-memory layout: [bars NST][tickets NST][issued] [part NST*TR*NPART] [x staging] [ring]
+__host__ __device__ inline size_t mv_part_offset(uint32_t nst)
+{
+    return (8ull * nst + 4ull * nst + 4 + 15) & ~15ull;
+}
+__host__ __device__ inline size_t mv_x_offset(uint32_t nst, uint32_t tr, uint32_t npart)
+{
+    return (mv_part_offset(nst) + 4ull * nst * tr * npart + 15) & ~15ull;
+}
+__host__ __device__ inline size_t mv_ring_offset(uint32_t nst, uint32_t tr, uint32_t npart, uint32_t xfloats)
+{
+    return (mv_x_offset(nst, tr, npart) + 4ull * xfloats + 127) & ~127ull;
+}
+// floats of the padded x copy: CS slots of 32*GPL activations, one pad float each
+__host__ __device__ inline uint32_t mv_x_floats(uint32_t cs, uint32_t gpl)
+{
+    return cs * (32 * gpl + 1);
+}
+
+template <class D>
+__global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31;
+    const uint32_t nwarps = nthr / 32;
 
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const uint32_t r_lo = static_cast<uint32_t>((static_cast<unsigned long long>(a.M) * c) / G);
     const uint32_t r_hi = static_cast<uint32_t>((static_cast<unsigned long long>(a.M) * (c + 1)) / G);
     if (r_lo >= r_hi) return;
-    const uint32_t U_lo = r_lo * a.upr, U = (r_hi - r_lo) * a.upr;
-    const uint32_t u0 = U_lo + static_cast<uint32_t>((static_cast<unsigned long long>(U) * warp) / NW);
-    const uint32_t u1 = U_lo + static_cast<uint32_t>((static_cast<unsigned long long>(U) * (warp + 1)) / NW);
-    const uint32_t n_it = (u1 - u0 + 31) / 32;
+    const uint32_t n_tiles = (r_hi - r_lo + a.tr - 1) / a.tr;
+    constexpr uint32_t SW = 32u * D::GPL;   // activations per slot
 
-    // ---- shared memory carve-up (mirrors mv_smem_bytes on the host) ----
-    float *xs = reinterpret_cast<float *>(smem);
-    const uint32_t xstride = a.upr * XSTRIDE;
-    float *xs16 = xs + D::NXA * xstride;
-    uintptr_t p = reinterpret_cast<uintptr_t>(xs16 + a.upr * 16);
-    p = (p + 15) & ~uintptr_t(15);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(p);
-    p += sizeof(uint64_t) * NW * a.nst;
-    int2 *bnd = reinterpret_cast<int2 *>(p);
-    p += sizeof(int2) * NW * 2;
-    p = (p + 127) & ~uintptr_t(127);
-    uint8_t *ring = reinterpret_cast<uint8_t *>(p) + static_cast<size_t>(warp) * a.nst * a.cap;
-    uint64_t *mybar = bars + warp * a.nst;
-
-    auto unit_addr = [&](uint32_t u, uint32_t &row, uint32_t &j) -> uintptr_t {
-        row = fdiv(u, a.fd_upr);
-        j = u - row * a.upr;
-        return reinterpret_cast<uintptr_t>(a.W) + row * a.row_bytes +
-               static_cast<unsigned long long>(j) * a.unit_bytes;
-    };
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    int *tickets = reinterpret_cast<int *>(smem + 8ull * a.nst);
+    int *issued = tickets + a.nst;
+    float *part = reinterpret_cast<float *>(smem + mv_part_offset(a.nst));
+    float *xst = reinterpret_cast<float *>(smem + mv_x_offset(a.nst, a.tr, a.npart));
+    uint8_t *ring = smem + mv_ring_offset(a.nst, a.tr, a.npart, mv_x_floats(a.cs, D::GPL));
 
     const uint64_t pol = l2_evict_first_policy();
-    auto issue = [&](uint32_t it) {   // lane 0 only
-        uint32_t r, j;
-        const uint32_t ua = u0 + 32 * it, ub = min(ua + 32, u1) - 1;
-        const uintptr_t g0 = unit_addr(ua, r, j) & ~uintptr_t(15);
-        const uintptr_t gb = unit_addr(ub, r, j);
-        const uintptr_t g1 = (gb + (j == a.upr - 1 ? a.last_unit_bytes : a.unit_bytes) + 15) & ~uintptr_t(15);
+    auto issue = [&](uint32_t it) {   // one thread
+        const uint32_t t0 = r_lo + it * a.tr;
+        const uint32_t nrows = min(a.tr, r_hi - t0);
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(a.W) + t0 * a.row_bytes;
+        const uintptr_t g0 = lo & ~uintptr_t(15);
+        const uintptr_t g1 = (lo + nrows * a.row_bytes + 15) & ~uintptr_t(15);
         const uint32_t s = it % a.nst;
-        const uint32_t bar = smem_u32(mybar + s);
+        const uint32_t bar = smem_u32(bars + s);
         mbar_expect_tx(bar, static_cast<uint32_t>(g1 - g0));
-        bulk_g2s(smem_u32(ring + s * a.cap), reinterpret_cast<const void *>(g0),
+        bulk_g2s(smem_u32(ring + static_cast<size_t>(s) * a.cap), reinterpret_cast<const void *>(g0),
                  static_cast<uint32_t>(g1 - g0), bar, pol);
     };
 
-    if (lane == 0) {
-        for (uint32_t s = 0; s < a.nst; ++s) mbar_init(smem_u32(mybar + s), 1);
+    if (tid == 0) {
+        for (uint32_t s = 0; s < a.nst; ++s) {
+            mbar_init(smem_u32(bars + s), 1);
+            tickets[s] = 0;
+        }
         fence_mbar_init();
-        const uint32_t pre = min(a.nst, n_it);
+        const uint32_t pre = min(a.nst, n_tiles);
         for (uint32_t it = 0; it < pre; ++it) issue(it);
+        *issued = static_cast<int>(pre);
     }
-    if (lane < 2) bnd[warp * 2 + lane] = make_int2(-1, 0);
-    __syncwarp();
 
-    // ---- stage x: prescaled arrays + 16-element sums, zero beyond K ----
-    const uint32_t kpad = a.upr * 256;
-    for (uint32_t k = tid; k < kpad; k += NW * 32) {
-        const float v = k < a.K ? __ldg(a.x + k) : 0.f;
-        const uint32_t jj = k >> 8, i = k & 255;
+    // ---- x: coalesced global read into the padded shared copy ----
+    // eight independent loads per thread in flight before any store
+    for (uint32_t base = 0; base < a.K; base += 8 * nthr) {
+        float v[8];
 #pragma unroll
-        for (int arr = 0; arr < D::NXA; ++arr)
-            xs[arr * xstride + jj * XSTRIDE + i] = v * D::xmul(arr, static_cast<int>(i));
-        float s = v;
-        s += __shfl_xor_sync(kFull, s, 8);
-        s += __shfl_xor_sync(kFull, s, 4);
-        s += __shfl_xor_sync(kFull, s, 2);
-        s += __shfl_xor_sync(kFull, s, 1);
-        if ((lane & 15) == 0) xs16[k >> 4] = s;
+        for (uint32_t u = 0; u < 8; ++u) {
+            const uint32_t k = base + u * nthr + tid;
+            v[u] = k < a.K ? __ldg(a.x + k) : 0.f;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u) {
+            const uint32_t k = base + u * nthr + tid;
+            if (k < a.K) xst[k + k / SW] = v[u];
+        }
     }
-    __syncthreads();
+    __syncthreads();   // x staged; barrier inits and tickets visible
 
-    // ---- main loop ----
-    uint32_t carry_row = kFull;
-    float carry = 0.f;
+    // ---- this thread's column slot and its activations ----
+    const bool active = tid < a.phases * a.cs;
+    const uint32_t cs = active ? tid % a.cs : 0;
+    const uint32_t ph = active ? tid / a.cs : 0;
+    const uint32_t g0 = cs * D::GPL;                 // first group of the slot
+    const uint32_t ngrp = (a.K + 31) / 32;           // groups per row
+    Pos pos;
+    if (a.block_weights == 256) {
+        pos.off = (g0 >> 3) * a.block_bytes;
+        pos.gi0 = g0 & 7u;
+    } else if (a.block_weights == 32) {
+        pos.off = g0 * a.block_bytes;
+        pos.gi0 = 0;
+    } else {
+        pos.off = g0 * 32u * a.block_bytes;
+        pos.gi0 = 0;
+    }
+    pos.ng = static_cast<int>(min(static_cast<uint32_t>(D::GPL), ngrp - min(ngrp, g0)));
+    pos.n = static_cast<int>(min(32u, a.K - min(a.K, 32u * (g0 + pos.ng - 1))));
+    typename D::Lane lane_x;
+    {
+        const int nv = active ? static_cast<int>(min(SW, a.K - min(a.K, 32u * g0))) : 0;
+        D::load(lane_x, xst + cs * (SW + 1), nv);
+    }
+    const uint32_t row_bytes32 = static_cast<uint32_t>(a.row_bytes);   // a tile's rows fit one stage
+    const bool writer = active && (cs % a.rw) == 0;
+    const uint32_t part_col = cs / a.rw;
+
     uint32_t consumed = 0;
-    bool ok = true;
-    for (uint32_t it = 0; it < n_it; ++it) {
-        const uint32_t s = it % a.nst, ph = (it / a.nst) & 1u;
-        const bool got = mbar_wait_bounded(smem_u32(mybar + s), ph, a.err, a.wait_limit);
-        if (!__all_sync(kFull, got)) { ok = false; break; }
+    bool fail = false;
+    for (uint32_t it = 0; it < n_tiles; ++it) {
+        const uint32_t s = it % a.nst;
+        bool got = mbar_wait_bounded(smem_u32(bars + s), (it / a.nst) & 1u, a.err, a.wait_limit);
+        if (!__all_sync(kFull, got)) {
+            fail = true;
+            break;
+        }
         consumed = it + 1;
-
-        const uint32_t ua = u0 + 32 * it;
-        uint32_t r0, j0;
-        const uintptr_t g0 = unit_addr(ua, r0, j0) & ~uintptr_t(15);
-        const uint32_t u = ua + lane;
-        const bool valid = u < u1;
-        uint32_t row = kFull, j = 0;
-        float v = 0.f;
-        if (valid) {
-            const uintptr_t gu = unit_addr(u, row, j);
-            const uint8_t *su = ring + s * a.cap + (gu - g0);
-            const int n = static_cast<int>(j == a.upr - 1 ? a.last_unit_n : a.unit_n);
-            v = D::dot(su, n, xs + j * XSTRIDE, xs + xstride + j * XSTRIDE, xs16 + j * 16);
+        const uint32_t t0 = r_lo + it * a.tr;
+        const uint32_t nrows = min(a.tr, r_hi - t0);
+        float *pb = part + static_cast<size_t>(s) * a.tr * a.npart;
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(a.W) + t0 * a.row_bytes;
+        const uint8_t *sbase = ring + static_cast<size_t>(s) * a.cap + (lo & 15u);
+#pragma unroll 2
+        for (uint32_t i = 0; i < a.rpl; ++i) {
+            const uint32_t rt = ph + i * a.phases;
+            const bool live = active && rt < nrows;
+            float v = 0.f;
+            if (live) v = D::row_dot(sbase + rt * row_bytes32, pos, lane_x);
+#pragma unroll
+            for (uint32_t o = 1; o < 8; o <<= 1)
+                if (o < a.rw) v += __shfl_xor_sync(kFull, v, o);
+            if (writer && rt < nrows) pb[rt * a.npart + part_col] = v;
         }
+        // ticket: the last warp through this tile reduces it and refills the stage
         __syncwarp();
-        if (lane == 0 && it + a.nst < n_it) {
-            fence_proxy_async_smem();   // order this warp's reads of stage s before the refill
-            issue(it + a.nst);
+        int t = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            t = atomicAdd(tickets + s, 1);
         }
-
-        // segmented suffix sum over lanes with equal row (rows are non-decreasing)
-        const uint32_t last_lane = min(31u, u1 - 1 - ua);
-        const uint32_t row_last = __shfl_sync(kFull, row, last_lane);
-        const uint32_t j_last = __shfl_sync(kFull, j, last_lane);
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float t = __shfl_down_sync(kFull, v, o);
-            const uint32_t rr = __shfl_down_sync(kFull, row, o);
-            if (lane + o < 32 && rr == row) v += t;
-        }
-        const uint32_t row_prev = __shfl_up_sync(kFull, row, 1);
-        const bool head = valid && (lane == 0 || row_prev != row);
-        if (lane == 0 && row == carry_row) v += carry;
-        const bool continues = (row == row_last) && (j_last < a.upr - 1);
-        const bool carry_next = (j_last < a.upr - 1) && (ua + last_lane + 1 < u1);
-        const uint32_t heads = __ballot_sync(kFull, head);
-        const int last_head = 31 - __clz(heads);
-        const float last_v = __shfl_sync(kFull, v, last_head);
-        if (head) {
-            const bool started_before = row * a.upr < u0;
-            if (continues && carry_next) {
-                // joins the next iteration through the carry
-            } else if (started_before) {
-                bnd[warp * 2 + 0] = make_int2(static_cast<int>(row), __float_as_int(v));
-            } else if (continues) {
-                bnd[warp * 2 + 1] = make_int2(static_cast<int>(row), __float_as_int(v));
-            } else {
-                a.y[row] = v;
+        t = __shfl_sync(kFull, t, 0);
+        if (t == static_cast<int>(nwarps) - 1) {
+            __threadfence_block();
+            for (uint32_t r = lane; r < nrows; r += 32) {
+                const float *pr = pb + r * a.npart;
+                float acc = 0.f;
+                for (uint32_t j = 0; j < a.npart; ++j) acc += pr[j];
+                a.y[t0 + r] = acc;
             }
-        }
-        if (carry_next) {
-            carry_row = row_last;
-            carry = last_v;
-        } else {
-            carry_row = kFull;
-        }
-    }
-
-    if (!ok && lane == 0) {
-        // A wait ran out: let this warp's copies still in flight land before the
-        // CTA exits (bounded again), leaving the error word set.
-        // The drain limit is fixed and generous (not the caller's wait_limit): the copies were
-        // issued to valid addresses and always land; the CTA must not exit before they do.
-        const uint32_t issued = min(n_it, consumed + a.nst);
-        for (uint32_t it = consumed; it < issued; ++it)
-            mbar_wait_bounded(smem_u32(mybar + it % a.nst), (it / a.nst) & 1u, nullptr, kDrainLimit);
-    }
-    __syncthreads();
-
-    // rows split between warps: combine the partials in warp order
-    if (tid == 0 && ok) {
-        int cur = -1;
-        float acc = 0.f;
-        for (int w = 0; w < NW; ++w) {
-#pragma unroll
-            for (int sl = 0; sl < 2; ++sl) {
-                const int2 e = bnd[w * 2 + sl];
-                if (e.x < 0) continue;
-                if (e.x == cur) {
-                    acc += __int_as_float(e.y);
-                } else {
-                    if (cur >= 0) a.y[cur] = acc;
-                    cur = e.x;
-                    acc = __int_as_float(e.y);
+            __syncwarp();
+            if (lane == 0) {
+                tickets[s] = 0;
+                if (it + a.nst < n_tiles) {
+                    fence_proxy_async_smem();   // the stage was read through the generic proxy
+                    issue(it + a.nst);
+                    atomicMax(issued, static_cast<int>(it + a.nst + 1));
                 }
             }
+            __syncwarp();
         }
-        if (cur >= 0) a.y[cur] = acc;
+    }
+
+    __syncthreads();
+    if (fail && tid == 0) {
+        // A wait ran out: let every copy still in flight land before the CTA exits
+        // (fixed, generous bound: they target valid memory and always complete).
+        const uint32_t n_issued = static_cast<uint32_t>(*issued);
+        for (uint32_t it = consumed; it < n_issued; ++it)
+            mbar_wait_bounded(smem_u32(bars + it % a.nst), (it / a.nst) & 1u, nullptr, kDrainLimit);
     }
 }
 
 // ---------------------------------------------------------------------------
-// host side
+// host side: launch planning
 // ---------------------------------------------------------------------------
-static constexpr int kSmemMax = 232448;   // 227 KB opt-in per CTA on sm_100
-
-static size_t mv_smem_bytes(int nxa, uint32_t upr, int nw, uint32_t nst, uint32_t cap)
-{
-    size_t b = static_cast<size_t>(nxa) * upr * XSTRIDE * 4 + static_cast<size_t>(upr) * 16 * 4;
-    b = (b + 15) & ~size_t(15);
-    b += 8ull * nw * nst + 8ull * nw * 2;
-    b = (b + 127) & ~size_t(127);
-    b += static_cast<size_t>(nw) * nst * cap;
-    return b + 16;   // tail pad: funnel reads of a stage's last unit may touch 8 bytes past it
-}
-
-template <class D, int NW>
-static int launch_one(MvArgs &a, int num_sms, cudaStream_t st)
-{
-    auto kern = k_matvec<D, NW>;
-    if (!smem_attr_once(reinterpret_cast<const void *>(kern), kSmemMax)) return 0;
-    size_t bytes = 0;
-    uint32_t nst = 0;
-    for (uint32_t cand = 4; cand >= 2; --cand) {
-        bytes = mv_smem_bytes(D::NXA, a.upr, NW, cand, a.cap);
-        if (bytes <= static_cast<size_t>(kSmemMax)) { nst = cand; break; }
-    }
-    if (!nst) return -1;   // does not fit: caller tries fewer warps
-    a.nst = nst;
-    const uint32_t grid = a.M < static_cast<uint32_t>(num_sms) ? a.M : static_cast<uint32_t>(num_sms);
-    kern<<<grid, NW * 32, bytes, st>>>(a);
-    return cudaGetLastError() == cudaSuccess ? 1 : 0;
-}
+static constexpr int kSmemMax = 232448;          // 227 KB opt-in per CTA on sm_100
+static constexpr uint32_t kStageTarget = 32768;  // bytes of weights per stage
 
 template <class D>
 static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
 {
-    int r = launch_one<D, 8>(a, num_sms, st);
-    if (r < 0) r = launch_one<D, 4>(a, num_sms, st);
-    if (r < 0) {
-        fprintf(stderr, "[tb_cuda] matvec: K=%u too large for the shared-memory x stage\n", a.K);
+    auto kern = k_matvec<D>;
+    const uint32_t groups = (a.K + 31) / 32;
+    a.cs = (groups + D::GPL - 1) / D::GPL;
+    if (!smem_attr_once(reinterpret_cast<const void *>(kern), kSmemMax)) return 0;
+    static thread_local cudaFuncAttributes fa{};
+    static thread_local const void *fa_for = nullptr;
+    if (fa_for != reinterpret_cast<const void *>(kern)) {
+        if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
+        fa_for = reinterpret_cast<const void *>(kern);
+    }
+    const uint32_t max_warps = static_cast<uint32_t>(fa.maxThreadsPerBlock) / 32;
+    if (a.cs > 32 * max_warps) {
+        fprintf(stderr, "[tb_cuda] matvec: K=%u needs %u column slots, more than %u threads\n", a.K,
+                a.cs, 32 * max_warps);
         return 0;
     }
-    return r;
+    // warps per CTA: best fraction of threads owning a slot, preferring 8..12 warps
+    uint32_t best_w = 0;
+    double best = -1.0;
+    for (uint32_t w = 4; w <= max_warps; ++w) {
+        const uint32_t P = (32 * w) / a.cs;
+        if (!P) continue;
+        double util = static_cast<double>(P * a.cs) / (32.0 * w);
+        if (w < 8) util -= 0.02 * (8 - w);
+        if (util > best + 1e-9) {
+            best = util;
+            best_w = w;
+        }
+    }
+    if (!best_w) return 0;
+    const uint32_t nthr = 32 * best_w;
+    a.phases = nthr / a.cs;
+    const unsigned long long tile_target = kStageTarget / (a.phases * a.row_bytes);
+    a.rpl = static_cast<uint32_t>(tile_target < 1 ? 1 : (tile_target > 8 ? 8 : tile_target));
+    a.tr = a.phases * a.rpl;
+    a.rw = (a.cs % 8 == 0) ? 8 : (a.cs % 4 == 0) ? 4 : (a.cs % 2 == 0) ? 2 : 1;
+    a.npart = a.cs / a.rw;
+    a.cap = static_cast<uint32_t>((a.tr * a.row_bytes + 32 + 127) & ~127ull);
+    const uint32_t xf = mv_x_floats(a.cs, D::GPL);
+    // ring depth: most weight bytes in flight per SM (CTAs per SM x stages ahead)
+    size_t bytes = 0;
+    int occ = 0;
+    unsigned long long best_inflight = 0;
+    a.nst = 0;
+    for (uint32_t n = 2; n <= 6; ++n) {
+        const size_t b = mv_ring_offset(n, a.tr, a.npart, xf) + static_cast<size_t>(n) * a.cap + 16;
+        if (b > static_cast<size_t>(kSmemMax)) break;
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, static_cast<int>(nthr), b) != cudaSuccess)
+            o = 0;
+        if (o < 1) continue;
+        const unsigned long long inflight = static_cast<unsigned long long>(o) * (n - 1) * a.cap;
+        if (inflight > best_inflight) {
+            best_inflight = inflight;
+            a.nst = n;
+            bytes = b;
+            occ = o;
+        }
+    }
+    if (!a.nst) {
+        fprintf(stderr, "[tb_cuda] matvec: a %u-row tile of %llu-byte rows does not fit shared memory\n",
+                a.tr, a.row_bytes);
+        return 0;
+    }
+    if (getenv("TB_MV_VERBOSE"))
+        fprintf(stderr, "[tb_cuda] matvec plan M=%u K=%u: threads %u cs %u phases %u rpl %u tr %u nst %u cap %u smem %zu occ %d\n",
+                a.M, a.K, nthr, a.cs, a.phases, a.rpl, a.tr, a.nst, a.cap, bytes, occ);
+    const unsigned long long want = static_cast<unsigned long long>(num_sms) * occ;
+    const uint32_t grid = static_cast<uint32_t>(want < a.M ? want : a.M);
+    kern<<<grid, nthr, bytes, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? 1 : 0;
 }
 
 int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d_y,
               cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit)
 {
     const Geom g = geom_of(qtype);
-    if (!g.block_weights || !W || !d_x || !d_y || M <= 0 || K <= 0 || K % g.block_weights)
-        return 0;
-    const uint32_t nb = static_cast<uint32_t>(K / g.block_weights);   // blocks per row
-    const uint32_t upr = (nb + g.unit_blocks - 1) / g.unit_blocks;
-    if (static_cast<unsigned long long>(upr) * static_cast<unsigned long long>(M) >= (1ull << 31))
-        return 0;
+    if (!g.block_weights || !W || !d_x || !d_y || M <= 0 || K <= 0 || K % g.block_weights) return 0;
     MvArgs a{};
     a.W = static_cast<const uint8_t *>(W);
     a.x = d_x;
@@ -282,16 +325,9 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
     a.err = d_err;
     a.M = static_cast<uint32_t>(M);
     a.K = static_cast<uint32_t>(K);
-    a.upr = upr;
-    a.unit_bytes = static_cast<uint32_t>(g.unit_blocks * g.block_bytes);
-    const uint32_t last_blocks = nb - (upr - 1) * g.unit_blocks;
-    a.last_unit_bytes = last_blocks * g.block_bytes;
-    const bool per_elem = g.block_weights == 1;
-    a.unit_n = per_elem ? 256u : static_cast<uint32_t>(g.unit_blocks);
-    a.last_unit_n = last_blocks;
-    a.row_bytes = static_cast<unsigned long long>(nb) * g.block_bytes;
-    a.fd_upr = make_fastdiv(upr);
-    a.cap = (32u * a.unit_bytes + 32u + 127u) & ~127u;
+    a.block_weights = static_cast<uint32_t>(g.block_weights);
+    a.block_bytes = static_cast<uint32_t>(g.block_bytes);
+    a.row_bytes = static_cast<unsigned long long>(K / g.block_weights) * g.block_bytes;
     a.wait_limit = wait_limit;
 
     const bool a16 = (reinterpret_cast<uintptr_t>(W) & 15u) == 0 && (a.row_bytes & 15u) == 0;
