@@ -6,10 +6,10 @@ Workload ("step") — BASELINE config 2, the per-type sweep at Qwen3-4B shapes:
 q 4096x2560, k 1024x2560, v 1024x2560, gate 9728x2560, up 9728x2560,
 down 2560x9728, lm_head 151936x2560, for each of Q2_K, Q3_K, Q4_K, Q5_K, Q6_K,
 Q8_0 (Q4_K added to the config's five types so the headline type is in the
-line): 42 matvecs, 1.99 GB of weights resident in HBM, seeded synthetic data
+line): 42 matvecs, 1.87 GB of weights resident in HBM, seeded synthetic data
 (trailblaze_b200.synth).  Algorithmic bytes per matvec = weights + 4K + 4M.
 One step reads every tensor once, so consecutive reads of a tensor are
-separated by ~2 GB of other traffic (> 126 MB L2): no L2 flush is needed.
+separated by ~1.9 GB of other traffic (> 126 MB L2): no L2 flush is needed.
 
 `value`      device time of K steps replayed from one CUDA graph, CUDA events on
              the launching stream, barrier + synchronize on both sides, max over
@@ -49,7 +49,7 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 from trailblaze_b200 import qtypes as Q  # noqa: E402
-from trailblaze_b200 import synth  # noqa: E402
+from trailblaze_b200 import shard, synth  # noqa: E402
 
 SHAPES = [("q_proj", 4096, 2560), ("k_proj", 1024, 2560), ("v_proj", 1024, 2560),
           ("gate", 9728, 2560), ("up", 9728, 2560), ("down", 2560, 9728), ("lm_head", 151936, 2560)]
@@ -74,18 +74,24 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def workload(rank: int, world: int):
-    """[(name, qtype, M, K, W bytes (rank's rows), x)] — rank-sharded rows of N*M-row matrices."""
+def workload(rank: int, world: int, shape: str | None = None):
+    """[(name, qtype, M, K, W bytes (rank's rows), x)] — rank-sharded rows of N*M-row matrices.
+
+    `shape` = "TYPE:M:K" restricts the step to that single matvec (for profiling one launch)."""
     out = []
-    for ti, qt in enumerate(TYPES):
-        for si, (nm, M, K) in enumerate(SHAPES):
+    types, shapes = TYPES, SHAPES
+    if shape:
+        tn, m, k = shape.split(":")
+        types, shapes = [Q.BY_NAME[tn]], [(f"{m}x{k}", int(m), int(k))]
+    for ti, qt in enumerate(types):
+        for si, (nm, M, K) in enumerate(shapes):
             tensor = 100 * ti + si
             rb = Q.row_bytes(qt, K)
             full = synth.weights(qt, M, K, seed=SEED + 7919 * rank, tensor=tensor) if world > 1 else \
                 synth.weights(qt, M, K, seed=SEED, tensor=tensor)
             assert full.size == M * rb
             out.append((f"{Q.NAMES[qt]}:{nm}", qt, M, K, full))
-    xs = {K: synth.activations(K, seed=SEED + K) for _, _, K in SHAPES}
+    xs = {K: synth.activations(K, seed=SEED + K) for _, _, K in shapes}
     return out, xs
 
 
@@ -221,11 +227,13 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--shape", default=None,
+                    help="TYPE:M:K — time this single matvec instead of the sweep (profiling aid)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -249,7 +257,7 @@ def main():
     assert k.tb_cuda_init() == 1
 
     t_gen = time.perf_counter()
-    items, xs_host = workload(rank, world)
+    items, xs_host = workload(rank, world, args.shape)
     log(f"[bench] rank {rank}: generated {sum(w.nbytes for *_, w in items) / 1e9:.2f} GB in "
         f"{time.perf_counter() - t_gen:.1f}s")
     stream = torch.cuda.Stream()
@@ -298,12 +306,9 @@ def main():
             dist.barrier()
         ms = ev0.elapsed_time(ev1)
     assert k.tb_cuda_last_error() == 0
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = shard.max_over_ranks(ms, dist if world > 1 else None, device="cuda")
     ms_step = ms / args.steps
-    value = world * step_bytes / (ms_step * 1e-3) / 1e9
+    value = shard.whole_job_rate(step_bytes, world, ms_step * 1e-3) / 1e9
 
     # ---- per-launch timing of the same launches (events on the launching stream) ----
     per = np.zeros(len(items))
@@ -354,11 +359,7 @@ def main():
             for i, (_, qt, M, K, _) in enumerate(items):
                 k.tb_cuda_matvec_device(dW[i].data_ptr(), qt, M, K, xh[K], outs[i])
         torch.cuda.synchronize()
-        dt = time.perf_counter() - t0
-        if world > 1:
-            t = torch.tensor([dt], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            dt = float(t.item())
+        dt = shard.max_over_ranks(time.perf_counter() - t0, dist if world > 1 else None, device="cuda")
         e2e = {"value": round(world * step_bytes * e_steps / dt / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": sum(4 * K for _, _, _, K, _ in items),
                "d2h_bytes_per_step": sum(4 * M for _, _, M, _, _ in items),
@@ -387,10 +388,12 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded; trailblaze_b200.synth)",
-        "config": {"workload": "qwen3-4b-shape per-type matvec sweep (BASELINE config 2 + Q4_K)",
+        "config": {"workload": (f"single matvec {args.shape} (profiling aid, not the headline)" if args.shape
+                                else "qwen3-4b-shape per-type matvec sweep (BASELINE config 2 + Q4_K)"),
                    "types": [Q.NAMES[t] for t in TYPES], "shapes": SHAPES,
                    "bytes_per_step_per_gpu": step_bytes,
-                   "l2": "no flush: each step streams 1.99 GB > 126 MB L2 before a tensor is re-read",
+                   "l2": (f"no flush: each step streams {step_bytes / 1e9:.2f} GB > 126 MB L2 before a tensor is re-read"
+                          if step_bytes > 2 * 126e6 else "inputs partly L2-resident between steps (profiling aid)"),
                    "parallelism": f"row-sharded x{world}, no data-path collective",
                    "timing": "CUDA graph of one step, CUDA events, max over ranks"},
         "frac_of_8TBps": round(value / world / 8000.0, 4),
