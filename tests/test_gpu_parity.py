@@ -2,9 +2,13 @@
 reference's own CUDA kernels, always through the C ABI.
 
 Tolerances (north star): dequantisation bit-exact; matvec relative L2 error
-<= 1e-3 against the fp64-accumulated oracle.  The kernels are fp32 throughout,
-so the observed error is ~1e-7; STRICT = 2e-5 is asserted as well to catch
-small systematic errors that the contract tolerance would hide.
+<= 1e-3 against the fp64-accumulated oracle.  The float-path types (Q3_K,
+F32, F16, BF16) accumulate in fp32 (observed ~1e-7); the integer-path types
+round x to 2^-15 of each column slot's largest |x| and are exact after that
+(observed 2e-5 to 4e-5 over many rows of Gaussian x, up to ~1e-4 for a
+single short row, whose rounding errors do not average out).  STRICT = 3e-4
+is asserted as well to catch systematic errors that the contract tolerance
+would hide.
 """
 import os
 import subprocess
@@ -19,7 +23,7 @@ from trailblaze_b200 import qtypes as Q, synth
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-3
-STRICT = 2e-5
+STRICT = 3e-4
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -200,7 +204,8 @@ def test_matvec_linearity(kq):
     buf, p = dev_bytes(W)
     y = gpu_matvec(kq, qt, p, M, K, x1 + x2)
     ys = gpu_matvec(kq, qt, p, M, K, x1).astype(np.float64) + gpu_matvec(kq, qt, p, M, K, x2)
-    assert rel_l2(y, ys) <= 1e-5
+    # each of the three results carries its own x rounding (2^-15 of a slot's max)
+    assert rel_l2(y, ys) <= STRICT
 
 
 def test_expert_slice_rows(kq, oracle):

@@ -189,6 +189,54 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
     return ok != 0;
 }
 
+// Plain arrival (release semantics at CTA scope) on a pipeline barrier.
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// ── 4-way byte dot products (dp4a), one form per operand signedness ──────────
+// a holds the weight fields, b the activation digits; c + sum_k a_k * b_k.
+__device__ __forceinline__ int dp_us(uint32_t a, uint32_t b, int c)   // a unsigned, b signed
+{
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp_uu(uint32_t a, uint32_t b, int c)   // both unsigned
+{
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp_ss(uint32_t a, uint32_t b, int c)   // both signed
+{
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp_su(uint32_t a, uint32_t b, int c)   // a signed, b unsigned
+{
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Byte k of w, zero- or sign-extended to 32 bits (one byte permute each).
+__device__ __forceinline__ int ubyte(uint32_t w, int k)
+{
+    return static_cast<int>(__byte_perm(w, 0u, 0x4440u | static_cast<uint32_t>(k)));
+}
+__device__ __forceinline__ int sbyte(uint32_t w, int k)
+{
+    // prmt selector nibble 8|k replicates the sign bit of byte k
+    const uint32_t s = 0x8u | static_cast<uint32_t>(k);
+    const uint32_t sel = (s << 12) | (s << 8) | (s << 4) | static_cast<uint32_t>(k);
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(w), "r"(0u), "r"(sel));
+    return static_cast<int>(r);
+}
+
 // Bounded wait: gives up after `limit` polls, records ERR_WAIT_TIMEOUT and
 // returns false.  Every wait in this library goes through here.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int *err,

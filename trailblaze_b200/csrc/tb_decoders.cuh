@@ -2,25 +2,28 @@
 //
 // The matvec kernel gives every thread ("lane") a fixed run of GPL consecutive
 // 32-weight groups of a row (a column slot) for the whole launch.  The lane's
-// activations for that slot live in registers (struct Lane, filled once by
-// load()), and row_dot() returns sum_i w_i * x_i over the slot for one row whose
-// raw GGUF bytes are staged in shared memory.  Decode semantics are those of
-// layer4/tb_gguf_dequant.cu:89-332 (Q2_K: layer4/tb_gguf.c:210-225).
+// activations for that slot live in registers (struct Lane), loaded once from
+// a per-slot record that the CTA prepares cooperatively in shared memory
+// (prep(): one thread per 32-activation group).  row_dot() then returns
+// sum_i w_i * x_i over the slot for one row whose raw GGUF bytes are staged in
+// shared memory.  Decode semantics are those of layer4/tb_gguf_dequant.cu:89-332
+// (Q2_K: layer4/tb_gguf.c:210-225).
 //
 // Two arithmetic paths:
 //
-// * Integer path (Q4_K, Q5_K, Q6_K, Q2_K, Q8_0, Q4_0, Q8_K).  Each group's 32
-//   activations are written exactly as X_i * 2^(E-20), E the exponent of the
-//   group's largest |x|, X_i = round(x_i * 2^(20-E)) a 22-bit integer, and X_i
-//   is split into three int8 digits X = H*2^14 + M*2^7 + L (H in [-128,127],
-//   M, L in [0,127]).  The quant fields are masked four at a time into the
-//   bytes of a word and multiplied against packed digits with dp4a (4 int8
-//   MACs per instruction, exact int32 sums); one group's sums are combined in
-//   fp32 and scaled by the block scales.  The only approximation is the
-//   rounding of x to 2^-21 of its group's largest magnitude, below fp32's own
-//   accumulation error for 32-term sums; products and sums are exact.
+// * Integer path (Q4_K, Q5_K, Q6_K, Q2_K, Q8_0, Q4_0, Q8_K).  The slot's
+//   activations are written exactly as X_i * 2^(E-14), E the exponent of the
+//   slot's largest |x|, X_i = round(x_i * 2^(14-E)) a 16-bit integer, split
+//   into two byte digits X = 256*H + L (H signed, L unsigned).  Quant fields
+//   are masked four at a time into the bytes of a word and multiplied against
+//   packed digits with dp4a: 4 exact byte MACs per instruction.  The sub-block
+//   scales are integers, so they are applied with one integer multiply-add per
+//   digit and the whole slot is summed exactly in int32; one float conversion
+//   per slot remains.  The only approximation is the rounding of x to 2^-15 of
+//   the slot's largest magnitude (a relative error of a few 1e-5 in y for
+//   Gaussian x, against the 1e-3 bar); every product and sum is exact.
 //   Digits are packed in the byte order in which a type's fields come out of
-//   their words (see pk_index), so no field is ever moved after masking.
+//   their words (see pk_index), so no field is moved after masking.
 //
 // * Float path (Q3_K, F32, F16, BF16), one group per lane.  A field of value q
 //   masked in place at bit position P (P + width <= 24) of a 32-bit word is,
@@ -45,17 +48,6 @@ __device__ __forceinline__ float fbits(uint32_t v) { return __uint_as_float(v); 
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float hsum(float2 a0, float2 a1) { return (a0.x + a0.y) + (a1.x + a1.y); }
-
-// byte b of w placed in the low byte of 0x4B000000 (= 2^23 + byte) minus 2^23:
-// an exact small-integer-to-float conversion with one PRMT and one FADD.
-__device__ __forceinline__ float byte_to_float(uint32_t w, uint32_t b)
-{
-    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u + b)) - 8388608.0f;
-}
-__device__ __forceinline__ float sbyte_to_float(uint32_t w, uint32_t b)
-{
-    return static_cast<float>(static_cast<int8_t>((w >> (8 * b)) & 0xFFu));
-}
 
 // Where, inside a row, a lane's slot starts.
 struct Pos {
@@ -84,12 +76,32 @@ struct Words {
     }
 };
 
-// Reads the 32 activations of the slot's group `g` from the slot's staged copy
-// `xs` (shared memory); `nv` = activations of the slot that exist (zeros after).
-__device__ __forceinline__ void load_group(const float *xs, int nv, int g, float (&v)[32])
+// ============================================================================
+// Slot records: what prep() writes to shared memory and load() reads back.
+// ============================================================================
+
+// Record stride in 32-bit words for `words` of content: a multiple of 4 (16-byte
+// records) with an odd number of 16-byte chunks, so the 128-bit loads of eight
+// consecutive lanes (consecutive slots) fall on eight different bank quads.
+__host__ __device__ constexpr int rec_stride(int words)
 {
+    return ((words + 3) / 4) % 2 ? ((words + 3) / 4) * 4 : ((words + 3) / 4 + 1) * 4;
+}
+
+// Copies a record of W words (W a multiple of 4) into registers, 16 bytes at a time.
+template <int W>
+__device__ __forceinline__ void load_rec(uint32_t (&r)[W], const uint32_t *rec)
+{
+    static_assert(W % 4 == 0, "records are whole 16-byte chunks");
+    const uint4 *p = reinterpret_cast<const uint4 *>(rec);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = (32 * g + i < nv) ? xs[32 * g + i] : 0.f;
+    for (int i = 0; i < W / 4; ++i) {
+        const uint4 v = p[i];
+        r[4 * i] = v.x;
+        r[4 * i + 1] = v.y;
+        r[4 * i + 2] = v.z;
+        r[4 * i + 3] = v.w;
+    }
 }
 
 // ============================================================================
@@ -114,101 +126,135 @@ __host__ __device__ constexpr int pk_index(int pk, int w, int b)
                           : 4 * w + b;
 }
 
-// A lane's activations for GPL groups: NPK digit packings x 3 digits x 8 words.
-template <int GPL, int NPK>
-struct LaneI8 {
-    int dg[GPL][NPK][3][8];
-    float sx[GPL];      // 2^(E-20) per group
-    float X[GPL][2];    // plain fp32 sums of x over each group's two 16-halves
+// Layout of an integer-path record (and of the lane registers, which hold a
+// copy of it): digit words dg[g][p][d][w] (group g < GPL, packing slot p < NPK,
+// digit d: 0 = H (signed bytes), 1 = L (unsigned bytes), word w < 8), then NC
+// type constants (int32), then sx = 2^(E-14) (fp32 bits).
+template <int GPL_, int NPK_, int NC_>
+struct IntLayout {
+    static constexpr int GPL = GPL_, NPK = NPK_, NC = NC_;
+    static constexpr int DG = GPL * NPK * 16;
+    static constexpr int CST = DG;
+    static constexpr int SX = DG + NC;
+    static constexpr int WORDS = (DG + NC + 1 + 3) / 4 * 4;
+    static constexpr int STRIDE = rec_stride(DG + NC + 1);
+    __host__ __device__ static constexpr int dg(int g, int p, int d, int w)
+    {
+        return ((g * NPK + p) * 2 + d) * 8 + w;
+    }
 };
 
-template <int GPL, int PK0, int PK1>
-__device__ __forceinline__ void load_i8(LaneI8<GPL, (PK1 < 0 ? 1 : 2)> &L, const float *xs, int nv)
+// A group's 32 activations as 16-bit integers at the slot's scale.
+struct GroupX {
+    int X[32];
+};
+
+// Slot exponent from the slot's largest |x| (0 for an all-zero slot; bounded
+// below so that 2^(E-14) and 2^(14-E) stay normal floats).
+__device__ __forceinline__ int slot_exponent(float mx)
 {
+    int E = mx > 0.f ? static_cast<int>((__float_as_uint(mx) >> 23) & 255u) - 127 : 0;
+    return E < -100 ? -100 : E;
+}
+
+// X_i = round(x_i * 2^(14-E)), clamped to the int16 range.
+__device__ __forceinline__ void quantize_group(const float (&v)[32], int E, GroupX &g)
+{
+    const float up = exp2i(14 - E);
 #pragma unroll
-    for (int g = 0; g < GPL; ++g) {
-        float v[32];
-        load_group(xs, nv, g, v);
-        float s0 = 0.f, s1 = 0.f, mx = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            s0 += v[i];
-            s1 += v[16 + i];
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
-        L.X[g][0] = s0;
-        L.X[g][1] = s1;
-        int E = mx > 0.f ? static_cast<int>((__float_as_uint(mx) >> 23) & 255u) - 127 : 0;
-        E = E < -100 ? -100 : E;
-        const float up = exp2i(20 - E);
-        L.sx[g] = exp2i(E - 20);
-        int H[32], Mi[32], Lo[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            int q = __float2int_rn(v[i] * up);   // |q| <= 2^21
-            q = q > 2097151 ? 2097151 : (q < -2097152 ? -2097152 : q);
-            H[i] = q >> 14;
-            Mi[i] = (q >> 7) & 127;
-            Lo[i] = q & 127;
-        }
-#pragma unroll
-        for (int pk = 0; pk < (PK1 < 0 ? 1 : 2); ++pk) {
-            const int P = pk == 0 ? PK0 : PK1;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                uint32_t a = 0, b = 0, c = 0;
-#pragma unroll
-                for (int byte = 0; byte < 4; ++byte) {
-                    const int i = pk_index(P, w, byte);
-                    a |= (static_cast<uint32_t>(H[i]) & 0xFFu) << (8 * byte);
-                    b |= (static_cast<uint32_t>(Mi[i]) & 0xFFu) << (8 * byte);
-                    c |= (static_cast<uint32_t>(Lo[i]) & 0xFFu) << (8 * byte);
-                }
-                L.dg[g][pk][0][w] = static_cast<int>(a);
-                L.dg[g][pk][1][w] = static_cast<int>(b);
-                L.dg[g][pk][2][w] = static_cast<int>(c);
-            }
-        }
+    for (int i = 0; i < 32; ++i) {
+        const int q = __float2int_rn(v[i] * up);
+        g.X[i] = q > 32767 ? 32767 : (q < -32768 ? -32768 : q);
     }
 }
 
-// Three-digit accumulator: I[d] += fields . digits[d], kept as two independent
-// chains (even / odd adds) so consecutive dp4a do not wait on each other.
-struct Acc3 {
-    int h0 = 0, m0 = 0, l0 = 0, h1 = 0, m1 = 0, l1 = 0;
-    bool odd = false;
-    __device__ __forceinline__ void add(uint32_t f, const int (&d)[3][8], int w)
-    {
-        if (!odd) {
-            h0 = __dp4a(static_cast<int>(f), d[0][w], h0);
-            m0 = __dp4a(static_cast<int>(f), d[1][w], m0);
-            l0 = __dp4a(static_cast<int>(f), d[2][w], l0);
-        } else {
-            h1 = __dp4a(static_cast<int>(f), d[0][w], h1);
-            m1 = __dp4a(static_cast<int>(f), d[1][w], m1);
-            l1 = __dp4a(static_cast<int>(f), d[2][w], l1);
+// Writes group j's digit words for packing P into packing slot p of the record.
+template <class LAYOUT, int P>
+__device__ __forceinline__ void put_digits(const GroupX &g, int j, int p, uint32_t *rec)
+{
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        uint32_t h = 0, l = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int x = g.X[pk_index(P, w, b)];
+            h |= (static_cast<uint32_t>(x >> 8) & 0xFFu) << (8 * b);
+            l |= (static_cast<uint32_t>(x) & 0xFFu) << (8 * b);
         }
-        odd = !odd;
+        rec[LAYOUT::dg(j, p, 0, w)] = h;
+        rec[LAYOUT::dg(j, p, 1, w)] = l;
     }
-    // sum_i f_i X_i = H*2^14 + M*2^7 + L as fp32 (exact up to the final rounding)
-    __device__ __forceinline__ float value() const
-    {
-        return fmaf(static_cast<float>(h0 + h1), 16384.f, static_cast<float>((m0 + m1) * 128 + l0 + l1));
+}
+
+// Sums of the H and of the L digits over activations [A, A + N) of a group.
+template <int A, int N>
+__device__ __forceinline__ void digit_sums(const GroupX &g, int &sh, int &sl)
+{
+    sh = 0;
+    sl = 0;
+#pragma unroll
+    for (int i = A; i < A + N; ++i) {
+        sh += g.X[i] >> 8;
+        sl += g.X[i] & 0xFF;
     }
-    // same, combined in int32: valid while |sum f_i H_i| * 2^14 stays below 2^31
-    // (fields below 32 on 32 weights, or below 64 on 16 weights)
-    __device__ __forceinline__ float value_i32() const
-    {
-        return static_cast<float>((h0 + h1) * 16384 + (m0 + m1) * 128 + l0 + l1);
-    }
+}
+
+// Byte k of the three byte planes (words c[0..2]) of a signed sum |v| < 2^23,
+// for dp4a against four packed unsigned byte multipliers: planes 0 and 1 are
+// read unsigned, plane 2 signed.
+__device__ __forceinline__ void put_planes(int v, int k, uint32_t *c)
+{
+    uint8_t *b = reinterpret_cast<uint8_t *>(c);
+    b[k] = static_cast<uint8_t>(v & 0xFF);
+    b[4 + k] = static_cast<uint8_t>((v >> 8) & 0xFF);
+    b[8 + k] = static_cast<uint8_t>((v >> 16) & 0xFF);
+}
+
+// sum_k m_k * v_k: four unsigned byte multipliers m against the planes of four
+// signed sums v.
+__device__ __forceinline__ int dot_planes(uint32_t m, uint32_t p0, uint32_t p1, uint32_t p2)
+{
+    return dp_uu(m, p0, 0) + (dp_uu(m, p1, 0) << 8) + (dp_us(m, p2, 0) << 16);
+}
+
+// One field word against digit word w of packing slot pk of group g: the H sum
+// into ah, the L sum into al.  mac_u: unsigned byte fields; mac_s: signed.
+template <class LAYOUT, int W>
+__device__ __forceinline__ void mac_u(int &ah, int &al, uint32_t f, const uint32_t (&r)[W], int g, int pk, int w)
+{
+    ah = dp_us(f, r[LAYOUT::dg(g, pk, 0, w)], ah);
+    al = dp_uu(f, r[LAYOUT::dg(g, pk, 1, w)], al);
+}
+template <class LAYOUT, int W>
+__device__ __forceinline__ void mac_s(int &ah, int &al, uint32_t f, const uint32_t (&r)[W], int g, int pk, int w)
+{
+    ah = dp_ss(f, r[LAYOUT::dg(g, pk, 0, w)], ah);
+    al = dp_su(f, r[LAYOUT::dg(g, pk, 1, w)], al);
+}
+
+// 256*H + L as a float (one rounding).
+__device__ __forceinline__ float hl_value(int th, int tl)
+{
+    return fmaf(static_cast<float>(th), 256.f, static_cast<float>(tl));
+}
+
+// Common lane type of the integer decoders: a register copy of the record.
+template <class LAYOUT>
+struct LaneInt {
+    uint32_t r[LAYOUT::WORDS];
+    __device__ __forceinline__ int cst(int i) const { return static_cast<int>(r[LAYOUT::CST + i]); }
+    __device__ __forceinline__ uint32_t cstu(int i) const { return r[LAYOUT::CST + i]; }
+    __device__ __forceinline__ float sx() const { return __uint_as_float(r[LAYOUT::SX]); }
 };
 
-// Low / high nibbles of a 4-byte word against PK_NIB words t and 4+t.
-__device__ __forceinline__ void nib_word(Acc3 &a, uint32_t w, const int (&d)[3][8], int t)
+// Shared part of every integer decoder's prep(): digits of group j for the
+// packings P0 (and P1 if >= 0), and sx from the group that is first in its slot.
+template <class LAYOUT, int P0, int P1>
+__device__ __forceinline__ void prep_digits(const GroupX &g, int E, bool finite, int j, uint32_t *rec)
 {
-    a.add(w & 0x0F0F0F0Fu, d, t);
-    a.add((w >> 4) & 0x0F0F0F0Fu, d, 4 + t);
+    put_digits<LAYOUT, P0>(g, j, 0, rec);
+    if (P1 >= 0) put_digits<LAYOUT, (P1 < 0 ? 0 : P1)>(g, j, 1, rec);
+    if (j == 0) rec[LAYOUT::SX] = finite ? __float_as_uint(exp2i(E - 14)) : 0x7FC00000u;
 }
 
 // The eight 6-bit Q4_K/Q5_K scales (or mins) of one half of a block as 4 bytes.
@@ -225,39 +271,69 @@ __device__ __forceinline__ uint32_t sm_half(uint32_t w_lo, uint32_t w_hi8, uint3
     return ((x & k) | (y & ~k)) & 0x3F3F3F3Fu;
 }
 
+// Byte planes of the per-group (or per-sub-block) x sums used by the mins:
+// slot j of 4 gets v; the group that is first in its slot also zeroes the
+// bytes no group of the slot writes (slots of fewer than 4 entries).
+template <int USED>
+__device__ __forceinline__ void put_planes_slot(int v, int k, uint32_t *c)
+{
+    put_planes(v, k, c);
+    if (k == 0)
+#pragma unroll
+        for (int u = USED; u < 4; ++u) put_planes(0, u, c);
+}
+
+// The 8 nibble fields of four ql/qs words (PK_NIB words t and 4+t).
+template <class LAYOUT, int W>
+__device__ __forceinline__ void nib4(int &ah, int &al, uint4 q, const uint32_t (&r)[W], int g)
+{
+    mac_u<LAYOUT>(ah, al, q.x & 0x0F0F0F0Fu, r, g, 0, 0);
+    mac_u<LAYOUT>(ah, al, (q.x >> 4) & 0x0F0F0F0Fu, r, g, 0, 4);
+    mac_u<LAYOUT>(ah, al, q.y & 0x0F0F0F0Fu, r, g, 0, 1);
+    mac_u<LAYOUT>(ah, al, (q.y >> 4) & 0x0F0F0F0Fu, r, g, 0, 5);
+    mac_u<LAYOUT>(ah, al, q.z & 0x0F0F0F0Fu, r, g, 0, 2);
+    mac_u<LAYOUT>(ah, al, (q.z >> 4) & 0x0F0F0F0Fu, r, g, 0, 6);
+    mac_u<LAYOUT>(ah, al, q.w & 0x0F0F0F0Fu, r, g, 0, 3);
+    mac_u<LAYOUT>(ah, al, (q.w >> 4) & 0x0F0F0F0Fu, r, g, 0, 7);
+}
+
 // ---- Q4_K — 144 B: d,dmin @0, scales @4, qs @16 (tb_gguf_dequant.cu:89-118) ----
-// w = d*s_g*q - dmin*m_g: group sum = d*s_g*sum(q x) - dmin*m_g*sum(x).
+// w = d*s_g*q - dmin*m_g.  Slot = half a block (4 groups):
+// sum = d * sum_g s_g * sum_i q_i X_i - dmin * sum_g m_g * sum_i X_i, all integer.
 template <bool A16>
 struct DecQ4K {
+    using LY = IntLayout<4, 1, 3>;
     static constexpr int GPL = 4;
-    using Lane = LaneI8<GPL, 1>;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        load_i8<GPL, PK_NIB, -1>(L, xs, nv);
+        prep_digits<LY, PK_NIB, -1>(g, E, fin, j, rec);
+        int sh, sl;
+        digit_sums<0, 32>(g, sh, sl);
+        put_planes_slot<4>(256 * sh + sl, j, rec + LY::CST);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
     {
         const Words<A16> W(row + p.off);
         const uint4 h = W.q4(0);
         const uint32_t upper = p.gi0 >> 2;
         const uint32_t sw = sm_half(h.y, h.w, upper, false), mw = sm_half(h.z, h.w, upper, true);
-        const float2 dd = h2f2_ref(h.x);
-        const float d = dd.x, dmin = dd.y;
-        float tot = 0.f;
+        int th = 0, tl = 0;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             const uint4 q = W.q4(16 + 16 * (p.gi0 + g));
-            Acc3 a;
-            nib_word(a, q.x, L.dg[g][0], 0);
-            nib_word(a, q.y, L.dg[g][0], 1);
-            nib_word(a, q.z, L.dg[g][0], 2);
-            nib_word(a, q.w, L.dg[g][0], 3);
-            const uint32_t sb = (p.gi0 & 3u) + g;
-            const float S = d * byte_to_float(sw, sb), Mn = dmin * byte_to_float(mw, sb);
-            tot = fmaf(S * L.sx[g], a.value_i32(), tot);
-            tot = fmaf(-Mn, L.X[g][0] + L.X[g][1], tot);
+            int ah = 0, al = 0;
+            nib4<LY>(ah, al, q, x.r, g);
+            const int sc = ubyte(sw, g);
+            th = sc * ah + th;
+            tl = sc * al + tl;
         }
-        return tot;
+        const int mn = dot_planes(mw, x.cstu(0), x.cstu(1), x.cstu(2));
+        const float2 dd = h2f2_ref(h.x);
+        return x.sx() * fmaf(dd.x, hl_value(th, tl), -dd.y * static_cast<float>(mn));
     }
 };
 
@@ -265,219 +341,276 @@ struct DecQ4K {
 // q = nibble | qh_bit<<4; the high bit is masked as 0x10 per byte (already x16).
 template <bool A16>
 struct DecQ5K {
+    using LY = IntLayout<2, 2, 3>;
     static constexpr int GPL = 2;
-    using Lane = LaneI8<GPL, 2>;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        load_i8<GPL, PK_NIB, PK_ONE32>(L, xs, nv);
+        prep_digits<LY, PK_NIB, PK_ONE32>(g, E, fin, j, rec);
+        int sh, sl;
+        digit_sums<0, 32>(g, sh, sl);
+        put_planes_slot<2>(256 * sh + sl, j, rec + LY::CST);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
     {
         const Words<A16> W(row + p.off);
         const uint4 h = W.q4(0);
-        const uint32_t upper = p.gi0 >> 2;
+        const uint32_t upper = p.gi0 >> 2, q0 = p.gi0 & 3u;
         const uint32_t sw = sm_half(h.y, h.w, upper, false), mw = sm_half(h.z, h.w, upper, true);
-        const float2 dd = h2f2_ref(h.x);
-        const float d = dd.x, dmin = dd.y;
-        float tot = 0.f;
+        int th = 0, tl = 0;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             const uint32_t gi = p.gi0 + g;
             const uint4 q = W.q4(48 + 16 * gi);
             const uint32_t hb = W(4 + gi);
-            Acc3 a;
-            nib_word(a, q.x, L.dg[g][0], 0);
-            nib_word(a, q.y, L.dg[g][0], 1);
-            nib_word(a, q.z, L.dg[g][0], 2);
-            nib_word(a, q.w, L.dg[g][0], 3);
-            a.add((hb << 4) & 0x10101010u, L.dg[g][1], 0);
-            a.add((hb << 3) & 0x10101010u, L.dg[g][1], 1);
-            a.add((hb << 2) & 0x10101010u, L.dg[g][1], 2);
-            a.add((hb << 1) & 0x10101010u, L.dg[g][1], 3);
-            a.add(hb & 0x10101010u, L.dg[g][1], 4);
-            a.add((hb >> 1) & 0x10101010u, L.dg[g][1], 5);
-            a.add((hb >> 2) & 0x10101010u, L.dg[g][1], 6);
-            a.add((hb >> 3) & 0x10101010u, L.dg[g][1], 7);
-            const uint32_t sb = (p.gi0 & 3u) + g;
-            const float S = d * byte_to_float(sw, sb), Mn = dmin * byte_to_float(mw, sb);
-            tot = fmaf(S * L.sx[g], a.value_i32(), tot);
-            tot = fmaf(-Mn, L.X[g][0] + L.X[g][1], tot);
+            int ah = 0, al = 0;
+            nib4<LY>(ah, al, q, x.r, g);
+            mac_u<LY>(ah, al, (hb << 4) & 0x10101010u, x.r, g, 1, 0);
+            mac_u<LY>(ah, al, (hb << 3) & 0x10101010u, x.r, g, 1, 1);
+            mac_u<LY>(ah, al, (hb << 2) & 0x10101010u, x.r, g, 1, 2);
+            mac_u<LY>(ah, al, (hb << 1) & 0x10101010u, x.r, g, 1, 3);
+            mac_u<LY>(ah, al, hb & 0x10101010u, x.r, g, 1, 4);
+            mac_u<LY>(ah, al, (hb >> 1) & 0x10101010u, x.r, g, 1, 5);
+            mac_u<LY>(ah, al, (hb >> 2) & 0x10101010u, x.r, g, 1, 6);
+            mac_u<LY>(ah, al, (hb >> 3) & 0x10101010u, x.r, g, 1, 7);
+            const int sc = ubyte(sw, static_cast<int>(q0) + g);
+            th = sc * ah + th;
+            tl = sc * al + tl;
         }
-        return tot;
+        // the slot's two mins moved to bytes 0..1; the planes are zero in bytes 2..3
+        const int mn = dot_planes(mw >> (8u * q0), x.cstu(0), x.cstu(1), x.cstu(2));
+        const float2 dd = h2f2_ref(h.x);
+        return x.sx() * fmaf(dd.x, hl_value(th, tl), -dd.y * static_cast<float>(mn));
     }
 };
 
 // ---- Q6_K — 210 B: ql @0, qh @128, int8 scales @192, d @208 (tb_gguf_dequant.cu:196-217) ----
 // w = d*sc[i>>4]*(q-32), q = ql nibble | (qh 2 bits)<<4; the high bits are
-// masked as 0x30 per byte (already x16); each 16-weight half has its own scale.
+// masked as 0x30 per byte (already x16).  The -32 enters as the initial value
+// of each 16-weight sub-block's sums (-32 * the sub-block's digit sums).
 struct DecQ6K {
+    using LY = IntLayout<2, 2, 8>;
     static constexpr int GPL = 2;
-    using Lane = LaneI8<GPL, 2>;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        load_i8<GPL, PK_NIB, PK_TWO16>(L, xs, nv);
+        prep_digits<LY, PK_NIB, PK_TWO16>(g, E, fin, j, rec);
+        int sh, sl;
+        digit_sums<0, 16>(g, sh, sl);
+        rec[LY::CST + 4 * j + 0] = static_cast<uint32_t>(-32 * sh);
+        rec[LY::CST + 4 * j + 1] = static_cast<uint32_t>(-32 * sl);
+        digit_sums<16, 16>(g, sh, sl);
+        rec[LY::CST + 4 * j + 2] = static_cast<uint32_t>(-32 * sh);
+        rec[LY::CST + 4 * j + 3] = static_cast<uint32_t>(-32 * sl);
     }
-    __device__ static void hi16(Acc3 &a, uint32_t hq, const int (&d)[3][8], int base)
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    __device__ static void hi16(int &ah, int &al, uint32_t hq, const uint32_t (&r)[LY::WORDS], int g, int base)
     {
-        a.add((hq << 4) & 0x30303030u, d, base + 0);
-        a.add((hq << 2) & 0x30303030u, d, base + 1);
-        a.add(hq & 0x30303030u, d, base + 2);
-        a.add((hq >> 2) & 0x30303030u, d, base + 3);
+        mac_u<LY>(ah, al, (hq << 4) & 0x30303030u, r, g, 1, base + 0);
+        mac_u<LY>(ah, al, (hq << 2) & 0x30303030u, r, g, 1, base + 1);
+        mac_u<LY>(ah, al, hq & 0x30303030u, r, g, 1, base + 2);
+        mac_u<LY>(ah, al, (hq >> 2) & 0x30303030u, r, g, 1, base + 3);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
     {
         const Words<false> W(row + p.off);
         const float d = h2f2_ref(W(52)).x;
-        const uint32_t scw = W.ub.at(192 + 2 * p.gi0);   // the slot's 2*GPL int8 scales
-        float tot = 0.f;
+        const uint32_t scw = W(48 + (p.gi0 >> 1));   // the slot's 4 int8 sub-block scales
+        int th = 0, tl = 0;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             const uint32_t gi = p.gi0 + g;
             const uint4 l = W.q4(16 * gi);
             const uint32_t h0 = W(32 + 2 * gi), h1 = W(33 + 2 * gi);
-            Acc3 a, b;
-            nib_word(a, l.x, L.dg[g][0], 0);
-            nib_word(a, l.y, L.dg[g][0], 1);
-            hi16(a, h0, L.dg[g][1], 0);
-            nib_word(b, l.z, L.dg[g][0], 2);
-            nib_word(b, l.w, L.dg[g][0], 3);
-            hi16(b, h1, L.dg[g][1], 4);
-            const float s0 = sbyte_to_float(scw, 2 * g), s1 = sbyte_to_float(scw, 2 * g + 1);
-            const float t0 = fmaf(a.value_i32(), L.sx[g], -32.f * L.X[g][0]);
-            const float t1 = fmaf(b.value_i32(), L.sx[g], -32.f * L.X[g][1]);
-            tot = fmaf(d * s0, t0, tot);
-            tot = fmaf(d * s1, t1, tot);
+            int ah = x.cst(4 * g), al = x.cst(4 * g + 1);
+            mac_u<LY>(ah, al, l.x & 0x0F0F0F0Fu, x.r, g, 0, 0);
+            mac_u<LY>(ah, al, (l.x >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 4);
+            mac_u<LY>(ah, al, l.y & 0x0F0F0F0Fu, x.r, g, 0, 1);
+            mac_u<LY>(ah, al, (l.y >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 5);
+            hi16(ah, al, h0, x.r, g, 0);
+            int s = sbyte(scw, 2 * g);
+            th = s * ah + th;
+            tl = s * al + tl;
+            int bh = x.cst(4 * g + 2), bl = x.cst(4 * g + 3);
+            mac_u<LY>(bh, bl, l.z & 0x0F0F0F0Fu, x.r, g, 0, 2);
+            mac_u<LY>(bh, bl, (l.z >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 6);
+            mac_u<LY>(bh, bl, l.w & 0x0F0F0F0Fu, x.r, g, 0, 3);
+            mac_u<LY>(bh, bl, (l.w >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 7);
+            hi16(bh, bl, h1, x.r, g, 4);
+            s = sbyte(scw, 2 * g + 1);
+            th = s * bh + th;
+            tl = s * bl + tl;
         }
-        return tot;
+        return x.sx() * d * hl_value(th, tl);
     }
 };
 
 // ---- Q2_K — 84 B: scales @0 (lo4 scale, hi4 min), qs @16, d @80, dmin @82 ----
-// (tb_gguf.c:210-225) w = d*(sc&15)*q - dmin*(sc>>4) per 16-weight scale block.
+// (tb_gguf.c:210-225) w = d*(sc&15)*q - dmin*(sc>>4) per 16-weight sub-block.
+// Slot = half a block: 4 groups, 8 sub-blocks, two scale words.
+template <bool A4>
 struct DecQ2K {
-    static constexpr int GPL = 2;   // the slot's 2*GPL scale bytes are read as one word
-    using Lane = LaneI8<GPL, 1>;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    using LY = IntLayout<4, 1, 6>;
+    static constexpr int GPL = 4;
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        load_i8<GPL, PK_TWO16, -1>(L, xs, nv);
+        prep_digits<LY, PK_TWO16, -1>(g, E, fin, j, rec);
+        int sh, sl;
+        uint32_t *c = rec + LY::CST + 3 * (j >> 1);   // planes of scale word j/2
+        digit_sums<0, 16>(g, sh, sl);
+        put_planes(256 * sh + sl, 2 * (j & 1), c);
+        digit_sums<16, 16>(g, sh, sl);
+        put_planes(256 * sh + sl, 2 * (j & 1) + 1, c);
     }
-    __device__ static void two16(Acc3 &a, uint32_t q, const int (&d)[3][8], int base)
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    __device__ static void two16(int &ah, int &al, uint32_t q, const uint32_t (&r)[LY::WORDS], int g, int base)
     {
-        a.add(q & 0x03030303u, d, base + 0);
-        a.add((q >> 2) & 0x03030303u, d, base + 1);
-        a.add((q >> 4) & 0x03030303u, d, base + 2);
-        a.add((q >> 6) & 0x03030303u, d, base + 3);
+        mac_u<LY>(ah, al, q & 0x03030303u, r, g, 0, base + 0);
+        mac_u<LY>(ah, al, (q >> 2) & 0x03030303u, r, g, 0, base + 1);
+        mac_u<LY>(ah, al, (q >> 4) & 0x03030303u, r, g, 0, base + 2);
+        mac_u<LY>(ah, al, (q >> 6) & 0x03030303u, r, g, 0, base + 3);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
     {
-        const Words<false> W(row + p.off);
-        const uint32_t dd = W(20);
-        const float2 df = h2f2_ref(dd);
-        const float d = df.x, dmin = df.y;
-        const uint32_t s01 = W(p.gi0 >> 1);   // the 2*GPL scale bytes of the slot
-        float tot = 0.f;
+        const Words<A4> W(row + p.off);
+        const float2 dd = h2f2_ref(W(20));
+        const uint32_t s0 = W(p.gi0 >> 1), s1 = W((p.gi0 >> 1) + 1);
+        const uint32_t c0 = s0 & 0x0F0F0F0Fu, c1 = s1 & 0x0F0F0F0Fu;
+        int th = 0, tl = 0;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             const uint32_t gi = p.gi0 + g;
-            const uint32_t q0 = W(4 + 2 * gi), q1 = W(5 + 2 * gi);
-            Acc3 a, b;
-            two16(a, q0, L.dg[g][0], 0);
-            two16(b, q1, L.dg[g][0], 4);
-            const uint32_t c0 = (s01 >> (16 * g)) & 0xFFu, c1 = (s01 >> (16 * g + 8)) & 0xFFu;
-            const float sc0 = d * byte_to_float(c0 & 15u, 0), mn0 = dmin * byte_to_float(c0 >> 4, 0);
-            const float sc1 = d * byte_to_float(c1 & 15u, 0), mn1 = dmin * byte_to_float(c1 >> 4, 0);
-            tot = fmaf(sc0 * L.sx[g], a.value_i32(), tot);
-            tot = fmaf(sc1 * L.sx[g], b.value_i32(), tot);
-            tot = fmaf(-mn0, L.X[g][0], tot);
-            tot = fmaf(-mn1, L.X[g][1], tot);
+            const uint32_t cw = g < 2 ? c0 : c1;
+            int ah = 0, al = 0;
+            two16(ah, al, W(4 + 2 * gi), x.r, g, 0);
+            int sc = ubyte(cw, 2 * (g & 1));
+            th = sc * ah + th;
+            tl = sc * al + tl;
+            int bh = 0, bl = 0;
+            two16(bh, bl, W(5 + 2 * gi), x.r, g, 4);
+            sc = ubyte(cw, 2 * (g & 1) + 1);
+            th = sc * bh + th;
+            tl = sc * bl + tl;
         }
-        return tot;
+        const int mn = dot_planes((s0 >> 4) & 0x0F0F0F0Fu, x.cstu(0), x.cstu(1), x.cstu(2)) +
+                       dot_planes((s1 >> 4) & 0x0F0F0F0Fu, x.cstu(3), x.cstu(4), x.cstu(5));
+        return x.sx() * fmaf(dd.x, hl_value(th, tl), -dd.y * static_cast<float>(mn));
     }
 };
 
 // ---- Q8_0 — 34 B / 32 weights: d @0, int8 qs @2 (tb_gguf_dequant.cu:246-262) ----
+// One fp16 d per group, so the group's sum is scaled in fp32.
 struct DecQ80 {
+    using LY = IntLayout<4, 1, 0>;
     static constexpr int GPL = 4;
-    using Lane = LaneI8<GPL, 1>;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        load_i8<GPL, PK_BYTE, -1>(L, xs, nv);
+        prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
     {
         float tot = 0.f;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             if (g >= p.ng) break;
-            const uint8_t *blk = row + p.off + 34 * g;
-            const UnitBytes hb(blk), qb(blk + 2);
-            const float d = h2f2_ref(hb.w(0)).x;
-            Acc3 a;
+            const UnitBytes ub(row + p.off + 34 * g);
+            const float d = h2f2_ref(ub.w(0)).x;
+            const UnitBytes qb(row + p.off + 34 * g + 2);
+            int ah = 0, al = 0;
 #pragma unroll
-            for (int t = 0; t < 8; ++t) a.add(qb.w(t), L.dg[g][0], t);
-            tot = fmaf(d * L.sx[g], a.value(), tot);
+            for (int t = 0; t < 8; ++t) mac_s<LY>(ah, al, qb.w(t), x.r, g, 0, t);
+            tot = fmaf(d, hl_value(ah, al), tot);
         }
-        return tot;
+        return x.sx() * tot;
     }
 };
 
 // ---- Q4_0 — 18 B / 32 weights: d @0, qs @2 (tb_gguf_dequant.cu:222-241) ----
-// w[2t] = d*(lo-8), w[2t+1] = d*(hi-8).
+// w[2t] = d*(lo-8), w[2t+1] = d*(hi-8); the -8 enters as the initial sums.
 struct DecQ40 {
+    using LY = IntLayout<4, 1, 8>;
     static constexpr int GPL = 4;
-    using Lane = LaneI8<GPL, 1>;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        load_i8<GPL, PK_NIB, -1>(L, xs, nv);
+        prep_digits<LY, PK_NIB, -1>(g, E, fin, j, rec);
+        int sh, sl;
+        digit_sums<0, 32>(g, sh, sl);
+        rec[LY::CST + 2 * j] = static_cast<uint32_t>(-8 * sh);
+        rec[LY::CST + 2 * j + 1] = static_cast<uint32_t>(-8 * sl);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
     {
         float tot = 0.f;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             if (g >= p.ng) break;
-            const uint8_t *blk = row + p.off + 18 * g;
-            const UnitBytes hb(blk), qb(blk + 2);
-            const float d = h2f2_ref(hb.w(0)).x;
-            Acc3 a;
-            nib_word(a, qb.w(0), L.dg[g][0], 0);
-            nib_word(a, qb.w(1), L.dg[g][0], 1);
-            nib_word(a, qb.w(2), L.dg[g][0], 2);
-            nib_word(a, qb.w(3), L.dg[g][0], 3);
-            tot = fmaf(d, fmaf(a.value_i32(), L.sx[g], -8.f * (L.X[g][0] + L.X[g][1])), tot);
+            const UnitBytes ub(row + p.off + 18 * g);
+            const float d = h2f2_ref(ub.w(0)).x;
+            const UnitBytes qb(row + p.off + 18 * g + 2);
+            int ah = x.cst(2 * g), al = x.cst(2 * g + 1);
+            nib4<LY>(ah, al, make_uint4(qb.w(0), qb.w(1), qb.w(2), qb.w(3)), x.r, g);
+            tot = fmaf(d, hl_value(ah, al), tot);
         }
-        return tot;
+        return x.sx() * tot;
     }
 };
 
 // ---- Q8_K — 292 B: f32 d @0, int8 qs @4, bsums ignored (tb_gguf_dequant.cu:268-284) ----
 struct DecQ8K {
+    using LY = IntLayout<4, 1, 0>;
     static constexpr int GPL = 4;
-    using Lane = LaneI8<GPL, 1>;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        load_i8<GPL, PK_BYTE, -1>(L, xs, nv);
+        prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &L)
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
     {
         const Words<false> W(row + p.off);
         const float d = __uint_as_float(W(0));
-        float tot = 0.f;
+        int th = 0, tl = 0;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             const int b = 1 + 8 * static_cast<int>(p.gi0 + g);
-            Acc3 a;
 #pragma unroll
-            for (int t = 0; t < 8; ++t) a.add(W(b + t), L.dg[g][0], t);
-            tot = fmaf(L.sx[g], a.value(), tot);
+            for (int t = 0; t < 8; ++t) mac_s<LY>(th, tl, W(b + t), x.r, g, 0, t);
         }
-        return d * tot;
+        return x.sx() * d * hl_value(th, tl);
     }
 };
 
 // ============================================================================
 // Float path
 // ============================================================================
+
+// Record: the group's 32 activations (zeros past K), padded to REC_F words.
+constexpr int REC_F = rec_stride(32);
+
+__device__ __forceinline__ void prep_float(const float (&v)[32], uint32_t *rec)
+{
+    float4 *p = reinterpret_cast<float4 *>(rec);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
 
 // The lane's 32 activations as 16 register pairs (two prescaled arrays) plus
 // the plain fp32 sums of each 16-half.
@@ -488,10 +621,18 @@ struct XRegs {
 };
 
 template <class MulA, class MulB>
-__device__ __forceinline__ void load_f32(XRegs &L, const float *xs, int nv, MulA ma, MulB mb)
+__device__ __forceinline__ void load_f32(XRegs &L, const uint32_t *rec, MulA ma, MulB mb)
 {
     float v[32];
-    load_group(xs, nv, 0, v);
+    const float4 *p = reinterpret_cast<const float4 *>(rec);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 t = p[i];
+        v[4 * i] = t.x;
+        v[4 * i + 1] = t.y;
+        v[4 * i + 2] = t.z;
+        v[4 * i + 3] = t.w;
+    }
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
@@ -501,9 +642,9 @@ __device__ __forceinline__ void load_f32(XRegs &L, const float *xs, int nv, MulA
     L.X0 = s0;
     L.X1 = s1;
 #pragma unroll
-    for (int p = 0; p < 16; ++p) {
-        L.a[p] = f2(v[2 * p] * ma(2 * p), v[2 * p + 1] * ma(2 * p + 1));
-        L.b[p] = f2(v[2 * p] * mb(2 * p), v[2 * p + 1] * mb(2 * p + 1));
+    for (int q = 0; q < 16; ++q) {
+        L.a[q] = f2(v[2 * q] * ma(2 * q), v[2 * q + 1] * ma(2 * q + 1));
+        L.b[q] = f2(v[2 * q] * mb(2 * q), v[2 * q + 1] * mb(2 * q + 1));
     }
 }
 
@@ -539,10 +680,12 @@ __device__ __forceinline__ void bit8f(uint32_t w, const float2 (&x)[16], float2 
 // against x*4 (second array), read 8 bits at a time at positions 0..7.
 struct DecQ3K {
     static constexpr int GPL = 1;
+    static constexpr bool kInt = false;
+    static constexpr int REC = REC_F;
     using Lane = XRegs;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    __device__ static void load(Lane &L, const uint32_t *rec)
     {
-        load_f32(L, xs, nv, [](int i) { return exp2i(149 - P2(i & 15) - XC); },
+        load_f32(L, rec, [](int i) { return exp2i(149 - P2(i & 15) - XC); },
                  [](int i) { return exp2i(149 + 2 - (i & 7) - XC); });
     }
     __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
@@ -575,10 +718,12 @@ struct DecQ3K {
 template <int QT>
 struct DecFloat {
     static constexpr int GPL = 1;
+    static constexpr bool kInt = false;
+    static constexpr int REC = REC_F;
     using Lane = XRegs;
-    __device__ static void load(Lane &L, const float *xs, int nv)
+    __device__ static void load(Lane &L, const uint32_t *rec)
     {
-        load_f32(L, xs, nv, [](int) { return 1.f; }, [](int) { return 0.f; });
+        load_f32(L, rec, [](int) { return 1.f; }, [](int) { return 0.f; });
     }
     __device__ static float elem(const UnitBytes &ub, int i)
     {
