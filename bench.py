@@ -310,20 +310,43 @@ def main():
     ms_step = ms / args.steps
     value = shard.whole_job_rate(step_bytes, world, ms_step * 1e-3) / 1e9
 
-    # ---- per-launch timing of the same launches (events on the launching stream) ----
+    # ---- per-launch timing: one step captured with a timing event between
+    # consecutive launches, replayed; the events run on the launching stream
+    # inside the graph, so no host launch gap enters the figures ----
     per = np.zeros(len(items))
     reps = max(3, min(args.steps, 10))
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
-    with torch.cuda.stream(stream):
-        for _ in range(reps):
+    per_how = "CUDA graph of one step with an event between launches"
+    try:
+        evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(items) + 1)]
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            evs[0].record(stream)
             for i, (_, qt, M, K, _) in enumerate(items):
-                evs[i][0].record(stream)
-                k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), sh)
-                evs[i][1].record(stream)
+                assert k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(),
+                                            stream.cuda_stream) == 1
+                evs[i + 1].record(stream)
+        for _ in range(reps):
+            g2.replay()
             torch.cuda.synchronize()
             for i in range(len(items)):
-                per[i] += evs[i][0].elapsed_time(evs[i][1])
+                per[i] += evs[i].elapsed_time(evs[i + 1])
+        del g2
+    except RuntimeError as e:   # no timing events inside graphs: time single launches
+        log(f"[bench] in-graph timing unavailable ({e}); timing single launches")
+        per[:] = 0
+        per_how = "single launches between CUDA events (includes the host launch gap)"
+        evs2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                for i, (_, qt, M, K, _) in enumerate(items):
+                    evs2[i][0].record(stream)
+                    k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), sh)
+                    evs2[i][1].record(stream)
+                torch.cuda.synchronize()
+                for i in range(len(items)):
+                    per[i] += evs2[i][0].elapsed_time(evs2[i][1])
     per /= reps
+    assert k.tb_cuda_last_error() == 0
     # dominant kernel: a (type) instantiation, ranked by its share of the step
     by_type = {}
     for i, (name, qt, M, K, _) in enumerate(items):
@@ -401,7 +424,7 @@ def main():
         "roofline": {"bound": "hbm", "kernel": f"k_matvec<{Q.NAMES[top_qt]}> on {items[top_i][0]}",
                      "achieved": round(ach, 1), "peak": hbm, "peak_kind": hbm_kind, "unit": "GB/s",
                      "frac": round(ach / hbm, 4), "traffic": traffic,
-                     "alg_bytes_per_launch": alg[top_i]},
+                     "alg_bytes_per_launch": alg[top_i], "timing": per_how},
         "per_matvec": per_mv,
         "clocks": clocks,
     }

@@ -11,36 +11,27 @@
 //
 // Two arithmetic paths:
 //
-// * Integer path (Q4_K, Q5_K, Q6_K, Q2_K, Q8_0, Q4_0, Q8_K).  The slot's
-//   activations are written exactly as X_i * 2^(E-14), E the exponent of the
-//   slot's largest |x|, X_i = round(x_i * 2^(14-E)) a 16-bit integer, split
-//   into two byte digits X = 256*H + L (H signed, L unsigned).  Quant fields
-//   are masked four at a time into the bytes of a word and multiplied against
-//   packed digits with dp4a: 4 exact byte MACs per instruction.  The sub-block
-//   scales are integers, so they are applied with one integer multiply-add per
-//   digit and the whole slot is summed exactly in int32; one float conversion
-//   per slot remains.  The only approximation is the rounding of x to 2^-15 of
-//   the slot's largest magnitude (a relative error of a few 1e-5 in y for
-//   Gaussian x, against the 1e-3 bar); every product and sum is exact.
-//   Digits are packed in the byte order in which a type's fields come out of
-//   their words (see pk_index), so no field is moved after masking.
+// * Integer path (every quantized type).  The slot's activations are written
+//   exactly as X_i * 2^(E-14), E the exponent of the slot's largest |x|,
+//   X_i = round(x_i * 2^(14-E)) a 16-bit integer, split into two byte digits
+//   X = 256*H + L (H signed, L unsigned).  Quant fields are masked four at a
+//   time into the bytes of a word and multiplied against packed digits with
+//   dp4a: 4 exact byte MACs per instruction.  The sub-block scales are
+//   integers, so they are applied with one integer multiply-add per digit and
+//   the whole slot is summed exactly in int32; one float conversion per slot
+//   remains.  The only approximation is the rounding of x to 2^-15 of the
+//   slot's largest magnitude (a relative error of a few 1e-5 in y for Gaussian
+//   x, against the 1e-3 bar); every product and sum is exact.  Digits are
+//   packed in the byte order in which a type's fields come out of their words
+//   (see pk_index), so no field is moved after masking.
 //
-// * Float path (Q3_K, F32, F16, BF16), one group per lane.  A field of value q
-//   masked in place at bit position P (P + width <= 24) of a 32-bit word is,
-//   read as an fp32 bit pattern, exactly q * 2^(P-149) (a subnormal, or the
-//   first normal binade, which has the same spacing).  Activations are stored
-//   prescaled by 2^(149-P-C) for the position of their field, so every product
-//   is q*x*2^-C with fp32 rounding; one power of two per group undoes the scale.
-//   The library is built without -ftz, so subnormal operands keep their value.
+// * Float path (F32, F16, BF16), one group per lane: paired fp32 FMAs
+//   (__ffma2_rn) of the converted weights against the lane's 32 activations.
 #pragma once
 
 #include "tb_common.cuh"
 
 namespace tb {
-
-constexpr int XC = 100;   // product scale exponent of the float path
-
-__host__ __device__ constexpr int P2(int m) { return m < 12 ? 2 * m : 2 * m - 8; }
 
 // 2^e as an fp32 bit pattern, e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __uint_as_float(uint32_t(127 + e) << 23); }
@@ -215,6 +206,12 @@ __device__ __forceinline__ void put_planes(int v, int k, uint32_t *c)
 __device__ __forceinline__ int dot_planes(uint32_t m, uint32_t p0, uint32_t p1, uint32_t p2)
 {
     return dp_uu(m, p0, 0) + (dp_uu(m, p1, 0) << 8) + (dp_us(m, p2, 0) << 16);
+}
+
+// The same for four signed byte multipliers.
+__device__ __forceinline__ int dot_planes_s(uint32_t m, uint32_t p0, uint32_t p1, uint32_t p2)
+{
+    return dp_su(m, p0, 0) + (dp_su(m, p1, 0) << 8) + (dp_ss(m, p2, 0) << 16);
 }
 
 // One field word against digit word w of packing slot pk of group g: the H sum
@@ -598,6 +595,88 @@ struct DecQ8K {
     }
 };
 
+// ---- Q3_K — 110 B: hmask @0, qs @32, scales @96, d @108 (tb_gguf_dequant.cu:124-151) ----
+// w_i = d * (sc_is - 32) * ((l_i | h_i << 2) - 4), l_i = qs bits 2(i&3) of byte
+// i>>2, h_i = hmask bit i&7 of byte i>>3, sub-block j = i>>4 using scale
+// is = j & 7 (the two halves of a block share the eight scales), scale bits:
+// lo4 = (sc[is>>1] >> 4(is&1)) & 15, hi2 = (sc[8+(is>>2)] >> 2(is&3)) & 3.
+// Slot = half a block (4 groups, 8 sub-blocks u = 2g + s), so sub-block u uses
+// scale is = u.  The 3-bit value l | h<<2 is assembled per byte: the 16 hmask
+// bits of a sub-block are spread to one nibble per byte (bit j of byte b =
+// weight 4b + j, the PK_TWO16 order of the qs fields) and merged with one LOP3.
+// The -4 enters as -4 * sum_u s_u * (sum of x over u), a dp4a of the signed
+// scale bytes against byte planes of the sub-block x sums.  Blocks are 110
+// bytes, so every other block is only 2-byte aligned: words are funnel-shifted.
+struct DecQ3K {
+    using LY = IntLayout<4, 1, 6>;
+    static constexpr int GPL = 4;
+    static constexpr bool kInt = true;
+    static constexpr int REC = LY::STRIDE;
+    using Lane = LaneInt<LY>;
+    __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
+    {
+        prep_digits<LY, PK_TWO16, -1>(g, E, fin, j, rec);
+        int sh, sl;
+        digit_sums<0, 16>(g, sh, sl);
+        put_planes(256 * sh + sl, j, rec + LY::CST);       // sub-block s = 0 of group j
+        digit_sums<16, 16>(g, sh, sl);
+        put_planes(256 * sh + sl, j, rec + LY::CST + 3);   // s = 1
+    }
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
+    // bits 4b..4b+3 of the 16-bit half selected by `sel` to byte b, bits 0..3
+    __device__ static uint32_t spread(uint32_t hm, uint32_t sel)
+    {
+        const uint32_t t = __byte_perm(hm, 0u, sel);   // [c0, c0, c1, c1]
+        return (t & 0x000F000Fu) | ((t >> 4) & 0x0F000F00u);
+    }
+    // the four 3-bit field words of one sub-block: qs word q, spread high bits h
+    __device__ static void sub16(int &ah, int &al, uint32_t q, uint32_t h, const uint32_t (&r)[LY::WORDS],
+                                 int g, int base)
+    {
+        mac_u<LY>(ah, al, (q & 0x03030303u) | ((h << 2) & 0x04040404u), r, g, 0, base + 0);
+        mac_u<LY>(ah, al, ((q >> 2) & 0x03030303u) | ((h << 1) & 0x04040404u), r, g, 0, base + 1);
+        mac_u<LY>(ah, al, ((q >> 4) & 0x03030303u) | (h & 0x04040404u), r, g, 0, base + 2);
+        mac_u<LY>(ah, al, ((q >> 6) & 0x03030303u) | ((h >> 1) & 0x04040404u), r, g, 0, base + 3);
+    }
+    // the eight 6-bit scales as signed bytes (value - 32): even is in `ev`, odd in `od`
+    __device__ static void scales(uint32_t r0, uint32_t r2, uint32_t &ev, uint32_t &od)
+    {
+        const uint32_t t = __byte_perm(r2, 0u, 0x1100u);   // [sc8, sc8, sc9, sc9]
+        const uint32_t he = (t & 0x00030003u) | ((t >> 4) & 0x03000300u);
+        const uint32_t ho = ((t >> 2) & 0x00030003u) | ((t >> 6) & 0x03000300u);
+        const uint32_t ue = ((r0 & 0x0F0F0F0Fu) | (he << 4)) ^ 0x20202020u;
+        const uint32_t uo = (((r0 >> 4) & 0x0F0F0F0Fu) | (ho << 4)) ^ 0x20202020u;
+        ev = ue | ((ue & 0x20202020u) * 6u);   // sign-extend bit 5 into bits 6..7
+        od = uo | ((uo & 0x20202020u) * 6u);
+    }
+    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    {
+        const Words<false> W(row + p.off);
+        const float d = h2f2_ref(W(27)).x;
+        uint32_t ev, od;
+        scales(W(24), W(26), ev, od);
+        int th = 0, tl = 0;
+#pragma unroll
+        for (int g = 0; g < GPL; ++g) {
+            const uint32_t gi = p.gi0 + g;
+            const uint32_t hm = W(gi);
+            int ah = 0, al = 0;
+            sub16(ah, al, W(8 + 2 * gi), spread(hm, 0x1100u), x.r, g, 0);
+            int s = sbyte(ev, g);
+            th = s * ah + th;
+            tl = s * al + tl;
+            int bh = 0, bl = 0;
+            sub16(bh, bl, W(9 + 2 * gi), spread(hm, 0x3322u), x.r, g, 4);
+            s = sbyte(od, g);
+            th = s * bh + th;
+            tl = s * bl + tl;
+        }
+        const int off = dot_planes_s(ev, x.cstu(0), x.cstu(1), x.cstu(2)) +
+                        dot_planes_s(od, x.cstu(3), x.cstu(4), x.cstu(5));
+        return x.sx() * d * (hl_value(th, tl) - 4.f * static_cast<float>(off));
+    }
+};
+
 // ============================================================================
 // Float path
 // ============================================================================
@@ -612,106 +691,21 @@ __device__ __forceinline__ void prep_float(const float (&v)[32], uint32_t *rec)
     for (int i = 0; i < 8; ++i) p[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
-// The lane's 32 activations as 16 register pairs (two prescaled arrays) plus
-// the plain fp32 sums of each 16-half.
+// The lane's 32 activations as 16 register pairs.
 struct XRegs {
     float2 a[16];
-    float2 b[16];
-    float X0, X1;
 };
 
-template <class MulA, class MulB>
-__device__ __forceinline__ void load_f32(XRegs &L, const uint32_t *rec, MulA ma, MulB mb)
+__device__ __forceinline__ void load_f32(XRegs &L, const uint32_t *rec)
 {
-    float v[32];
     const float4 *p = reinterpret_cast<const float4 *>(rec);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float4 t = p[i];
-        v[4 * i] = t.x;
-        v[4 * i + 1] = t.y;
-        v[4 * i + 2] = t.z;
-        v[4 * i + 3] = t.w;
-    }
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        s0 += v[i];
-        s1 += v[16 + i];
-    }
-    L.X0 = s0;
-    L.X1 = s1;
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-        L.a[q] = f2(v[2 * q] * ma(2 * q), v[2 * q + 1] * ma(2 * q + 1));
-        L.b[q] = f2(v[2 * q] * mb(2 * q), v[2 * q + 1] * mb(2 * q + 1));
+        L.a[2 * i] = f2(t.x, t.y);
+        L.a[2 * i + 1] = f2(t.z, t.w);
     }
 }
-
-// 16 two-bit fields at P2 positions against x pairs O..O+7.
-template <int O>
-__device__ __forceinline__ void two16f(uint32_t w, const float2 (&x)[16], float2 &a0, float2 &a1)
-{
-    const uint32_t w8 = w >> 8;
-    a0 = ffma2(f2(fbits(w & 0x3u), fbits(w & 0xCu)), x[O + 0], a0);
-    a1 = ffma2(f2(fbits(w & 0x30u), fbits(w & 0xC0u)), x[O + 1], a1);
-    a0 = ffma2(f2(fbits(w & 0x300u), fbits(w & 0xC00u)), x[O + 2], a0);
-    a1 = ffma2(f2(fbits(w & 0x3000u), fbits(w & 0xC000u)), x[O + 3], a1);
-    a0 = ffma2(f2(fbits(w & 0x30000u), fbits(w & 0xC0000u)), x[O + 4], a0);
-    a1 = ffma2(f2(fbits(w & 0x300000u), fbits(w & 0xC00000u)), x[O + 5], a1);
-    a0 = ffma2(f2(fbits(w8 & 0x30000u), fbits(w8 & 0xC0000u)), x[O + 6], a0);
-    a1 = ffma2(f2(fbits(w8 & 0x300000u), fbits(w8 & 0xC00000u)), x[O + 7], a1);
-}
-
-// 8 one-bit fields at bits m (m < 8) against x pairs O..O+3.
-template <int O>
-__device__ __forceinline__ void bit8f(uint32_t w, const float2 (&x)[16], float2 &a0, float2 &a1)
-{
-    a0 = ffma2(f2(fbits(w & 0x1u), fbits(w & 0x2u)), x[O + 0], a0);
-    a1 = ffma2(f2(fbits(w & 0x4u), fbits(w & 0x8u)), x[O + 1], a1);
-    a0 = ffma2(f2(fbits(w & 0x10u), fbits(w & 0x20u)), x[O + 2], a0);
-    a1 = ffma2(f2(fbits(w & 0x40u), fbits(w & 0x80u)), x[O + 3], a1);
-}
-
-// ---- Q3_K — 110 B: hmask @0, qs @32, scales @96, d @108 (tb_gguf_dequant.cu:124-151) ----
-// Scale block j uses is = (j<8 ? j : j-8): lo4 = (sc[is>>1] >> 4(is&1)) & 15 =
-// (word24 >> 4is) & 15, hi2 = (sc[8+(is>>2)] >> 2(is&3)) & 3 = (word26 >> 2is) & 3;
-// w = d*((lo4|hi2<<4)-32) * (low2 | hbit<<2 - 4).  The high bit accumulates
-// against x*4 (second array), read 8 bits at a time at positions 0..7.
-struct DecQ3K {
-    static constexpr int GPL = 1;
-    static constexpr bool kInt = false;
-    static constexpr int REC = REC_F;
-    using Lane = XRegs;
-    __device__ static void load(Lane &L, const uint32_t *rec)
-    {
-        load_f32(L, rec, [](int i) { return exp2i(149 - P2(i & 15) - XC); },
-                 [](int i) { return exp2i(149 + 2 - (i & 7) - XC); });
-    }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
-    {
-        const Words<false> W(row + p.off);
-        const uint32_t hm = W(p.gi0);
-        const uint32_t q0 = W(8 + 2 * p.gi0), q1 = W(9 + 2 * p.gi0);
-        const uint32_t r0 = W(24), r2 = W(26), dw = W(27);
-        float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f), b0 = f2(0.f, 0.f), b1 = f2(0.f, 0.f);
-        two16f<0>(q0, x.a, a0, a1);
-        bit8f<0>(hm, x.b, a0, a1);
-        bit8f<4>(hm >> 8, x.b, a0, a1);
-        two16f<8>(q1, x.a, b0, b1);
-        bit8f<8>(hm >> 16, x.b, b0, b1);
-        bit8f<12>(hm >> 24, x.b, b0, b1);
-        const float d = h2f2_ref(dw).x;
-        const uint32_t j0 = 2 * p.gi0, is0 = j0 < 8 ? j0 : j0 - 8, is1 = is0 + 1;
-        const int v0 = static_cast<int>(((r0 >> (4 * is0)) & 15u) | (((r2 >> (2 * is0)) & 3u) << 4)) - 32;
-        const int v1 = static_cast<int>(((r0 >> (4 * is1)) & 15u) | (((r2 >> (2 * is1)) & 3u) << 4)) - 32;
-        const float S0 = d * static_cast<float>(v0), S1 = d * static_cast<float>(v1);
-        const float C = exp2i(XC);
-        const float t0 = fmaf(hsum(a0, a1), C, -4.f * x.X0);
-        const float t1 = fmaf(hsum(b0, b1), C, -4.f * x.X1);
-        return fmaf(S0, t0, S1 * t1);
-    }
-};
 
 // ---- F32 / F16 / BF16 — `n` valid elements in the slot's group ----
 // F16 uses the reference converter (tb_gguf_dequant.cu:54-63).
@@ -721,10 +715,7 @@ struct DecFloat {
     static constexpr bool kInt = false;
     static constexpr int REC = REC_F;
     using Lane = XRegs;
-    __device__ static void load(Lane &L, const uint32_t *rec)
-    {
-        load_f32(L, rec, [](int) { return 1.f; }, [](int) { return 0.f; });
-    }
+    __device__ static void load(Lane &L, const uint32_t *rec) { load_f32(L, rec); }
     __device__ static float elem(const UnitBytes &ub, int i)
     {
         if (QT == QT_F32) return __uint_as_float(ub.w(i));

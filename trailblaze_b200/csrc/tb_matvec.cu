@@ -59,18 +59,17 @@ static constexpr uint32_t kDrainLimit = 1u << 26;
 static constexpr int kMaxThreads = 512;      // 15 consumer warps + 1 producer, <= 128 registers
 static constexpr uint32_t kMaxConsumerWarps = kMaxThreads / 32 - 1;
 
-// Shared-memory layout: [full NST][empty NST] [group maxima] [slot records]
+// Shared-memory layout: [full NST][empty NST] [slot records]
 // [partials NST*TR*NPART] [ring NST*CAP].
 struct MvSmem {
-    size_t gmax, table, part, ring, total;
+    size_t table, part, ring, total;
 };
 __host__ __device__ inline size_t up16(size_t v) { return (v + 15) & ~size_t(15); }
-__host__ __device__ inline MvSmem mv_smem(uint32_t nst, uint32_t ngp, uint32_t cs, uint32_t rec,
-                                          uint32_t tr, uint32_t npart, uint32_t cap)
+__host__ __device__ inline MvSmem mv_smem(uint32_t nst, uint32_t cs, uint32_t rec, uint32_t tr,
+                                          uint32_t npart, uint32_t cap)
 {
     MvSmem s;
-    s.gmax = up16(16ull * nst);
-    s.table = up16(s.gmax + 4ull * ngp);
+    s.table = up16(16ull * nst);
     s.part = up16(s.table + 4ull * cs * rec);
     s.ring = (s.part + 4ull * nst * tr * npart + 127) & ~size_t(127);
     s.total = s.ring + static_cast<size_t>(nst) * cap;
@@ -110,10 +109,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     const uint32_t n_tiles = (r_hi - r_lo + a.tr - 1) / a.tr;
     const uint32_t ngp = a.cs * D::GPL;   // groups of all slots (past K: zeros)
 
-    const MvSmem L = mv_smem(a.nst, ngp, a.cs, D::REC, a.tr, a.npart, a.cap);
+    const MvSmem L = mv_smem(a.nst, a.cs, D::REC, a.tr, a.npart, a.cap);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + a.nst;
-    float *gmax = reinterpret_cast<float *>(smem + L.gmax);
     uint32_t *table = reinterpret_cast<uint32_t *>(smem + L.table);
     float *part = reinterpret_cast<float *>(smem + L.part);
     uint8_t *ring = smem + L.ring;
@@ -139,15 +137,34 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             mbar_init(smem_u32(empty + s), a.ncw);
         }
         fence_mbar_init();
+    }
+    // Programmatic dependent launch: the next kernel of the stream may be
+    // scheduled from here on (it waits in its own griddepcontrol.wait), and
+    // nothing below touches global memory before the previous kernel has
+    // finished and its writes are visible.  Both are no-ops without the launch
+    // attribute.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (producer && lane == 0) {
         const uint32_t pre = min(a.nst, n_tiles);
         for (uint32_t it = 0; it < pre; ++it) issue(it);
     }
 
     // ---- prologue: x -> one record per column slot ----
-    if constexpr (D::kInt) {
-        for (uint32_t g = tid; g < ngp; g += nthr) {
-            float v[32];
+    // Thread g handles group g (then g + nthr, ...).  The GPL groups of a slot
+    // are neighbouring lanes of one warp, so the slot's largest |x| is a shuffle.
+    for (uint32_t base = 0; base < ngp; base += nthr) {   // same trip count in every thread
+        const uint32_t g = base + tid;
+        const bool have = g < ngp;
+        float v[32];
+        if (have) {
             load_x_group(a.x, a.K, g, v);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+        uint32_t *rec = table + (g / D::GPL) * D::REC;
+        if constexpr (D::kInt) {
             float mx = 0.f;
             bool fin = true;
 #pragma unroll
@@ -155,29 +172,21 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
                 mx = fmaxf(mx, fabsf(v[i]));
                 fin = fin && isfinite(v[i]);
             }
-            gmax[g] = fin ? mx : __int_as_float(0x7F800000);   // +inf marks a non-finite group
-        }
-    }
-    __syncthreads();   // group maxima written; barrier inits visible
-    for (uint32_t g = tid; g < ngp; g += nthr) {
-        float v[32];
-        load_x_group(a.x, a.K, g, v);
-        const uint32_t s = g / D::GPL, j = g % D::GPL;
-        uint32_t *rec = table + s * D::REC;
-        if constexpr (D::kInt) {
-            float smax = 0.f;
+            mx = fin ? mx : __int_as_float(0x7F800000);   // +inf marks a non-finite group
 #pragma unroll
-            for (int q = 0; q < D::GPL; ++q) smax = fmaxf(smax, gmax[s * D::GPL + q]);
-            const bool fin = smax <= 3.402823466e38f;
-            const int E = slot_exponent(fin ? smax : 0.f);
-            GroupX gx;
-            quantize_group(v, E, gx);
-            D::prep(gx, E, fin, static_cast<int>(j), rec);
+            for (int o = 1; o < D::GPL; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+            if (have) {
+                const bool sfin = mx <= 3.402823466e38f;
+                const int E = slot_exponent(sfin ? mx : 0.f);
+                GroupX gx;
+                quantize_group(v, E, gx);
+                D::prep(gx, E, sfin, static_cast<int>(g % D::GPL), rec);
+            }
         } else {
-            prep_float(v, rec);
+            if (have) prep_float(v, rec);
         }
     }
-    __syncthreads();   // records complete
+    __syncthreads();   // records complete; barrier inits visible
 
     if (producer) {
         // ---- producer: reduce each finished tile, write y, refill its stage ----
@@ -320,7 +329,7 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
     p.cap = static_cast<uint32_t>((p.tr * row_bytes + 32 + 127) & ~127ull);
     p.nst = 0;
     for (uint32_t n = 8; n >= 2; --n) {
-        const MvSmem s = mv_smem(n, p.cs * D::GPL, p.cs, D::REC, p.tr, p.npart, p.cap);
+        const MvSmem s = mv_smem(n, p.cs, D::REC, p.tr, p.npart, p.cap);
         if (s.total <= static_cast<size_t>(kSmemMax)) {
             p.nst = n;
             p.smem = s.total;
@@ -378,7 +387,22 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
     a.nst = p->nst;
     a.cap = p->cap;
     a.ncw = p->ncw;
-    kern<<<p->grid, p->nthr, p->smem, st>>>(a);
+    // launched with programmatic stream serialization, so back-to-back matvecs
+    // overlap one kernel's launch with the previous one's tail
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(p->grid);
+    cfg.blockDim = dim3(p->nthr);
+    cfg.dynamicSmemBytes = p->smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
     return cudaGetLastError() == cudaSuccess ? 1 : 0;
 }
 
