@@ -118,13 +118,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     const bool producer = warp == a.ncw;
 
     const uint64_t pol = l2_evict_first_policy();
-    auto issue = [&](uint32_t it) {   // one thread of the producer warp
-        const uint32_t t0 = r_lo + it * a.tr;
+    // Tiles advance by TR rows and TR*row_bytes bytes; stage index and barrier
+    // phase are carried along, so the loops below need no division.
+    const uintptr_t w_lo = reinterpret_cast<uintptr_t>(a.W) + static_cast<uintptr_t>(r_lo) * a.row_bytes;
+    const uintptr_t tile_bytes = static_cast<uintptr_t>(a.tr) * a.row_bytes;
+    auto issue = [&](uint32_t s, uint32_t t0, uintptr_t lo) {   // one thread of the producer warp
         const uint32_t nrows = min(a.tr, r_hi - t0);
-        const uintptr_t lo = reinterpret_cast<uintptr_t>(a.W) + t0 * a.row_bytes;
         const uintptr_t g0 = lo & ~uintptr_t(15);
         const uintptr_t g1 = (lo + nrows * a.row_bytes + 15) & ~uintptr_t(15);
-        const uint32_t s = it % a.nst;
         const uint32_t bar = smem_u32(full + s);
         mbar_expect_tx(bar, static_cast<uint32_t>(g1 - g0));
         bulk_g2s(smem_u32(ring + static_cast<size_t>(s) * a.cap), reinterpret_cast<const void *>(g0),
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (producer && lane == 0) {
         const uint32_t pre = min(a.nst, n_tiles);
-        for (uint32_t it = 0; it < pre; ++it) issue(it);
+        for (uint32_t it = 0; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
     }
 
     // ---- prologue: x -> one record per column slot ----
@@ -192,17 +193,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         // ---- producer: reduce each finished tile, write y, refill its stage ----
         uint32_t issued = min(a.nst, n_tiles), done = 0;
         bool fail = false;
+        uint32_t s = 0, par = 0, t0 = r_lo;
+        uintptr_t lo_next = w_lo + static_cast<uintptr_t>(a.nst) * tile_bytes;   // tile it + NST
+        const uint32_t rows_ahead = a.nst * a.tr;
+        const float *pb = part;
+        const uint32_t pstride = a.tr * a.npart;
         for (uint32_t it = 0; it < n_tiles; ++it) {
-            const uint32_t s = it % a.nst;
-            const bool ok = mbar_wait_bounded(smem_u32(empty + s), (it / a.nst) & 1u, a.err, a.wait_limit);
+            const bool ok = mbar_wait_bounded(smem_u32(empty + s), par, a.err, a.wait_limit);
             if (!__all_sync(kFull, ok)) {
                 fail = true;
                 break;
             }
             done = it + 1;
-            const uint32_t t0 = r_lo + it * a.tr;
             const uint32_t nrows = min(a.tr, r_hi - t0);
-            const float *pb = part + static_cast<size_t>(s) * a.tr * a.npart;
             for (uint32_t r = lane; r < nrows; r += 32) {
                 const float *pr = pb + r * a.npart;
                 float acc = 0.f;
@@ -213,11 +216,20 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             if (it + a.nst < n_tiles) {
                 if (lane == 0) {
                     fence_proxy_async_smem();   // the stage was read through the generic proxy
-                    issue(it + a.nst);
+                    issue(s, t0 + rows_ahead, lo_next);
                 }
                 ++issued;
             }
             __syncwarp();
+            t0 += a.tr;
+            lo_next += tile_bytes;
+            if (++s == a.nst) {
+                s = 0;
+                par ^= 1u;
+                pb = part;
+            } else {
+                pb += pstride;
+            }
         }
         if (fail && lane == 0) {
             // A wait ran out: let every copy still in flight land before the CTA
@@ -253,15 +265,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     const bool writer = active && (cs % a.rw) == 0;
     const uint32_t part_col = cs / a.rw;
 
+    uint32_t s = 0, par = 0, t0 = r_lo;
+    uintptr_t lo = w_lo;
+    float *pb = part;
+    const uint8_t *stage = ring;
+    const uint32_t pstride = a.tr * a.npart;
     for (uint32_t it = 0; it < n_tiles; ++it) {
-        const uint32_t s = it % a.nst;
-        const bool ok = mbar_wait_bounded(smem_u32(full + s), (it / a.nst) & 1u, a.err, a.wait_limit);
+        const bool ok = mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit);
         if (!__all_sync(kFull, ok)) break;   // no arrival: the producer's wait runs out as well
-        const uint32_t t0 = r_lo + it * a.tr;
         const uint32_t nrows = min(a.tr, r_hi - t0);
-        float *pb = part + static_cast<size_t>(s) * a.tr * a.npart;
-        const uintptr_t lo = reinterpret_cast<uintptr_t>(a.W) + t0 * a.row_bytes;
-        const uint8_t *sbase = ring + static_cast<size_t>(s) * a.cap + (lo & 15u);
+        const uint8_t *sbase = stage + (lo & 15u);
 #pragma unroll 2
         for (uint32_t i = 0; i < a.rpl; ++i) {
             const uint32_t rt = ph + i * a.phases;
@@ -275,6 +288,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(empty + s));
+        t0 += a.tr;
+        lo += tile_bytes;
+        if (++s == a.nst) {
+            s = 0;
+            par ^= 1u;
+            pb = part;
+            stage = ring;
+        } else {
+            pb += pstride;
+            stage += a.cap;
+        }
     }
 }
 
