@@ -109,6 +109,19 @@ unsigned long long tb_cuda_launch_count(void);
 /* Library build identifier, e.g. "tb_cuda_sm100 1.0 sm_100a". */
 const char *tb_cuda_version(void);
 
+/* No counterpart in the reference.  Blocking matvec like tb_cuda_matvec_device
+ * (x_host must not be NULL), but it allocates nothing, not even on first use:
+ * x, y and the device error word live in static device buffers of fixed size
+ * (K <= 65536 floats of x, M <= 262144 floats of y), whose addresses are looked
+ * up once per device.  Larger M or K are rejected with 0.  It runs on the
+ * legacy default stream and copies straight from / to the caller's buffers.
+ * The buffers are shared by every call on a device, so overlapping calls race:
+ * this library serialises its own callers with its lock, and a caller must not
+ * run two of these at once by any other route (e.g. two processes sharing a
+ * context).  1 = out_host filled; 0 = bad arguments, oversize, or an error. */
+int   tb_cuda_matvec_device_noalloc(const void *W_device, int qtype, int M, int K,
+                                    const float *x_host, float *out_host);
+
 #ifdef __cplusplus
 }
 #endif

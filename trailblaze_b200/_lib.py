@@ -41,6 +41,7 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_last_error": (c_int, []),
         "tb_cuda_launch_count": (ctypes.c_ulonglong, []),
         "tb_cuda_version": (ctypes.c_char_p, []),
+        "tb_cuda_matvec_device_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, fp, fp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -56,5 +57,5 @@ def exported_symbols() -> list[str]:
         "tb_cuda_init", "tb_cuda_upload_tensor", "tb_cuda_free_tensor", "tb_cuda_upload_x",
         "tb_cuda_set_snap", "tb_cuda_matvec_device", "tb_cuda_sync_all", "tb_cuda_cleanup",
         "tb_cuda_matvec_dev", "tb_cuda_dequant_dev", "tb_cuda_qtype_info", "tb_cuda_last_error",
-        "tb_cuda_launch_count", "tb_cuda_version",
+        "tb_cuda_launch_count", "tb_cuda_version", "tb_cuda_matvec_device_noalloc",
     ]

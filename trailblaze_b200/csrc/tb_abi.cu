@@ -110,6 +110,48 @@ bool grow(size_t K, size_t M)
     return true;
 }
 
+// ---- static device staging of tb_cuda_matvec_device_noalloc ----
+// One fixed set per device, fixed at build time: x up to kNaMaxK floats
+// (256 KB), y up to kNaMaxM floats (1 MB), and the device error word.
+constexpr int kNaMaxK = 65536;
+constexpr int kNaMaxM = 262144;
+__device__ __align__(256) float g_na_x[kNaMaxK];
+__device__ __align__(256) float g_na_y[kNaMaxM];
+__device__ __align__(256) int g_na_err[64];
+
+struct NaDev {
+    int dev;
+    int sms;
+    float *x, *y;
+    int *err;
+};
+NaDev g_na[32];
+int g_nna = 0;
+
+// Addresses of the static buffers on the current device, looked up once per
+// device (cudaGetSymbolAddress; nothing is allocated).  Caller holds g_mu.
+const NaDev *na_device_locked()
+{
+    int dev = 0;
+    if (!cuda_ok(cudaGetDevice(&dev), "cudaGetDevice")) return nullptr;
+    for (int i = 0; i < g_nna; ++i)
+        if (g_na[i].dev == dev) return &g_na[i];
+    if (g_nna == 32) return nullptr;
+    NaDev d{};
+    d.dev = dev;
+    void *px = nullptr, *py = nullptr, *pe = nullptr;
+    if (!cuda_ok(cudaGetSymbolAddress(&px, g_na_x), "symbol x") ||
+        !cuda_ok(cudaGetSymbolAddress(&py, g_na_y), "symbol y") ||
+        !cuda_ok(cudaGetSymbolAddress(&pe, g_na_err), "symbol err") ||
+        !cuda_ok(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev), "sm count"))
+        return nullptr;
+    d.x = static_cast<float *>(px);
+    d.y = static_cast<float *>(py);
+    d.err = static_cast<int *>(pe);
+    g_na[g_nna] = d;
+    return &g_na[g_nna++];
+}
+
 }  // namespace
 
 namespace tb {
@@ -307,5 +349,39 @@ int tb_cuda_last_error(void)
 }
 
 unsigned long long tb_cuda_launch_count(void) { return g_launches.load(); }
+
+int tb_cuda_matvec_device_noalloc(const void *W_device, int qtype, int M, int K, const float *x_host,
+                                  float *out_host)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!W_device || !x_host || !out_host || M <= 0 || K <= 0) return 0;
+    const tb::Geom gg = tb::geom_of(qtype);
+    if (!gg.block_weights || K % gg.block_weights) return 0;
+    if (K > kNaMaxK || M > kNaMaxM) {
+        fprintf(stderr, "[tb_cuda] matvec_device_noalloc: M=%d K=%d exceed the static buffers (M <= %d, K <= %d)\n",
+                M, K, kNaMaxM, kNaMaxK);
+        return 0;
+    }
+    const NaDev *d = na_device_locked();
+    if (!d) return 0;
+    const uint32_t lim = g.stream ? g.wait_limit : (1u << 22);
+    const cudaStream_t st = nullptr;   // legacy default stream: no stream is created
+    const size_t xb = static_cast<size_t>(K) * sizeof(float), yb = static_cast<size_t>(M) * sizeof(float);
+    // the error word must start at zero; x and y are fully overwritten
+    if (!cuda_ok(cudaMemsetAsync(d->err, 0, sizeof(int), st), "noalloc err clear")) return 0;
+    if (!cuda_ok(cudaMemcpyAsync(d->x, x_host, xb, cudaMemcpyHostToDevice, st), "noalloc x H2D")) return 0;
+    if (!tb::mv_launch(W_device, qtype, M, K, d->x, d->y, st, d->err, d->sms, lim)) return 0;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    int e = 0;
+    if (!cuda_ok(cudaMemcpyAsync(out_host, d->y, yb, cudaMemcpyDeviceToHost, st), "noalloc y D2H")) return 0;
+    if (!cuda_ok(cudaMemcpyAsync(&e, d->err, sizeof(int), cudaMemcpyDeviceToHost, st), "noalloc err D2H"))
+        return 0;
+    if (!cuda_ok(cudaStreamSynchronize(st), "noalloc sync")) return 0;
+    if (e != 0) {
+        fprintf(stderr, "[tb_cuda] matvec_device_noalloc: device error %d\n", e);
+        return 0;
+    }
+    return 1;
+}
 
 }  // extern "C"

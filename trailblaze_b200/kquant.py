@@ -57,6 +57,13 @@ class KQuantLib:
             x = np.ascontiguousarray(x, dtype=np.float32)
         return self.L.tb_cuda_matvec_device(ctypes.c_void_p(W_dev), qtype, M, K, _fptr(x), _fptr(out))
 
+    def tb_cuda_matvec_device_noalloc(self, W_dev: int, qtype: int, M: int, K: int,
+                                      x: np.ndarray, out: np.ndarray) -> int:
+        """The allocation-free blocking variant (static device staging, bounded M and K)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        assert out.dtype == np.float32 and out.flags.c_contiguous
+        return self.L.tb_cuda_matvec_device_noalloc(ctypes.c_void_p(W_dev), qtype, M, K, _fptr(x), _fptr(out))
+
     def tb_cuda_sync_all(self) -> None:
         self.L.tb_cuda_sync_all()
 
