@@ -306,7 +306,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
 // host side: launch planning (cached per kernel, shape and device)
 // ---------------------------------------------------------------------------
 static constexpr int kSmemMax = 232448;          // 227 KB opt-in per CTA on sm_100
-static constexpr uint32_t kStageTarget = 32768;  // bytes of weights per stage
+static constexpr uint32_t kStageMax = 98304;     // bytes of weights per stage at most
+static constexpr uint32_t kMaxRpl = 8;           // rows per thread per tile at most
+static constexpr uint32_t kMaxStages = 8;
 
 struct Plan {
     const void *kern;
@@ -344,24 +346,31 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
     if (!p.ncw) return false;
     p.nthr = 32 * (p.ncw + 1);
     p.phases = (32 * p.ncw) / p.cs;
-    const unsigned long long per = static_cast<unsigned long long>(p.phases) * row_bytes;
-    const unsigned long long rpl = kStageTarget / per;
-    p.rpl = static_cast<uint32_t>(rpl < 1 ? 1 : (rpl > 4 ? 4 : rpl));
-    p.tr = p.phases * p.rpl;
     p.rw = (p.cs % 8 == 0) ? 8 : (p.cs % 4 == 0) ? 4 : (p.cs % 2 == 0) ? 2 : 1;
     p.npart = p.cs / p.rw;
-    p.cap = static_cast<uint32_t>((p.tr * row_bytes + 32 + 127) & ~127ull);
+    // Rows per thread per tile: as many as keep a stage within kStageMax and
+    // two stages in shared memory (the per-tile cost is paid once per rpl
+    // rows); then as many stages as fit.
     p.nst = 0;
-    for (uint32_t n = 8; n >= 2; --n) {
-        const MvSmem s = mv_smem(n, p.cs, D::REC, p.tr, p.npart, p.cap);
-        if (s.total <= static_cast<size_t>(kSmemMax)) {
-            p.nst = n;
-            p.smem = s.total;
-            break;
+    for (uint32_t rpl = kMaxRpl; rpl >= 1 && !p.nst; --rpl) {
+        const unsigned long long bytes = static_cast<unsigned long long>(p.phases) * rpl * row_bytes;
+        if (rpl > 1 && bytes > kStageMax) continue;
+        const uint32_t tr = p.phases * rpl;
+        const uint32_t cap = static_cast<uint32_t>((bytes + 32 + 127) & ~127ull);
+        for (uint32_t n = kMaxStages; n >= 2; --n) {
+            const MvSmem s = mv_smem(n, p.cs, D::REC, tr, p.npart, cap);
+            if (s.total <= static_cast<size_t>(kSmemMax)) {
+                p.rpl = rpl;
+                p.tr = tr;
+                p.cap = cap;
+                p.nst = n;
+                p.smem = s.total;
+                break;
+            }
         }
     }
     if (!p.nst) {
-        fprintf(stderr, "[tb_cuda] matvec: a %u-row tile of %llu-byte rows does not fit shared memory\n", p.tr,
+        fprintf(stderr, "[tb_cuda] matvec: a %u-row tile of %llu-byte rows does not fit shared memory\n", p.phases,
                 row_bytes);
         return false;
     }
