@@ -135,7 +135,8 @@ struct IntLayout {
     }
 };
 
-// A group's 32 activations as 16-bit integers at the slot's scale.
+// A group's 32 activations as 16-bit integers at the slot's scale (held
+// sign-extended in 32-bit registers: byte 0 is the L digit, byte 1 the H digit).
 struct GroupX {
     int X[32];
 };
@@ -148,45 +149,64 @@ __device__ __forceinline__ int slot_exponent(float mx)
     return E < -100 ? -100 : E;
 }
 
-// X_i = round(x_i * 2^(14-E)), clamped to the int16 range.
+// X_i = round(x_i * 2^(14-E)), saturated to the int16 range by the conversion.
 __device__ __forceinline__ void quantize_group(const float (&v)[32], int E, GroupX &g)
 {
     const float up = exp2i(14 - E);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const int q = __float2int_rn(v[i] * up);
-        g.X[i] = q > 32767 ? 32767 : (q < -32768 ? -32768 : q);
+        int q;
+        asm("{\n\t.reg .s16 t;\n\tcvt.rni.sat.s16.f32 t, %1;\n\tcvt.s32.s16 %0, t;\n\t}" : "=r"(q) : "f"(v[i] * up));
+        g.X[i] = q;
     }
 }
 
-// Writes group j's digit words for packing P into packing slot p of the record.
-template <class LAYOUT, int P>
-__device__ __forceinline__ void put_digits(const GroupX &g, int j, int p, uint32_t *rec)
+// One packing of a group: the H and L digit words.
+struct PackedX {
+    uint32_t h[8], l[8];
+};
+
+// Packs the digits of packing P: word w, byte b holds activation pk_index(P, w, b).
+// Four byte permutes give both digit words of four activations.
+template <int P>
+__device__ __forceinline__ void pack_digits(const GroupX &g, PackedX &pk)
 {
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
-        uint32_t h = 0, l = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int x = g.X[pk_index(P, w, b)];
-            h |= (static_cast<uint32_t>(x >> 8) & 0xFFu) << (8 * b);
-            l |= (static_cast<uint32_t>(x) & 0xFFu) << (8 * b);
-        }
-        rec[LAYOUT::dg(j, p, 0, w)] = h;
-        rec[LAYOUT::dg(j, p, 1, w)] = l;
+        const uint32_t x0 = static_cast<uint32_t>(g.X[pk_index(P, w, 0)]);
+        const uint32_t x1 = static_cast<uint32_t>(g.X[pk_index(P, w, 1)]);
+        const uint32_t x2 = static_cast<uint32_t>(g.X[pk_index(P, w, 2)]);
+        const uint32_t x3 = static_cast<uint32_t>(g.X[pk_index(P, w, 3)]);
+        const uint32_t p01 = __byte_perm(x0, x1, 0x5140u);   // [L0, L1, H0, H1]
+        const uint32_t p23 = __byte_perm(x2, x3, 0x5140u);   // [L2, L3, H2, H3]
+        pk.l[w] = __byte_perm(p01, p23, 0x5410u);
+        pk.h[w] = __byte_perm(p01, p23, 0x7632u);
     }
 }
 
-// Sums of the H and of the L digits over activations [A, A + N) of a group.
-template <int A, int N>
-__device__ __forceinline__ void digit_sums(const GroupX &g, int &sh, int &sl)
+// Writes group j's digit words of one packing into packing slot p of the record
+// (each 8-word run is 32-byte aligned: four 128-bit stores).
+template <class LAYOUT>
+__device__ __forceinline__ void store_packed(const PackedX &pk, int j, int p, uint32_t *rec)
+{
+    uint4 *h = reinterpret_cast<uint4 *>(rec + LAYOUT::dg(j, p, 0, 0));
+    uint4 *l = reinterpret_cast<uint4 *>(rec + LAYOUT::dg(j, p, 1, 0));
+    h[0] = make_uint4(pk.h[0], pk.h[1], pk.h[2], pk.h[3]);
+    h[1] = make_uint4(pk.h[4], pk.h[5], pk.h[6], pk.h[7]);
+    l[0] = make_uint4(pk.l[0], pk.l[1], pk.l[2], pk.l[3]);
+    l[1] = make_uint4(pk.l[4], pk.l[5], pk.l[6], pk.l[7]);
+}
+
+// Sums of the H and of the L digits over the activations of words [W0, W0 + N).
+template <int W0, int N>
+__device__ __forceinline__ void psums(const PackedX &pk, int &sh, int &sl)
 {
     sh = 0;
     sl = 0;
 #pragma unroll
-    for (int i = A; i < A + N; ++i) {
-        sh += g.X[i] >> 8;
-        sl += g.X[i] & 0xFF;
+    for (int w = W0; w < W0 + N; ++w) {
+        sh = dp_ss(pk.h[w], 0x01010101u, sh);
+        sl = dp_uu(pk.l[w], 0x01010101u, sl);
     }
 }
 
@@ -245,12 +265,18 @@ struct LaneInt {
 };
 
 // Shared part of every integer decoder's prep(): digits of group j for the
-// packings P0 (and P1 if >= 0), and sx from the group that is first in its slot.
+// packings P0 (and P1 if >= 0), returned in p0 / p1 for the type's constants,
+// and sx from the group that is first in its slot.
 template <class LAYOUT, int P0, int P1>
-__device__ __forceinline__ void prep_digits(const GroupX &g, int E, bool finite, int j, uint32_t *rec)
+__device__ __forceinline__ void prep_digits(const GroupX &g, int E, bool finite, int j, uint32_t *rec,
+                                            PackedX &p0, PackedX &p1)
 {
-    put_digits<LAYOUT, P0>(g, j, 0, rec);
-    if (P1 >= 0) put_digits<LAYOUT, (P1 < 0 ? 0 : P1)>(g, j, 1, rec);
+    pack_digits<P0>(g, p0);
+    store_packed<LAYOUT>(p0, j, 0, rec);
+    if constexpr (P1 >= 0) {
+        pack_digits<P1>(g, p1);
+        store_packed<LAYOUT>(p1, j, 1, rec);
+    }
     if (j == 0) rec[LAYOUT::SX] = finite ? __float_as_uint(exp2i(E - 14)) : 0x7FC00000u;
 }
 
@@ -306,9 +332,10 @@ struct DecQ4K {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_NIB, -1>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_NIB, -1>(g, E, fin, j, rec, a, b);
         int sh, sl;
-        digit_sums<0, 32>(g, sh, sl);
+        psums<0, 8>(a, sh, sl);
         put_planes_slot<4>(256 * sh + sl, j, rec + LY::CST);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
@@ -345,9 +372,10 @@ struct DecQ5K {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_NIB, PK_ONE32>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_NIB, PK_ONE32>(g, E, fin, j, rec, a, b);
         int sh, sl;
-        digit_sums<0, 32>(g, sh, sl);
+        psums<0, 8>(a, sh, sl);
         put_planes_slot<2>(256 * sh + sl, j, rec + LY::CST);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
@@ -396,12 +424,13 @@ struct DecQ6K {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_NIB, PK_TWO16>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_NIB, PK_TWO16>(g, E, fin, j, rec, a, b);
         int sh, sl;
-        digit_sums<0, 16>(g, sh, sl);
+        psums<0, 4>(b, sh, sl);   // PK_TWO16 words 0..3 = activations 0..15
         rec[LY::CST + 4 * j + 0] = static_cast<uint32_t>(-32 * sh);
         rec[LY::CST + 4 * j + 1] = static_cast<uint32_t>(-32 * sl);
-        digit_sums<16, 16>(g, sh, sl);
+        psums<4, 4>(b, sh, sl);   // activations 16..31
         rec[LY::CST + 4 * j + 2] = static_cast<uint32_t>(-32 * sh);
         rec[LY::CST + 4 * j + 3] = static_cast<uint32_t>(-32 * sl);
     }
@@ -459,12 +488,13 @@ struct DecQ2K {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_TWO16, -1>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_TWO16, -1>(g, E, fin, j, rec, a, b);
         int sh, sl;
         uint32_t *c = rec + LY::CST + 3 * (j >> 1);   // planes of scale word j/2
-        digit_sums<0, 16>(g, sh, sl);
+        psums<0, 4>(a, sh, sl);
         put_planes(256 * sh + sl, 2 * (j & 1), c);
-        digit_sums<16, 16>(g, sh, sl);
+        psums<4, 4>(a, sh, sl);
         put_planes(256 * sh + sl, 2 * (j & 1) + 1, c);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
@@ -513,7 +543,8 @@ struct DecQ80 {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec, a, b);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
     __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
@@ -544,9 +575,10 @@ struct DecQ40 {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_NIB, -1>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_NIB, -1>(g, E, fin, j, rec, a, b);
         int sh, sl;
-        digit_sums<0, 32>(g, sh, sl);
+        psums<0, 8>(a, sh, sl);
         rec[LY::CST + 2 * j] = static_cast<uint32_t>(-8 * sh);
         rec[LY::CST + 2 * j + 1] = static_cast<uint32_t>(-8 * sl);
     }
@@ -577,7 +609,8 @@ struct DecQ8K {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec, a, b);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
     __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
@@ -615,11 +648,12 @@ struct DecQ3K {
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
-        prep_digits<LY, PK_TWO16, -1>(g, E, fin, j, rec);
+        PackedX a, b;
+        prep_digits<LY, PK_TWO16, -1>(g, E, fin, j, rec, a, b);
         int sh, sl;
-        digit_sums<0, 16>(g, sh, sl);
+        psums<0, 4>(a, sh, sl);
         put_planes(256 * sh + sl, j, rec + LY::CST);       // sub-block s = 0 of group j
-        digit_sums<16, 16>(g, sh, sl);
+        psums<4, 4>(a, sh, sl);
         put_planes(256 * sh + sl, j, rec + LY::CST + 3);   // s = 1
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }

@@ -166,19 +166,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         }
         uint32_t *rec = table + (g / D::GPL) * D::REC;
         if constexpr (D::kInt) {
-            float mx = 0.f;
-            bool fin = true;
+            // largest |x| as an integer max of the magnitude bits: an inf or NaN
+            // gives bits >= 0x7F800000, which marks the slot non-finite
+            uint32_t mb = 0;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                mx = fmaxf(mx, fabsf(v[i]));
-                fin = fin && isfinite(v[i]);
-            }
-            mx = fin ? mx : __int_as_float(0x7F800000);   // +inf marks a non-finite group
+            for (int i = 0; i < 32; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
 #pragma unroll
-            for (int o = 1; o < D::GPL; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+            for (int o = 1; o < D::GPL; o <<= 1) mb = max(mb, __shfl_xor_sync(kFull, mb, o));
             if (have) {
-                const bool sfin = mx <= 3.402823466e38f;
-                const int E = slot_exponent(sfin ? mx : 0.f);
+                const bool sfin = mb < 0x7F800000u;
+                const int E = slot_exponent(sfin ? __uint_as_float(mb) : 0.f);
                 GroupX gx;
                 quantize_group(v, E, gx);
                 D::prep(gx, E, sfin, static_cast<int>(g % D::GPL), rec);
