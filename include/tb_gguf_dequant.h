@@ -87,6 +87,21 @@ void  tb_cuda_cleanup(void);
 int   tb_cuda_matvec_dev(const void *W_dev, int qtype, int M, int K,
                          const float *d_x, float *d_y, void *stream);
 
+/* The matvec with the decode step's neighbours fused in (no reference
+ * counterpart; the unfused ops are layer1/tb_tensor.c:194-199 tb_rms_norm,
+ * layer4/tb_infer.c:130-135 tb_swiglu and the residual adds of
+ * tb_infer.c:731, 876).  The input is transformed on the fly:
+ *   xmode 0: x                      (d_x2, d_norm_w unused)
+ *   xmode 1: x[k] * rms * d_norm_w[k], rms = 1/sqrt(sum(x^2)/K + eps)
+ *   xmode 2: silu(x[k]) * d_x2[k],  silu(g) = g / (1 + e^-g)
+ * and y[m] = (dequant(W) @ x')[m] + d_res[m] when d_res is not NULL (d_res
+ * may be d_y only if nothing else reads d_y meanwhile).  Stream-ordered like
+ * tb_cuda_matvec_dev.  1 = issued. */
+int   tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K,
+                               const float *d_x, float *d_y, int xmode, const float *d_x2,
+                               const float *d_norm_w, float eps, const float *d_res,
+                               void *stream);
+
 /* Bit-exact dequantisation of M rows of K weights into d_out[M*K] (fp32),
  * stream-ordered.  sem = 0 gives the reference CUDA-kernel semantics (the
  * parity contract); sem = 1 gives layer4/tb_gguf.c's shipped decoders, which
@@ -121,6 +136,64 @@ const char *tb_cuda_version(void);
  * context).  1 = out_host filled; 0 = bad arguments, oversize, or an error. */
 int   tb_cuda_matvec_device_noalloc(const void *W_device, int qtype, int M, int K,
                                     const float *x_host, float *out_host);
+
+/* ───────────── Part 3: the decode step (no reference counterpart) ────────────
+ *
+ * The GPU form of layer4/tb_infer.c:889-1050 tb_infer_decode for a dense
+ * Qwen3-style model, built on the matvec.  Per token: embedding row; per layer
+ * RMSNorm + QKV matvec, per-head QK-norm + RoPE + KV-cache append + attention
+ * (layer1/tb_tensor.c:303-409), output projection + residual, RMSNorm +
+ * gate/up matvec, SwiGLU + down matvec + residual; final RMSNorm + output
+ * matvec; greedy argmax (tb_tensor.c:415-420).  One CUDA graph per token,
+ * token and position kept on the device.
+ *
+ * quirks = 1 follows tb_layer_forward's order: RoPE before the per-head
+ * QK-norm, and each K head rotated n_heads/n_kv_heads times
+ * (tb_infer.c:665); quirks = 0 is the Qwen3 order (norm, then one rotation).
+ * head_dim must be 128 and n_heads/n_kv_heads at most 8. */
+typedef struct {
+    int   n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_ctx;
+    float rope_base, norm_eps;
+    int   quirks;
+} tb_dec_config;
+
+/* One layer's device tensors.  w_qkv is the fused projection (rows: the
+ * n_heads*head_dim q rows, then n_kv_heads*head_dim k rows, then v rows; the
+ * reference's blk.N.attn_qkv layout, tb_infer.c:640-649); w_gate_up holds the
+ * ffn_dim gate rows followed by the ffn_dim up rows.  Norm weights are fp32
+ * device vectors; q_norm / k_norm may be NULL (no QK-norm).  The decoder keeps
+ * the pointers; the caller keeps ownership. */
+typedef struct {
+    const void  *w_qkv;     int qkv_qtype;
+    const void  *w_o;       int o_qtype;
+    const void  *w_gate_up; int gate_up_qtype;
+    const void  *w_down;    int down_qtype;
+    const float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+} tb_dec_layer;
+
+/* Creates a decoder on the current device: the fp32 KV cache
+ * (n_layers x n_kv_heads x max_ctx x head_dim, zeroed) and scratch vectors.
+ * NULL on unsupported shapes or allocation failure. */
+void  *tb_cuda_dec_create(const tb_dec_config *cfg);
+int    tb_cuda_dec_set_layer(void *dec, int layer, const tb_dec_layer *w);
+int    tb_cuda_dec_set_head(void *dec, const void *tok_embd, int embd_qtype, const float *out_norm,
+                            const void *w_out, int out_qtype);
+/* Device pointer of a layer's K (which = 0) or V (which = 1) cache,
+ * [n_kv_heads][max_ctx][head_dim] fp32, e.g. to load a prefix. */
+float *tb_cuda_dec_kv(void *dec, int layer, int which);
+/* Copies positions [p0, p0 + n) of a layer's K (which = 0) or V (1) cache to
+ * the device (to_device = 1, e.g. a prefix) or back to the host (0); the host
+ * side is [n_kv_heads][n][head_dim] fp32.  Blocking.  1 = ok. */
+int    tb_cuda_dec_kv_copy(void *dec, int layer, int which, int p0, int n, float *host, int to_device);
+/* One token at position pos: *next_token = greedy argmax; logits_host (may be
+ * NULL) receives the vocab logits.  Blocking.  1 = ok. */
+int    tb_cuda_dec_step(void *dec, int token, int pos, int *next_token, float *logits_host);
+/* n tokens back to back from (token, pos), each step fed the previous argmax;
+ * tokens_out (may be NULL) receives them, logits_host (may be NULL) the last
+ * step's logits, device_ms (may be NULL) the device time of the n steps. */
+int    tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_out, float *logits_host,
+                            float *device_ms);
+void   tb_cuda_dec_destroy(void *dec);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,184 @@
+"""CPU restatement of the reference's batch-1 decode step (TEST INFRASTRUCTURE ONLY).
+
+numpy, float64, following layer4/tb_infer.c:553-887 (tb_layer_forward) and
+:889-1050 (tb_infer_decode) for a dense model with the fused QKV layout
+(tb_infer.c:640-649) and explicit positions:
+
+  embedding row       tb_infer.c:936-963 (tb_gguf_dequant_row of the token's row)
+  attention RMSNorm   tb_infer.c:609-620, layer1/tb_tensor.c:194-199
+  QKV projection      tb_infer.c:640-649 (fused attn_qkv: q | k | v rows)
+  RoPE                tb_infer.c:142-155, applied at :665
+  QK-norm             tb_infer.c:667-709 (sc = 1/sqrt(sum/HD + eps), x*sc*w)
+  KV append, attn     layer1/tb_tensor.c:303-409 (scale 1/sqrt(HD), softmax over 0..pos)
+  output + residual   tb_infer.c:719-731
+  FFN RMSNorm         tb_infer.c:734-745
+  gate/up, SwiGLU     tb_infer.c:862-866, :130-135 (g / (1 + e^-g) * u)
+  down + residual     tb_infer.c:866, :876
+  final norm, head    tb_infer.c:987-1019
+  greedy              layer1/tb_tensor.c:415-420 (first index of the maximum)
+
+quirks=True keeps the reference's order: RoPE before the QK-norm, and K head
+j rotated once for every query head h with h % NK == j (tb_infer.c:665).
+quirks=False is the Qwen3 order (norm, then a single rotation).
+
+Only tests/ use this module; the shipped library never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import ctypes.util
+import functools
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .oracle import SEM_CUDA, Oracle
+
+
+@dataclass
+class DecodeModel:
+    """Raw GGUF weight bytes (numpy uint8) plus fp32 norm vectors."""
+    n_layers: int
+    hidden: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn_dim: int
+    vocab: int
+    max_ctx: int
+    rope_base: float = 1e6
+    norm_eps: float = 1e-6
+    emb: np.ndarray = None
+    emb_qt: int = 12
+    out_norm: np.ndarray = None
+    lm: np.ndarray = None
+    lm_qt: int = 14
+    layers: list = field(default_factory=list)   # dicts: wqkv, qkv_qt, wo, o_qt, wgu, gu_qt, wd, d_qt,
+                                                # attn_norm, ffn_norm, q_norm, k_norm
+
+
+def rms_norm(x, w, eps):
+    """layer1/tb_tensor.c:194-199: x * (1/sqrt(sum(x^2)/n + eps)) * w."""
+    x = np.asarray(x, np.float64)
+    return x * (1.0 / np.sqrt(np.dot(x, x) / x.size + eps)) * np.asarray(w, np.float64)
+
+
+_libm = ctypes.CDLL(ctypes.util.find_library("m") or "libm.so.6")
+_libm.powf.restype = ctypes.c_float
+_libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+
+
+@functools.lru_cache(maxsize=4096)
+def _rope_theta(pos, base, hd):
+    """The reference's fp32 angles (float)pos / powf(base, 2.0f*i/hd), with the
+    C library's powf (the one the reference links): at large positions one ulp
+    of theta is a visible rotation, so an fp64 angle would not be the reference's."""
+    th = np.empty(hd // 2, dtype=np.float32)
+    for i in range(hd // 2):
+        e = np.float32(np.float32(2.0) * np.float32(i)) / np.float32(hd)
+        th[i] = np.float32(pos) / np.float32(_libm.powf(np.float32(base), e))
+    return th.astype(np.float64)
+
+
+def rope(v, pos, base, hd):
+    """tb_rope_apply (layer4/tb_infer.c:142-155) on one head: interleaved pairs
+    (2i, 2i+1) rotated by theta_i = pos / base^(2i/hd)."""
+    theta = _rope_theta(int(pos), float(np.float32(base)), int(hd))
+    c, s = np.cos(theta), np.sin(theta)
+    v = np.asarray(v, np.float64)
+    a, b = v[0::2].copy(), v[1::2].copy()
+    out = v.copy()
+    out[0::2] = a * c - b * s
+    out[1::2] = a * s + b * c
+    return out
+
+
+def swiglu(g, u):
+    """layer4/tb_infer.c:130-135: (g / (1 + e^-g)) * u."""
+    g, u = np.asarray(g, np.float64), np.asarray(u, np.float64)
+    return (g / (1.0 + np.exp(-g))) * u
+
+
+def attention(q, kc, vc, n_heads, n_kv_heads):
+    """layer1/tb_tensor.c:303-409 for one token: q [NH][HD] against cached
+    kc, vc [NK][T][HD] (the new position already appended); query head h uses
+    KV head h / (NH/NK); scores * 1/sqrt(HD); softmax over the T positions."""
+    NH, NK = n_heads, n_kv_heads
+    rep = NH // NK
+    HD = q.shape[1]
+    out = np.zeros((NH, HD))
+    for h in range(NH):
+        j = h // rep
+        s = (kc[j] @ q[h]) * (1.0 / np.sqrt(HD))
+        p = np.exp(s - s.max())
+        out[h] = (p @ vc[j]) / p.sum()
+    return out
+
+
+class DecodeOracle:
+    def __init__(self, m: DecodeModel, quirks: bool = True):
+        self.m = m
+        self.quirks = quirks
+        o = Oracle()
+        H, NH, NK, HD, F = m.hidden, m.n_heads, m.n_kv_heads, m.head_dim, m.ffn_dim
+        deq = lambda W, qt, M, K: o.dequant(qt, W, M, K, SEM_CUDA).astype(np.float64)  # noqa: E731
+        self.emb = deq(m.emb, m.emb_qt, m.vocab, H)
+        self.lm = deq(m.lm, m.lm_qt, m.vocab, H)
+        self.out_norm = m.out_norm.astype(np.float64)
+        self.L = []
+        for w in m.layers:
+            self.L.append(dict(
+                wqkv=deq(w["wqkv"], w["qkv_qt"], (NH + 2 * NK) * HD, H),
+                wo=deq(w["wo"], w["o_qt"], H, NH * HD),
+                wgu=deq(w["wgu"], w["gu_qt"], 2 * F, H),
+                wd=deq(w["wd"], w["d_qt"], H, F),
+                attn_norm=w["attn_norm"].astype(np.float64), ffn_norm=w["ffn_norm"].astype(np.float64),
+                q_norm=None if w.get("q_norm") is None else w["q_norm"].astype(np.float64),
+                k_norm=None if w.get("k_norm") is None else w["k_norm"].astype(np.float64)))
+        # caches [layer][NK][max_ctx][HD]
+        self.kc = np.zeros((m.n_layers, NK, m.max_ctx, HD))
+        self.vc = np.zeros((m.n_layers, NK, m.max_ctx, HD))
+
+    def step(self, token: int, pos: int):
+        """One token at position pos; returns (logits, next_token).  Updates the caches."""
+        m = self.m
+        H, NH, NK, HD, F = m.hidden, m.n_heads, m.n_kv_heads, m.head_dim, m.ffn_dim
+        rep = NH // NK
+        eps = m.norm_eps
+        x = self.emb[token].copy()
+        for li, w in enumerate(self.L):
+            xn = rms_norm(x, w["attn_norm"], eps)
+            qkv = w["wqkv"] @ xn
+            q = qkv[:NH * HD].reshape(NH, HD).copy()
+            k = qkv[NH * HD:(NH + NK) * HD].reshape(NK, HD).copy()
+            v = qkv[(NH + NK) * HD:].reshape(NK, HD).copy()
+
+            def rope_all():
+                for h in range(NH):
+                    q[h] = rope(q[h], pos, m.rope_base, HD)
+                for j in range(NK):
+                    for _ in range(rep if self.quirks else 1):
+                        k[j] = rope(k[j], pos, m.rope_base, HD)
+
+            def norm_all():
+                if w["q_norm"] is not None:
+                    for h in range(NH):
+                        q[h] = rms_norm(q[h], w["q_norm"], eps)
+                if w["k_norm"] is not None:
+                    for j in range(NK):
+                        k[j] = rms_norm(k[j], w["k_norm"], eps)
+
+            if self.quirks:
+                rope_all()
+                norm_all()
+            else:
+                norm_all()
+                rope_all()
+            self.kc[li, :, pos] = k
+            self.vc[li, :, pos] = v
+            att = attention(q, self.kc[li, :, :pos + 1], self.vc[li, :, :pos + 1], NH, NK)
+            x2 = x + w["wo"] @ att.reshape(-1)
+            gu = w["wgu"] @ rms_norm(x2, w["ffn_norm"], eps)
+            x = x2 + w["wd"] @ swiglu(gu[:F], gu[F:])
+        logits = self.lm @ rms_norm(x, self.out_norm, eps)
+        return logits, int(np.argmax(logits))

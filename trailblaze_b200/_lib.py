@@ -15,6 +15,23 @@ LIB_PATH = os.path.join(_HERE, "libtb_cuda_sm100.so")
 _lib = None
 
 
+class DecConfig(ctypes.Structure):
+    """tb_dec_config (include/tb_gguf_dequant.h, part 3)."""
+    _fields_ = [(n, ctypes.c_int) for n in ("n_layers", "hidden", "n_heads", "n_kv_heads", "head_dim",
+                                            "ffn_dim", "vocab", "max_ctx")] + \
+               [("rope_base", ctypes.c_float), ("norm_eps", ctypes.c_float), ("quirks", ctypes.c_int)]
+
+
+class DecLayer(ctypes.Structure):
+    """tb_dec_layer (include/tb_gguf_dequant.h, part 3)."""
+    _fields_ = [("w_qkv", ctypes.c_void_p), ("qkv_qtype", ctypes.c_int),
+                ("w_o", ctypes.c_void_p), ("o_qtype", ctypes.c_int),
+                ("w_gate_up", ctypes.c_void_p), ("gate_up_qtype", ctypes.c_int),
+                ("w_down", ctypes.c_void_p), ("down_qtype", ctypes.c_int),
+                ("attn_norm", ctypes.c_void_p), ("ffn_norm", ctypes.c_void_p),
+                ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p)]
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
@@ -42,6 +59,16 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_launch_count": (ctypes.c_ulonglong, []),
         "tb_cuda_version": (ctypes.c_char_p, []),
         "tb_cuda_matvec_device_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, fp, fp]),
+        "tb_cuda_matvec_fused_dev": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
+                                             c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p]),
+        "tb_cuda_dec_create": (c_void_p, [ctypes.POINTER(DecConfig)]),
+        "tb_cuda_dec_set_layer": (c_int, [c_void_p, c_int, ctypes.POINTER(DecLayer)]),
+        "tb_cuda_dec_set_head": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int]),
+        "tb_cuda_dec_kv": (c_void_p, [c_void_p, c_int, c_int]),
+        "tb_cuda_dec_kv_copy": (c_int, [c_void_p, c_int, c_int, c_int, c_int, fp, c_int]),
+        "tb_cuda_dec_step": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_int), fp]),
+        "tb_cuda_dec_generate": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_int), fp, fp]),
+        "tb_cuda_dec_destroy": (None, [c_void_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -58,4 +85,6 @@ def exported_symbols() -> list[str]:
         "tb_cuda_set_snap", "tb_cuda_matvec_device", "tb_cuda_sync_all", "tb_cuda_cleanup",
         "tb_cuda_matvec_dev", "tb_cuda_dequant_dev", "tb_cuda_qtype_info", "tb_cuda_last_error",
         "tb_cuda_launch_count", "tb_cuda_version", "tb_cuda_matvec_device_noalloc",
+        "tb_cuda_matvec_fused_dev", "tb_cuda_dec_create", "tb_cuda_dec_set_layer", "tb_cuda_dec_set_head",
+        "tb_cuda_dec_kv", "tb_cuda_dec_kv_copy", "tb_cuda_dec_step", "tb_cuda_dec_generate", "tb_cuda_dec_destroy",
     ]

@@ -326,6 +326,33 @@ int tb_cuda_matvec_dev(const void *W_dev, int qtype, int M, int K, const float *
     return r;
 }
 
+int tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K, const float *d_x, float *d_y,
+                             int xmode, const float *d_x2, const float *d_norm_w, float eps,
+                             const float *d_res, void *stream)
+{
+    int nsm;
+    int *derr;
+    uint32_t lim;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!ensure_init_locked(false)) return 0;
+        nsm = g.num_sms;
+        derr = g.d_err;
+        lim = g.wait_limit;
+    }
+    if (xmode < 0) return 0;
+    tb::MvFuse f;
+    f.xmode = static_cast<uint32_t>(xmode);
+    f.x2 = d_x2;
+    f.nw = d_norm_w;
+    f.eps = eps;
+    f.res = d_res;
+    const int r = tb::mv_launch(W_dev, qtype, M, K, d_x, d_y, static_cast<cudaStream_t>(stream), derr, nsm,
+                                lim, &f);
+    if (r) g_launches.fetch_add(1, std::memory_order_relaxed);
+    return r;
+}
+
 int tb_cuda_dequant_dev(const void *W_dev, int qtype, int M, int K, float *d_out, int sem, void *stream)
 {
     {

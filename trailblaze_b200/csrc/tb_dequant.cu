@@ -132,6 +132,63 @@ __global__ void __launch_bounds__(256) k_dequant(const uint8_t *__restrict__ W, 
     }
 }
 
+// One embedding row, selected on the device (the decode step's first kernel).
+template <int QT>
+__global__ void __launch_bounds__(256) k_embed_row(const uint8_t *__restrict__ W, uint32_t vocab, uint32_t K,
+                                                   unsigned long long row_bytes, const int *token,
+                                                   float *__restrict__ out)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    constexpr Geom g = geom_of(QT);
+    const int t = *token;
+    const bool ok = t >= 0 && static_cast<uint32_t>(t) < vocab;
+    const uint8_t *row = W + (ok ? static_cast<unsigned long long>(t) * row_bytes : 0ull);
+    for (uint32_t k = blockIdx.x * 256u + threadIdx.x; k < K; k += gridDim.x * 256u)
+        out[k] = ok ? deq1<QT, 0>(row + static_cast<unsigned long long>(k / g.block_weights) * g.block_bytes,
+                                  static_cast<int>(k % g.block_weights))
+                    : 0.f;
+}
+
+template <int QT>
+static int embed_go(const void *W, int vocab, int K, const int *tok, float *out, cudaStream_t st)
+{
+    constexpr Geom g = geom_of(QT);
+    const unsigned long long row_bytes = static_cast<unsigned long long>(K / g.block_weights) * g.block_bytes;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>((K + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_embed_row<QT>, static_cast<const uint8_t *>(W), static_cast<uint32_t>(vocab),
+                              static_cast<uint32_t>(K), row_bytes, tok, out) == cudaSuccess ? 1 : 0;
+}
+
+int dq_embed_launch(const void *W, int qtype, int vocab, int K, const int *d_token, float *d_out, cudaStream_t st)
+{
+    const Geom g = geom_of(qtype);
+    if (!g.block_weights || !W || !d_token || !d_out || vocab <= 0 || K <= 0 || K % g.block_weights) return 0;
+    switch (qtype) {
+    case QT_F32: return embed_go<QT_F32>(W, vocab, K, d_token, d_out, st);
+    case QT_F16: return embed_go<QT_F16>(W, vocab, K, d_token, d_out, st);
+    case QT_BF16: return embed_go<QT_BF16>(W, vocab, K, d_token, d_out, st);
+    case QT_Q4_0: return embed_go<QT_Q4_0>(W, vocab, K, d_token, d_out, st);
+    case QT_Q8_0: return embed_go<QT_Q8_0>(W, vocab, K, d_token, d_out, st);
+    case QT_Q8_K: return embed_go<QT_Q8_K>(W, vocab, K, d_token, d_out, st);
+    case QT_Q2_K: return embed_go<QT_Q2_K>(W, vocab, K, d_token, d_out, st);
+    case QT_Q3_K:
+    case QT_IQ3_S: return embed_go<QT_Q3_K>(W, vocab, K, d_token, d_out, st);
+    case QT_Q4_K: return embed_go<QT_Q4_K>(W, vocab, K, d_token, d_out, st);
+    case QT_Q5_K: return embed_go<QT_Q5_K>(W, vocab, K, d_token, d_out, st);
+    case QT_Q6_K: return embed_go<QT_Q6_K>(W, vocab, K, d_token, d_out, st);
+    default: return 0;
+    }
+}
+
 template <int QT, int SEM>
 static int dq_go(const void *W, int M, int K, float *out, cudaStream_t st)
 {

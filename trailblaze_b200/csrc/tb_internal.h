@@ -6,13 +6,36 @@
 
 namespace tb {
 
+// Fused transforms of the matvec's input and output (see tb_cuda_matvec_fused_dev).
+enum MvXMode : uint32_t { MV_X_PLAIN = 0, MV_X_RMSNORM = 1, MV_X_SWIGLU = 2 };
+struct MvFuse {
+    uint32_t xmode = MV_X_PLAIN;
+    const float *x2 = nullptr;    // SwiGLU: the up vector
+    const float *nw = nullptr;    // RMSNorm: the norm weights
+    float eps = 0.f;              // RMSNorm epsilon
+    const float *res = nullptr;   // added to y when not null
+};
+
 // Launch the matvec d_y[M] = dequant(W) @ d_x[K] on `st`.  Returns 1 when the
 // launch was issued, 0 for unsupported arguments or a launch error.
 int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d_y,
-              cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit);
+              cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit,
+              const MvFuse *fuse = nullptr);
 
 // Launch the bit-exact dequantisation of M rows of K weights into d_out.
 int dq_launch(const void *W, int qtype, int M, int K, float *d_out, int sem, cudaStream_t st);
+
+// Dequantise row *d_token of a [vocab x K] table into d_out (zeros for a token
+// outside [0, vocab)); programmatic-dependent-launch aware.
+int dq_embed_launch(const void *W, int qtype, int vocab, int K, const int *d_token, float *d_out,
+                    cudaStream_t st);
+
+// Shape of the decode step (tb_decode.cu); mirrors tb_dec_config.
+struct DecConfig {
+    int n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn_dim, vocab, max_ctx;
+    float rope_base, norm_eps;
+    int quirks;
+};
 
 // Raise a kernel's dynamic shared-memory limit once per device.
 bool smem_attr_once(const void *kernel, int bytes);

@@ -52,6 +52,12 @@ struct MvArgs {
     uint32_t cap;      // bytes per stage
     uint32_t ncw;      // consumer warps; warp ncw is the producer
     uint32_t wait_limit;
+    // fused input / output transforms (MvFuse): x is x (plain), x*rms*nw
+    // (RMSNorm, rms = 1/sqrt(mean(x^2) + eps)) or silu(x)*x2 (SwiGLU); y gets
+    // res added when res is not null
+    uint32_t xmode;
+    const float *x2, *nw, *res;
+    float eps;
 };
 
 static constexpr uint32_t kFull = 0xFFFFFFFFu;
@@ -59,28 +65,32 @@ static constexpr uint32_t kDrainLimit = 1u << 26;
 static constexpr int kMaxThreads = 512;      // 15 consumer warps + 1 producer, <= 128 registers
 static constexpr uint32_t kMaxConsumerWarps = kMaxThreads / 32 - 1;
 
-// Shared-memory layout: [full NST][empty NST] [slot records]
-// [partials NST*TR*NPART] [ring NST*CAP].
+// Shared-memory layout: [full NST][empty NST] [reduction scratch 64 floats]
+// [slot records] [partials NST*TR*NPART] [ring NST*CAP].
 struct MvSmem {
-    size_t table, part, ring, total;
+    size_t red, table, part, ring, total;
 };
 __host__ __device__ inline size_t up16(size_t v) { return (v + 15) & ~size_t(15); }
 __host__ __device__ inline MvSmem mv_smem(uint32_t nst, uint32_t cs, uint32_t rec, uint32_t tr,
                                           uint32_t npart, uint32_t cap)
 {
     MvSmem s;
-    s.table = up16(16ull * nst);
+    s.red = up16(16ull * nst);
+    s.table = up16(s.red + 256);
     s.part = up16(s.table + 4ull * cs * rec);
     s.ring = (s.part + 4ull * nst * tr * npart + 127) & ~size_t(127);
     s.total = s.ring + static_cast<size_t>(nst) * cap;
     return s;
 }
 
-// The 32 activations of group g (zeros past K).
-__device__ __forceinline__ void load_x_group(const float *x, uint32_t K, uint32_t g, float (&v)[32])
+// The 32 activations of group g (zeros past K), after the fused input
+// transform: x * rms * nw (layer/tb_tensor.c:194-199 order) or
+// silu(x) * x2 with silu(g) = g / (1 + e^-g) (layer4/tb_infer.c:130-135).
+__device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t g, float rms, float (&v)[32])
 {
     const uint32_t k0 = 32 * g;
-    if (k0 + 32 <= K && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    const float *x = a.x;
+    if (k0 + 32 <= a.K && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
         const float4 *p = reinterpret_cast<const float4 *>(x + k0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -92,8 +102,40 @@ __device__ __forceinline__ void load_x_group(const float *x, uint32_t K, uint32_
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = k0 + i < K ? __ldg(x + k0 + i) : 0.f;
+        for (int i = 0; i < 32; ++i) v[i] = k0 + i < a.K ? __ldg(x + k0 + i) : 0.f;
     }
+    if (a.xmode == MV_X_RMSNORM) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (k0 + i < a.K) v[i] = v[i] * rms * __ldg(a.nw + k0 + i);
+    } else if (a.xmode == MV_X_SWIGLU) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (k0 + i < a.K) v[i] = (v[i] / (1.0f + expf(-v[i]))) * __ldg(a.x2 + k0 + i);
+    }
+}
+
+// 1/sqrt(sum(x^2)/K + eps) over the whole of x, computed by every CTA (K is a
+// few thousand floats); red = 64 floats of shared scratch.
+__device__ __forceinline__ float block_rms(const MvArgs &a, float *red)
+{
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float ss = 0.f;
+    for (uint32_t k = tid; k < a.K; k += blockDim.x) {
+        const float t = __ldg(a.x + k);
+        ss = fmaf(t, t, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (uint32_t w = 0; w < blockDim.x / 32; ++w) t += red[w];
+        red[32] = 1.0f / sqrtf(t / static_cast<float>(a.K) + a.eps);
+    }
+    __syncthreads();
+    return red[32];
 }
 
 template <class D>
@@ -152,6 +194,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     }
 
     // ---- prologue: x -> one record per column slot ----
+    const float rms = a.xmode == MV_X_RMSNORM ? block_rms(a, reinterpret_cast<float *>(smem + L.red)) : 1.f;
     // Thread g handles group g (then g + nthr, ...).  The GPL groups of a slot
     // are neighbouring lanes of one warp, so the slot's largest |x| is a shuffle.
     for (uint32_t base = 0; base < ngp; base += nthr) {   // same trip count in every thread
@@ -159,7 +202,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         const bool have = g < ngp;
         float v[32];
         if (have) {
-            load_x_group(a.x, a.K, g, v);
+            load_x_group(a, g, rms, v);
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -207,7 +250,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
                 const float *pr = pb + r * a.npart;
                 float acc = 0.f;
                 for (uint32_t j = 0; j < a.npart; ++j) acc += pr[j];
-                a.y[t0 + r] = acc;
+                a.y[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
             }
             __syncwarp();
             if (it + a.nst < n_tiles) {
@@ -437,11 +480,21 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
 }
 
 int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d_y,
-              cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit)
+              cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit, const MvFuse *fuse)
 {
     const Geom g = geom_of(qtype);
     if (!g.block_weights || !W || !d_x || !d_y || M <= 0 || K <= 0 || K % g.block_weights) return 0;
     MvArgs a{};
+    if (fuse) {
+        if (fuse->xmode > MV_X_SWIGLU || (fuse->xmode == MV_X_RMSNORM && !fuse->nw) ||
+            (fuse->xmode == MV_X_SWIGLU && !fuse->x2))
+            return 0;
+        a.xmode = fuse->xmode;
+        a.x2 = fuse->x2;
+        a.nw = fuse->nw;
+        a.eps = fuse->eps;
+        a.res = fuse->res;
+    }
     a.W = static_cast<const uint8_t *>(W);
     a.x = d_x;
     a.y = d_y;
