@@ -193,6 +193,38 @@ def cpu_sample(items, budget_s: float, nthreads: int, repeat: int = 1):
     return tot_b / tot_t / 1e9, info
 
 
+def decode_bench(ctx: int, n: int, e2e_tokens: int = 16):
+    """batch-1 greedy decode of a random-init Qwen3-8B-shape model
+    (Q4_K weights, Q6_K ffn_down and output) with an N(0,1) fp32 KV prefix of ctx
+    positions, through the library's graph-replayed decoder (tb_cuda_dec_*)."""
+    from trailblaze_b200.decoder import QWEN3_8B, synthetic_model
+    shape = QWEN3_8B
+    t0 = time.perf_counter()
+    dec = synthetic_model(shape, max_ctx=ctx + n + e2e_tokens + 8, ctx=ctx)
+    log(f"[bench] decode model built in {time.perf_counter() - t0:.1f}s")
+    try:
+        dec.generate(1, ctx, 4, want_tokens=False)          # captures the graph, warms up
+        _, ms = dec.generate(1, ctx, n, want_tokens=False)  # n steps back to back, device time
+        tok_s = n / (ms * 1e-3)
+        bpt = shape.bytes_per_token(ctx + n // 2)
+        tok = 1
+        t1 = time.perf_counter()
+        for i in range(e2e_tokens):   # blocking step with the token read back each time
+            tok = dec.step(tok, ctx + i)
+        e2e = e2e_tokens / (time.perf_counter() - t1)
+    finally:
+        dec.close()
+    hbm, kind = peaks()
+    return {"model": "qwen3-8b shape: 36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, ffn 12288, "
+                     "vocab 151936; Q4_K weights, Q6_K ffn_down and output; fp32 KV",
+            "ctx": ctx, "tokens": n, "tok_per_s": round(tok_s, 2), "ms_per_token": round(ms / n, 4),
+            "bytes_per_token": bpt, "GBps": round(bpt * tok_s / 1e9, 1),
+            "frac_of_hbm": round(bpt * tok_s / 1e9 / hbm, 4), "hbm_peak_kind": kind,
+            "e2e_tok_per_s": round(e2e, 2), "e2e_api": "tb_cuda_dec_step (blocking, token read back)",
+            "launches_per_token": 1 + 5 * shape.n_layers + 2,
+            "order": "reference (RoPE before QK-norm, K rotated n_heads/n_kv_heads times)"}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -234,6 +266,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--shape", default=None,
                     help="TYPE:M:K — time this single matvec instead of the sweep (profiling aid)")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3-8B-shape decode tok/s leg")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the decode tok/s leg (its line's value is tok/s; profiling aid)")
+    ap.add_argument("--decode-ctx", type=int, default=4096)
+    ap.add_argument("--decode-tokens", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -255,6 +292,17 @@ def main():
     from trailblaze_b200 import load
     k = load()
     assert k.tb_cuda_init() == 1
+
+    if args.decode_only:
+        with Clocks(local) as clk:
+            d = decode_bench(args.decode_ctx, args.decode_tokens)
+        if rank == 0:
+            print(json.dumps({"metric": "Qwen3-8B-shape Q4_K decode tok/s", "value": d["tok_per_s"],
+                              "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
+                              "dtype": "fp32", "data": "synthetic (seeded torch generator on the device)",
+                              "config": {"workload": "decode only (profiling aid)"}, "decode": d,
+                              "clocks": clk.summary()}), flush=True)
+        return
 
     t_gen = time.perf_counter()
     items, xs_host = workload(rank, world, args.shape)
@@ -401,6 +449,12 @@ def main():
                    "sample": f"unavailable: {type(e).__name__}: {e}"}
 
     clocks = clk.summary()
+    decode = None
+    if world == 1 and not args.no_decode and not args.shape:
+        try:
+            decode = decode_bench(args.decode_ctx, args.decode_tokens)
+        except Exception as e:  # noqa: BLE001 - the decode leg must not sink the sweep line
+            decode = {"unavailable": f"{type(e).__name__}: {e}"}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -430,6 +484,8 @@ def main():
     }
     if e2e:
         line["e2e"] = e2e
+    if decode:
+        line["decode"] = decode
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)

@@ -94,13 +94,16 @@ int   tb_cuda_matvec_dev(const void *W_dev, int qtype, int M, int K,
  *   xmode 0: x                      (d_x2, d_norm_w unused)
  *   xmode 1: x[k] * rms * d_norm_w[k], rms = 1/sqrt(sum(x^2)/K + eps)
  *   xmode 2: silu(x[k]) * d_x2[k],  silu(g) = g / (1 + e^-g)
- * and y[m] = (dequant(W) @ x')[m] + d_res[m] when d_res is not NULL (d_res
- * may be d_y only if nothing else reads d_y meanwhile).  Stream-ordered like
- * tb_cuda_matvec_dev.  1 = issued. */
+ * and the output:
+ *   ymode 0: y[m] = (dequant(W) @ x')[m] + d_res[m] (d_res may be NULL)
+ *   ymode 1: W's rows are (gate, up) pairs and y[i] = silu(row 2i . x') *
+ *            (row 2i+1 . x'), M/2 outputs (M even, d_res must be NULL)
+ * d_res may be d_y only if nothing else reads d_y meanwhile.  Stream-ordered
+ * like tb_cuda_matvec_dev.  1 = issued. */
 int   tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K,
                                const float *d_x, float *d_y, int xmode, const float *d_x2,
                                const float *d_norm_w, float eps, const float *d_res,
-                               void *stream);
+                               int ymode, void *stream);
 
 /* Bit-exact dequantisation of M rows of K weights into d_out[M*K] (fp32),
  * stream-ordered.  sem = 0 gives the reference CUDA-kernel semantics (the
@@ -159,8 +162,9 @@ typedef struct {
 
 /* One layer's device tensors.  w_qkv is the fused projection (rows: the
  * n_heads*head_dim q rows, then n_kv_heads*head_dim k rows, then v rows; the
- * reference's blk.N.attn_qkv layout, tb_infer.c:640-649); w_gate_up holds the
- * ffn_dim gate rows followed by the ffn_dim up rows.  Norm weights are fp32
+ * reference's blk.N.attn_qkv layout, tb_infer.c:640-649); w_gate_up holds
+ * the gate and up rows interleaved (row 2i = gate row i, row 2i+1 = up row i),
+ * so that one matvec also applies SwiGLU.  Norm weights are fp32
  * device vectors; q_norm / k_norm may be NULL (no QK-norm).  The decoder keeps
  * the pointers; the caller keeps ownership. */
 typedef struct {
@@ -181,9 +185,9 @@ int    tb_cuda_dec_set_head(void *dec, const void *tok_embd, int embd_qtype, con
 /* Device pointer of a layer's K (which = 0) or V (which = 1) cache,
  * [n_kv_heads][max_ctx][head_dim] fp32, e.g. to load a prefix. */
 float *tb_cuda_dec_kv(void *dec, int layer, int which);
-/* Copies positions [p0, p0 + n) of a layer's K (which = 0) or V (1) cache to
- * the device (to_device = 1, e.g. a prefix) or back to the host (0); the host
- * side is [n_kv_heads][n][head_dim] fp32.  Blocking.  1 = ok. */
+/* Copies positions [p0, p0 + n) of a layer's K (which = 0) or V (1) cache in
+ * (to_device = 1, e.g. a prefix) or out (0); the other side, `host`, is
+ * [n_kv_heads][n][head_dim] fp32 in host or device memory.  Blocking.  1 = ok. */
 int    tb_cuda_dec_kv_copy(void *dec, int layer, int which, int p0, int n, float *host, int to_device);
 /* One token at position pos: *next_token = greedy argmax; logits_host (may be
  * NULL) receives the vocab logits.  Blocking.  1 = ok. */

@@ -12,7 +12,8 @@ numpy, float64, following layer4/tb_infer.c:553-887 (tb_layer_forward) and
   KV append, attn     layer1/tb_tensor.c:303-409 (scale 1/sqrt(HD), softmax over 0..pos)
   output + residual   tb_infer.c:719-731
   FFN RMSNorm         tb_infer.c:734-745
-  gate/up, SwiGLU     tb_infer.c:862-866, :130-135 (g / (1 + e^-g) * u)
+  gate/up, SwiGLU     tb_infer.c:862-866, :130-135 (g / (1 + e^-g) * u); the two
+                      projections are one tensor here, rows interleaved (gate_i, up_i)
   down + residual     tb_infer.c:866, :876
   final norm, head    tb_infer.c:987-1019
   greedy              layer1/tb_tensor.c:415-420 (first index of the maximum)
@@ -179,6 +180,6 @@ class DecodeOracle:
             att = attention(q, self.kc[li, :, :pos + 1], self.vc[li, :, :pos + 1], NH, NK)
             x2 = x + w["wo"] @ att.reshape(-1)
             gu = w["wgu"] @ rms_norm(x2, w["ffn_norm"], eps)
-            x = x2 + w["wd"] @ swiglu(gu[:F], gu[F:])
+            x = x2 + w["wd"] @ swiglu(gu[0::2], gu[1::2])   # (gate, up) rows interleaved
         logits = self.lm @ rms_norm(x, self.out_norm, eps)
         return logits, int(np.argmax(logits))

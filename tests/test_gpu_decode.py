@@ -188,7 +188,21 @@ def test_fused_matvec_modes(kq):
     ]
     for xmode, _, ref in cases:
         assert kq.tb_cuda_matvec_fused_dev(dW.data_ptr(), Q.Q4_K, M, K, dx.data_ptr(), dy.data_ptr(), xmode,
-                                           dx2.data_ptr(), dnw.data_ptr(), 1e-5, dres.data_ptr(), st) == 1
+                                           dx2.data_ptr(), dnw.data_ptr(), 1e-5, dres.data_ptr(), ymode=0,
+                                           stream=st) == 1
         torch.cuda.synchronize()
         assert rel_l2(dy.cpu().numpy(), ref) <= 3e-4, xmode
+    # (gate, up) row pairs: y[i] = silu(row 2i . x') * (row 2i+1 . x'), RMSNorm input
+    xn = xd / np.sqrt(np.mean(xd * xd) + 1e-5) * nw
+    ref = (Wd[0::2] @ xn / (1 + np.exp(-(Wd[0::2] @ xn)))) * (Wd[1::2] @ xn)
+    dy.zero_()
+    assert kq.tb_cuda_matvec_fused_dev(dW.data_ptr(), Q.Q4_K, M, K, dx.data_ptr(), dy.data_ptr(), 1, 0,
+                                       dnw.data_ptr(), 1e-5, 0, ymode=1, stream=st) == 1
+    torch.cuda.synchronize()
+    assert rel_l2(dy.cpu().numpy()[:M // 2], ref) <= 3e-4
+    # the pair mode rejects an odd row count and a residual
+    assert kq.tb_cuda_matvec_fused_dev(dW.data_ptr(), Q.Q4_K, M - 1, K, dx.data_ptr(), dy.data_ptr(), 0, 0, 0,
+                                       0.0, 0, ymode=1, stream=st) == 0
+    assert kq.tb_cuda_matvec_fused_dev(dW.data_ptr(), Q.Q4_K, M, K, dx.data_ptr(), dy.data_ptr(), 0, 0, 0,
+                                       0.0, dres.data_ptr(), ymode=1, stream=st) == 0
     assert kq.tb_cuda_last_error() == 0

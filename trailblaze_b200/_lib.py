@@ -60,7 +60,7 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_version": (ctypes.c_char_p, []),
         "tb_cuda_matvec_device_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, fp, fp]),
         "tb_cuda_matvec_fused_dev": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
-                                             c_void_p, c_void_p, ctypes.c_float, c_void_p, c_void_p]),
+                                             c_void_p, c_void_p, ctypes.c_float, c_void_p, c_int, c_void_p]),
         "tb_cuda_dec_create": (c_void_p, [ctypes.POINTER(DecConfig)]),
         "tb_cuda_dec_set_layer": (c_int, [c_void_p, c_int, ctypes.POINTER(DecLayer)]),
         "tb_cuda_dec_set_head": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int]),

@@ -328,7 +328,7 @@ int tb_cuda_matvec_dev(const void *W_dev, int qtype, int M, int K, const float *
 
 int tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K, const float *d_x, float *d_y,
                              int xmode, const float *d_x2, const float *d_norm_w, float eps,
-                             const float *d_res, void *stream)
+                             const float *d_res, int ymode, void *stream)
 {
     int nsm;
     int *derr;
@@ -340,9 +340,10 @@ int tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K, const f
         derr = g.d_err;
         lim = g.wait_limit;
     }
-    if (xmode < 0) return 0;
+    if (xmode < 0 || ymode < 0) return 0;
     tb::MvFuse f;
     f.xmode = static_cast<uint32_t>(xmode);
+    f.ymode = static_cast<uint32_t>(ymode);
     f.x2 = d_x2;
     f.nw = d_norm_w;
     f.eps = eps;

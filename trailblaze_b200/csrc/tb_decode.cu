@@ -83,17 +83,30 @@ __device__ __forceinline__ void head_norm_warp(float *hv, const float *w, float 
     __syncwarp();
 }
 
+static constexpr int kVMax = 128;          // context positions per attention CTA at most
+static constexpr int kKB = (kVMax + 7) / 8; // K rows held in registers per warp
+
 __host__ __device__ inline size_t attn_smem_floats(int rep, int lmax)
 {
     const size_t area = static_cast<size_t>(rep) * lmax > 8ull * rep * kHD ? static_cast<size_t>(rep) * lmax
                                                                            : 8ull * rep * kHD;
-    return static_cast<size_t>(rep) * kHD + kHD + 32 + area;
+    return static_cast<size_t>(rep) * kHD + kHD + 32 + area + static_cast<size_t>(lmax) * kHD;
 }
 
-// grid (NK, nchunk), kAttnThreads threads.  Shared memory (attn_smem_floats):
-// q[rep][HD], k[HD], chunk statistics [2][16], then one area used first for
-// the scores [rep][lmax] and then for the pass-2 partials [8][rep][HD].
-__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a)
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+
+// grid (NK, nchunk), kAttnThreads threads, 2 CTAs per SM.  Shared memory
+// (attn_smem_floats): q[rep][HD], k[HD], chunk statistics [32], a work area
+// (the scores [rep][lmax], later the pass-2 partials [8][rep][HD] and the
+// chunk weights), and the chunk's V rows [lmax][HD].
+//
+// Every load of the chunk is issued at the start: each warp's K rows into
+// registers, every V row into shared memory with cp.async; q is rotated and
+// normed meanwhile, so the DRAM latency is paid about once per CTA.
+__global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs a)
 {
     extern __shared__ __align__(16) float sm[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -110,9 +123,29 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a)
 
     float *qs = sm;                         // [rep][HD]
     float *ks = qs + rep * kHD;             // [HD]
-    float *red = ks + kHD;                  // [2][16]: m, l per head
-    float *sc = red + 32;                   // scores, then pass-2 partials
+    float *red = ks + kHD;                  // [32]: m, l per head; later 1/L per head
+    float *sc = red + 32;                   // scores / pass-2 partials / chunk weights
+    const size_t area = static_cast<size_t>(rep) * a.lmax > 8ull * rep * kHD ? static_cast<size_t>(rep) * a.lmax
+                                                                             : 8ull * rep * kHD;
+    float *vs = sc + area;                  // [lmax][HD]
     __shared__ int s_last;
+
+    const float *kcache = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
+    float *kcw = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
+    float *vcache = a.vc + static_cast<size_t>(kh) * a.max_ctx * kHD;
+    const float *vnew = a.qkv + (a.NH + a.NK) * kHD + kh * kHD;
+
+    // ---- every load of the chunk, issued up front ----
+    for (int e = tid; e < (t1 - t0) * (kHD / 4); e += kAttnThreads)
+        cp_async16(vs + 4 * e, vcache + static_cast<size_t>(t0) * kHD + 4 * e);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    float4 kv[kKB];
+#pragma unroll
+    for (int j = 0; j < kKB; ++j) {
+        const int t = t0 + warp + j * nwarp;
+        kv[j] = t < t1 ? __ldg(reinterpret_cast<const float4 *>(kcache + static_cast<size_t>(t) * kHD) + lane)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 
     // ---- q (and, for the owner, k) of this KV head, normed and rotated ----
     const float *qsrc = a.qkv + kh * rep * kHD;
@@ -147,27 +180,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a)
         norm_all();
         rope_all();
     }
-    float *kcache = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
-    float *vcache = a.vc + static_cast<size_t>(kh) * a.max_ctx * kHD;
-    if (owner) {   // append (tb_tensor.c:314-323); only this CTA reads position pos
+    if (owner)   // append (tb_tensor.c:314-323); nothing else reads position pos now
         for (int e = tid; e < kHD; e += kAttnThreads) {
-            kcache[static_cast<size_t>(pos) * kHD + e] = ks[e];
-            vcache[static_cast<size_t>(pos) * kHD + e] = __ldg(a.qkv + (a.NH + a.NK) * kHD + kh * kHD + e);
+            kcw[static_cast<size_t>(pos) * kHD + e] = ks[e];
+            vcache[static_cast<size_t>(pos) * kHD + e] = __ldg(vnew + e);
         }
-        __threadfence_block();
-        __syncthreads();
-    }
 
-    // ---- pass 1: scores of this chunk, one warp per position, lanes over dims ----
-    for (int t = t0 + warp; t < t1; t += nwarp) {
-        const float4 kv = (t == pos && owner) ? reinterpret_cast<const float4 *>(ks)[lane]
-                                              : __ldg(reinterpret_cast<const float4 *>(kcache + static_cast<size_t>(t) * kHD) + lane);
+    // ---- pass 1: scores; warp w holds the K rows of positions t0 + w + 8j ----
+#pragma unroll
+    for (int j = 0; j < kKB; ++j) {
+        const int t = t0 + warp + j * nwarp;
+        if (t >= t1) break;
+        const float4 k4 = (t == pos && owner) ? reinterpret_cast<const float4 *>(ks)[lane] : kv[j];
         for (int h = 0; h < rep; ++h) {
             const float4 q = reinterpret_cast<const float4 *>(qs + h * kHD)[lane];
-            float d = q.x * kv.x;
-            d = fmaf(q.y, kv.y, d);
-            d = fmaf(q.z, kv.z, d);
-            d = fmaf(q.w, kv.w, d);
+            float d = q.x * k4.x;
+            d = fmaf(q.y, k4.y, d);
+            d = fmaf(q.z, k4.z, d);
+            d = fmaf(q.w, k4.w, d);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
             if (lane == 0) sc[h * a.lmax + (t - t0)] = d * a.scale;
@@ -195,26 +225,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a)
             red[2 * h + 1] = l;
         }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    if (owner)   // the new V row replaces the stale one copied from the cache
+        for (int e = tid; e < kHD; e += kAttnThreads) vs[(pos - t0) * kHD + e] = __ldg(vnew + e);
     __syncthreads();
 
     // ---- pass 2: o[h][d] = sum_t p[h][t] * v[t][d]; thread = (dim quad, position lane) ----
-    // 32 dim quads x 8 position lanes; each thread keeps rep float4 partials.
     {
         const int dq = tid & 31, tl = tid >> 5;   // dims 4*dq..4*dq+3, positions t0 + tl + 8k
         float4 acc[8];
 #pragma unroll
         for (int h = 0; h < 8; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int t = t0 + tl; t < t1; t += 8) {
-            float4 v;
-            if (t == pos && owner) {
-                v = __ldg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK) * kHD + kh * kHD) + dq);
-            } else {
-                v = __ldg(reinterpret_cast<const float4 *>(vcache + static_cast<size_t>(t) * kHD) + dq);
-            }
+        for (int j = tl; j < n; j += 8) {
+            const float4 v = reinterpret_cast<const float4 *>(vs + j * kHD)[dq];
 #pragma unroll
             for (int h = 0; h < 8; ++h) {
                 if (h < rep) {
-                    const float p = sc[h * a.lmax + (t - t0)];
+                    const float p = sc[h * a.lmax + j];
                     acc[h].x = fmaf(p, v.x, acc[h].x);
                     acc[h].y = fmaf(p, v.y, acc[h].y);
                     acc[h].z = fmaf(p, v.z, acc[h].z);
@@ -254,19 +282,50 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnArgs a)
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int e = tid; e < rep * kHD; e += kAttnThreads) {
-        const int h = e / kHD, d = e % kHD;
-        const float *ph = a.part + static_cast<size_t>(kh * rep + h) * a.nchunk * kPS;
+    // chunk weights w[h][u] = e^(m_u - M_h) and 1/L per head into shared memory,
+    // then each output float4 is a weighted sum over the chunks
+    float *wts = sc;                                  // [rep][nchunk]
+    float *hm = red;                                  // [rep] 1/L
+    const float *pk = a.part + static_cast<size_t>(kh * rep) * a.nchunk * kPS;
+    for (int h = warp; h < rep; h += nwarp) {
+        const float *ph = pk + static_cast<size_t>(h) * a.nchunk * kPS;
         float M = -1e38f;
-        for (int u = 0; u < a.nchunk; ++u) M = fmaxf(M, __ldcg(ph + u * kPS + kHD));
-        float Lsum = 0.f, o = 0.f;
-        for (int u = 0; u < a.nchunk; ++u) {
-            const float *pu = ph + u * kPS;
-            const float w = expf(__ldcg(pu + kHD) - M);
-            Lsum = fmaf(__ldcg(pu + kHD + 1), w, Lsum);
-            o = fmaf(__ldcg(pu + d), w, o);
+        for (int u = lane; u < a.nchunk; u += 32) M = fmaxf(M, __ldcg(ph + u * kPS + kHD));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+        float Ls = 0.f;
+        for (int u = lane; u < a.nchunk; u += 32) {
+            const float w = expf(__ldcg(ph + u * kPS + kHD) - M);
+            wts[h * a.nchunk + u] = w;
+            Ls = fmaf(__ldcg(ph + u * kPS + kHD + 1), w, Ls);
         }
-        a.out[(kh * rep + h) * kHD + d] = Lsum > 0.f ? o * (1.0f / Lsum) : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xFFFFFFFFu, Ls, o);
+        if (lane == 0) hm[h] = Ls > 0.f ? 1.0f / Ls : 0.f;
+    }
+    __syncthreads();
+    constexpr int kCB = 8;
+    for (int e = tid; e < rep * (kHD / 4); e += kAttnThreads) {   // one float4 of one head per thread
+        const int h = e / (kHD / 4), q4 = e % (kHD / 4);
+        const float *ph = pk + static_cast<size_t>(h) * a.nchunk * kPS;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int u0 = 0; u0 < a.nchunk; u0 += kCB) {
+            float4 ob[kCB];
+#pragma unroll
+            for (int j = 0; j < kCB; ++j)
+                ob[j] = u0 + j < a.nchunk ? __ldcg(reinterpret_cast<const float4 *>(ph + (u0 + j) * kPS) + q4)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < kCB; ++j) {
+                const float w = u0 + j < a.nchunk ? wts[h * a.nchunk + u0 + j] : 0.f;
+                o.x = fmaf(ob[j].x, w, o.x);
+                o.y = fmaf(ob[j].y, w, o.y);
+                o.z = fmaf(ob[j].z, w, o.z);
+                o.w = fmaf(ob[j].w, w, o.w);
+            }
+        }
+        const float il = hm[h];
+        reinterpret_cast<float4 *>(a.out + (kh * rep + h) * kHD)[q4] = make_float4(o.x * il, o.y * il, o.z * il, o.w * il);
     }
     if (tid == 0) a.count[kh] = 0u;   // ready for the next layer / token
 }
@@ -436,16 +495,15 @@ bool Decoder::enqueue(cudaStream_t s)
         f = MvFuse{};
         f.res = x;
         if (!mv_launch(w.wo, w.o_qt, H, NH * HD, att, x2, s, err, sms, lim, &f)) return false;
-        // gate | up = Wgu @ rmsnorm(x2)
+        // act = swiglu(gate, up), (gate | up) rows interleaved in Wgu, of rmsnorm(x2)
         f = MvFuse{};
         f.xmode = MV_X_RMSNORM;
         f.nw = w.ffn_norm;
         f.eps = c.norm_eps;
+        f.ymode = MV_Y_SWIGLU_PAIRS;
         if (!mv_launch(w.wgu, w.gu_qt, 2 * F, H, x2, gu, s, err, sms, lim, &f)) return false;
-        // x = x2 + Wd @ swiglu(gate, up)
+        // x = x2 + Wd @ act
         f = MvFuse{};
-        f.xmode = MV_X_SWIGLU;
-        f.x2 = gu + F;
         f.res = x2;
         if (!mv_launch(w.wd, w.d_qt, H, F, gu, x, s, err, sms, lim, &f)) return false;
     }
@@ -496,8 +554,10 @@ Decoder *dec_create(const DecConfig &c)
     cudaGetDevice(&d->dev);
     cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, d->dev);
     // context chunks: about four attention CTAs per SM over all KV heads
-    d->nchunk = (4 * d->sms + c.n_kv_heads - 1) / c.n_kv_heads;
-    if (d->nchunk > (c.max_ctx + 15) / 16) d->nchunk = (c.max_ctx + 15) / 16;
+    // context chunks: one wave of two attention CTAs per SM over all KV heads,
+    // more if a chunk would exceed kVMax positions (its V rows live in shared memory)
+    d->nchunk = (2 * d->sms) / c.n_kv_heads;
+    if (d->nchunk < (c.max_ctx + kVMax - 1) / kVMax) d->nchunk = (c.max_ctx + kVMax - 1) / kVMax;
     if (d->nchunk < 1) d->nchunk = 1;
     d->lmax = (c.max_ctx + d->nchunk - 1) / d->nchunk;
     const int NH = c.n_heads, NK = c.n_kv_heads, HD = c.head_dim;
@@ -674,9 +734,10 @@ int tb_cuda_dec_kv_copy(void *dec, int layer, int which, int p0, int n, float *h
     // host [n_kv_heads][n][head_dim] <-> device [n_kv_heads][max_ctx][head_dim] at position p0
     float *dev = base + static_cast<size_t>(p0) * d->cfg.head_dim;
     const size_t dpitch = static_cast<size_t>(d->cfg.max_ctx) * hd, hpitch = static_cast<size_t>(n) * hd;
+    // cudaMemcpyDefault: `host` may also be device memory (unified addressing)
     const cudaError_t e = to_device
-        ? cudaMemcpy2DAsync(dev, dpitch, host, hpitch, hpitch, d->cfg.n_kv_heads, cudaMemcpyHostToDevice, d->st)
-        : cudaMemcpy2DAsync(host, hpitch, dev, dpitch, hpitch, d->cfg.n_kv_heads, cudaMemcpyDeviceToHost, d->st);
+        ? cudaMemcpy2DAsync(dev, dpitch, host, hpitch, hpitch, d->cfg.n_kv_heads, cudaMemcpyDefault, d->st)
+        : cudaMemcpy2DAsync(host, hpitch, dev, dpitch, hpitch, d->cfg.n_kv_heads, cudaMemcpyDefault, d->st);
     if (!tb::dec_ok(e, "kv copy")) return 0;
     return tb::dec_ok(cudaStreamSynchronize(d->st), "kv copy sync") ? 1 : 0;
 }

@@ -8,8 +8,11 @@ namespace tb {
 
 // Fused transforms of the matvec's input and output (see tb_cuda_matvec_fused_dev).
 enum MvXMode : uint32_t { MV_X_PLAIN = 0, MV_X_RMSNORM = 1, MV_X_SWIGLU = 2 };
+// MV_Y_SWIGLU_PAIRS: rows come in (gate, up) pairs; y[i] = silu(row 2i) * row 2i+1 (M/2 outputs)
+enum MvYMode : uint32_t { MV_Y_PLAIN = 0, MV_Y_SWIGLU_PAIRS = 1 };
 struct MvFuse {
     uint32_t xmode = MV_X_PLAIN;
+    uint32_t ymode = MV_Y_PLAIN;
     const float *x2 = nullptr;    // SwiGLU: the up vector
     const float *nw = nullptr;    // RMSNorm: the norm weights
     float eps = 0.f;              // RMSNorm epsilon

@@ -55,7 +55,7 @@ struct MvArgs {
     // fused input / output transforms (MvFuse): x is x (plain), x*rms*nw
     // (RMSNorm, rms = 1/sqrt(mean(x^2) + eps)) or silu(x)*x2 (SwiGLU); y gets
     // res added when res is not null
-    uint32_t xmode;
+    uint32_t xmode, ymode;
     const float *x2, *nw, *res;
     float eps;
 };
@@ -83,18 +83,15 @@ __host__ __device__ inline MvSmem mv_smem(uint32_t nst, uint32_t cs, uint32_t re
     return s;
 }
 
-// The 32 activations of group g (zeros past K), after the fused input
-// transform: x * rms * nw (layer/tb_tensor.c:194-199 order) or
-// silu(x) * x2 with silu(g) = g / (1 + e^-g) (layer4/tb_infer.c:130-135).
-__device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t g, float rms, float (&v)[32])
+// Elements [k0, k0 + 32) of p (zeros past K): eight 16-byte loads when the
+// whole run is inside K and p is 16-byte aligned.
+__device__ __forceinline__ void load32(const float *p, uint32_t k0, uint32_t K, float (&v)[32])
 {
-    const uint32_t k0 = 32 * g;
-    const float *x = a.x;
-    if (k0 + 32 <= a.K && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
-        const float4 *p = reinterpret_cast<const float4 *>(x + k0);
+    if (k0 + 32 <= K && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        const float4 *q = reinterpret_cast<const float4 *>(p + k0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float4 t = __ldg(p + i);
+            const float4 t = __ldg(q + i);
             v[4 * i] = t.x;
             v[4 * i + 1] = t.y;
             v[4 * i + 2] = t.z;
@@ -102,40 +99,46 @@ __device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t g, float 
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = k0 + i < a.K ? __ldg(x + k0 + i) : 0.f;
-    }
-    if (a.xmode == MV_X_RMSNORM) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (k0 + i < a.K) v[i] = v[i] * rms * __ldg(a.nw + k0 + i);
-    } else if (a.xmode == MV_X_SWIGLU) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (k0 + i < a.K) v[i] = (v[i] / (1.0f + expf(-v[i]))) * __ldg(a.x2 + k0 + i);
+        for (int i = 0; i < 32; ++i) v[i] = k0 + i < K ? __ldg(p + k0 + i) : 0.f;
     }
 }
 
-// 1/sqrt(sum(x^2)/K + eps) over the whole of x, computed by every CTA (K is a
-// few thousand floats); red = 64 floats of shared scratch.
-__device__ __forceinline__ float block_rms(const MvArgs &a, float *red)
+// The 32 activations of group g (zeros past K) after the fused input
+// transform, and ss += the sum of the squares of the raw x.
+//   RMSNorm: x * nw; the scalar 1/rms of layer1/tb_tensor.c:194-199 is applied
+//            to each slot's scale once the whole sum of squares is known.
+//   SwiGLU:  silu(x) * x2, silu(g) = g / (1 + e^-g) (layer4/tb_infer.c:130-135).
+__device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t g, float (&v)[32], float &ss)
 {
-    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float ss = 0.f;
-    for (uint32_t k = tid; k < a.K; k += blockDim.x) {
-        const float t = __ldg(a.x + k);
-        ss = fmaf(t, t, ss);
-    }
+    const uint32_t k0 = 32 * g;
+    load32(a.x, k0, a.K, v);
+    if (a.xmode == MV_X_RMSNORM) {
+        float w[32];
+        load32(a.nw, k0, a.K, w);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    if (tid == 0) {
-        float t = 0.f;
-        for (uint32_t w = 0; w < blockDim.x / 32; ++w) t += red[w];
-        red[32] = 1.0f / sqrtf(t / static_cast<float>(a.K) + a.eps);
+        for (int i = 0; i < 32; ++i) {
+            ss = fmaf(v[i], v[i], ss);
+            v[i] *= w[i];
+        }
+    } else if (a.xmode == MV_X_SWIGLU) {
+        float u[32];
+        load32(a.x2, k0, a.K, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = (v[i] / (1.0f + expf(-v[i]))) * u[i];
     }
-    __syncthreads();
-    return red[32];
+}
+
+// A lane's activations scaled by f (the RMSNorm factor): the slot scale of the
+// integer path, the activation registers of the float path.
+template <class LY>
+__device__ __forceinline__ void lane_scale(LaneInt<LY> &L, float f)
+{
+    L.r[LY::SX] = __float_as_uint(__uint_as_float(L.r[LY::SX]) * f);
+}
+__device__ __forceinline__ void lane_scale(XRegs &L, float f)
+{
+#pragma unroll
+    for (int q = 0; q < 16; ++q) L.a[q] = make_float2(L.a[q].x * f, L.a[q].y * f);
 }
 
 template <class D>
@@ -145,8 +148,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
 
     const uint32_t G = gridDim.x, c = blockIdx.x;
-    const uint32_t r_lo = static_cast<uint32_t>((static_cast<unsigned long long>(a.M) * c) / G);
-    const uint32_t r_hi = static_cast<uint32_t>((static_cast<unsigned long long>(a.M) * (c + 1)) / G);
+    const uint32_t ua = a.ymode == MV_Y_SWIGLU_PAIRS ? 2u : 1u;   // rows per output unit
+    const uint32_t r_lo = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * c) / G);
+    const uint32_t r_hi = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * (c + 1)) / G);
     if (r_lo >= r_hi) return;
     const uint32_t n_tiles = (r_hi - r_lo + a.tr - 1) / a.tr;
     const uint32_t ngp = a.cs * D::GPL;   // groups of all slots (past K: zeros)
@@ -194,15 +198,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     }
 
     // ---- prologue: x -> one record per column slot ----
-    const float rms = a.xmode == MV_X_RMSNORM ? block_rms(a, reinterpret_cast<float *>(smem + L.red)) : 1.f;
     // Thread g handles group g (then g + nthr, ...).  The GPL groups of a slot
     // are neighbouring lanes of one warp, so the slot's largest |x| is a shuffle.
+    float ss = 0.f;   // RMSNorm: this thread's share of sum(x^2)
+    float *red = reinterpret_cast<float *>(smem + L.red);
     for (uint32_t base = 0; base < ngp; base += nthr) {   // same trip count in every thread
         const uint32_t g = base + tid;
         const bool have = g < ngp;
         float v[32];
         if (have) {
-            load_x_group(a, g, rms, v);
+            load_x_group(a, g, v, ss);
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -227,6 +232,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             if (have) prep_float(v, rec);
         }
     }
+    if (a.xmode == MV_X_RMSNORM) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+        if (lane == 0) red[warp] = ss;
+    }
     __syncthreads();   // records complete; barrier inits visible
 
     if (producer) {
@@ -246,11 +256,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             }
             done = it + 1;
             const uint32_t nrows = min(a.tr, r_hi - t0);
-            for (uint32_t r = lane; r < nrows; r += 32) {
-                const float *pr = pb + r * a.npart;
-                float acc = 0.f;
-                for (uint32_t j = 0; j < a.npart; ++j) acc += pr[j];
-                a.y[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
+            if (a.ymode == MV_Y_SWIGLU_PAIRS) {   // tiles hold whole (gate, up) pairs
+                for (uint32_t r = 2 * lane; r < nrows; r += 64) {
+                    const float *pg = pb + r * a.npart, *pu = pg + a.npart;
+                    float gs = 0.f, us = 0.f;
+                    for (uint32_t j = 0; j < a.npart; ++j) {
+                        gs += pg[j];
+                        us += pu[j];
+                    }
+                    a.y[(t0 + r) / 2] = (gs / (1.0f + expf(-gs))) * us;
+                }
+            } else {
+                for (uint32_t r = lane; r < nrows; r += 32) {
+                    const float *pr = pb + r * a.npart;
+                    float acc = 0.f;
+                    for (uint32_t j = 0; j < a.npart; ++j) acc += pr[j];
+                    a.y[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
+                }
             }
             __syncwarp();
             if (it + a.nst < n_tiles) {
@@ -301,6 +323,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     pos.n = static_cast<int>(min(32u, a.K - min(a.K, 32u * (g0 + pos.ng - 1))));
     typename D::Lane lx;
     D::load(lx, table + cs * D::REC);
+    if (a.xmode == MV_X_RMSNORM) {   // 1/sqrt(sum(x^2)/K + eps), summed in warp order
+        float t = 0.f;
+        for (uint32_t w = 0; w < nthr / 32; ++w) t += red[w];
+        lane_scale(lx, 1.0f / sqrtf(t / static_cast<float>(a.K) + a.eps));
+    }
     const uint32_t row_bytes32 = static_cast<uint32_t>(a.row_bytes);   // a tile's rows fit one stage
     const bool writer = active && (cs % a.rw) == 0;
     const uint32_t part_col = cs / a.rw;
@@ -352,7 +379,7 @@ static constexpr uint32_t kMaxStages = 8;
 
 struct Plan {
     const void *kern;
-    uint32_t M, K, sms;
+    uint32_t M, K, sms, ymode;
     int dev;
     uint32_t nthr, grid, cs, phases, rpl, tr, rw, npart, nst, cap, ncw;
     size_t smem;
@@ -395,6 +422,7 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
     for (uint32_t rpl = kMaxRpl; rpl >= 1 && !p.nst; --rpl) {
         const unsigned long long bytes = static_cast<unsigned long long>(p.phases) * rpl * row_bytes;
         if (rpl > 1 && bytes > kStageMax) continue;
+        if (p.ymode == MV_Y_SWIGLU_PAIRS && (p.phases * rpl) % 2) continue;   // tiles of whole pairs
         const uint32_t tr = p.phases * rpl;
         const uint32_t cap = static_cast<uint32_t>((bytes + 32 + 127) & ~127ull);
         for (uint32_t n = kMaxStages; n >= 2; --n) {
@@ -428,7 +456,8 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
     const Plan *p = nullptr;
     for (int i = 0; i < t_nplans; ++i) {
         const Plan &q = t_plans[i];
-        if (q.kern == kp && q.M == a.M && q.K == a.K && q.dev == dev && q.sms == static_cast<uint32_t>(num_sms)) {
+        if (q.kern == kp && q.M == a.M && q.K == a.K && q.dev == dev && q.sms == static_cast<uint32_t>(num_sms) &&
+            q.ymode == a.ymode) {
             p = &q;
             break;
         }
@@ -441,6 +470,7 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
         np.K = a.K;
         np.dev = dev;
         np.sms = static_cast<uint32_t>(num_sms);
+        np.ymode = a.ymode;
         if (!make_plan<D>(np, a.row_bytes)) return 0;
         if (getenv("TB_MV_VERBOSE"))
             fprintf(stderr,
@@ -489,7 +519,10 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
         if (fuse->xmode > MV_X_SWIGLU || (fuse->xmode == MV_X_RMSNORM && !fuse->nw) ||
             (fuse->xmode == MV_X_SWIGLU && !fuse->x2))
             return 0;
+        if (fuse->ymode > MV_Y_SWIGLU_PAIRS || (fuse->ymode == MV_Y_SWIGLU_PAIRS && (M % 2 || fuse->res)))
+            return 0;
         a.xmode = fuse->xmode;
+        a.ymode = fuse->ymode;
         a.x2 = fuse->x2;
         a.nw = fuse->nw;
         a.eps = fuse->eps;

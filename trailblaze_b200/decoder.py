@@ -1,0 +1,148 @@
+"""Python handle on the library's decode step (tb_cuda_dec_*, include/tb_gguf_dequant.h part 3).
+
+`Decoder` wraps the C ABI; `synthetic_model` fills one with random-init
+weights of a given shape directly in device memory (for benchmarks):
+
+  quant bytes        uniform random bytes
+  fp16 d / dmin      |N(0,1)| * 0.01 at the type's header offsets
+  norm weights       1 + 0.1 * N(0,1) (fp32)
+  KV prefix          N(0,1) (fp32), positions [0, ctx)
+
+Everything is drawn from one seeded torch generator on the device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+from . import qtypes as Q
+from ._lib import DecConfig, DecLayer, lib
+
+
+@dataclass
+class ModelShape:
+    n_layers: int
+    hidden: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn_dim: int
+    vocab: int
+    rope_base: float = 1e6
+    norm_eps: float = 1e-6
+    w_qt: int = Q.Q4_K       # q/k/v/o/gate/up and the token embedding
+    down_qt: int = Q.Q6_K    # ffn_down
+    out_qt: int = Q.Q6_K     # output (lm head)
+
+    def bytes_per_token(self, ctx: int) -> int:
+        """Algorithmic HBM bytes of one decode step at context ctx (weights once,
+        K and V of every layer over ctx positions, activations negligible)."""
+        H, NH, NK, HD, F = self.hidden, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn_dim
+        per_layer = (Q.row_bytes(self.w_qt, H) * ((NH + 2 * NK) * HD + 2 * F) +
+                     Q.row_bytes(self.w_qt, NH * HD) * H + Q.row_bytes(self.down_qt, F) * H +
+                     2 * NK * ctx * HD * 4)
+        return self.n_layers * per_layer + Q.row_bytes(self.out_qt, H) * self.vocab + Q.row_bytes(self.w_qt, H)
+
+
+# Qwen3-8B shape
+QWEN3_8B = ModelShape(36, 4096, 32, 8, 128, 12288, 151936)
+
+
+class Decoder:
+    def __init__(self, shape: ModelShape, max_ctx: int, quirks: bool = True):
+        self.L = lib()
+        self.shape, self.max_ctx = shape, max_ctx
+        s = shape
+        self.cfg = DecConfig(s.n_layers, s.hidden, s.n_heads, s.n_kv_heads, s.head_dim, s.ffn_dim, s.vocab,
+                             max_ctx, s.rope_base, s.norm_eps, 1 if quirks else 0)
+        self.d = self.L.tb_cuda_dec_create(ctypes.byref(self.cfg))
+        if not self.d:
+            raise RuntimeError("tb_cuda_dec_create failed")
+        self._keep = []
+
+    def set_layer(self, li: int, wqkv, qkv_qt, wo, o_qt, wgu, gu_qt, wd, d_qt, attn_norm, ffn_norm,
+                  q_norm=None, k_norm=None):
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        lw = DecLayer(ptr(wqkv), qkv_qt, ptr(wo), o_qt, ptr(wgu), gu_qt, ptr(wd), d_qt, ptr(attn_norm),
+                      ptr(ffn_norm), ptr(q_norm), ptr(k_norm))
+        self._keep += [wqkv, wo, wgu, wd, attn_norm, ffn_norm, q_norm, k_norm]
+        if self.L.tb_cuda_dec_set_layer(self.d, li, ctypes.byref(lw)) != 1:
+            raise RuntimeError(f"tb_cuda_dec_set_layer({li}) failed")
+
+    def set_head(self, emb, emb_qt, out_norm, w_out, out_qt):
+        self._keep += [emb, out_norm, w_out]
+        if self.L.tb_cuda_dec_set_head(self.d, emb.data_ptr(), emb_qt, out_norm.data_ptr(), w_out.data_ptr(),
+                                       out_qt) != 1:
+            raise RuntimeError("tb_cuda_dec_set_head failed")
+
+    def load_kv(self, li: int, which: int, t) -> None:
+        """t: [n_kv_heads][n][head_dim] fp32 (host or device tensor), loaded at positions [0, n)."""
+        t = t.contiguous()
+        fp = ctypes.cast(ctypes.c_void_p(t.data_ptr()), ctypes.POINTER(ctypes.c_float))
+        if self.L.tb_cuda_dec_kv_copy(self.d, li, which, 0, t.shape[1], fp, 1) != 1:
+            raise RuntimeError("tb_cuda_dec_kv_copy failed")
+
+    def generate(self, token: int, pos: int, n: int, want_tokens: bool = True):
+        """n greedy tokens from (token, pos); returns (tokens or None, device milliseconds)."""
+        toks = (ctypes.c_int * n)() if want_tokens else None
+        ms = ctypes.c_float(0.0)
+        if self.L.tb_cuda_dec_generate(self.d, token, pos, n, toks, None, ctypes.byref(ms)) != 1:
+            raise RuntimeError("tb_cuda_dec_generate failed")
+        return (list(toks) if want_tokens else None), ms.value
+
+    def step(self, token: int, pos: int) -> int:
+        nxt = ctypes.c_int(-1)
+        if self.L.tb_cuda_dec_step(self.d, token, pos, ctypes.byref(nxt), None) != 1:
+            raise RuntimeError("tb_cuda_dec_step failed")
+        return nxt.value
+
+    def close(self):
+        if self.d:
+            self.L.tb_cuda_dec_destroy(self.d)
+            self.d = None
+
+
+# header offsets of the fp16 d (and dmin) fields per quant type
+_D_OFFSETS = {Q.Q4_K: (0, 2), Q.Q5_K: (0, 2), Q.Q6_K: (208,), Q.Q2_K: (80, 82), Q.Q3_K: (108,),
+              Q.Q8_0: (0,), Q.Q4_0: (0,)}
+
+
+def device_weights(qt: int, M: int, K: int, gen):
+    """Random-init raw GGUF bytes of an M x K tensor, drawn on the device."""
+    import torch
+    bw, bb = Q.geometry(qt)
+    nblk = M * (K // bw)
+    t = torch.randint(0, 256, (nblk, bb), dtype=torch.uint8, device="cuda", generator=gen)
+    for off in _D_OFFSETS.get(qt, ()):
+        d = (torch.randn(nblk, device="cuda", generator=gen).abs() * 0.01).to(torch.float16)
+        t[:, off:off + 2] = d.view(torch.uint8).view(nblk, 2)
+    return t.view(-1)
+
+
+def synthetic_model(shape: ModelShape, max_ctx: int, ctx: int, seed: int = 20261201, quirks: bool = True,
+                    log=None) -> Decoder:
+    """A Decoder loaded with random-init weights of `shape` and an N(0,1) KV prefix of ctx positions."""
+    import torch
+    s = shape
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    dec = Decoder(s, max_ctx, quirks)
+    H, NH, NK, HD, F = s.hidden, s.n_heads, s.n_kv_heads, s.head_dim, s.ffn_dim
+
+    def norm(n):
+        return 1.0 + 0.1 * torch.randn(n, device="cuda", generator=gen)
+
+    for li in range(s.n_layers):
+        dec.set_layer(li,
+                      device_weights(s.w_qt, (NH + 2 * NK) * HD, H, gen), s.w_qt,
+                      device_weights(s.w_qt, H, NH * HD, gen), s.w_qt,
+                      device_weights(s.w_qt, 2 * F, H, gen), s.w_qt,
+                      device_weights(s.down_qt, H, F, gen), s.down_qt,
+                      norm(H), norm(H), norm(HD), norm(HD))
+        if ctx > 0:
+            for which in (0, 1):
+                dec.load_kv(li, which, torch.randn(NK, ctx, HD, device="cuda", generator=gen))
+    dec.set_head(device_weights(s.w_qt, s.vocab, H, gen), s.w_qt, norm(H),
+                 device_weights(s.out_qt, s.vocab, H, gen), s.out_qt)
+    torch.cuda.synchronize()
+    return dec

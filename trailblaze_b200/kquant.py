@@ -78,10 +78,11 @@ class KQuantLib:
 
     def tb_cuda_matvec_fused_dev(self, W_dev: int, qtype: int, M: int, K: int, d_x: int, d_y: int,
                                  xmode: int = 0, d_x2: int = 0, d_norm_w: int = 0, eps: float = 0.0,
-                                 d_res: int = 0, stream: int = 0) -> int:
+                                 d_res: int = 0, ymode: int = 0, stream: int = 0) -> int:
         v = lambda p: ctypes.c_void_p(p) if p else None  # noqa: E731
         return self.L.tb_cuda_matvec_fused_dev(ctypes.c_void_p(W_dev), qtype, M, K, v(d_x), v(d_y), xmode,
-                                               v(d_x2), v(d_norm_w), ctypes.c_float(eps), v(d_res), v(stream))
+                                               v(d_x2), v(d_norm_w), ctypes.c_float(eps), v(d_res), ymode,
+                                               v(stream))
 
     def tb_cuda_dequant_dev(self, W_dev: int, qtype: int, M: int, K: int, d_out: int, sem: int = 0,
                             stream: int = 0) -> int:
