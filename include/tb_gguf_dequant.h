@@ -6,7 +6,9 @@
  * same eight symbols with the same argument meaning, return codes and
  * ownership, so layer4/tb_gguf.c and layer4/tb_infer.c built with -DTB_CUDA
  * link against this library unchanged.  Part 2 adds stream-ordered
- * device-pointer entry points that have no reference counterpart.
+ * device-pointer entry points that have no reference counterpart.  Part 3
+ * is the batch-1 decode step built on the matvec (a GPU form of
+ * layer4/tb_infer.c's tb_infer_decode).
  *
  * Conventions (shared with the reference):
  *   - int returns are 1 = success, 0 = failure (the caller may fall back);
@@ -197,6 +199,13 @@ int    tb_cuda_dec_step(void *dec, int token, int pos, int *next_token, float *l
  * step's logits, device_ms (may be NULL) the device time of the n steps. */
 int    tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_out, float *logits_host,
                             float *device_ms);
+/* Copies n floats of one of the last step's activation vectors to host:
+ * which = 0 the hidden state after the last layer (hidden), 1 the state after
+ * the last layer's attention block (hidden), 2 the last layer's q | k | v
+ * before QK-norm and RoPE ((n_heads + 2 n_kv_heads) head_dim), 3 its attention
+ * output (n_heads head_dim), 4 its SwiGLU activation (ffn_dim), 5 the logits
+ * (vocab).  Blocking.  1 = ok, 0 for an unknown vector or n past its size. */
+int    tb_cuda_dec_read(void *dec, int which, float *host, int n);
 void   tb_cuda_dec_destroy(void *dec);
 
 #ifdef __cplusplus

@@ -180,6 +180,9 @@ class DecodeOracle:
             att = attention(q, self.kc[li, :, :pos + 1], self.vc[li, :, :pos + 1], NH, NK)
             x2 = x + w["wo"] @ att.reshape(-1)
             gu = w["wgu"] @ rms_norm(x2, w["ffn_norm"], eps)
-            x = x2 + w["wd"] @ swiglu(gu[0::2], gu[1::2])   # (gate, up) rows interleaved
+            act = swiglu(gu[0::2], gu[1::2])   # (gate, up) rows interleaved
+            x = x2 + w["wd"] @ act
+            # the last layer's vectors, for tests that read the GPU's
+            self.last = dict(x2=x2, qkv=qkv, att=att.reshape(-1), act=act)
         logits = self.lm @ rms_norm(x, self.out_norm, eps)
         return logits, int(np.argmax(logits))

@@ -88,6 +88,11 @@ class GpuDecoder:
         assert self.kq.L.tb_cuda_dec_kv_copy(self.d, li, which, p0, n, fp, 0) == 1
         return out
 
+    def read(self, which, n):
+        out = np.zeros(n, dtype=np.float32)
+        assert self.kq.L.tb_cuda_dec_read(self.d, which, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n) == 1
+        return out
+
     def step(self, token, pos):
         nxt = ctypes.c_int(-1)
         logits = np.zeros(self.m.vocab, dtype=np.float32)
@@ -125,9 +130,35 @@ def test_decode_step_matches_oracle(kq, quirks):
         lg, nxt = dec.step(17, pos)
         lr, _ = orc.step(17, pos)
         check_token(lg, nxt, lr)
+        H, NH, NK, F = m.hidden, m.n_heads, m.n_kv_heads, m.ffn_dim
+        assert rel_l2(dec.read(2, (NH + 2 * NK) * 128), orc.last["qkv"]) <= TOL
+        assert rel_l2(dec.read(3, NH * 128), orc.last["att"]) <= TOL
+        assert rel_l2(dec.read(1, H), orc.last["x2"]) <= TOL
+        assert rel_l2(dec.read(4, F), orc.last["act"]) <= TOL
+        assert kq.L.tb_cuda_dec_read(dec.d, 6, None, 0) == 0
         for li in range(m.n_layers):   # the rows appended at pos: rotated/normed k, raw v
             assert rel_l2(dec.read_kv(li, 0, pos, 1)[:, 0], orc.kc[li, :, pos]) <= 1e-4
             assert rel_l2(dec.read_kv(li, 1, pos, 1)[:, 0], orc.vc[li, :, pos]) <= 1e-4
+    finally:
+        dec.close()
+
+
+@pytest.mark.parametrize("nh,nk", [(32, 8), (28, 4), (12, 4), (4, 4)])
+def test_decode_long_context(kq, nh, nk):
+    """Chunks of up to 128 cached positions (every K-register group of the
+    score pass in use), query heads per KV head 4, 7, 3 and 1 (padded to 4, 8,
+    4 and 1 in the score reduction)."""
+    m = make_model(n_layers=1, hidden=256, nh=nh, nk=nk, ffn=256, vocab=300, max_ctx=4736, seed=nh + nk)
+    dec, orc = GpuDecoder(kq, m, False), DecodeOracle(m, quirks=False)
+    try:
+        pos = 4700
+        prefill(m, dec, orc, pos, seed=nh)
+        lg, nxt = dec.step(5, pos)
+        lr, _ = orc.step(5, pos)
+        check_token(lg, nxt, lr)
+        assert rel_l2(dec.read_kv(0, 0, pos, 1)[:, 0], orc.kc[0, :, pos]) <= 1e-4
+        # the attention output itself (the logits barely see it at this context)
+        assert rel_l2(dec.read(3, nh * 128), orc.last["att"]) <= TOL
     finally:
         dec.close()
 

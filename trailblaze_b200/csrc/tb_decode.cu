@@ -50,14 +50,21 @@ struct AttnArgs {
     float eps, rope_base, scale;
 };
 
-// RoPE of one (even, odd) pair by the reference's angle (tb_infer.c:143-145).
-__device__ __forceinline__ void rope_pair(float &a, float &b, int pos, int i, float base)
+// The reference's RoPE angle for pair i at position pos (tb_infer.c:143-145):
+// theta = pos / base^(2i/HD); cos and sin of it.  Every rotation by pair i at
+// this position uses the same angle, so it is computed once per launch.
+__device__ __forceinline__ float2 rope_cs(int pos, int i, float base)
 {
     const float theta = static_cast<float>(pos) / powf(base, 2.0f * static_cast<float>(i) / static_cast<float>(kHD));
-    const float c = cosf(theta), s = sinf(theta);
+    return make_float2(cosf(theta), sinf(theta));
+}
+
+// One rotation of the (even, odd) pair by (c, s) (tb_infer.c:146-153).
+__device__ __forceinline__ void rope_rot(float &a, float &b, float2 cs)
+{
     const float a0 = a, b0 = b;
-    a = a0 * c - b0 * s;
-    b = a0 * s + b0 * c;
+    a = a0 * cs.x - b0 * cs.y;
+    b = a0 * cs.y + b0 * cs.x;
 }
 
 // In-place per-head RMSNorm of hv[kHD] in shared memory by one warp
@@ -83,14 +90,44 @@ __device__ __forceinline__ void head_norm_warp(float *hv, const float *w, float 
     __syncwarp();
 }
 
-static constexpr int kVMax = 128;          // context positions per attention CTA at most
-static constexpr int kKB = (kVMax + 7) / 8; // K rows held in registers per warp
+// Sums 32 per-lane values over the warp, one sum per lane: on return lane l
+// holds sum over all lanes of v[l].  Each step halves the values a lane keeps
+// (it keeps the half selected by its lane bit and sends the other half to its
+// partner), so the 32 sums take 31 shuffles instead of 32 x 5.
+__device__ __forceinline__ float transpose_sum(float (&v)[32])
+{
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool up = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < off; ++i) {
+            const float send = up ? v[i] : v[i + off];
+            const float keep = up ? v[i + off] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, off);
+        }
+    }
+    return v[0];
+}
+
+static constexpr int kVMax = 128;            // context positions per attention CTA at most
+static constexpr int kKB = kVMax / 8;        // K rows held in registers per warp
+
+// Work area (floats) for the scores [rep][lmax], the pass-2 partials
+// [8][rep][HD] and the combine's per-group state [256][8].
+__host__ __device__ inline size_t attn_area_floats(int rep, int lmax)
+{
+    size_t area = static_cast<size_t>(rep) * lmax;
+    if (area < 8ull * rep * kHD) area = 8ull * rep * kHD;
+    if (area < 8ull * 256) area = 8ull * 256;
+    return area;
+}
 
 __host__ __device__ inline size_t attn_smem_floats(int rep, int lmax)
 {
-    const size_t area = static_cast<size_t>(rep) * lmax > 8ull * rep * kHD ? static_cast<size_t>(rep) * lmax
-                                                                           : 8ull * rep * kHD;
-    return static_cast<size_t>(rep) * kHD + kHD + 32 + area + static_cast<size_t>(lmax) * kHD;
+    // q[rep][HD] | k[HD] | (cos, sin)[HD/2] | statistics [32] | area | V rows [lmax][HD]
+    return static_cast<size_t>(rep) * kHD + kHD + kHD + 32 + attn_area_floats(rep, lmax) +
+           static_cast<size_t>(lmax) * kHD;
 }
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc)
@@ -98,72 +135,90 @@ __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc)
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
 }
 
-// grid (NK, nchunk), kAttnThreads threads, 2 CTAs per SM.  Shared memory
-// (attn_smem_floats): q[rep][HD], k[HD], chunk statistics [32], a work area
-// (the scores [rep][lmax], later the pass-2 partials [8][rep][HD] and the
-// chunk weights), and the chunk's V rows [lmax][HD].
+__device__ __forceinline__ float dot4(float4 a, float4 b)
+{
+    float d = a.x * b.x;
+    d = fmaf(a.y, b.y, d);
+    d = fmaf(a.z, b.z, d);
+    return fmaf(a.w, b.w, d);
+}
+
+// grid (NK, nchunk), kAttnThreads threads, 2 CTAs per SM; R2 = query heads per
+// KV head rounded up to a power of two (1, 2, 4 or 8).  Shared memory
+// (attn_smem_floats): q[rep][HD], k[HD], the RoPE (cos, sin) of the position,
+// chunk statistics [32], the work area and the chunk's V rows [lmax][HD].
 //
-// Every load of the chunk is issued at the start: each warp's K rows into
-// registers, every V row into shared memory with cp.async; q is rotated and
-// normed meanwhile, so the DRAM latency is paid about once per CTA.
+// The chunk's cached K and V rows are requested before the programmatic-
+// dependency wait: the rows below pos were written by earlier token steps,
+// which completed before this step began (each step is its own graph launch),
+// and row pos, this step's, is never read from the cache.  Each warp keeps its
+// K rows in registers (positions t0 + warp + 8j); the V rows go to shared
+// memory by cp.async.  Scores: each lane forms the partial dot products of
+// its four dimensions for 32 (position, head) items and one transposed
+// reduction turns them into 32 whole scores, one per lane.
+template <int R2>
 __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs a)
 {
     extern __shared__ __align__(16) float sm[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = kAttnThreads / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int nwarp = kAttnThreads / 32;
     const int kh = blockIdx.x, c = blockIdx.y;
     const int rep = a.NH / a.NK;
-    const int pos = *a.pos;
+    const int pos = *a.pos;   // written by the previous step's argmax, which has completed
     const int total = pos + 1;
     const int L = (total + a.nchunk - 1) / a.nchunk;
     const int t0 = min(c * L, total), t1 = min(t0 + L, total);
-    const bool owner = pos >= t0 && pos < t1;   // this chunk holds the new position
+    const bool owner = pos >= t0 && pos < t1;   // this chunk holds the new position (its last)
+    const int tc = min(t1, pos);                // cached rows of the chunk: [t0, tc)
 
-    float *qs = sm;                         // [rep][HD]
-    float *ks = qs + rep * kHD;             // [HD]
-    float *red = ks + kHD;                  // [32]: m, l per head; later 1/L per head
-    float *sc = red + 32;                   // scores / pass-2 partials / chunk weights
-    const size_t area = static_cast<size_t>(rep) * a.lmax > 8ull * rep * kHD ? static_cast<size_t>(rep) * a.lmax
-                                                                             : 8ull * rep * kHD;
-    float *vs = sc + area;                  // [lmax][HD]
+    float *qs = sm;                                          // [rep][HD]
+    float *ks = qs + rep * kHD;                              // [HD]
+    float2 *csr = reinterpret_cast<float2 *>(ks + kHD);      // [HD/2] (cos, sin)
+    float *red = ks + 2 * kHD;                               // [32]: m, l per head
+    float *sc = red + 32;                                    // work area
+    float *vs = sc + attn_area_floats(rep, a.lmax);          // [lmax][HD]
     __shared__ int s_last;
 
     const float *kcache = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
     float *kcw = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
     float *vcache = a.vc + static_cast<size_t>(kh) * a.max_ctx * kHD;
-    const float *vnew = a.qkv + (a.NH + a.NK) * kHD + kh * kHD;
 
-    // ---- every load of the chunk, issued up front ----
-    for (int e = tid; e < (t1 - t0) * (kHD / 4); e += kAttnThreads)
+    // ---- the chunk's cached rows, requested before the dependency wait ----
+    for (int e = tid; e < (tc - t0) * (kHD / 4); e += kAttnThreads)
         cp_async16(vs + 4 * e, vcache + static_cast<size_t>(t0) * kHD + 4 * e);
     asm volatile("cp.async.commit_group;" ::: "memory");
     float4 kv[kKB];
 #pragma unroll
     for (int j = 0; j < kKB; ++j) {
         const int t = t0 + warp + j * nwarp;
-        kv[j] = t < t1 ? __ldg(reinterpret_cast<const float4 *>(kcache + static_cast<size_t>(t) * kHD) + lane)
+        kv[j] = t < tc ? __ldg(reinterpret_cast<const float4 *>(kcache + static_cast<size_t>(t) * kHD) + lane)
                        : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // ---- q (and, for the owner, k) of this KV head, normed and rotated ----
-    const float *qsrc = a.qkv + kh * rep * kHD;
-    for (int e = tid; e < rep * kHD; e += kAttnThreads) qs[e] = __ldg(qsrc + e);
-    if (owner)
-        for (int e = tid; e < kHD; e += kAttnThreads) ks[e] = __ldg(a.qkv + a.NH * kHD + kh * kHD + e);
+    // ---- this token's q (and, in the owner chunk, k) of this KV head ----
+    {
+        const float4 *qsrc = reinterpret_cast<const float4 *>(a.qkv + kh * rep * kHD);
+        for (int e = tid; e < rep * (kHD / 4); e += kAttnThreads) reinterpret_cast<float4 *>(qs)[e] = __ldcg(qsrc + e);
+        if (owner && tid < kHD / 4)
+            reinterpret_cast<float4 *>(ks)[tid] =
+                __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + kh) * kHD) + tid);
+        if (tid < kHD / 2) csr[tid] = rope_cs(pos, tid, a.rope_base);
+    }
     __syncthreads();
     auto rope_all = [&]() {
         for (int e = tid; e < rep * (kHD / 2); e += kAttnThreads) {
             const int h = e / (kHD / 2), i = e % (kHD / 2);
-            rope_pair(qs[h * kHD + 2 * i], qs[h * kHD + 2 * i + 1], pos, i, a.rope_base);
+            rope_rot(qs[h * kHD + 2 * i], qs[h * kHD + 2 * i + 1], csr[i]);
         }
-        if (owner) {
+        if (owner && tid < kHD / 2) {
             // reference order: the K head is rotated once per query head mapped
             // to it by h % NK; the Qwen3 order rotates it once
-            const int times = a.quirks ? a.NH / a.NK : 1;
-            for (int i = tid; i < kHD / 2; i += kAttnThreads)
-                for (int r = 0; r < times; ++r) rope_pair(ks[2 * i], ks[2 * i + 1], pos, i, a.rope_base);
+            const int times = a.quirks ? rep : 1;
+            const float2 r = csr[tid];
+            for (int u = 0; u < times; ++u) rope_rot(ks[2 * tid], ks[2 * tid + 1], r);
         }
         __syncthreads();
     };
@@ -180,27 +235,41 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
         norm_all();
         rope_all();
     }
-    if (owner)   // append (tb_tensor.c:314-323); nothing else reads position pos now
-        for (int e = tid; e < kHD; e += kAttnThreads) {
-            kcw[static_cast<size_t>(pos) * kHD + e] = ks[e];
-            vcache[static_cast<size_t>(pos) * kHD + e] = __ldg(vnew + e);
-        }
+    if (owner && tid < kHD / 4) {   // append (tb_tensor.c:314-323) and stage the new V row
+        const float4 k4 = reinterpret_cast<const float4 *>(ks)[tid];
+        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK + kh) * kHD) + tid);
+        reinterpret_cast<float4 *>(kcw + static_cast<size_t>(pos) * kHD)[tid] = k4;
+        reinterpret_cast<float4 *>(vcache + static_cast<size_t>(pos) * kHD)[tid] = v4;
+        reinterpret_cast<float4 *>(vs + (pos - t0) * kHD)[tid] = v4;
+    }
 
-    // ---- pass 1: scores; warp w holds the K rows of positions t0 + w + 8j ----
+    // ---- pass 1: scores ----
+    float4 qr[R2];
 #pragma unroll
-    for (int j = 0; j < kKB; ++j) {
-        const int t = t0 + warp + j * nwarp;
-        if (t >= t1) break;
-        const float4 k4 = (t == pos && owner) ? reinterpret_cast<const float4 *>(ks)[lane] : kv[j];
-        for (int h = 0; h < rep; ++h) {
-            const float4 q = reinterpret_cast<const float4 *>(qs + h * kHD)[lane];
-            float d = q.x * k4.x;
-            d = fmaf(q.y, k4.y, d);
-            d = fmaf(q.z, k4.z, d);
-            d = fmaf(q.w, k4.w, d);
+    for (int h = 0; h < R2; ++h)
+        qr[h] = h < rep ? reinterpret_cast<const float4 *>(qs + h * kHD)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (owner) {   // the new position's k replaces the (unloaded) cache row
+        const float4 k4 = reinterpret_cast<const float4 *>(ks)[lane];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
-            if (lane == 0) sc[h * a.lmax + (t - t0)] = d * a.scale;
+        for (int j = 0; j < kKB; ++j)
+            if (t0 + warp + j * nwarp == pos) kv[j] = k4;
+    }
+    {
+        constexpr int PP = 32 / R2;                // positions per 32 items
+        constexpr int P = PP < kKB ? PP : kKB;     // of them backed by K rows
+        constexpr int NG = kKB / P;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+            if (t0 + warp + g * P * nwarp >= t1) break;   // warp-uniform
+            float v[32];
+#pragma unroll
+            for (int p = 0; p < PP; ++p)
+#pragma unroll
+                for (int h = 0; h < R2; ++h) v[p * R2 + h] = p < P ? dot4(qr[h], kv[g * P + p]) : 0.f;
+            const float d = transpose_sum(v);
+            const int p = lane / R2, h = lane % R2;
+            const int t = t0 + warp + (g * P + p) * nwarp;
+            if (p < P && h < rep && t < t1) sc[h * a.lmax + (t - t0)] = d * a.scale;
         }
     }
     __syncthreads();
@@ -227,20 +296,17 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    if (owner)   // the new V row replaces the stale one copied from the cache
-        for (int e = tid; e < kHD; e += kAttnThreads) vs[(pos - t0) * kHD + e] = __ldg(vnew + e);
-    __syncthreads();
 
     // ---- pass 2: o[h][d] = sum_t p[h][t] * v[t][d]; thread = (dim quad, position lane) ----
     {
         const int dq = tid & 31, tl = tid >> 5;   // dims 4*dq..4*dq+3, positions t0 + tl + 8k
-        float4 acc[8];
+        float4 acc[R2];
 #pragma unroll
-        for (int h = 0; h < 8; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int h = 0; h < R2; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = tl; j < n; j += 8) {
             const float4 v = reinterpret_cast<const float4 *>(vs + j * kHD)[dq];
 #pragma unroll
-            for (int h = 0; h < 8; ++h) {
+            for (int h = 0; h < R2; ++h) {
                 if (h < rep) {
                     const float p = sc[h * a.lmax + j];
                     acc[h].x = fmaf(p, v.x, acc[h].x);
@@ -253,12 +319,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
         __syncthreads();   // scores no longer needed: reuse sc as [8][rep][HD] partials
         float4 *pr = reinterpret_cast<float4 *>(sc);
 #pragma unroll
-        for (int h = 0; h < 8; ++h)
+        for (int h = 0; h < R2; ++h)
             if (h < rep) pr[(tl * rep + h) * (kHD / 4) + dq] = acc[h];
         __syncthreads();
         for (int e = tid; e < rep * (kHD / 4); e += kAttnThreads) {
             const int h = e / (kHD / 4), q4 = e % (kHD / 4);
             float4 s = pr[h * (kHD / 4) + q4];
+#pragma unroll
             for (int u = 1; u < 8; ++u) {
                 const float4 t = pr[(u * rep + h) * (kHD / 4) + q4];
                 s.x += t.x;
@@ -268,66 +335,100 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
             }
             float *dst = a.part + (static_cast<size_t>(kh * rep + h) * a.nchunk + c) * kPS;
             reinterpret_cast<float4 *>(dst)[q4] = s;
-            if (q4 == 0) {
-                dst[kHD] = red[2 * h];
-                dst[kHD + 1] = red[2 * h + 1];
-            }
+            if (q4 == 0) reinterpret_cast<float2 *>(dst + kHD)[0] = make_float2(red[2 * h], red[2 * h + 1]);
         }
     }
 
     // ---- the last chunk of this KV head combines all chunks ----
-    __threadfence();
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.count + kh, 1u) == static_cast<unsigned>(a.nchunk) - 1u;
+    if (tid == 0) {   // release the partials (the barrier orders the CTA's writes before the fence)
+        __threadfence();
+        const bool last = atomicAdd(a.count + kh, 1u) == static_cast<unsigned>(a.nchunk) - 1u;
+        if (last) __threadfence();
+        s_last = last;
+    }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
-    // chunk weights w[h][u] = e^(m_u - M_h) and 1/L per head into shared memory,
-    // then each output float4 is a weighted sum over the chunks
-    float *wts = sc;                                  // [rep][nchunk]
-    float *hm = red;                                  // [rep] 1/L
-    const float *pk = a.part + static_cast<size_t>(kh * rep) * a.nchunk * kPS;
-    for (int h = warp; h < rep; h += nwarp) {
-        const float *ph = pk + static_cast<size_t>(h) * a.nchunk * kPS;
-        float M = -1e38f;
-        for (int u = lane; u < a.nchunk; u += 32) M = fmaxf(M, __ldcg(ph + u * kPS + kHD));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
-        float Ls = 0.f;
-        for (int u = lane; u < a.nchunk; u += 32) {
-            const float w = expf(__ldcg(ph + u * kPS + kHD) - M);
-            wts[h * a.nchunk + u] = w;
-            Ls = fmaf(__ldcg(ph + u * kPS + kHD + 1), w, Ls);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(0xFFFFFFFFu, Ls, o);
-        if (lane == 0) hm[h] = Ls > 0.f ? 1.0f / Ls : 0.f;
-    }
-    __syncthreads();
-    constexpr int kCB = 8;
-    for (int e = tid; e < rep * (kHD / 4); e += kAttnThreads) {   // one float4 of one head per thread
-        const int h = e / (kHD / 4), q4 = e % (kHD / 4);
-        const float *ph = pk + static_cast<size_t>(h) * a.nchunk * kPS;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int u0 = 0; u0 < a.nchunk; u0 += kCB) {
+
+    // thread = (output float4 (head, quad), chunk group); each thread merges its
+    // chunks with a running maximum (online softmax), all loads of a batch of
+    // kCB chunks in flight together; then the groups are merged in shared memory
+    constexpr int NO = R2 * 32, NGc = kAttnThreads / NO, kCB = 8;
+    const int o = tid % NO, grp = tid / NO, h = o >> 5, q4 = o & 31;
+    float Mx = -1e38f, Ls = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (h < rep) {
+        const float *ph = a.part + static_cast<size_t>(kh * rep + h) * a.nchunk * kPS;
+        for (int u0 = grp; u0 < a.nchunk; u0 += NGc * kCB) {
+            float mb[kCB], lb[kCB];
             float4 ob[kCB];
 #pragma unroll
-            for (int j = 0; j < kCB; ++j)
-                ob[j] = u0 + j < a.nchunk ? __ldcg(reinterpret_cast<const float4 *>(ph + (u0 + j) * kPS) + q4)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < kCB; ++j) {
+                const int u = u0 + j * NGc;
+                const float *pu = ph + static_cast<size_t>(u) * kPS;
+                const bool ok = u < a.nchunk;
+                ob[j] = ok ? __ldcg(reinterpret_cast<const float4 *>(pu) + q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float2 ml = ok ? __ldcg(reinterpret_cast<const float2 *>(pu + kHD)) : make_float2(-1e38f, 0.f);
+                mb[j] = ml.x;
+                lb[j] = ml.y;
+            }
+            float Mn = Mx;
+#pragma unroll
+            for (int j = 0; j < kCB; ++j) Mn = fmaxf(Mn, mb[j]);
+            const float f = expf(Mx - Mn);
+            acc = make_float4(acc.x * f, acc.y * f, acc.z * f, acc.w * f);
+            Ls *= f;
 #pragma unroll
             for (int j = 0; j < kCB; ++j) {
-                const float w = u0 + j < a.nchunk ? wts[h * a.nchunk + u0 + j] : 0.f;
-                o.x = fmaf(ob[j].x, w, o.x);
-                o.y = fmaf(ob[j].y, w, o.y);
-                o.z = fmaf(ob[j].z, w, o.z);
-                o.w = fmaf(ob[j].w, w, o.w);
+                const float w = expf(mb[j] - Mn);
+                acc.x = fmaf(ob[j].x, w, acc.x);
+                acc.y = fmaf(ob[j].y, w, acc.y);
+                acc.z = fmaf(ob[j].z, w, acc.z);
+                acc.w = fmaf(ob[j].w, w, acc.w);
+                Ls = fmaf(lb[j], w, Ls);
+            }
+            Mx = Mn;
+        }
+    }
+    if constexpr (NGc > 1) {
+        float4 *gs = reinterpret_cast<float4 *>(sc);   // [NGc][NO][2] float4: (M, L, -, -), o
+        gs[2 * (grp * NO + o)] = make_float4(Mx, Ls, 0.f, 0.f);
+        gs[2 * (grp * NO + o) + 1] = acc;
+        __syncthreads();
+        if (grp == 0 && h < rep) {
+#pragma unroll
+            for (int g = 1; g < NGc; ++g) {
+                const float4 ml = gs[2 * (g * NO + o)], og = gs[2 * (g * NO + o) + 1];
+                const float Mn = fmaxf(Mx, ml.x);
+                const float fa = expf(Mx - Mn), fg = expf(ml.x - Mn);
+                acc = make_float4(acc.x * fa + og.x * fg, acc.y * fa + og.y * fg, acc.z * fa + og.z * fg,
+                                  acc.w * fa + og.w * fg);
+                Ls = Ls * fa + ml.y * fg;
+                Mx = Mn;
             }
         }
-        const float il = hm[h];
-        reinterpret_cast<float4 *>(a.out + (kh * rep + h) * kHD)[q4] = make_float4(o.x * il, o.y * il, o.z * il, o.w * il);
+    }
+    if (grp == 0 && h < rep) {
+        const float il = Ls > 0.f ? 1.0f / Ls : 0.f;
+        reinterpret_cast<float4 *>(a.out + (kh * rep + h) * kHD)[q4] =
+            make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
     }
     if (tid == 0) a.count[kh] = 0u;   // ready for the next layer / token
+}
+
+static int attn_r2(int rep)
+{
+    return rep <= 1 ? 1 : rep <= 2 ? 2 : rep <= 4 ? 4 : 8;
+}
+
+static void (*attn_kernel(int rep))(const AttnArgs)
+{
+    switch (attn_r2(rep)) {
+    case 1: return k_attn_decode<1>;
+    case 2: return k_attn_decode<2>;
+    case 4: return k_attn_decode<4>;
+    default: return k_attn_decode<8>;
+    }
 }
 
 // Greedy sampling (tb_tensor.c:415-420: the first index of the largest logit)
@@ -466,6 +567,7 @@ bool Decoder::enqueue(cudaStream_t s)
         f = MvFuse{};
         f.xmode = MV_X_RMSNORM;
         f.nw = w.attn_norm;
+        f.w_early = true;
         f.eps = c.norm_eps;
         if (!mv_launch(w.wqkv, w.qkv_qt, QKV, H, x, qkv, s, err, sms, lim, &f)) return false;
         // attention (QK-norm, RoPE, cache append, split-context softmax)
@@ -490,10 +592,11 @@ bool Decoder::enqueue(cudaStream_t s)
         a.rope_base = c.rope_base;
         a.scale = 1.0f / sqrtf(static_cast<float>(HD));
         const size_t smem = attn_smem_floats(NH / NK, lmax) * sizeof(float);
-        if (!launch_pdl(k_attn_decode, dim3(NK, nchunk), dim3(kAttnThreads), smem, s, a)) return false;
+        if (!launch_pdl(attn_kernel(NH / NK), dim3(NK, nchunk), dim3(kAttnThreads), smem, s, a)) return false;
         // x2 = x + Wo @ att
         f = MvFuse{};
         f.res = x;
+        f.w_early = true;
         if (!mv_launch(w.wo, w.o_qt, H, NH * HD, att, x2, s, err, sms, lim, &f)) return false;
         // act = swiglu(gate, up), (gate | up) rows interleaved in Wgu, of rmsnorm(x2)
         f = MvFuse{};
@@ -501,16 +604,19 @@ bool Decoder::enqueue(cudaStream_t s)
         f.nw = w.ffn_norm;
         f.eps = c.norm_eps;
         f.ymode = MV_Y_SWIGLU_PAIRS;
+        f.w_early = true;
         if (!mv_launch(w.wgu, w.gu_qt, 2 * F, H, x2, gu, s, err, sms, lim, &f)) return false;
         // x = x2 + Wd @ act
         f = MvFuse{};
         f.res = x2;
+        f.w_early = true;
         if (!mv_launch(w.wd, w.d_qt, H, F, gu, x, s, err, sms, lim, &f)) return false;
     }
     MvFuse f;
     f.xmode = MV_X_RMSNORM;
     f.nw = out_norm;
     f.eps = c.norm_eps;
+    f.w_early = true;
     if (!mv_launch(lm, lm_qt, c.vocab, H, x, logits, s, err, sms, lim, &f)) return false;
     const int G = sms;
     return launch_pdl(k_argmax_step, dim3(G), dim3(kArgThreads), 0, s, static_cast<const float *>(logits),
@@ -586,7 +692,7 @@ Decoder *dec_create(const DecConfig &c)
              dec_ok(cudaMemset(d->vc, 0, sizeof(float) * kvf), "memset");
         const size_t smem = attn_smem_floats(NH / NK, d->lmax) * sizeof(float);
         if (ok && smem > 48 * 1024)
-            ok = dec_ok(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            ok = dec_ok(cudaFuncSetAttribute(attn_kernel(NH / NK), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem)), "attention smem");
     }
     if (!ok) {
@@ -751,6 +857,29 @@ int tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_out, 
 int tb_cuda_dec_step(void *dec, int token, int pos, int *next_token, float *logits_host)
 {
     return tb::dec_run(static_cast<tb::Decoder *>(dec), token, pos, 1, next_token, logits_host, nullptr);
+}
+
+int tb_cuda_dec_read(void *dec, int which, float *host, int n)
+{
+    tb::Decoder *d = static_cast<tb::Decoder *>(dec);
+    if (!d || !host || n < 0) return 0;
+    const tb::DecConfig &c = d->cfg;
+    const float *src = nullptr;
+    long long size = 0;
+    switch (which) {
+    case 0: src = d->x, size = c.hidden; break;
+    case 1: src = d->x2, size = c.hidden; break;
+    case 2: src = d->qkv, size = static_cast<long long>(c.n_heads + 2 * c.n_kv_heads) * c.head_dim; break;
+    case 3: src = d->att, size = static_cast<long long>(c.n_heads) * c.head_dim; break;
+    case 4: src = d->gu, size = c.ffn_dim; break;
+    case 5: src = d->logits, size = c.vocab; break;
+    default: return 0;
+    }
+    if (n > size) return 0;
+    if (!tb::dec_ok(cudaMemcpyAsync(host, src, sizeof(float) * static_cast<size_t>(n), cudaMemcpyDeviceToHost, d->st),
+                    "read"))
+        return 0;
+    return tb::dec_ok(cudaStreamSynchronize(d->st), "read sync") ? 1 : 0;
 }
 
 void tb_cuda_dec_destroy(void *dec)

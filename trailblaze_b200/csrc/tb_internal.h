@@ -17,6 +17,8 @@ struct MvFuse {
     const float *nw = nullptr;    // RMSNorm: the norm weights
     float eps = 0.f;              // RMSNorm epsilon
     const float *res = nullptr;   // added to y when not null
+    bool w_early = false;         // W is constant over the launch chain: stream it before the
+                                  // programmatic-dependency wait
 };
 
 // Launch the matvec d_y[M] = dequant(W) @ d_x[K] on `st`.  Returns 1 when the

@@ -58,6 +58,7 @@ struct MvArgs {
     uint32_t xmode, ymode;
     const float *x2, *nw, *res;
     float eps;
+    uint32_t w_early;   // W is not written by the previous kernel: prefetch before griddepcontrol.wait
 };
 
 static constexpr uint32_t kFull = 0xFFFFFFFFu;
@@ -190,12 +191,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     // nothing below touches global memory before the previous kernel has
     // finished and its writes are visible.  Both are no-ops without the launch
     // attribute.
+    // With w_early the first stages of W are requested before the wait, so the
+    // weight stream overlaps the previous kernel's tail (W is never written by
+    // a kernel of the same chain in that case).
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (producer && lane == 0) {
+    auto prefetch = [&]() {
         const uint32_t pre = min(a.nst, n_tiles);
         for (uint32_t it = 0; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
-    }
+    };
+    if (a.w_early && producer && lane == 0) prefetch();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (!a.w_early && producer && lane == 0) prefetch();
 
     // ---- prologue: x -> one record per column slot ----
     // Thread g handles group g (then g + nthr, ...).  The GPL groups of a slot
@@ -527,6 +533,7 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
         a.nw = fuse->nw;
         a.eps = fuse->eps;
         a.res = fuse->res;
+        a.w_early = fuse->w_early ? 1u : 0u;
     }
     a.W = static_cast<const uint8_t *>(W);
     a.x = d_x;
