@@ -148,25 +148,25 @@ __device__ __forceinline__ float dot4(float4 a, float4 b)
 // (attn_smem_floats): q[rep][HD], k[HD], the RoPE (cos, sin) of the position,
 // chunk statistics [32], the work area and the chunk's V rows [lmax][HD].
 //
-// The chunk's cached K and V rows are requested before the programmatic-
-// dependency wait: the rows below pos were written by earlier token steps,
-// which completed before this step began (each step is its own graph launch),
-// and row pos, this step's, is never read from the cache.  Each warp keeps its
-// K rows in registers (positions t0 + warp + 8j); the V rows go to shared
-// memory by cp.async.  Scores: each lane forms the partial dot products of
-// its four dimensions for 32 (position, head) items and one transposed
-// reduction turns them into 32 whole scores, one per lane.
+// This token's q, k and v are requested first, then the chunk's cached K and V
+// rows (row pos, this step's, is never read from the cache), so q is rotated
+// and normed while the cache rows stream in.  Each warp keeps its K rows in
+// registers (positions t0 + warp + 8j); the V rows go to shared memory by
+// cp.async.  Scores: each lane forms the partial dot products of its four
+// dimensions for 32 (position, head) items and one transposed reduction turns
+// them into 32 whole scores, one per lane.
 template <int R2>
 __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs a)
 {
     extern __shared__ __align__(16) float sm[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nwarp = kAttnThreads / 32;
     const int kh = blockIdx.x, c = blockIdx.y;
     const int rep = a.NH / a.NK;
-    const int pos = *a.pos;   // written by the previous step's argmax, which has completed
+    const int pos = *a.pos;
     const int total = pos + 1;
     const int L = (total + a.nchunk - 1) / a.nchunk;
     const int t0 = min(c * L, total), t1 = min(t0 + L, total);
@@ -185,7 +185,17 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     float *kcw = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
     float *vcache = a.vc + static_cast<size_t>(kh) * a.max_ctx * kHD;
 
-    // ---- the chunk's cached rows, requested before the dependency wait ----
+    // ---- this token's q (and, in the owner chunk, k and v), requested first:
+    // behind the chunk's ~60 KB of cache rows they would arrive last ----
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 qv = z4, kn = z4, vn = z4;
+    if (tid < rep * (kHD / 4)) qv = __ldcg(reinterpret_cast<const float4 *>(a.qkv + kh * rep * kHD) + tid);
+    if (owner && tid < kHD / 4) {
+        kn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + kh) * kHD) + tid);
+        vn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK + kh) * kHD) + tid);
+    }
+
+    // ---- then the chunk's cached rows (row pos, this step's, is not read) ----
     for (int e = tid; e < (tc - t0) * (kHD / 4); e += kAttnThreads)
         cp_async16(vs + 4 * e, vcache + static_cast<size_t>(t0) * kHD + 4 * e);
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -193,20 +203,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
 #pragma unroll
     for (int j = 0; j < kKB; ++j) {
         const int t = t0 + warp + j * nwarp;
-        kv[j] = t < tc ? __ldg(reinterpret_cast<const float4 *>(kcache + static_cast<size_t>(t) * kHD) + lane)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        kv[j] = t < tc ? __ldg(reinterpret_cast<const float4 *>(kcache + static_cast<size_t>(t) * kHD) + lane) : z4;
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // ---- this token's q (and, in the owner chunk, k) of this KV head ----
-    {
-        const float4 *qsrc = reinterpret_cast<const float4 *>(a.qkv + kh * rep * kHD);
-        for (int e = tid; e < rep * (kHD / 4); e += kAttnThreads) reinterpret_cast<float4 *>(qs)[e] = __ldcg(qsrc + e);
-        if (owner && tid < kHD / 4)
-            reinterpret_cast<float4 *>(ks)[tid] =
-                __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + kh) * kHD) + tid);
-        if (tid < kHD / 2) csr[tid] = rope_cs(pos, tid, a.rope_base);
-    }
+    // ---- q and k normed and rotated in shared memory ----
+    if (tid < rep * (kHD / 4)) reinterpret_cast<float4 *>(qs)[tid] = qv;
+    if (owner && tid < kHD / 4) reinterpret_cast<float4 *>(ks)[tid] = kn;
+    if (tid < kHD / 2) csr[tid] = rope_cs(pos, tid, a.rope_base);
     __syncthreads();
     auto rope_all = [&]() {
         for (int e = tid; e < rep * (kHD / 2); e += kAttnThreads) {
@@ -237,10 +240,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     }
     if (owner && tid < kHD / 4) {   // append (tb_tensor.c:314-323) and stage the new V row
         const float4 k4 = reinterpret_cast<const float4 *>(ks)[tid];
-        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK + kh) * kHD) + tid);
         reinterpret_cast<float4 *>(kcw + static_cast<size_t>(pos) * kHD)[tid] = k4;
-        reinterpret_cast<float4 *>(vcache + static_cast<size_t>(pos) * kHD)[tid] = v4;
-        reinterpret_cast<float4 *>(vs + (pos - t0) * kHD)[tid] = v4;
+        reinterpret_cast<float4 *>(vcache + static_cast<size_t>(pos) * kHD)[tid] = vn;
+        reinterpret_cast<float4 *>(vs + (pos - t0) * kHD)[tid] = vn;
     }
 
     // ---- pass 1: scores ----
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     // thread = (output float4 (head, quad), chunk group); each thread merges its
     // chunks with a running maximum (online softmax), all loads of a batch of
     // kCB chunks in flight together; then the groups are merged in shared memory
-    constexpr int NO = R2 * 32, NGc = kAttnThreads / NO, kCB = 8;
+    constexpr int NO = R2 * 32, NGc = kAttnThreads / NO, kCB = 10;
     const int o = tid % NO, grp = tid / NO, h = o >> 5, q4 = o & 31;
     float Mx = -1e38f, Ls = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);

@@ -191,17 +191,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     // nothing below touches global memory before the previous kernel has
     // finished and its writes are visible.  Both are no-ops without the launch
     // attribute.
-    // With w_early the first stages of W are requested before the wait, so the
+    // Stage 0 is requested before the prologue and the other stages after it:
+    // the prologue's x loads would otherwise queue behind NST stages of weight
+    // misses (up to ~200 KB per SM) and the consumers could not start any
+    // sooner.  With w_early stage 0 is requested before the wait, so the
     // weight stream overlaps the previous kernel's tail (W is never written by
     // a kernel of the same chain in that case).
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    auto prefetch = [&]() {
-        const uint32_t pre = min(a.nst, n_tiles);
-        for (uint32_t it = 0; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
-    };
-    if (a.w_early && producer && lane == 0) prefetch();
+    if (a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (!a.w_early && producer && lane == 0) prefetch();
+    if (!a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
 
     // ---- prologue: x -> one record per column slot ----
     // Thread g handles group g (then g + nthr, ...).  The GPL groups of a slot
@@ -245,6 +244,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     }
     __syncthreads();   // records complete; barrier inits visible
 
+    if (producer && lane == 0) {
+        const uint32_t pre = min(a.nst, n_tiles);
+        for (uint32_t it = 1; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
+    }
     if (producer) {
         // ---- producer: reduce each finished tile, write y, refill its stage ----
         uint32_t issued = min(a.nst, n_tiles), done = 0;
