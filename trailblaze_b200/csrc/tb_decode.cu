@@ -35,7 +35,7 @@ namespace tb {
 
 static constexpr int kHD = 128;            // head_dim supported by the attention kernel
 static constexpr int kPS = kHD + 4;        // floats per chunk partial: o[HD], m, l, 2 pad (16-byte rows)
-static constexpr int kAttnThreads = 256;
+static constexpr int kAttnThreads = 512;
 
 struct AttnArgs {
     const float *qkv;      // [NH*HD | NK*HD | NK*HD]: this token's q, k, v
@@ -46,9 +46,12 @@ struct AttnArgs {
     unsigned *count;       // [NK] chunk tickets; 0 on entry and left at 0
     float *out;            // [NH*HD]
     int *err;
-    int NH, NK, max_ctx, nchunk, lmax, quirks;
+    int NH, NK, max_ctx, nchunk, quirks;
     float eps, rope_base, scale;
+    uint32_t wait_limit;   // iterations of a bounded ring wait
 };
+
+static constexpr uint32_t kAttnDrain = 1u << 26;   // bound of the drain after a failed wait
 
 // The reference's RoPE angle for pair i at position pos (tb_infer.c:143-145):
 // theta = pos / base^(2i/HD); cos and sin of it.  Every rotation by pair i at
@@ -68,7 +71,8 @@ __device__ __forceinline__ void rope_rot(float &a, float &b, float2 cs)
 }
 
 // In-place per-head RMSNorm of hv[kHD] in shared memory by one warp
-// (tb_infer.c:689-693: sc = 1/sqrtf(sum/HD + eps), x*sc*w).
+// (tb_infer.c:689-693: sc = 1/sqrtf(sum/HD + eps), x*sc*w); w is in shared
+// memory too.
 __device__ __forceinline__ void head_norm_warp(float *hv, const float *w, float eps)
 {
     const int lane = threadIdx.x & 31;
@@ -85,20 +89,23 @@ __device__ __forceinline__ void head_norm_warp(float *hv, const float *w, float 
 #pragma unroll
     for (int j = 0; j < kHD / 32; ++j) {
         const int d = lane + 32 * j;
-        hv[d] = hv[d] * sc * __ldg(w + d);
+        hv[d] = hv[d] * sc * w[d];
     }
     __syncwarp();
 }
 
-// Sums 32 per-lane values over the warp, one sum per lane: on return lane l
-// holds sum over all lanes of v[l].  Each step halves the values a lane keeps
-// (it keeps the half selected by its lane bit and sends the other half to its
-// partner), so the 32 sums take 31 shuffles instead of 32 x 5.
-__device__ __forceinline__ float transpose_sum(float (&v)[32])
+// Sums V per-lane values (V a power of two, at most 32) over the warp: on return
+// lane l holds the sum over all 32 lanes of v[l % V].  The first log2(V) steps
+// transpose while they add (each lane keeps the half of its values selected by
+// its lane bit and sends the other half to its partner), the rest are plain
+// butterfly adds, so the V sums take V - 1 + (5 - log2 V) shuffles instead of
+// 5 V.
+template <int V>
+__device__ __forceinline__ float transpose_sum(float (&v)[V])
 {
     const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
+    for (int off = V / 2; off >= 1; off >>= 1) {
         const bool up = (lane & off) != 0;
 #pragma unroll
         for (int i = 0; i < off; ++i) {
@@ -107,32 +114,30 @@ __device__ __forceinline__ float transpose_sum(float (&v)[32])
             v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, off);
         }
     }
-    return v[0];
+    float r = v[0];
+#pragma unroll
+    for (int off = V; off < 32; off <<= 1) r += __shfl_xor_sync(0xFFFFFFFFu, r, off);
+    return r;
 }
 
-static constexpr int kVMax = 128;            // context positions per attention CTA at most
-static constexpr int kKB = kVMax / 8;        // K rows held in registers per warp
+// The chunk's cached K and V rows stream through a ring of kNS stages, one
+// block of kBP positions per stage (its K rows, then its V rows), by 1-D bulk
+// copies that one thread issues; every block is consumed as it lands.
+static constexpr int kBP = 32;                                   // positions per block (one per lane)
+static constexpr int kNS = 4;                                    // ring stages
+static constexpr uint32_t kStageBytes = 2u * kBP * kHD * sizeof(float);
+static constexpr int kPW = kBP / (kAttnThreads / 32);            // positions of a block per warp
+static_assert(kBP == 32 && kPW * (kAttnThreads / 32) == kBP, "one position per lane, whole warps");
 
-// Work area (floats) for the scores [rep][lmax], the pass-2 partials
-// [8][rep][HD] and the combine's per-group state [256][8].
-__host__ __device__ inline size_t attn_area_floats(int rep, int lmax)
+// Dynamic shared memory: ring [kNS][K rows | V rows] | q[rep][HD] | k[HD] |
+// new v[HD] | q-norm and k-norm weights [2][HD] | (cos, sin)[HD/2] | full
+// barriers [kNS] | stage release counters [kNS] | last block issued per stage
+// [kNS].  The ring doubles as scratch once every block is consumed.
+__host__ __device__ inline size_t attn_smem_bytes(int rep)
 {
-    size_t area = static_cast<size_t>(rep) * lmax;
-    if (area < 8ull * rep * kHD) area = 8ull * rep * kHD;
-    if (area < 8ull * 256) area = 8ull * 256;
-    return area;
-}
-
-__host__ __device__ inline size_t attn_smem_floats(int rep, int lmax)
-{
-    // q[rep][HD] | k[HD] | (cos, sin)[HD/2] | statistics [32] | area | V rows [lmax][HD]
-    return static_cast<size_t>(rep) * kHD + kHD + kHD + 32 + attn_area_floats(rep, lmax) +
-           static_cast<size_t>(lmax) * kHD;
-}
-
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc)
-{
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+    return static_cast<size_t>(kNS) * kStageBytes +
+           sizeof(float) * (static_cast<size_t>(rep) * kHD + 5 * kHD) +
+           kNS * (sizeof(uint64_t) + 2 * sizeof(uint32_t));
 }
 
 __device__ __forceinline__ float dot4(float4 a, float4 b)
@@ -143,22 +148,43 @@ __device__ __forceinline__ float dot4(float4 a, float4 b)
     return fmaf(a.w, b.w, d);
 }
 
-// grid (NK, nchunk), kAttnThreads threads, 2 CTAs per SM; R2 = query heads per
-// KV head rounded up to a power of two (1, 2, 4 or 8).  Shared memory
-// (attn_smem_floats): q[rep][HD], k[HD], the RoPE (cos, sin) of the position,
-// chunk statistics [32], the work area and the chunk's V rows [lmax][HD].
-//
-// This token's q, k and v are requested first, then the chunk's cached K and V
-// rows (row pos, this step's, is never read from the cache), so q is rotated
-// and normed while the cache rows stream in.  Each warp keeps its K rows in
-// registers (positions t0 + warp + 8j); the V rows go to shared memory by
-// cp.async.  Scores: each lane forms the partial dot products of its four
-// dimensions for 32 (position, head) items and one transposed reduction turns
-// them into 32 whole scores, one per lane.
-template <int R2>
-__global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs a)
+__device__ __forceinline__ float warp_max(float v)
 {
-    extern __shared__ __align__(16) float sm[];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// grid (NK, nchunk), kAttnThreads threads, one CTA per SM; R2 = query heads
+// per KV head rounded up to a power of two (1, 2, 4 or 8).
+//
+// After the programmatic-dependency wait this token's q (and, in the chunk
+// that owns pos, k and v) is requested first, then thread 0 starts the ring,
+// so q is rotated and normed while the cache rows stream in (row pos, this
+// step's, is never read from the cache).  Warp w takes positions kPW w ..
+// kPW w + kPW - 1 of every block and runs its own online softmax over them,
+// with no CTA barrier per block:
+//   scores   each lane forms the partial dot products of its four dimensions
+//            for the warp's (position, head) items; one transposed reduction
+//            gives whole scores, lane l holding item l % (kPW R2);
+//   softmax  per head, the block maximum over the warp's positions, the
+//            rescale factor of the running sums, the probabilities;
+//   p . V    lane l: dimensions 4 l .. 4 l + 3, every head, the probabilities
+//            broadcast by shuffles.
+// The last warp done with a stage (a shared-memory counter) refills it with
+// the block kNS further on.  At the end the warps' (m, l, o) are merged in
+// shared memory into the chunk's partial.
+template <int R2>
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs a)
+{
+    extern __shared__ __align__(128) uint8_t smraw[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -172,43 +198,68 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     const int t0 = min(c * L, total), t1 = min(t0 + L, total);
     const bool owner = pos >= t0 && pos < t1;   // this chunk holds the new position (its last)
     const int tc = min(t1, pos);                // cached rows of the chunk: [t0, tc)
+    const int nb = (t1 - t0 + kBP - 1) / kBP;   // blocks of the chunk
 
-    float *qs = sm;                                          // [rep][HD]
-    float *ks = qs + rep * kHD;                              // [HD]
-    float2 *csr = reinterpret_cast<float2 *>(ks + kHD);      // [HD/2] (cos, sin)
-    float *red = ks + 2 * kHD;                               // [32]: m, l per head
-    float *sc = red + 32;                                    // work area
-    float *vs = sc + attn_area_floats(rep, a.lmax);          // [lmax][HD]
+    uint8_t *ring = smraw;
+    float *qs = reinterpret_cast<float *>(smraw + kNS * kStageBytes);   // [rep][HD]
+    float *ks = qs + rep * kHD;                                          // [HD]
+    float *vnw = ks + kHD;                                               // [HD]
+    float *qnw = vnw + kHD;                                              // [HD]
+    float *knw = qnw + kHD;                                              // [HD]
+    float2 *csr = reinterpret_cast<float2 *>(knw + kHD);                 // [HD/2]
+    uint64_t *full = reinterpret_cast<uint64_t *>(csr + kHD / 2);        // [kNS]
+    unsigned *cnt = reinterpret_cast<unsigned *>(full + kNS);            // [kNS] warps done with a stage
+    int *iss = reinterpret_cast<int *>(cnt + kNS);                       // [kNS] last block issued
     __shared__ int s_last;
 
     const float *kcache = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
     float *kcw = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
     float *vcache = a.vc + static_cast<size_t>(kh) * a.max_ctx * kHD;
+    const uint64_t pol = l2_evict_first_policy();
 
-    // ---- this token's q (and, in the owner chunk, k and v), requested first:
-    // behind the chunk's ~60 KB of cache rows they would arrive last ----
+    // ---- this token's q (and, in the owner chunk, k and v) and the QK-norm
+    // weights, requested first: behind the ring's copies they would arrive last ----
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 qv = z4, kn = z4, vn = z4;
+    float4 qv = z4, kn = z4, vn = z4, qnv = z4, knv = z4;
+    if (a.qn && tid < kHD / 4) qnv = __ldg(reinterpret_cast<const float4 *>(a.qn) + tid);
+    if (owner && a.kn && tid < kHD / 4) knv = __ldg(reinterpret_cast<const float4 *>(a.kn) + tid);
     if (tid < rep * (kHD / 4)) qv = __ldcg(reinterpret_cast<const float4 *>(a.qkv + kh * rep * kHD) + tid);
     if (owner && tid < kHD / 4) {
         kn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + kh) * kHD) + tid);
         vn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK + kh) * kHD) + tid);
     }
 
-    // ---- then the chunk's cached rows (row pos, this step's, is not read) ----
-    for (int e = tid; e < (tc - t0) * (kHD / 4); e += kAttnThreads)
-        cp_async16(vs + 4 * e, vcache + static_cast<size_t>(t0) * kHD + 4 * e);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    float4 kv[kKB];
-#pragma unroll
-    for (int j = 0; j < kKB; ++j) {
-        const int t = t0 + warp + j * nwarp;
-        kv[j] = t < tc ? __ldg(reinterpret_cast<const float4 *>(kcache + static_cast<size_t>(t) * kHD) + lane) : z4;
+    // ---- the ring: block b's K rows and V rows into stage b % kNS ----
+    auto issue = [&](int b, int s) {   // one thread
+        const int tb = t0 + b * kBP;
+        const int n = max(0, min(tb + kBP, tc) - tb);
+        const uint32_t bytes = static_cast<uint32_t>(n) * kHD * sizeof(float);
+        const uint32_t bar = smem_u32(full + s);
+        mbar_expect_tx(bar, 2u * bytes);   // with n == 0 a plain arrival completes the phase
+        if (n > 0) {
+            uint8_t *st = ring + static_cast<size_t>(s) * kStageBytes;
+            bulk_g2s(smem_u32(st), kcache + static_cast<size_t>(tb) * kHD, bytes, bar, pol);
+            bulk_g2s(smem_u32(st + kStageBytes / 2), vcache + static_cast<size_t>(tb) * kHD, bytes, bar, pol);
+        }
+    };
+    if (tid == 0) {
+        for (int u = 0; u < kNS; ++u) {
+            mbar_init(smem_u32(full + u), 1);
+            cnt[u] = 0u;
+            iss[u] = u < nb ? u : -1;
+        }
+        fence_mbar_init();
+        for (int u = 0; u < min(nb, kNS); ++u) issue(u, u);
     }
 
     // ---- q and k normed and rotated in shared memory ----
     if (tid < rep * (kHD / 4)) reinterpret_cast<float4 *>(qs)[tid] = qv;
-    if (owner && tid < kHD / 4) reinterpret_cast<float4 *>(ks)[tid] = kn;
+    if (owner && tid < kHD / 4) {
+        reinterpret_cast<float4 *>(ks)[tid] = kn;
+        reinterpret_cast<float4 *>(vnw)[tid] = vn;
+        reinterpret_cast<float4 *>(knw)[tid] = knv;
+    }
+    if (tid < kHD / 4) reinterpret_cast<float4 *>(qnw)[tid] = qnv;
     if (tid < kHD / 2) csr[tid] = rope_cs(pos, tid, a.rope_base);
     __syncthreads();
     auto rope_all = [&]() {
@@ -227,8 +278,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     };
     auto norm_all = [&]() {
         if (a.qn)
-            for (int h = warp; h < rep; h += nwarp) head_norm_warp(qs + h * kHD, a.qn, a.eps);
-        if (owner && a.kn && warp == nwarp - 1) head_norm_warp(ks, a.kn, a.eps);
+            for (int h = warp; h < rep; h += nwarp) head_norm_warp(qs + h * kHD, qnw, a.eps);
+        if (owner && a.kn && warp == nwarp - 1) head_norm_warp(ks, knw, a.eps);
         __syncthreads();
     };
     if (a.quirks) {
@@ -238,106 +289,147 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
         norm_all();
         rope_all();
     }
-    if (owner && tid < kHD / 4) {   // append (tb_tensor.c:314-323) and stage the new V row
-        const float4 k4 = reinterpret_cast<const float4 *>(ks)[tid];
-        reinterpret_cast<float4 *>(kcw + static_cast<size_t>(pos) * kHD)[tid] = k4;
+    if (owner && tid < kHD / 4) {   // append (tb_tensor.c:314-323); the ring never reads row pos
+        reinterpret_cast<float4 *>(kcw + static_cast<size_t>(pos) * kHD)[tid] = reinterpret_cast<const float4 *>(ks)[tid];
         reinterpret_cast<float4 *>(vcache + static_cast<size_t>(pos) * kHD)[tid] = vn;
-        reinterpret_cast<float4 *>(vs + (pos - t0) * kHD)[tid] = vn;
     }
 
-    // ---- pass 1: scores ----
     float4 qr[R2];
 #pragma unroll
     for (int h = 0; h < R2; ++h)
-        qr[h] = h < rep ? reinterpret_cast<const float4 *>(qs + h * kHD)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-    if (owner) {   // the new position's k replaces the (unloaded) cache row
-        const float4 k4 = reinterpret_cast<const float4 *>(ks)[lane];
-#pragma unroll
-        for (int j = 0; j < kKB; ++j)
-            if (t0 + warp + j * nwarp == pos) kv[j] = k4;
-    }
-    {
-        constexpr int PP = 32 / R2;                // positions per 32 items
-        constexpr int P = PP < kKB ? PP : kKB;     // of them backed by K rows
-        constexpr int NG = kKB / P;
-#pragma unroll
-        for (int g = 0; g < NG; ++g) {
-            if (t0 + warp + g * P * nwarp >= t1) break;   // warp-uniform
-            float v[32];
-#pragma unroll
-            for (int p = 0; p < PP; ++p)
-#pragma unroll
-                for (int h = 0; h < R2; ++h) v[p * R2 + h] = p < P ? dot4(qr[h], kv[g * P + p]) : 0.f;
-            const float d = transpose_sum(v);
-            const int p = lane / R2, h = lane % R2;
-            const int t = t0 + warp + (g * P + p) * nwarp;
-            if (p < P && h < rep && t < t1) sc[h * a.lmax + (t - t0)] = d * a.scale;
-        }
-    }
-    __syncthreads();
+        qr[h] = h < rep ? reinterpret_cast<const float4 *>(qs + h * kHD)[lane] : z4;
+    const float4 kn4 = owner ? reinterpret_cast<const float4 *>(ks)[lane] : z4;
+    const float4 vn4 = owner ? reinterpret_cast<const float4 *>(vnw)[lane] : z4;
 
-    // ---- softmax statistics of the chunk: one warp per head ----
-    const int n = t1 - t0;
-    for (int h = warp; h < rep; h += nwarp) {
-        float m = -1e38f;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * a.lmax + j]);
+    // ---- the blocks: every warp runs its own online softmax over its kPW
+    // positions of each block, lanes sharing values by shuffles only.  Lane l
+    // holds head l % R2 (its running maximum and sum) and, for the scores of a
+    // block, the item (position (l % V) / R2, head l % R2) ----
+    constexpr int V = kPW * R2;   // (position, head) items of a warp per block
+    float4 acc[R2];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-        float l = 0.f;
-        for (int j = lane; j < n; j += 32) {
-            const float p = expf(sc[h * a.lmax + j] - m);
-            sc[h * a.lmax + j] = p;
-            l += p;
+    for (int h = 0; h < R2; ++h) acc[h] = z4;
+    float m_run = -1e38f, l_run = 0.f;
+    bool fail = false;
+    int s = 0;
+    uint32_t par = 0;
+    for (int b = 0; b < nb; ++b) {
+        if (!mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit)) {
+            fail = true;   // the other warps' waits run out as well: nothing refills the ring
+            break;
         }
+        const float *Ks = reinterpret_cast<const float *>(ring + static_cast<size_t>(s) * kStageBytes);
+        const float *Vs = Ks + kBP * kHD;
+        const int tb = t0 + b * kBP;
+        const int nv = min(kBP, t1 - tb);   // positions of this block
+        float v[V];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+        for (int p = 0; p < kPW; ++p) {
+            const int pl = warp * kPW + p;
+            const float4 k4 = (tb + pl == pos) ? kn4 : reinterpret_cast<const float4 *>(Ks + pl * kHD)[lane];
+#pragma unroll
+            for (int h = 0; h < R2; ++h) v[p * R2 + h] = dot4(qr[h], k4);
+        }
+        const bool valid = warp * kPW + (lane % V) / R2 < nv;
+        const float dsum = transpose_sum<V>(v);   // every lane takes part in the shuffles
+        const float sv = valid ? dsum * a.scale : -1e38f;
+        float bm = sv;   // block maximum of head lane % R2 over the warp's positions
+#pragma unroll
+        for (int off = R2; off < V; off <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xFFFFFFFFu, bm, off));
+        const float mn = fmaxf(m_run, bm);
+        const float al = expf(m_run - mn);
+        const float pv = valid ? expf(sv - mn) : 0.f;
+        float ps = pv;
+#pragma unroll
+        for (int off = R2; off < V; off <<= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, off);
+        l_run = l_run * al + ps;
+        m_run = mn;
+#pragma unroll
+        for (int h = 0; h < R2; ++h)
+            if (h < rep) {
+                const float ah = __shfl_sync(0xFFFFFFFFu, al, h);
+                acc[h] = make_float4(acc[h].x * ah, acc[h].y * ah, acc[h].z * ah, acc[h].w * ah);
+            }
+#pragma unroll
+        for (int p = 0; p < kPW; ++p) {
+            const int pl = warp * kPW + p;
+            if (pl < nv) {
+                const float4 v4 = (tb + pl == pos) ? vn4 : reinterpret_cast<const float4 *>(Vs + pl * kHD)[lane];
+#pragma unroll
+                for (int h = 0; h < R2; ++h)
+                    if (h < rep) {
+                        const float pr = __shfl_sync(0xFFFFFFFFu, pv, p * R2 + h);
+                        acc[h].x = fmaf(pr, v4.x, acc[h].x);
+                        acc[h].y = fmaf(pr, v4.y, acc[h].y);
+                        acc[h].z = fmaf(pr, v4.z, acc[h].z);
+                        acc[h].w = fmaf(pr, v4.w, acc[h].w);
+                    }
+            }
+        }
+        // the last warp done with this stage refills it with block b + kNS
+        __syncwarp();
         if (lane == 0) {
-            red[2 * h] = m;
-            red[2 * h + 1] = l;
-        }
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-
-    // ---- pass 2: o[h][d] = sum_t p[h][t] * v[t][d]; thread = (dim quad, position lane) ----
-    {
-        const int dq = tid & 31, tl = tid >> 5;   // dims 4*dq..4*dq+3, positions t0 + tl + 8k
-        float4 acc[R2];
-#pragma unroll
-        for (int h = 0; h < R2; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int j = tl; j < n; j += 8) {
-            const float4 v = reinterpret_cast<const float4 *>(vs + j * kHD)[dq];
-#pragma unroll
-            for (int h = 0; h < R2; ++h) {
-                if (h < rep) {
-                    const float p = sc[h * a.lmax + j];
-                    acc[h].x = fmaf(p, v.x, acc[h].x);
-                    acc[h].y = fmaf(p, v.y, acc[h].y);
-                    acc[h].z = fmaf(p, v.z, acc[h].z);
-                    acc[h].w = fmaf(p, v.w, acc[h].w);
+            __threadfence_block();
+            if (atomicAdd(cnt + s, 1u) == static_cast<unsigned>(nwarp) - 1u) {
+                cnt[s] = 0u;
+                __threadfence_block();
+                if (b + kNS < nb) {
+                    fence_proxy_async_smem();
+                    issue(b + kNS, s);
+                    iss[s] = b + kNS;
                 }
             }
         }
-        __syncthreads();   // scores no longer needed: reuse sc as [8][rep][HD] partials
-        float4 *pr = reinterpret_cast<float4 *>(sc);
+        if (++s == kNS) {
+            s = 0;
+            par ^= 1u;
+        }
+    }
+    if (__syncthreads_or(fail)) {
+        // a wait ran out: let the copies still in flight land before the ring
+        // is reused (bounded; only a stage's last block can be in flight), and
+        // hand in an empty partial so the tickets stay consistent; the error
+        // word is already set
+        if (tid == 0)
+            for (int u = 0; u < kNS; ++u)
+                if (iss[u] >= 0) mbar_wait_bounded(smem_u32(full + u), (iss[u] / kNS) & 1u, nullptr, kAttnDrain);
+#pragma unroll
+        for (int h = 0; h < R2; ++h) acc[h] = z4;
+        m_run = -1e38f;
+        l_run = 0.f;
+    }
+    __syncthreads();   // every block consumed (or drained): the ring is free
+
+    // ---- the chunk's partial: the warps' states merged, o, m, l per head ----
+    {
+        float4 *pr = reinterpret_cast<float4 *>(ring);                       // [nwarp][rep][HD/4]
+        float *wml = reinterpret_cast<float *>(pr + nwarp * rep * (kHD / 4));  // [nwarp][R2][2]
 #pragma unroll
         for (int h = 0; h < R2; ++h)
-            if (h < rep) pr[(tl * rep + h) * (kHD / 4) + dq] = acc[h];
+            if (h < rep) pr[(warp * rep + h) * (kHD / 4) + lane] = acc[h];
+        if (lane < R2) {
+            wml[(warp * R2 + lane) * 2] = m_run;
+            wml[(warp * R2 + lane) * 2 + 1] = l_run;
+        }
         __syncthreads();
         for (int e = tid; e < rep * (kHD / 4); e += kAttnThreads) {
             const int h = e / (kHD / 4), q4 = e % (kHD / 4);
-            float4 s = pr[h * (kHD / 4) + q4];
-#pragma unroll
-            for (int u = 1; u < 8; ++u) {
+            float M = -1e38f;
+            for (int u = 0; u < nwarp; ++u) M = fmaxf(M, wml[(u * R2 + h) * 2]);
+            float4 so = z4;
+            float sl = 0.f;
+            for (int u = 0; u < nwarp; ++u) {
+                const float w = expf(wml[(u * R2 + h) * 2] - M);
                 const float4 t = pr[(u * rep + h) * (kHD / 4) + q4];
-                s.x += t.x;
-                s.y += t.y;
-                s.z += t.z;
-                s.w += t.w;
+                so.x = fmaf(t.x, w, so.x);
+                so.y = fmaf(t.y, w, so.y);
+                so.z = fmaf(t.z, w, so.z);
+                so.w = fmaf(t.w, w, so.w);
+                sl = fmaf(wml[(u * R2 + h) * 2 + 1], w, sl);
             }
             float *dst = a.part + (static_cast<size_t>(kh * rep + h) * a.nchunk + c) * kPS;
-            reinterpret_cast<float4 *>(dst)[q4] = s;
-            if (q4 == 0) reinterpret_cast<float2 *>(dst + kHD)[0] = make_float2(red[2 * h], red[2 * h + 1]);
+            reinterpret_cast<float4 *>(dst)[q4] = so;
+            if (q4 == 0) reinterpret_cast<float2 *>(dst + kHD)[0] = make_float2(M, sl);
         }
     }
 
@@ -355,10 +447,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     // thread = (output float4 (head, quad), chunk group); each thread merges its
     // chunks with a running maximum (online softmax), all loads of a batch of
     // kCB chunks in flight together; then the groups are merged in shared memory
-    constexpr int NO = R2 * 32, NGc = kAttnThreads / NO, kCB = 10;
+    constexpr int NO = R2 * 32, NGc = kAttnThreads / NO, kCB = 8;
     const int o = tid % NO, grp = tid / NO, h = o >> 5, q4 = o & 31;
     float Mx = -1e38f, Ls = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 oc = make_float4(0.f, 0.f, 0.f, 0.f);
     if (h < rep) {
         const float *ph = a.part + static_cast<size_t>(kh * rep + h) * a.nchunk * kPS;
         for (int u0 = grp; u0 < a.nchunk; u0 += NGc * kCB) {
@@ -378,24 +470,24 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
 #pragma unroll
             for (int j = 0; j < kCB; ++j) Mn = fmaxf(Mn, mb[j]);
             const float f = expf(Mx - Mn);
-            acc = make_float4(acc.x * f, acc.y * f, acc.z * f, acc.w * f);
+            oc = make_float4(oc.x * f, oc.y * f, oc.z * f, oc.w * f);
             Ls *= f;
 #pragma unroll
             for (int j = 0; j < kCB; ++j) {
                 const float w = expf(mb[j] - Mn);
-                acc.x = fmaf(ob[j].x, w, acc.x);
-                acc.y = fmaf(ob[j].y, w, acc.y);
-                acc.z = fmaf(ob[j].z, w, acc.z);
-                acc.w = fmaf(ob[j].w, w, acc.w);
+                oc.x = fmaf(ob[j].x, w, oc.x);
+                oc.y = fmaf(ob[j].y, w, oc.y);
+                oc.z = fmaf(ob[j].z, w, oc.z);
+                oc.w = fmaf(ob[j].w, w, oc.w);
                 Ls = fmaf(lb[j], w, Ls);
             }
             Mx = Mn;
         }
     }
     if constexpr (NGc > 1) {
-        float4 *gs = reinterpret_cast<float4 *>(sc);   // [NGc][NO][2] float4: (M, L, -, -), o
+        float4 *gs = reinterpret_cast<float4 *>(ring);   // [NGc][NO][2] float4: (M, L, -, -), o
         gs[2 * (grp * NO + o)] = make_float4(Mx, Ls, 0.f, 0.f);
-        gs[2 * (grp * NO + o) + 1] = acc;
+        gs[2 * (grp * NO + o) + 1] = oc;
         __syncthreads();
         if (grp == 0 && h < rep) {
 #pragma unroll
@@ -403,8 +495,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
                 const float4 ml = gs[2 * (g * NO + o)], og = gs[2 * (g * NO + o) + 1];
                 const float Mn = fmaxf(Mx, ml.x);
                 const float fa = expf(Mx - Mn), fg = expf(ml.x - Mn);
-                acc = make_float4(acc.x * fa + og.x * fg, acc.y * fa + og.y * fg, acc.z * fa + og.z * fg,
-                                  acc.w * fa + og.w * fg);
+                oc = make_float4(oc.x * fa + og.x * fg, oc.y * fa + og.y * fg, oc.z * fa + og.z * fg,
+                                  oc.w * fa + og.w * fg);
                 Ls = Ls * fa + ml.y * fg;
                 Mx = Mn;
             }
@@ -413,7 +505,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnArgs 
     if (grp == 0 && h < rep) {
         const float il = Ls > 0.f ? 1.0f / Ls : 0.f;
         reinterpret_cast<float4 *>(a.out + (kh * rep + h) * kHD)[q4] =
-            make_float4(acc.x * il, acc.y * il, acc.z * il, acc.w * il);
+            make_float4(oc.x * il, oc.y * il, oc.z * il, oc.w * il);
     }
     if (tid == 0) a.count[kh] = 0u;   // ready for the next layer / token
 }
@@ -524,7 +616,7 @@ struct DecLayer {
 
 struct Decoder {
     DecConfig cfg{};
-    int dev = 0, sms = 0, nchunk = 1, lmax = 1;
+    int dev = 0, sms = 0, nchunk = 1;
     DecLayer *layers = nullptr;
     const void *emb = nullptr, *lm = nullptr;
     int emb_qt = -1, lm_qt = -1;
@@ -588,12 +680,12 @@ bool Decoder::enqueue(cudaStream_t s)
         a.NK = NK;
         a.max_ctx = c.max_ctx;
         a.nchunk = nchunk;
-        a.lmax = lmax;
+        a.wait_limit = lim;
         a.quirks = c.quirks;
         a.eps = c.norm_eps;
         a.rope_base = c.rope_base;
         a.scale = 1.0f / sqrtf(static_cast<float>(HD));
-        const size_t smem = attn_smem_floats(NH / NK, lmax) * sizeof(float);
+        const size_t smem = attn_smem_bytes(NH / NK);
         if (!launch_pdl(attn_kernel(NH / NK), dim3(NK, nchunk), dim3(kAttnThreads), smem, s, a)) return false;
         // x2 = x + Wo @ att
         f = MvFuse{};
@@ -661,13 +753,9 @@ Decoder *dec_create(const DecConfig &c)
     d->layers = new DecLayer[c.n_layers];
     cudaGetDevice(&d->dev);
     cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, d->dev);
-    // context chunks: about four attention CTAs per SM over all KV heads
-    // context chunks: one wave of two attention CTAs per SM over all KV heads,
-    // more if a chunk would exceed kVMax positions (its V rows live in shared memory)
-    d->nchunk = (2 * d->sms) / c.n_kv_heads;
-    if (d->nchunk < (c.max_ctx + kVMax - 1) / kVMax) d->nchunk = (c.max_ctx + kVMax - 1) / kVMax;
+    // context chunks: one wave of one attention CTA per SM over all KV heads
+    d->nchunk = d->sms / c.n_kv_heads;
     if (d->nchunk < 1) d->nchunk = 1;
-    d->lmax = (c.max_ctx + d->nchunk - 1) / d->nchunk;
     const int NH = c.n_heads, NK = c.n_kv_heads, HD = c.head_dim;
     const size_t kvf = static_cast<size_t>(c.n_layers) * d->kv_layer_floats();
     bool ok = dec_ok(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "stream") &&
@@ -692,7 +780,7 @@ Decoder *dec_create(const DecConfig &c)
              dec_ok(cudaMemset(d->err, 0, sizeof(int)), "memset") &&
              dec_ok(cudaMemset(d->kc, 0, sizeof(float) * kvf), "memset") &&
              dec_ok(cudaMemset(d->vc, 0, sizeof(float) * kvf), "memset");
-        const size_t smem = attn_smem_floats(NH / NK, d->lmax) * sizeof(float);
+        const size_t smem = attn_smem_bytes(NH / NK);
         if (ok && smem > 48 * 1024)
             ok = dec_ok(cudaFuncSetAttribute(attn_kernel(NH / NK), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem)), "attention smem");
