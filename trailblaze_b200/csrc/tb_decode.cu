@@ -120,23 +120,39 @@ __device__ __forceinline__ float transpose_sum(float (&v)[V])
     return r;
 }
 
-// The chunk's cached K and V rows stream through a ring of kNS stages, one
-// block of kBP positions per stage (its K rows, then its V rows), by 1-D bulk
-// copies that one thread issues; every block is consumed as it lands.
-static constexpr int kBP = 32;                                   // positions per block (one per lane)
-static constexpr int kNS = 4;                                    // ring stages
-static constexpr uint32_t kStageBytes = 2u * kBP * kHD * sizeof(float);
-static constexpr int kPW = kBP / (kAttnThreads / 32);            // positions of a block per warp
-static_assert(kBP == 32 && kPW * (kAttnThreads / 32) == kBP, "one position per lane, whole warps");
+// The chunk's cached rows stream through a ring of kNS stages by 1-D bulk
+// copies that one thread issues: first the K rows of every block of kBP
+// positions, then the V rows (2 nb loads for nb blocks).  The scores need only
+// K and are cheap, so the K stages are released, and refilled with V rows,
+// while the stream is still running.
+static constexpr int kBP = 64;                                   // positions per load
+static constexpr int kNS = 3;                                    // ring stages
+static constexpr uint32_t kStageBytes = kBP * kHD * sizeof(float);   // the K or V rows of a block
+static constexpr int kPW = kBP / (kAttnThreads / 32);            // positions of a load per warp
+static_assert(kPW * 8 <= 32 && kPW * (kAttnThreads / 32) == kBP, "a warp's (position, head) items fit its lanes");
+static constexpr int kSmemCap = 232448;                          // 227 KB opt-in per CTA
 
-// Dynamic shared memory: ring [kNS][K rows | V rows] | q[rep][HD] | k[HD] |
-// new v[HD] | q-norm and k-norm weights [2][HD] | (cos, sin)[HD/2] | full
-// barriers [kNS] | stage release counters [kNS] | last block issued per stage
-// [kNS].  The ring doubles as scratch once every block is consumed.
-__host__ __device__ inline size_t attn_smem_bytes(int rep)
+__host__ __device__ inline int attn_r2(int rep)
+{
+    return rep <= 1 ? 1 : rep <= 2 ? 2 : rep <= 4 ? 4 : 8;
+}
+
+// Positions of the score buffer, a multiple of 4 so its rows stay 16-byte aligned.
+__host__ __device__ inline int attn_lmax4(int lmax)
+{
+    return (lmax + 3) & ~3;
+}
+
+// Dynamic shared memory: ring [kNS][kBP][HD] | scores, then probabilities
+// [lmax4][R2] | q[rep][HD] | k[HD] | new v[HD] | q-norm and k-norm weights
+// [2][HD] | (cos, sin)[HD/2] | chunk statistics [32] | full barriers [kNS] |
+// stage release counters [kNS] | last load issued per stage [kNS].  The ring
+// doubles as scratch once every load is consumed.
+__host__ __device__ inline size_t attn_smem_bytes(int rep, int lmax)
 {
     return static_cast<size_t>(kNS) * kStageBytes +
-           sizeof(float) * (static_cast<size_t>(rep) * kHD + 5 * kHD) +
+           sizeof(float) * (static_cast<size_t>(attn_lmax4(lmax)) * attn_r2(rep) +
+                            static_cast<size_t>(rep) * kHD + 5 * kHD + 32) +
            kNS * (sizeof(uint64_t) + 2 * sizeof(uint32_t));
 }
 
@@ -162,25 +178,45 @@ __device__ __forceinline__ float warp_sum(float v)
     return v;
 }
 
+// R2 probabilities of one position (row of the [lmax4][R2] buffer).
+template <int R2>
+__device__ __forceinline__ void load_probs(const float *row, float (&p)[R2])
+{
+    if constexpr (R2 >= 4) {
+#pragma unroll
+        for (int i = 0; i < R2; i += 4) {
+            const float4 t = reinterpret_cast<const float4 *>(row)[i / 4];
+            p[i] = t.x;
+            p[i + 1] = t.y;
+            p[i + 2] = t.z;
+            p[i + 3] = t.w;
+        }
+    } else if constexpr (R2 == 2) {
+        const float2 t = reinterpret_cast<const float2 *>(row)[0];
+        p[0] = t.x;
+        p[1] = t.y;
+    } else {
+        p[0] = row[0];
+    }
+}
+
 // grid (NK, nchunk), kAttnThreads threads, one CTA per SM; R2 = query heads
 // per KV head rounded up to a power of two (1, 2, 4 or 8).
 //
 // After the programmatic-dependency wait this token's q (and, in the chunk
-// that owns pos, k and v) is requested first, then thread 0 starts the ring,
-// so q is rotated and normed while the cache rows stream in (row pos, this
-// step's, is never read from the cache).  Warp w takes positions kPW w ..
-// kPW w + kPW - 1 of every block and runs its own online softmax over them,
-// with no CTA barrier per block:
-//   scores   each lane forms the partial dot products of its four dimensions
-//            for the warp's (position, head) items; one transposed reduction
-//            gives whole scores, lane l holding item l % (kPW R2);
-//   softmax  per head, the block maximum over the warp's positions, the
-//            rescale factor of the running sums, the probabilities;
-//   p . V    lane l: dimensions 4 l .. 4 l + 3, every head, the probabilities
-//            broadcast by shuffles.
+// that owns pos, k and v) and the QK-norm weights are requested first, then
+// thread 0 starts the ring, so q is rotated and normed while the cache rows
+// stream in (row pos, this step's, is never read from the cache).  Warp w
+// takes positions kPW w .. kPW w + kPW - 1 of every block:
+//   scores   (K loads) each lane forms the partial dot products of its four
+//            dimensions for the warp's (position, head) items; one transposed
+//            reduction gives whole scores, lane l holding item l % (kPW R2);
+//   softmax  (once, between the K and the V loads) warp h: maximum, sum and
+//            probabilities of head h over the chunk;
+//   p . V    (V loads) lane l: dimensions 4 l .. 4 l + 3, every head.
 // The last warp done with a stage (a shared-memory counter) refills it with
-// the block kNS further on.  At the end the warps' (m, l, o) are merged in
-// shared memory into the chunk's partial.
+// the load kNS further on.  The warps' o are summed in shared memory into the
+// chunk's partial (o, m, l).
 template <int R2>
 __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs a)
 {
@@ -199,17 +235,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
     const bool owner = pos >= t0 && pos < t1;   // this chunk holds the new position (its last)
     const int tc = min(t1, pos);                // cached rows of the chunk: [t0, tc)
     const int nb = (t1 - t0 + kBP - 1) / kBP;   // blocks of the chunk
+    const int nl = 2 * nb;                      // loads: K rows of every block, then V rows
+    const int lmax4 = attn_lmax4((a.max_ctx + a.nchunk - 1) / a.nchunk);
 
     uint8_t *ring = smraw;
-    float *qs = reinterpret_cast<float *>(smraw + kNS * kStageBytes);   // [rep][HD]
+    float *sc = reinterpret_cast<float *>(smraw + kNS * kStageBytes);   // [lmax4][R2]
+    float *qs = sc + lmax4 * R2;                                         // [rep][HD]
     float *ks = qs + rep * kHD;                                          // [HD]
     float *vnw = ks + kHD;                                               // [HD]
     float *qnw = vnw + kHD;                                              // [HD]
     float *knw = qnw + kHD;                                              // [HD]
     float2 *csr = reinterpret_cast<float2 *>(knw + kHD);                 // [HD/2]
-    uint64_t *full = reinterpret_cast<uint64_t *>(csr + kHD / 2);        // [kNS]
+    float *red = reinterpret_cast<float *>(csr + kHD / 2);              // [32]: m, l per head
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + 32);             // [kNS]
     unsigned *cnt = reinterpret_cast<unsigned *>(full + kNS);            // [kNS] warps done with a stage
-    int *iss = reinterpret_cast<int *>(cnt + kNS);                       // [kNS] last block issued
+    int *iss = reinterpret_cast<int *>(cnt + kNS);                       // [kNS] last load issued
     __shared__ int s_last;
 
     const float *kcache = a.kc + static_cast<size_t>(kh) * a.max_ctx * kHD;
@@ -229,27 +269,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         vn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK + kh) * kHD) + tid);
     }
 
-    // ---- the ring: block b's K rows and V rows into stage b % kNS ----
-    auto issue = [&](int b, int s) {   // one thread
-        const int tb = t0 + b * kBP;
+    // ---- the ring: load j (the K rows of block j for j < nb, else the V rows
+    // of block j - nb) into stage j % kNS ----
+    auto issue = [&](int j, int s) {   // one thread
+        const int blk = j < nb ? j : j - nb;
+        const int tb = t0 + blk * kBP;
         const int n = max(0, min(tb + kBP, tc) - tb);
         const uint32_t bytes = static_cast<uint32_t>(n) * kHD * sizeof(float);
         const uint32_t bar = smem_u32(full + s);
-        mbar_expect_tx(bar, 2u * bytes);   // with n == 0 a plain arrival completes the phase
-        if (n > 0) {
-            uint8_t *st = ring + static_cast<size_t>(s) * kStageBytes;
-            bulk_g2s(smem_u32(st), kcache + static_cast<size_t>(tb) * kHD, bytes, bar, pol);
-            bulk_g2s(smem_u32(st + kStageBytes / 2), vcache + static_cast<size_t>(tb) * kHD, bytes, bar, pol);
-        }
+        mbar_expect_tx(bar, bytes);   // with n == 0 a plain arrival completes the phase
+        if (n > 0)
+            bulk_g2s(smem_u32(ring + static_cast<size_t>(s) * kStageBytes),
+                     (j < nb ? kcache : vcache) + static_cast<size_t>(tb) * kHD, bytes, bar, pol);
     };
     if (tid == 0) {
         for (int u = 0; u < kNS; ++u) {
             mbar_init(smem_u32(full + u), 1);
             cnt[u] = 0u;
-            iss[u] = u < nb ? u : -1;
+            iss[u] = u < nl ? u : -1;
         }
         fence_mbar_init();
-        for (int u = 0; u < min(nb, kNS); ++u) issue(u, u);
+        for (int u = 0; u < min(nl, kNS); ++u) issue(u, u);
     }
 
     // ---- q and k normed and rotated in shared memory ----
@@ -260,6 +300,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         reinterpret_cast<float4 *>(knw)[tid] = knv;
     }
     if (tid < kHD / 4) reinterpret_cast<float4 *>(qnw)[tid] = qnv;
+    if (tid < 32) red[tid] = (tid & 1) ? 0.f : -1e38f;   // an empty chunk's statistics
     if (tid < kHD / 2) csr[tid] = rope_cs(pos, tid, a.rope_base);
     __syncthreads();
     auto rope_all = [&]() {
@@ -301,82 +342,91 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
     const float4 kn4 = owner ? reinterpret_cast<const float4 *>(ks)[lane] : z4;
     const float4 vn4 = owner ? reinterpret_cast<const float4 *>(vnw)[lane] : z4;
 
-    // ---- the blocks: every warp runs its own online softmax over its kPW
-    // positions of each block, lanes sharing values by shuffles only.  Lane l
-    // holds head l % R2 (its running maximum and sum) and, for the scores of a
-    // block, the item (position (l % V) / R2, head l % R2) ----
+    // ---- the loads: scores from the K rows, the softmax once, p . V from the V rows ----
     constexpr int V = kPW * R2;   // (position, head) items of a warp per block
     float4 acc[R2];
 #pragma unroll
     for (int h = 0; h < R2; ++h) acc[h] = z4;
-    float m_run = -1e38f, l_run = 0.f;
     bool fail = false;
     int s = 0;
     uint32_t par = 0;
-    for (int b = 0; b < nb; ++b) {
-        if (!mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit)) {
-            fail = true;   // the other warps' waits run out as well: nothing refills the ring
-            break;
-        }
-        const float *Ks = reinterpret_cast<const float *>(ring + static_cast<size_t>(s) * kStageBytes);
-        const float *Vs = Ks + kBP * kHD;
-        const int tb = t0 + b * kBP;
-        const int nv = min(kBP, t1 - tb);   // positions of this block
-        float v[V];
-#pragma unroll
-        for (int p = 0; p < kPW; ++p) {
-            const int pl = warp * kPW + p;
-            const float4 k4 = (tb + pl == pos) ? kn4 : reinterpret_cast<const float4 *>(Ks + pl * kHD)[lane];
-#pragma unroll
-            for (int h = 0; h < R2; ++h) v[p * R2 + h] = dot4(qr[h], k4);
-        }
-        const bool valid = warp * kPW + (lane % V) / R2 < nv;
-        const float dsum = transpose_sum<V>(v);   // every lane takes part in the shuffles
-        const float sv = valid ? dsum * a.scale : -1e38f;
-        float bm = sv;   // block maximum of head lane % R2 over the warp's positions
-#pragma unroll
-        for (int off = R2; off < V; off <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xFFFFFFFFu, bm, off));
-        const float mn = fmaxf(m_run, bm);
-        const float al = expf(m_run - mn);
-        const float pv = valid ? expf(sv - mn) : 0.f;
-        float ps = pv;
-#pragma unroll
-        for (int off = R2; off < V; off <<= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, off);
-        l_run = l_run * al + ps;
-        m_run = mn;
-#pragma unroll
-        for (int h = 0; h < R2; ++h)
-            if (h < rep) {
-                const float ah = __shfl_sync(0xFFFFFFFFu, al, h);
-                acc[h] = make_float4(acc[h].x * ah, acc[h].y * ah, acc[h].z * ah, acc[h].w * ah);
+    for (int j = 0; j < nl; ++j) {
+        if (j == nb) {
+            // every score of the chunk is in sc: maximum, probabilities and sum
+            // of each head over the chunk, one warp per head
+            __syncthreads();
+            const int n = t1 - t0;
+            if (warp < rep) {
+                const int h = warp;
+                float m = -1e38f;
+                for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[t * R2 + h]);
+                m = warp_max(m);
+                float l = 0.f;
+                for (int t = lane; t < n; t += 32) {
+                    const float p = expf(sc[t * R2 + h] - m);
+                    sc[t * R2 + h] = p;
+                    l += p;
+                }
+                l = warp_sum(l);
+                if (lane == 0) {
+                    red[2 * h] = m;
+                    red[2 * h + 1] = l;
+                }
             }
+            __syncthreads();
+        }
+        // a warp whose wait ran out stops consuming (and releasing) loads; the
+        // others' waits then run out as well, nothing refills the ring
+        fail = fail || !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit));
+        if (!fail) {
+            const float *R = reinterpret_cast<const float *>(ring + static_cast<size_t>(s) * kStageBytes);
+            const int blk = j < nb ? j : j - nb;
+            const int tb = t0 + blk * kBP;
+            const int nv = min(kBP, t1 - tb);   // positions of this block
+            if (j < nb) {
+                float v[V];
 #pragma unroll
-        for (int p = 0; p < kPW; ++p) {
-            const int pl = warp * kPW + p;
-            if (pl < nv) {
-                const float4 v4 = (tb + pl == pos) ? vn4 : reinterpret_cast<const float4 *>(Vs + pl * kHD)[lane];
+                for (int p = 0; p < kPW; ++p) {
+                    const int pl = warp * kPW + p;
+                    const float4 k4 = (tb + pl == pos) ? kn4 : reinterpret_cast<const float4 *>(R + pl * kHD)[lane];
 #pragma unroll
-                for (int h = 0; h < R2; ++h)
-                    if (h < rep) {
-                        const float pr = __shfl_sync(0xFFFFFFFFu, pv, p * R2 + h);
-                        acc[h].x = fmaf(pr, v4.x, acc[h].x);
-                        acc[h].y = fmaf(pr, v4.y, acc[h].y);
-                        acc[h].z = fmaf(pr, v4.z, acc[h].z);
-                        acc[h].w = fmaf(pr, v4.w, acc[h].w);
+                    for (int h = 0; h < R2; ++h) v[p * R2 + h] = dot4(qr[h], k4);
+                }
+                const float d = transpose_sum<V>(v);
+                const int it = lane % V, p = it / R2, h = it % R2;
+                const int pl = warp * kPW + p;
+                if (lane < V && h < rep && pl < nv) sc[(blk * kBP + pl) * R2 + h] = d * a.scale;
+            } else {
+#pragma unroll
+                for (int p = 0; p < kPW; ++p) {
+                    const int pl = warp * kPW + p;
+                    if (pl < nv) {
+                        const float4 v4 = (tb + pl == pos) ? vn4 : reinterpret_cast<const float4 *>(R + pl * kHD)[lane];
+                        float pr[R2];
+                        load_probs<R2>(sc + (blk * kBP + pl) * R2, pr);
+#pragma unroll
+                        for (int h = 0; h < R2; ++h)
+                            if (h < rep) {
+                                acc[h].x = fmaf(pr[h], v4.x, acc[h].x);
+                                acc[h].y = fmaf(pr[h], v4.y, acc[h].y);
+                                acc[h].z = fmaf(pr[h], v4.z, acc[h].z);
+                                acc[h].w = fmaf(pr[h], v4.w, acc[h].w);
+                            }
                     }
+                }
             }
-        }
-        // the last warp done with this stage refills it with block b + kNS
-        __syncwarp();
-        if (lane == 0) {
-            __threadfence_block();
-            if (atomicAdd(cnt + s, 1u) == static_cast<unsigned>(nwarp) - 1u) {
-                cnt[s] = 0u;
+            // the last warp done with this stage refills it with load j + kNS
+            __syncwarp();
+            if (lane == 0) {
                 __threadfence_block();
-                if (b + kNS < nb) {
-                    fence_proxy_async_smem();
-                    issue(b + kNS, s);
-                    iss[s] = b + kNS;
+                if (atomicAdd(cnt + s, 1u) == static_cast<unsigned>(nwarp) - 1u) {
+                    cnt[s] = 0u;
+                    __threadfence_block();
+                    if (j + kNS < nl) {
+                        fence_proxy_async_smem();
+                        issue(j + kNS, s);
+                        iss[s] = j + kNS;
+                    }
                 }
             }
         }
@@ -386,50 +436,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         }
     }
     if (__syncthreads_or(fail)) {
-        // a wait ran out: let the copies still in flight land before the ring
-        // is reused (bounded; only a stage's last block can be in flight), and
-        // hand in an empty partial so the tickets stay consistent; the error
-        // word is already set
+        // let the copies still in flight land before the ring is reused
+        // (bounded; only a stage's last load can be in flight) and hand in an
+        // empty partial so the tickets stay consistent; the error word is set
         if (tid == 0)
             for (int u = 0; u < kNS; ++u)
                 if (iss[u] >= 0) mbar_wait_bounded(smem_u32(full + u), (iss[u] / kNS) & 1u, nullptr, kAttnDrain);
 #pragma unroll
         for (int h = 0; h < R2; ++h) acc[h] = z4;
-        m_run = -1e38f;
-        l_run = 0.f;
+        if (tid < 16) red[tid] = (tid & 1) ? 0.f : -1e38f;
     }
-    __syncthreads();   // every block consumed (or drained): the ring is free
+    __syncthreads();   // every load consumed (or drained): the ring is free
 
-    // ---- the chunk's partial: the warps' states merged, o, m, l per head ----
+    // ---- the chunk's partial: o summed over the warps, m and l per head ----
     {
-        float4 *pr = reinterpret_cast<float4 *>(ring);                       // [nwarp][rep][HD/4]
-        float *wml = reinterpret_cast<float *>(pr + nwarp * rep * (kHD / 4));  // [nwarp][R2][2]
+        float4 *pr4 = reinterpret_cast<float4 *>(ring);   // [nwarp][rep][HD/4]
 #pragma unroll
         for (int h = 0; h < R2; ++h)
-            if (h < rep) pr[(warp * rep + h) * (kHD / 4) + lane] = acc[h];
-        if (lane < R2) {
-            wml[(warp * R2 + lane) * 2] = m_run;
-            wml[(warp * R2 + lane) * 2 + 1] = l_run;
-        }
+            if (h < rep) pr4[(warp * rep + h) * (kHD / 4) + lane] = acc[h];
         __syncthreads();
         for (int e = tid; e < rep * (kHD / 4); e += kAttnThreads) {
             const int h = e / (kHD / 4), q4 = e % (kHD / 4);
-            float M = -1e38f;
-            for (int u = 0; u < nwarp; ++u) M = fmaxf(M, wml[(u * R2 + h) * 2]);
-            float4 so = z4;
-            float sl = 0.f;
-            for (int u = 0; u < nwarp; ++u) {
-                const float w = expf(wml[(u * R2 + h) * 2] - M);
-                const float4 t = pr[(u * rep + h) * (kHD / 4) + q4];
-                so.x = fmaf(t.x, w, so.x);
-                so.y = fmaf(t.y, w, so.y);
-                so.z = fmaf(t.z, w, so.z);
-                so.w = fmaf(t.w, w, so.w);
-                sl = fmaf(wml[(u * R2 + h) * 2 + 1], w, sl);
+            float4 so = pr4[h * (kHD / 4) + q4];
+            for (int u = 1; u < nwarp; ++u) {
+                const float4 t = pr4[(u * rep + h) * (kHD / 4) + q4];
+                so.x += t.x;
+                so.y += t.y;
+                so.z += t.z;
+                so.w += t.w;
             }
             float *dst = a.part + (static_cast<size_t>(kh * rep + h) * a.nchunk + c) * kPS;
             reinterpret_cast<float4 *>(dst)[q4] = so;
-            if (q4 == 0) reinterpret_cast<float2 *>(dst + kHD)[0] = make_float2(M, sl);
+            if (q4 == 0) reinterpret_cast<float2 *>(dst + kHD)[0] = make_float2(red[2 * h], red[2 * h + 1]);
         }
     }
 
@@ -510,10 +548,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
     if (tid == 0) a.count[kh] = 0u;   // ready for the next layer / token
 }
 
-static int attn_r2(int rep)
-{
-    return rep <= 1 ? 1 : rep <= 2 ? 2 : rep <= 4 ? 4 : 8;
-}
 
 static void (*attn_kernel(int rep))(const AttnArgs)
 {
@@ -685,7 +719,7 @@ bool Decoder::enqueue(cudaStream_t s)
         a.eps = c.norm_eps;
         a.rope_base = c.rope_base;
         a.scale = 1.0f / sqrtf(static_cast<float>(HD));
-        const size_t smem = attn_smem_bytes(NH / NK);
+        const size_t smem = attn_smem_bytes(NH / NK, (c.max_ctx + nchunk - 1) / nchunk);
         if (!launch_pdl(attn_kernel(NH / NK), dim3(NK, nchunk), dim3(kAttnThreads), smem, s, a)) return false;
         // x2 = x + Wo @ att
         f = MvFuse{};
@@ -753,9 +787,22 @@ Decoder *dec_create(const DecConfig &c)
     d->layers = new DecLayer[c.n_layers];
     cudaGetDevice(&d->dev);
     cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, d->dev);
-    // context chunks: one wave of one attention CTA per SM over all KV heads
+    // context chunks: one wave of one attention CTA per SM over all KV heads,
+    // more if a chunk's scores would not fit the shared memory left by the ring
     d->nchunk = d->sms / c.n_kv_heads;
     if (d->nchunk < 1) d->nchunk = 1;
+    {
+        const int rep = c.n_heads / c.n_kv_heads;
+        const long long room = static_cast<long long>(kSmemCap) - static_cast<long long>(attn_smem_bytes(rep, 0));
+        const int lcap = static_cast<int>(room / (static_cast<long long>(sizeof(float)) * attn_r2(rep))) & ~3;
+        if (lcap < 4) {
+            fprintf(stderr, "[tb_cuda] decoder: attention does not fit shared memory\n");
+            dec_free(d);
+            return nullptr;
+        }
+        const int need = (c.max_ctx + lcap - 1) / lcap;
+        if (d->nchunk < need) d->nchunk = need;
+    }
     const int NH = c.n_heads, NK = c.n_kv_heads, HD = c.head_dim;
     const size_t kvf = static_cast<size_t>(c.n_layers) * d->kv_layer_floats();
     bool ok = dec_ok(cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking), "stream") &&
@@ -780,7 +827,7 @@ Decoder *dec_create(const DecConfig &c)
              dec_ok(cudaMemset(d->err, 0, sizeof(int)), "memset") &&
              dec_ok(cudaMemset(d->kc, 0, sizeof(float) * kvf), "memset") &&
              dec_ok(cudaMemset(d->vc, 0, sizeof(float) * kvf), "memset");
-        const size_t smem = attn_smem_bytes(NH / NK);
+        const size_t smem = attn_smem_bytes(NH / NK, (c.max_ctx + d->nchunk - 1) / d->nchunk);
         if (ok && smem > 48 * 1024)
             ok = dec_ok(cudaFuncSetAttribute(attn_kernel(NH / NK), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem)), "attention smem");
