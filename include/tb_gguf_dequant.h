@@ -206,6 +206,28 @@ int    tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_ou
  * output (n_heads head_dim), 4 its SwiGLU activation (ffn_dim), 5 the logits
  * (vocab).  Blocking.  1 = ok, 0 for an unknown vector or n past its size. */
 int    tb_cuda_dec_read(void *dec, int which, float *host, int n);
+
+/* Tensor parallelism over `world` GPUs (2, 4 or 8; one process per GPU), the
+ * sharding of SURVEY-style Megatron decode: rank r holds
+ *   w_qkv      rows of its q heads [r NH/w, (r+1) NH/w), then of its k heads and
+ *              its v heads (the same split of n_kv_heads), H columns;
+ *   w_o        all H rows, the K columns of its q heads (K = NH/w * head_dim);
+ *   w_gate_up  its FFN row pairs [r F/w, (r+1) F/w), interleaved gate_i, up_i;
+ *   w_down     all H rows, the K columns [r F/w, (r+1) F/w);
+ *   w_out      its vocabulary rows [r V/w, (r+1) V/w); tok_embd is whole;
+ *   the norm weights whole.
+ * The ranks exchange the o and down partials and the greedy pairs over NVLink
+ * through peer stores into each other's exchange region (mapped with CUDA IPC;
+ * no collective library).  Every rank must run the same steps: a rank that
+ * stops makes the others' bounded waits run out (their call returns 0).
+ * tb_cuda_dec_step / _generate return the same token on every rank; logits and
+ * tb_cuda_dec_read vectors are this rank's; the KV cache holds its kv heads. */
+void  *tb_cuda_dec_create_tp(const tb_dec_config *c, int rank, int world);
+/* The 64-byte CUDA IPC handle of this rank's exchange region.  1 = ok. */
+int    tb_cuda_dec_tp_handle(void *dec, void *handle_out);
+/* Maps the other ranks' regions; handles = world x 64 bytes in rank order (as
+ * gathered from every rank's tb_cuda_dec_tp_handle).  1 = ok. */
+int    tb_cuda_dec_tp_connect(void *dec, const void *handles);
 void   tb_cuda_dec_destroy(void *dec);
 
 #ifdef __cplusplus

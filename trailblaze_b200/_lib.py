@@ -67,6 +67,9 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_dec_kv": (c_void_p, [c_void_p, c_int, c_int]),
         "tb_cuda_dec_kv_copy": (c_int, [c_void_p, c_int, c_int, c_int, c_int, fp, c_int]),
         "tb_cuda_dec_read": (c_int, [c_void_p, c_int, fp, c_int]),
+        "tb_cuda_dec_create_tp": (c_void_p, [ctypes.POINTER(DecConfig), c_int, c_int]),
+        "tb_cuda_dec_tp_handle": (c_int, [c_void_p, c_void_p]),
+        "tb_cuda_dec_tp_connect": (c_int, [c_void_p, c_void_p]),
         "tb_cuda_dec_step": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_int), fp]),
         "tb_cuda_dec_generate": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_int), fp, fp]),
         "tb_cuda_dec_destroy": (None, [c_void_p]),
@@ -87,5 +90,6 @@ def exported_symbols() -> list[str]:
         "tb_cuda_matvec_dev", "tb_cuda_dequant_dev", "tb_cuda_qtype_info", "tb_cuda_last_error",
         "tb_cuda_launch_count", "tb_cuda_version", "tb_cuda_matvec_device_noalloc",
         "tb_cuda_matvec_fused_dev", "tb_cuda_dec_create", "tb_cuda_dec_set_layer", "tb_cuda_dec_set_head",
-        "tb_cuda_dec_kv", "tb_cuda_dec_kv_copy", "tb_cuda_dec_read", "tb_cuda_dec_step", "tb_cuda_dec_generate", "tb_cuda_dec_destroy",
+        "tb_cuda_dec_kv", "tb_cuda_dec_kv_copy", "tb_cuda_dec_read", "tb_cuda_dec_create_tp",
+        "tb_cuda_dec_tp_handle", "tb_cuda_dec_tp_connect", "tb_cuda_dec_step", "tb_cuda_dec_generate", "tb_cuda_dec_destroy",
     ]

@@ -248,4 +248,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     return false;
 }
 
+// Bounded wait until *ctr >= target (system-scope acquire load); the counter
+// is raised by peers over NVLink.  False when the limit runs out.
+__device__ __forceinline__ bool wait_counter(const unsigned long long *ctr, unsigned long long target, uint32_t limit)
+{
+    for (uint32_t i = 0; i < limit; ++i) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ctr) : "memory");
+        if (v >= target) return true;
+        __nanosleep(32);
+    }
+    return false;
+}
+
 }  // namespace tb

@@ -582,8 +582,29 @@ __device__ __forceinline__ ArgBest warp_best(ArgBest b)
     return b;
 }
 
+// Tensor-parallel exchange of the ranks' best (value, vocabulary index)
+// pairs; world 1 leaves it unused.
+struct ArgTP {
+    int rank, world, base;                  // base: this rank's first vocabulary index
+    unsigned long long *am[kMaxRanks];      // every rank's pair slots ([world])
+    unsigned long long *ctr[kMaxRanks];     // every rank's argmax arrival counter
+    const unsigned long long *own_am, *own_ctr;
+    int *epoch;                             // steps completed
+    uint32_t wait_limit;
+    int *err;
+};
+
+__device__ __forceinline__ unsigned long long pack_best(ArgBest b)
+{
+    return (static_cast<unsigned long long>(static_cast<uint32_t>(b.i)) << 32) | __float_as_uint(b.v);
+}
+__device__ __forceinline__ ArgBest unpack_best(unsigned long long u)
+{
+    return ArgBest{__uint_as_float(static_cast<uint32_t>(u)), static_cast<int>(u >> 32)};
+}
+
 __global__ void __launch_bounds__(kArgThreads) k_argmax_step(const float *logits, int n, float *pv, int *pi,
-                                                              unsigned *count, int *token, int *pos)
+                                                              unsigned *count, int *token, int *pos, const ArgTP tp)
 {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -613,9 +634,27 @@ __global__ void __launch_bounds__(kArgThreads) k_argmax_step(const float *logits
     b = ArgBest{-FLT_MAX, 0x7FFFFFFF};
     for (int u = lane; u < G; u += 32) b = better(b, ArgBest{__ldcg(pv + u), __ldcg(pi + u)});
     b = warp_best(b);
+    if (tp.world > 1) {
+        // this rank's best to every rank, then the best of all ranks (the
+        // first index of the largest value, as on one device)
+        const ArgBest mine{b.v, b.i == 0x7FFFFFFF ? 0x7FFFFFFF : tp.base + b.i};
+        if (lane < tp.world) tp.am[lane][tp.rank] = pack_best(mine);
+        __threadfence_system();
+        __syncwarp();
+        if (lane < tp.world) atomicAdd_system(tp.ctr[lane], 1ull);
+        bool ok = true;
+        if (lane == 0)
+            ok = wait_counter(tp.own_ctr, static_cast<unsigned long long>(*tp.epoch + 1) * tp.world, tp.wait_limit);
+        ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
+        if (!ok && lane == 0) atomicExch(tp.err, ERR_WAIT_TIMEOUT);
+        b = ArgBest{-FLT_MAX, 0x7FFFFFFF};
+        if (lane < tp.world) b = unpack_best(__ldcg(tp.own_am + lane));
+        b = warp_best(b);
+    }
     if (lane == 0) {
         *token = b.i == 0x7FFFFFFF ? 0 : b.i;
         *pos = *pos + 1;
+        if (tp.epoch) *tp.epoch = *tp.epoch + 1;
         *count = 0u;
     }
 }
@@ -664,6 +703,28 @@ struct Decoder {
     float *kc = nullptr, *vc = nullptr, *part = nullptr, *argv = nullptr;
     int *argi = nullptr, *tok = nullptr, *pos = nullptr, *hostio = nullptr;
     unsigned *counts = nullptr;   // [NK] attention tickets + [1] argmax ticket
+    // tensor parallelism: cfg holds this rank's shape (heads, FFN rows and
+    // vocabulary divided by world); vocab_full is the embedding table's rows.
+    int rank = 0, world = 1, vocab_full = 0;
+    // exchange region (own memory, mapped by the peers through CUDA IPC):
+    // [o partials world x H][down partials world x H][argmax pairs world]
+    // [arrival counters: o, down, argmax]
+    uint8_t *xch = nullptr;
+    size_t off_xd = 0, off_am = 0, off_ctr = 0, xch_bytes = 0;
+    uint8_t *peer[kMaxRanks] = {};   // every rank's region, this rank's own included
+    bool peer_opened[kMaxRanks] = {};
+    int *epoch = nullptr;            // steps completed (device)
+
+    float *slot_o(int p) const { return reinterpret_cast<float *>(peer[p]); }
+    float *slot_d(int p) const { return reinterpret_cast<float *>(peer[p] + off_xd); }
+    unsigned long long *am(int p) const { return reinterpret_cast<unsigned long long *>(peer[p] + off_am); }
+    unsigned long long *ctr(int p, int k) const { return reinterpret_cast<unsigned long long *>(peer[p] + off_ctr) + k; }
+    bool connected() const
+    {
+        for (int p = 0; p < world; ++p)
+            if (!peer[p]) return false;
+        return true;
+    }
 
     size_t kv_layer_floats() const
     {
@@ -679,10 +740,12 @@ struct Decoder {
         return true;
     }
     bool enqueue(cudaStream_t s);
+    bool enqueue_tp(cudaStream_t s);
 };
 
 bool Decoder::enqueue(cudaStream_t s)
 {
+    if (world > 1) return enqueue_tp(s);
     const DecConfig &c = cfg;
     const int H = c.hidden, NH = c.n_heads, NK = c.n_kv_heads, HD = c.head_dim, F = c.ffn_dim;
     const int QKV = (NH + 2 * NK) * HD;
@@ -747,8 +810,123 @@ bool Decoder::enqueue(cudaStream_t s)
     f.w_early = true;
     if (!mv_launch(lm, lm_qt, c.vocab, H, x, logits, s, err, sms, lim, &f)) return false;
     const int G = sms;
+    ArgTP tp{};
+    tp.world = 1;
     return launch_pdl(k_argmax_step, dim3(G), dim3(kArgThreads), 0, s, static_cast<const float *>(logits),
-                      c.vocab, argv, argi, counts + NK, tok, pos);
+                      c.vocab, argv, argi, counts + NK, tok, pos, tp);
+}
+
+// Tensor-parallel step (world > 1).  q/k/v and gate/up hold this rank's heads
+// and FFN row pairs, attention is local; o and down hold this rank's K slice
+// and write their partial y into every rank's slots over NVLink.  The next
+// matvec sums the world partials (rank order, so every rank gets the same
+// bits) onto the residual once its arrival counter shows all of them, and its
+// CTA 0 writes the new residual.  Residual stream: x (after the down exchange)
+// and x2 (after the o exchange), alternating.  Arrival targets follow the
+// device-side step count: the down exchange of layer l in step e completes at
+// (e L + l + 1) world G_x arrivals, G_x the CTAs of the o / down launch; the o
+// exchange likewise on its own counter.
+bool Decoder::enqueue_tp(cudaStream_t s)
+{
+    const DecConfig &c = cfg;
+    const int H = c.hidden, NH = c.n_heads, NK = c.n_kv_heads, HD = c.head_dim, F = c.ffn_dim, L = c.n_layers;
+    const int QKV = (NH + 2 * NK) * HD;
+    const uint32_t lim = 1u << 22;
+    const unsigned long long per_x = static_cast<unsigned long long>(world) * static_cast<unsigned long long>(H < sms ? H : sms);
+    const unsigned long long per_step = static_cast<unsigned long long>(L) * per_x;
+    auto gather_in = [&](MvFuse &f, int kind, unsigned long long add, float *xout) {
+        f.xs = kind == 0 ? slot_o(rank) : slot_d(rank);
+        f.nsl = static_cast<uint32_t>(world);
+        f.xs_ctr = ctr(rank, kind);
+        f.xs_epoch = epoch;
+        f.xs_mul = per_step;
+        f.xs_add = add;
+        f.xout = xout;
+    };
+    auto scatter_out = [&](MvFuse &f, int kind) {
+        f.ny = static_cast<uint32_t>(world);
+        for (int p = 0; p < world; ++p) {
+            f.ys[p] = (kind == 0 ? slot_o(p) : slot_d(p)) + static_cast<size_t>(rank) * H;
+            f.yctr[p] = ctr(p, kind);
+        }
+    };
+    if (!dq_embed_launch(emb, emb_qt, vocab_full, H, tok, x, s)) return false;
+    for (int l = 0; l < L; ++l) {
+        const DecLayer &w = layers[l];
+        MvFuse f;
+        // q | k | v of this rank's heads = Wqkv @ rmsnorm(x), x = x2 + the down partials
+        f = MvFuse{};
+        f.xmode = MV_X_RMSNORM;
+        f.nw = w.attn_norm;
+        f.eps = c.norm_eps;
+        f.w_early = true;
+        if (l > 0) gather_in(f, 1, static_cast<unsigned long long>(l) * per_x, x);
+        if (!mv_launch(w.wqkv, w.qkv_qt, QKV, H, l > 0 ? x2 : x, qkv, s, err, sms, lim, &f)) return false;
+        AttnArgs a{};
+        a.qkv = qkv;
+        a.qn = w.q_norm;
+        a.kn = w.k_norm;
+        a.kc = kc + static_cast<size_t>(l) * kv_layer_floats();
+        a.vc = vc + static_cast<size_t>(l) * kv_layer_floats();
+        a.pos = pos;
+        a.part = part;
+        a.count = counts;
+        a.out = att;
+        a.err = err;
+        a.NH = NH;
+        a.NK = NK;
+        a.max_ctx = c.max_ctx;
+        a.nchunk = nchunk;
+        a.wait_limit = lim;
+        a.quirks = c.quirks;
+        a.eps = c.norm_eps;
+        a.rope_base = c.rope_base;
+        a.scale = 1.0f / sqrtf(static_cast<float>(HD));
+        const size_t smem = attn_smem_bytes(NH / NK, (c.max_ctx + nchunk - 1) / nchunk);
+        if (!launch_pdl(attn_kernel(NH / NK), dim3(NK, nchunk), dim3(kAttnThreads), smem, s, a)) return false;
+        // this rank's share of Wo @ att to every rank
+        f = MvFuse{};
+        f.w_early = true;
+        scatter_out(f, 0);
+        if (!mv_launch(w.wo, w.o_qt, H, NH * HD, att, x2, s, err, sms, lim, &f)) return false;
+        // act = swiglu(gate, up) of this rank's rows, of rmsnorm(x2), x2 = x + the o partials
+        f = MvFuse{};
+        f.xmode = MV_X_RMSNORM;
+        f.nw = w.ffn_norm;
+        f.eps = c.norm_eps;
+        f.ymode = MV_Y_SWIGLU_PAIRS;
+        f.w_early = true;
+        gather_in(f, 0, static_cast<unsigned long long>(l + 1) * per_x, x2);
+        if (!mv_launch(w.wgu, w.gu_qt, 2 * F, H, x, gu, s, err, sms, lim, &f)) return false;
+        // this rank's share of Wd @ act to every rank
+        f = MvFuse{};
+        f.w_early = true;
+        scatter_out(f, 1);
+        if (!mv_launch(w.wd, w.d_qt, H, F, gu, x, s, err, sms, lim, &f)) return false;
+    }
+    MvFuse f;
+    f.xmode = MV_X_RMSNORM;
+    f.nw = out_norm;
+    f.eps = c.norm_eps;
+    f.w_early = true;
+    gather_in(f, 1, static_cast<unsigned long long>(L) * per_x, nullptr);
+    if (!mv_launch(lm, lm_qt, c.vocab, H, x2, logits, s, err, sms, lim, &f)) return false;
+    ArgTP tp{};
+    tp.rank = rank;
+    tp.world = world;
+    tp.base = rank * c.vocab;
+    for (int p = 0; p < world; ++p) {
+        tp.am[p] = am(p);
+        tp.ctr[p] = ctr(p, 2);
+    }
+    tp.own_am = am(rank);
+    tp.own_ctr = ctr(rank, 2);
+    tp.epoch = epoch;
+    tp.wait_limit = lim;
+    tp.err = err;
+    const int G = sms;
+    return launch_pdl(k_argmax_step, dim3(G), dim3(kArgThreads), 0, s, static_cast<const float *>(logits), c.vocab,
+                      argv, argi, counts + NK, tok, pos, tp);
 }
 
 static bool dec_ok(cudaError_t e, const char *what)
@@ -770,12 +948,29 @@ static void dec_free(Decoder *d)
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->hostio) cudaFreeHost(d->hostio);
+    for (int p = 0; p < kMaxRanks; ++p)
+        if (d->peer_opened[p]) cudaIpcCloseMemHandle(d->peer[p]);
+    if (d->xch) cudaFree(d->xch);
+    if (d->epoch) cudaFree(d->epoch);
     delete[] d->layers;
     delete d;
 }
 
-Decoder *dec_create(const DecConfig &c)
+// full: the whole model's shape; rank / world: this process's share
+// (world 1 = the whole model on one device).
+Decoder *dec_create(const DecConfig &full, int rank, int world)
 {
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || full.n_heads % world ||
+        full.n_kv_heads % world || full.ffn_dim % world || full.vocab % world) {
+        fprintf(stderr, "[tb_cuda] decoder: rank %d of %d does not divide the heads, FFN rows and vocabulary\n",
+                rank, world);
+        return nullptr;
+    }
+    DecConfig c = full;
+    c.n_heads /= world;
+    c.n_kv_heads /= world;
+    c.ffn_dim /= world;
+    c.vocab /= world;
     if (c.n_layers <= 0 || c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim != kHD ||
         c.n_heads % c.n_kv_heads || c.n_heads / c.n_kv_heads > 8 || c.ffn_dim <= 0 || c.vocab <= 0 ||
         c.max_ctx <= 0) {
@@ -784,6 +979,9 @@ Decoder *dec_create(const DecConfig &c)
     }
     Decoder *d = new Decoder;
     d->cfg = c;
+    d->rank = rank;
+    d->world = world;
+    d->vocab_full = full.vocab;
     d->layers = new DecLayer[c.n_layers];
     cudaGetDevice(&d->dev);
     cudaDeviceGetAttribute(&d->sms, cudaDevAttrMultiProcessorCount, d->dev);
@@ -822,6 +1020,20 @@ Decoder *dec_create(const DecConfig &c)
               dec_ok(cudaMalloc(&d->counts, sizeof(unsigned) * (NK + 1)), "tickets") &&
               dec_ok(cudaMalloc(&d->err, sizeof(int)), "err") &&
               dec_ok(cudaMallocHost(&d->hostio, sizeof(int) * 4), "host io");
+    if (ok && world > 1) {
+        // the exchange region, 256-byte aligned parts; CUDA IPC maps whole allocations
+        auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+        const size_t slots = up(sizeof(float) * static_cast<size_t>(world) * c.hidden);
+        d->off_xd = slots;
+        d->off_am = 2 * slots;
+        d->off_ctr = d->off_am + up(sizeof(unsigned long long) * world);
+        d->xch_bytes = d->off_ctr + up(3 * sizeof(unsigned long long));
+        ok = dec_ok(cudaMalloc(&d->xch, d->xch_bytes), "exchange region") &&
+             dec_ok(cudaMemset(d->xch, 0, d->xch_bytes), "memset") &&
+             dec_ok(cudaMalloc(&d->epoch, sizeof(int)), "epoch") &&
+             dec_ok(cudaMemset(d->epoch, 0, sizeof(int)), "memset");
+        d->peer[rank] = d->xch;
+    }
     if (ok) {
         ok = dec_ok(cudaMemset(d->counts, 0, sizeof(unsigned) * (NK + 1)), "memset") &&
              dec_ok(cudaMemset(d->err, 0, sizeof(int)), "memset") &&
@@ -868,7 +1080,11 @@ static bool dec_graph(Decoder *d)
 // time of the n replays (CUDA events on the decoder's stream).
 int dec_run(Decoder *d, int token, int pos, int n, int *tokens, float *logits_host, float *ms)
 {
-    if (!d || n <= 0 || token < 0 || token >= d->cfg.vocab || pos < 0 || pos + n > d->cfg.max_ctx) return 0;
+    if (!d || n <= 0 || token < 0 || token >= d->vocab_full || pos < 0 || pos + n > d->cfg.max_ctx) return 0;
+    if (d->world > 1 && !d->connected()) {
+        fprintf(stderr, "[tb_cuda] decoder: tensor-parallel ranks not connected (tb_cuda_dec_tp_connect)\n");
+        return 0;
+    }
     if (!dec_graph(d)) return 0;
     d->hostio[0] = token;
     d->hostio[1] = pos;
@@ -912,7 +1128,46 @@ void *tb_cuda_dec_create(const tb_dec_config *c)
     if (!c) return nullptr;
     tb::DecConfig k{c->n_layers, c->hidden, c->n_heads, c->n_kv_heads, c->head_dim, c->ffn_dim,
                     c->vocab, c->max_ctx, c->rope_base, c->norm_eps, c->quirks};
-    return tb::dec_create(k);
+    return tb::dec_create(k, 0, 1);
+}
+
+void *tb_cuda_dec_create_tp(const tb_dec_config *c, int rank, int world)
+{
+    if (!c) return nullptr;
+    tb::DecConfig k{c->n_layers, c->hidden, c->n_heads, c->n_kv_heads, c->head_dim, c->ffn_dim,
+                    c->vocab, c->max_ctx, c->rope_base, c->norm_eps, c->quirks};
+    return tb::dec_create(k, rank, world);
+}
+
+int tb_cuda_dec_tp_handle(void *dec, void *handle_out)
+{
+    tb::Decoder *d = static_cast<tb::Decoder *>(dec);
+    if (!d || !handle_out || d->world < 2 || !d->xch) return 0;
+    cudaIpcMemHandle_t h;
+    if (!tb::dec_ok(cudaIpcGetMemHandle(&h, d->xch), "ipc handle")) return 0;
+    memcpy(handle_out, &h, sizeof(h));
+    return 1;
+}
+
+int tb_cuda_dec_tp_connect(void *dec, const void *handles)
+{
+    tb::Decoder *d = static_cast<tb::Decoder *>(dec);
+    if (!d || !handles || d->world < 2) return 0;
+    const uint8_t *hb = static_cast<const uint8_t *>(handles);
+    for (int p = 0; p < d->world; ++p) {
+        if (p == d->rank || d->peer_opened[p]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + static_cast<size_t>(p) * sizeof(h), sizeof(h));
+        void *ptr = nullptr;
+        if (!tb::dec_ok(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess), "ipc open")) return 0;
+        d->peer[p] = static_cast<uint8_t *>(ptr);
+        d->peer_opened[p] = true;
+    }
+    if (d->gexec) {   // peers changed: capture again on the next step
+        cudaGraphExecDestroy(d->gexec);
+        d->gexec = nullptr;
+    }
+    return 1;
 }
 
 int tb_cuda_dec_set_layer(void *dec, int layer, const tb_dec_layer *w)

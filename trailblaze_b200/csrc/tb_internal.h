@@ -10,6 +10,8 @@ namespace tb {
 enum MvXMode : uint32_t { MV_X_PLAIN = 0, MV_X_RMSNORM = 1, MV_X_SWIGLU = 2 };
 // MV_Y_SWIGLU_PAIRS: rows come in (gate, up) pairs; y[i] = silu(row 2i) * row 2i+1 (M/2 outputs)
 enum MvYMode : uint32_t { MV_Y_PLAIN = 0, MV_Y_SWIGLU_PAIRS = 1 };
+static constexpr int kMaxRanks = 8;   // tensor-parallel ranks at most
+
 struct MvFuse {
     uint32_t xmode = MV_X_PLAIN;
     uint32_t ymode = MV_Y_PLAIN;
@@ -19,6 +21,19 @@ struct MvFuse {
     const float *res = nullptr;   // added to y when not null
     bool w_early = false;         // W is constant over the launch chain: stream it before the
                                   // programmatic-dependency wait
+    // Tensor-parallel exchange over peer memory (unused when nsl / ny are 0).
+    // Input: x <- x + the nsl rows of xs ([nsl][K], summed in row order) once
+    // *xs_ctr >= (*xs_epoch) * xs_mul + xs_add; CTA 0 also writes that x to
+    // xout when not null.  Output: y[row] goes to ys[p][row] for the ny ranks
+    // p instead of y, then every CTA adds 1 to each yctr[p] (system scope).
+    const float *xs = nullptr;
+    const unsigned long long *xs_ctr = nullptr;
+    const int *xs_epoch = nullptr;
+    unsigned long long xs_mul = 0, xs_add = 0;
+    float *xout = nullptr;
+    uint32_t nsl = 0, ny = 0;
+    float *ys[kMaxRanks] = {};
+    unsigned long long *yctr[kMaxRanks] = {};
 };
 
 // Launch the matvec d_y[M] = dequant(W) @ d_x[K] on `st`.  Returns 1 when the

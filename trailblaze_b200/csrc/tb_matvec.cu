@@ -59,6 +59,15 @@ struct MvArgs {
     const float *x2, *nw, *res;
     float eps;
     uint32_t w_early;   // W is not written by the previous kernel: prefetch before griddepcontrol.wait
+    // tensor-parallel exchange (MvFuse)
+    const float *xs;
+    const unsigned long long *xs_ctr;
+    const int *xs_epoch;
+    unsigned long long xs_mul, xs_add;
+    float *xout;
+    uint32_t nsl, ny;
+    float *ys[kMaxRanks];
+    unsigned long long *yctr[kMaxRanks];
 };
 
 static constexpr uint32_t kFull = 0xFFFFFFFFu;
@@ -104,6 +113,26 @@ __device__ __forceinline__ void load32(const float *p, uint32_t k0, uint32_t K, 
     }
 }
 
+// load32 through L2 (ld.global.cg): the slots are written by peers over NVLink
+// during the launch chain, so no non-coherent cached copy may be used.
+__device__ __forceinline__ void load32_cg(const float *p, uint32_t k0, uint32_t K, float (&v)[32])
+{
+    if (k0 + 32 <= K && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        const float4 *q = reinterpret_cast<const float4 *>(p + k0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 t = __ldcg(q + i);
+            v[4 * i] = t.x;
+            v[4 * i + 1] = t.y;
+            v[4 * i + 2] = t.z;
+            v[4 * i + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = k0 + i < K ? __ldcg(p + k0 + i) : 0.f;
+    }
+}
+
 // The 32 activations of group g (zeros past K) after the fused input
 // transform, and ss += the sum of the squares of the raw x.
 //   RMSNorm: x * nw; the scalar 1/rms of layer1/tb_tensor.c:194-199 is applied
@@ -113,6 +142,18 @@ __device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t g, float 
 {
     const uint32_t k0 = 32 * g;
     load32(a.x, k0, a.K, v);
+    if (a.nsl) {   // tensor-parallel input: the residual plus the ranks' partials
+        for (uint32_t r = 0; r < a.nsl; ++r) {
+            float t[32];
+            load32_cg(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += t[i];
+        }
+        if (a.xout && blockIdx.x == 0)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (k0 + i < a.K) a.xout[k0 + i] = v[i];
+    }
     if (a.xmode == MV_X_RMSNORM) {
         float w[32];
         load32(a.nw, k0, a.K, w);
@@ -201,6 +242,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     if (a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (!a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
+    if (a.nsl) {   // the ranks' partials of x have all arrived
+        if (tid == 0) {
+            const unsigned long long target = static_cast<unsigned long long>(*a.xs_epoch) * a.xs_mul + a.xs_add;
+            if (!wait_counter(a.xs_ctr, target, a.wait_limit)) atomicExch(a.err, ERR_WAIT_TIMEOUT);
+        }
+        __syncthreads();
+    }
 
     // ---- prologue: x -> one record per column slot ----
     // Thread g handles group g (then g + nthr, ...).  The GPL groups of a slot
@@ -280,7 +328,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
                     const float *pr = pb + r * a.npart;
                     float acc = 0.f;
                     for (uint32_t j = 0; j < a.npart; ++j) acc += pr[j];
-                    a.y[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
+                    if (a.ny) {   // tensor-parallel output: this rank's partial to every rank
+                        for (uint32_t p = 0; p < a.ny; ++p) a.ys[p][t0 + r] = acc;
+                    } else {
+                        a.y[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
+                    }
                 }
             }
             __syncwarp();
@@ -301,6 +353,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             } else {
                 pb += pstride;
             }
+        }
+        if (a.ny && !fail) {
+            // the partials are visible system-wide before each rank counts this CTA
+            // (a failed CTA never counts, so the ranks' own waits run out)
+            __threadfence_system();
+            __syncwarp();
+            if (lane < a.ny) atomicAdd_system(a.yctr[lane], 1ull);
         }
         if (fail && lane == 0) {
             // A wait ran out: let every copy still in flight land before the CTA
@@ -537,6 +596,24 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
         a.eps = fuse->eps;
         a.res = fuse->res;
         a.w_early = fuse->w_early ? 1u : 0u;
+        if (fuse->nsl > static_cast<uint32_t>(kMaxRanks) || fuse->ny > static_cast<uint32_t>(kMaxRanks) ||
+            (fuse->nsl && (!fuse->xs || !fuse->xs_ctr || !fuse->xs_epoch || fuse->xmode == MV_X_SWIGLU)) ||
+            (fuse->ny && (fuse->res || fuse->ymode != MV_Y_PLAIN)))
+            return 0;
+        for (uint32_t p = 0; p < fuse->ny; ++p)
+            if (!fuse->ys[p] || !fuse->yctr[p]) return 0;
+        a.xs = fuse->xs;
+        a.xs_ctr = fuse->xs_ctr;
+        a.xs_epoch = fuse->xs_epoch;
+        a.xs_mul = fuse->xs_mul;
+        a.xs_add = fuse->xs_add;
+        a.xout = fuse->xout;
+        a.nsl = fuse->nsl;
+        a.ny = fuse->ny;
+        for (int p = 0; p < kMaxRanks; ++p) {
+            a.ys[p] = fuse->ys[p];
+            a.yctr[p] = fuse->yctr[p];
+        }
     }
     a.W = static_cast<const uint8_t *>(W);
     a.x = d_x;
