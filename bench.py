@@ -193,33 +193,49 @@ def cpu_sample(items, budget_s: float, nthreads: int, repeat: int = 1):
     return tot_b / tot_t / 1e9, info
 
 
-def decode_bench(ctx: int, n: int, e2e_tokens: int = 16):
+def decode_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: int = 1, dist=None):
     """batch-1 greedy decode of a random-init Qwen3-8B-shape model
     (Q4_K weights, Q6_K ffn_down and output) with an N(0,1) fp32 KV prefix of ctx
-    positions, through the library's graph-replayed decoder (tb_cuda_dec_*)."""
+    positions, through the library's graph-replayed decoder (tb_cuda_dec_*).  With
+    world > 1 each rank holds its tensor-parallel share (heads, FFN rows, vocabulary
+    split; the o / down partials and the greedy pairs cross NVLink by the library's
+    own peer stores); times are the slowest rank's."""
     from trailblaze_b200.decoder import QWEN3_8B, synthetic_model
     shape = QWEN3_8B
     t0 = time.perf_counter()
-    dec = synthetic_model(shape, max_ctx=ctx + n + e2e_tokens + 8, ctx=ctx)
+    dec = synthetic_model(shape, max_ctx=ctx + n + e2e_tokens + 8, ctx=ctx, rank=rank, world=world)
     log(f"[bench] decode model built in {time.perf_counter() - t0:.1f}s")
     try:
+        if world > 1:
+            hs = [None] * world
+            dist.all_gather_object(hs, dec.tp_handle())
+            dec.tp_connect(hs)
+            dist.barrier()
         dec.generate(1, ctx, 4, want_tokens=False)          # captures the graph, warms up
+        if world > 1:
+            dist.barrier()
         _, ms = dec.generate(1, ctx, n, want_tokens=False)  # n steps back to back, device time
+        ms = shard.max_over_ranks(ms, dist if world > 1 else None, device="cuda")
         tok_s = n / (ms * 1e-3)
         bpt = shape.bytes_per_token(ctx + n // 2)
         tok = 1
+        if world > 1:
+            dist.barrier()
         t1 = time.perf_counter()
         for i in range(e2e_tokens):   # blocking step with the token read back each time
             tok = dec.step(tok, ctx + i)
-        e2e = e2e_tokens / (time.perf_counter() - t1)
+        e2e = e2e_tokens / shard.max_over_ranks(time.perf_counter() - t1, dist if world > 1 else None, device="cuda")
     finally:
+        if world > 1:
+            dist.barrier()   # no rank unmaps its region while a peer may still store into it
         dec.close()
     hbm, kind = peaks()
     return {"model": "qwen3-8b shape: 36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, ffn 12288, "
                      "vocab 151936; Q4_K weights, Q6_K ffn_down and output; fp32 KV",
             "ctx": ctx, "tokens": n, "tok_per_s": round(tok_s, 2), "ms_per_token": round(ms / n, 4),
+            "parallelism": f"tensor-parallel x{world}" if world > 1 else "one GPU",
             "bytes_per_token": bpt, "GBps": round(bpt * tok_s / 1e9, 1),
-            "frac_of_hbm": round(bpt * tok_s / 1e9 / hbm, 4), "hbm_peak_kind": kind,
+            "frac_of_hbm": round(bpt * tok_s / 1e9 / (hbm * world), 4), "hbm_peak_kind": kind,
             "e2e_tok_per_s": round(e2e, 2), "e2e_api": "tb_cuda_dec_step (blocking, token read back)",
             "launches_per_token": 1 + 5 * shape.n_layers + 2,
             "order": "reference (RoPE before QK-norm, K rotated n_heads/n_kv_heads times)"}
@@ -295,7 +311,10 @@ def main():
 
     if args.decode_only:
         with Clocks(local) as clk:
-            d = decode_bench(args.decode_ctx, args.decode_tokens)
+            d = decode_bench(args.decode_ctx, args.decode_tokens, rank=rank, world=world,
+                             dist=dist if world > 1 else None)
+        if world > 1:
+            dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"metric": "Qwen3-8B-shape Q4_K decode tok/s", "value": d["tok_per_s"],
                               "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
@@ -450,9 +469,10 @@ def main():
 
     clocks = clk.summary()
     decode = None
-    if world == 1 and not args.no_decode and not args.shape:
+    if not args.no_decode and not args.shape:
         try:
-            decode = decode_bench(args.decode_ctx, args.decode_tokens)
+            decode = decode_bench(args.decode_ctx, args.decode_tokens, rank=rank, world=world,
+                                  dist=dist if world > 1 else None)
         except Exception as e:  # noqa: BLE001 - the decode leg must not sink the sweep line
             decode = {"unavailable": f"{type(e).__name__}: {e}"}
     if world > 1:

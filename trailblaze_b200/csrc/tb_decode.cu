@@ -643,7 +643,7 @@ __global__ void __launch_bounds__(kArgThreads) k_argmax_step(const float *logits
         __syncwarp();
         if (lane < tp.world) atomicAdd_system(tp.ctr[lane], 1ull);
         bool ok = true;
-        if (lane == 0)
+        if (lane == 0 && *reinterpret_cast<volatile int *>(tp.err) == 0)
             ok = wait_counter(tp.own_ctr, static_cast<unsigned long long>(*tp.epoch + 1) * tp.world, tp.wait_limit);
         ok = __shfl_sync(0xFFFFFFFFu, ok ? 1 : 0, 0) != 0;
         if (!ok && lane == 0) atomicExch(tp.err, ERR_WAIT_TIMEOUT);

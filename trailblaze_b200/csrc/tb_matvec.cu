@@ -244,8 +244,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     if (!a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     if (a.nsl) {   // the ranks' partials of x have all arrived
         if (tid == 0) {
+            // after a wait of this device ran out the chain only finishes (fast,
+            // with the error word set) instead of waiting again at every exchange
             const unsigned long long target = static_cast<unsigned long long>(*a.xs_epoch) * a.xs_mul + a.xs_add;
-            if (!wait_counter(a.xs_ctr, target, a.wait_limit)) atomicExch(a.err, ERR_WAIT_TIMEOUT);
+            if (*reinterpret_cast<volatile int *>(a.err) == 0 && !wait_counter(a.xs_ctr, target, a.wait_limit))
+                atomicExch(a.err, ERR_WAIT_TIMEOUT);
         }
         __syncthreads();
     }

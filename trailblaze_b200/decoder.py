@@ -49,16 +49,34 @@ QWEN3_8B = ModelShape(36, 4096, 32, 8, 128, 12288, 151936)
 
 
 class Decoder:
-    def __init__(self, shape: ModelShape, max_ctx: int, quirks: bool = True):
+    """rank / world > 1: this process's tensor-parallel share of the model
+    (tb_cuda_dec_create_tp; weight shard shapes in include/tb_gguf_dequant.h)."""
+
+    def __init__(self, shape: ModelShape, max_ctx: int, quirks: bool = True, rank: int = 0, world: int = 1):
         self.L = lib()
-        self.shape, self.max_ctx = shape, max_ctx
+        self.shape, self.max_ctx, self.rank, self.world = shape, max_ctx, rank, world
         s = shape
         self.cfg = DecConfig(s.n_layers, s.hidden, s.n_heads, s.n_kv_heads, s.head_dim, s.ffn_dim, s.vocab,
                              max_ctx, s.rope_base, s.norm_eps, 1 if quirks else 0)
-        self.d = self.L.tb_cuda_dec_create(ctypes.byref(self.cfg))
+        if world > 1:
+            self.d = self.L.tb_cuda_dec_create_tp(ctypes.byref(self.cfg), rank, world)
+        else:
+            self.d = self.L.tb_cuda_dec_create(ctypes.byref(self.cfg))
         if not self.d:
             raise RuntimeError("tb_cuda_dec_create failed")
         self._keep = []
+
+    def tp_handle(self) -> bytes:
+        h = (ctypes.c_ubyte * 64)()
+        if self.L.tb_cuda_dec_tp_handle(self.d, h) != 1:
+            raise RuntimeError("tb_cuda_dec_tp_handle failed")
+        return bytes(h)
+
+    def tp_connect(self, handles: list[bytes]) -> None:
+        """handles: every rank's tp_handle(), in rank order."""
+        buf = (ctypes.c_ubyte * (64 * len(handles))).from_buffer_copy(b"".join(handles))
+        if self.L.tb_cuda_dec_tp_connect(self.d, buf) != 1:
+            raise RuntimeError("tb_cuda_dec_tp_connect failed")
 
     def set_layer(self, li: int, wqkv, qkv_qt, wo, o_qt, wgu, gu_qt, wd, d_qt, attn_norm, ffn_norm,
                   q_norm=None, k_norm=None):
@@ -120,17 +138,21 @@ def device_weights(qt: int, M: int, K: int, gen):
 
 
 def synthetic_model(shape: ModelShape, max_ctx: int, ctx: int, seed: int = 20261201, quirks: bool = True,
-                    log=None) -> Decoder:
-    """A Decoder loaded with random-init weights of `shape` and an N(0,1) KV prefix of ctx positions."""
+                    log=None, rank: int = 0, world: int = 1) -> Decoder:
+    """A Decoder loaded with random-init weights of `shape` and an N(0,1) KV prefix of ctx positions;
+    with world > 1 the shard shapes of rank `rank` (drawn from that rank's own seed stream)."""
     import torch
     s = shape
-    gen = torch.Generator(device="cuda")
-    gen.manual_seed(seed)
-    dec = Decoder(s, max_ctx, quirks)
-    H, NH, NK, HD, F = s.hidden, s.n_heads, s.n_kv_heads, s.head_dim, s.ffn_dim
+    gen = torch.Generator(device="cuda")        # this rank's shards
+    gen.manual_seed(seed + 7919 * rank)
+    shared = torch.Generator(device="cuda")     # tensors every rank holds whole (same on every rank)
+    shared.manual_seed(seed)
+    dec = Decoder(s, max_ctx, quirks, rank, world)
+    H, HD = s.hidden, s.head_dim
+    NH, NK, F = s.n_heads // world, s.n_kv_heads // world, s.ffn_dim // world
 
     def norm(n):
-        return 1.0 + 0.1 * torch.randn(n, device="cuda", generator=gen)
+        return 1.0 + 0.1 * torch.randn(n, device="cuda", generator=shared)
 
     for li in range(s.n_layers):
         dec.set_layer(li,
@@ -142,7 +164,7 @@ def synthetic_model(shape: ModelShape, max_ctx: int, ctx: int, seed: int = 20261
         if ctx > 0:
             for which in (0, 1):
                 dec.load_kv(li, which, torch.randn(NK, ctx, HD, device="cuda", generator=gen))
-    dec.set_head(device_weights(s.w_qt, s.vocab, H, gen), s.w_qt, norm(H),
-                 device_weights(s.out_qt, s.vocab, H, gen), s.out_qt)
+    dec.set_head(device_weights(s.w_qt, s.vocab, H, shared), s.w_qt, norm(H),
+                 device_weights(s.out_qt, s.vocab // world, H, gen), s.out_qt)
     torch.cuda.synchronize()
     return dec
