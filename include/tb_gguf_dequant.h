@@ -142,6 +142,17 @@ const char *tb_cuda_version(void);
 int   tb_cuda_matvec_device_noalloc(const void *W_device, int qtype, int M, int K,
                                     const float *x_host, float *out_host);
 
+/* Prefill GEMM on the tensor cores (tcgen05, bf16 x bf16 -> fp32):
+ * C_dev[T][N] = A_bf16_dev[T][K] x dequant(W_dev)[N][K]^T, row t of C being
+ * the matvec of W with token t (the batched form of the reference's
+ * token-by-token prefill, layer4/tb_infer.c:1071-1074).  The weights are
+ * dequantised exactly (as tb_cuda_dequant_dev) and rounded to bf16 on the way
+ * into shared memory.  qtype Q4_K or Q6_K; N a multiple of 128, K of 256;
+ * T a multiple of 16 in [16, 512]; A 16-byte aligned (and W for Q4_K).
+ * Stream-ordered, no host synchronisation.  1 = launched, 0 = unsupported. */
+int tb_cuda_qgemm_dev(const void *W_dev, int qtype, int N, int K, const void *A_bf16_dev, int T, float *C_dev,
+                      void *stream);
+
 /* ───────────── Part 3: the decode step (no reference counterpart) ────────────
  *
  * The GPU form of layer4/tb_infer.c:889-1050 tb_infer_decode for a dense

@@ -326,6 +326,25 @@ int tb_cuda_matvec_dev(const void *W_dev, int qtype, int M, int K, const float *
     return r;
 }
 
+int tb_cuda_qgemm_dev(const void *W_dev, int qtype, int N, int K, const void *A_bf16_dev, int T, float *C_dev,
+                      void *stream)
+{
+    int nsm;
+    int *derr;
+    uint32_t lim;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!ensure_init_locked(false)) return 0;
+        nsm = g.num_sms;
+        derr = g.d_err;
+        lim = g.wait_limit;
+    }
+    const int r = tb::qg_launch(W_dev, qtype, N, K, A_bf16_dev, T, C_dev, static_cast<cudaStream_t>(stream), derr,
+                                nsm, lim);
+    if (r) g_launches.fetch_add(1, std::memory_order_relaxed);
+    return r;
+}
+
 int tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K, const float *d_x, float *d_y,
                              int xmode, const float *d_x2, const float *d_norm_w, float eps,
                              const float *d_res, int ymode, void *stream)

@@ -42,6 +42,11 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
               cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit,
               const MvFuse *fuse = nullptr);
 
+// Launch the prefill GEMM C[T][N] = A[T][K] (bf16) x dequant(W)[N][K]^T on the
+// tensor cores (tb_qgemm.cu).  Returns 1 when launched, 0 for unsupported shapes.
+int qg_launch(const void *W, int qtype, int N, int K, const void *A, int T, float *C, cudaStream_t st, int *d_err,
+              int num_sms, uint32_t wait_limit);
+
 // Launch the bit-exact dequantisation of M rows of K weights into d_out.
 int dq_launch(const void *W, int qtype, int M, int K, float *d_out, int sem, cudaStream_t st);
 

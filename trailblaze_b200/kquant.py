@@ -76,6 +76,12 @@ class KQuantLib:
         return self.L.tb_cuda_matvec_dev(ctypes.c_void_p(W_dev), qtype, M, K, ctypes.c_void_p(d_x),
                                          ctypes.c_void_p(d_y), ctypes.c_void_p(stream or None))
 
+    def tb_cuda_qgemm_dev(self, W_dev: int, qtype: int, N: int, K: int, d_a_bf16: int, T: int, d_c: int,
+                          stream: int = 0) -> int:
+        """Prefill GEMM C[T][N] = A[T][K] (bf16) x dequant(W)^T on the tensor cores."""
+        return self.L.tb_cuda_qgemm_dev(ctypes.c_void_p(W_dev), qtype, N, K, ctypes.c_void_p(d_a_bf16), T,
+                                        ctypes.c_void_p(d_c), ctypes.c_void_p(stream or None))
+
     def tb_cuda_matvec_fused_dev(self, W_dev: int, qtype: int, M: int, K: int, d_x: int, d_y: int,
                                  xmode: int = 0, d_x2: int = 0, d_norm_w: int = 0, eps: float = 0.0,
                                  d_res: int = 0, ymode: int = 0, stream: int = 0) -> int:
