@@ -148,7 +148,8 @@ int   tb_cuda_matvec_device_noalloc(const void *W_device, int qtype, int M, int 
  * token-by-token prefill, layer4/tb_infer.c:1071-1074).  The weights are
  * dequantised exactly (as tb_cuda_dequant_dev) and rounded to bf16 on the way
  * into shared memory.  qtype Q4_K or Q6_K; N a multiple of 128, K of 256;
- * T a multiple of 16 in [16, 512]; A 16-byte aligned (and W for Q4_K).
+ * T a multiple of 16 in [16, 512]; A and W 16-byte aligned and W's rows a
+ * multiple of 16 bytes (always for Q4_K; K a multiple of 2048 for Q6_K).
  * Stream-ordered, no host synchronisation.  1 = launched, 0 = unsupported. */
 int tb_cuda_qgemm_dev(const void *W_dev, int qtype, int N, int K, const void *A_bf16_dev, int T, float *C_dev,
                       void *stream);

@@ -7,7 +7,9 @@ sums fp32.  So the reference is oracle dequant -> bf16 -> fp64 products and
 sums: rel L2 <= 2e-5 (fp32 accumulation only).  Against the unrounded weights
 the bf16 rounding of W costs about 1e-3 relative; <= 4e-3 is asserted.
 Shapes: T = 16, 128 and 512 tokens (one and two MMAs per K step), several
-128-row tiles, and a single tile with split K (partial sums added into C)."""
+128-row tiles, and a single tile with split K (partial sums added into C).
+Q6_K rows must be a multiple of 16 bytes (K a multiple of 2048) for the
+weight tensor map."""
 import numpy as np
 import pytest
 
@@ -28,8 +30,11 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
 
 
-@pytest.mark.parametrize("qt", [Q.Q4_K, Q.Q6_K])
-@pytest.mark.parametrize("N,K,T", [(256, 512, 16), (384, 1024, 128), (256, 768, 512), (128, 2048, 32)])
+CASES = [(Q.Q4_K, 256, 512, 16), (Q.Q4_K, 384, 1024, 128), (Q.Q4_K, 256, 768, 512), (Q.Q4_K, 128, 2048, 32),
+         (Q.Q6_K, 256, 2048, 16), (Q.Q6_K, 384, 2048, 128), (Q.Q6_K, 256, 4096, 512), (Q.Q6_K, 128, 4096, 48)]
+
+
+@pytest.mark.parametrize("qt,N,K,T", CASES)
 def test_qgemm_matches_oracle(kq, qt, N, K, T):
     import torch
     from oracle.oracle import Oracle
@@ -59,3 +64,5 @@ def test_qgemm_rejects_unsupported(kq):
     assert kq.tb_cuda_qgemm_dev(W.data_ptr(), Q.Q8_0, 128, 512, A.data_ptr(), 16, C.data_ptr()) == 0   # type
     assert kq.tb_cuda_qgemm_dev(W.data_ptr(), Q.Q4_K, 100, 512, A.data_ptr(), 16, C.data_ptr()) == 0   # N % 128
     assert kq.tb_cuda_qgemm_dev(W.data_ptr(), Q.Q4_K, 128, 512, A.data_ptr(), 24, C.data_ptr()) == 0   # T % 16
+    W6 = torch.zeros(Q.row_bytes(Q.Q6_K, 512) * 128, dtype=torch.uint8, device="cuda")
+    assert kq.tb_cuda_qgemm_dev(W6.data_ptr(), Q.Q6_K, 128, 512, A.data_ptr(), 16, C.data_ptr()) == 0  # 420-B rows

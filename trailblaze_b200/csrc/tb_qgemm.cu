@@ -11,15 +11,19 @@
 //
 // One CTA owns 128 rows of W (the MMA's M) and all T tokens (the MMA's N, at
 // most 256 per instruction; T = 512 takes two), accumulating in TMEM (T fp32
-// columns).  Per stage of 64 K:
-//   warp 0     one thread: the TMA load of A's [T][64] bf16 tile (128-byte
-//              swizzle) and, once both tiles are in, four tcgen05.mma of K 16
-//              (kind::f16, bf16 x bf16 -> f32), then tcgen05.commit to the
-//              stage's "empty" barrier;
+// columns per accumulator; MMAs into one accumulator wait for each other, so
+// for T <= 256 consecutive K-16 steps rotate over 2 or 4 accumulators that the
+// epilogue adds in a fixed order).  Per stage of 64 K:
+//   warp 9     one thread: the TMA load of A's [T][64] bf16 tile (128-byte
+//              swizzle), nst stages ahead;
 //   warps 1-8  dequantise W's [128][64] tile into bf16 in shared memory, in
 //              the same 128-byte-swizzled K-major layout, with the arithmetic
 //              of the bit-exact dequant (tb_dequant.cu deq1) before the bf16
-//              rounding.
+//              rounding; the raw blocks arrive by bulk copies a few
+//              super-blocks ahead;
+//   warp 0     one thread: once both tiles are in, four tcgen05.mma of K 16
+//              (kind::f16, bf16 x bf16 -> f32), then tcgen05.commit to the
+//              stage's "empty" barrier.  It never waits for an MMA to finish.
 // After the last stage warps 1-4 read the accumulators back (tcgen05.ld, one
 // TMEM lane quarter each) and store C.  With split K (few 128-row tiles) the
 // CTAs of one tile add their partial sums into C (C is zeroed first).
@@ -35,7 +39,7 @@ namespace tb {
 
 static constexpr int kGM = 128;                    // W rows per CTA (MMA M)
 static constexpr int kGK = 64;                     // K per stage (one 128-byte bf16 row)
-static constexpr int kGThreads = 288;              // warp 0 + 8 dequant warps
+static constexpr int kGThreads = 352;              // warp 0 (MMA), 8 dequant warps, warp 9 (A), warp 10 (W)
 static constexpr int kGDeqThreads = 256;
 static constexpr uint32_t kGTileW = kGM * kGK * 2; // 16 KB of bf16 W per stage
 
@@ -43,7 +47,8 @@ struct QgArgs {
     const uint8_t *W;
     float *C;
     int *err;
-    uint32_t N, K, T, ksplit, k_per_split, row_bytes, nst, tcols;
+    uint32_t N, K, T, ksplit, k_per_split, row_bytes, nst, nraw, tcols, bw;
+    uint32_t nacc;   // independent accumulators (consecutive K-16 steps rotate over them)
     uint32_t wait_limit;
 };
 
@@ -111,6 +116,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+// One lane of a converged warp (elect.sync): the tensor-core and TMA issue
+// below runs with the whole warp in step and one lane elected per instruction.
+__device__ __forceinline__ bool elect_one()
+{
+    uint32_t p = 0;
+    asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.u32 %0, 1, 0, P;\n\t}" : "=r"(p));
+    return p != 0;
+}
+
 // Shared-memory matrix descriptor of a K-major bf16 tile with the 128-byte
 // swizzle: rows of 128 bytes, 8-row atoms of 1 KB one after another (stride
 // byte offset 1024), version 1 (sm_100), layout type 2 (128-byte swizzle).
@@ -143,7 +157,8 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t chunk)
 
 // ---- the 32 weights of group g (0..7) of one super-block, fp32, with the
 // operations of tb_dequant.cu deq1 (so bit-identical before the bf16 rounding)
-__device__ __forceinline__ uint32_t ld8(const uint8_t *p, int i) { return __ldg(p + i); }
+// (the block bytes sit in shared memory, staged by bulk copies)
+__device__ __forceinline__ uint32_t ld8(const uint8_t *p, int i) { return p[i]; }
 __device__ __forceinline__ uint32_t ld16(const uint8_t *p, int i) { return ld8(p, i) | (ld8(p, i + 1) << 8); }
 
 // Q4_K (tb_gguf_dequant.cu:98-116): w = d*s[g]*q - dmin*m[g]; byte 16 + 16 g + t
@@ -162,7 +177,7 @@ __device__ __forceinline__ void group_q4k(const uint8_t *b, int g, float (&w)[32
     }
     const float S = __fmul_rn(d, static_cast<float>(s));
     const float Mn = __fmul_rn(dmin, static_cast<float>(m));
-    const uint4 q4 = __ldg(reinterpret_cast<const uint4 *>(b + 16 + 16 * g));   // 16-byte aligned
+    const uint4 q4 = *reinterpret_cast<const uint4 *>(b + 16 + 16 * g);   // 16-byte aligned
     const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
     for (int t = 0; t < 16; ++t) {
@@ -193,29 +208,44 @@ __device__ __forceinline__ void group_q6k(const uint8_t *b, int g, float (&w)[32
     }
 }
 
-// Shared memory: [nst][W tile 16 KB | A tile T*128 B] (1 KB aligned), then the
-// barriers fullA[nst], fullW[nst], empty[nst], done, and the TMEM base slot.
+// Raw weight bytes are staged one super-block (256 K) of the CTA's 128 rows at
+// a time, by one 2-D TMA load of W viewed as [N rows][row_bytes / 2] uint16: a
+// box of 128 rows x kGEnv / 2 elements starting at the block rounded down to 16
+// bytes (a Q6_K block of 210 bytes then sits 0-14 bytes into its 224-byte box
+// row; past the row's end TMA fills zeros).
+static constexpr uint32_t kGEnv = 224;
+static constexpr uint32_t kGRawStage = kGM * kGEnv;
+
+// Shared memory: [nst][W tile 16 KB | A tile T*128 B] (1 KB aligned), the raw
+// ring [nraw][128][kGEnv], then the barriers fullA[nst], fullW[nst],
+// empty[nst], rawfull[nraw], rawempty[nraw], done, and the TMEM base slot.
 __host__ __device__ inline size_t qg_stage_bytes(uint32_t T)
 {
     return static_cast<size_t>(kGTileW) + static_cast<size_t>(T) * 128u;
 }
-__host__ __device__ inline size_t qg_smem_bytes(uint32_t T, uint32_t nst)
+__host__ __device__ inline size_t qg_smem_bytes(uint32_t T, uint32_t nst, uint32_t nraw)
 {
-    return 1024 + static_cast<size_t>(nst) * qg_stage_bytes(T) + 8 * (3 * nst + 1) + 16;
+    return 1024 + static_cast<size_t>(nst) * qg_stage_bytes(T) + static_cast<size_t>(nraw) * kGRawStage +
+           8 * (3 * nst + 2 * nraw + 1) + 16;
 }
 
 template <int QT>
-__global__ void __launch_bounds__(kGThreads, 1) k_qgemm(const __grid_constant__ CUtensorMap amap, const QgArgs a)
+__global__ void __launch_bounds__(kGThreads, 2) k_qgemm(const __grid_constant__ CUtensorMap amap,
+                                                        const __grid_constant__ CUtensorMap wmap, const QgArgs a)
 {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t nst = a.nst, T = a.T;
     const size_t sb = qg_stage_bytes(T);
-    uint64_t *fullA = reinterpret_cast<uint64_t *>(sm + nst * sb);
+    uint8_t *raw = sm + nst * sb;
+    const uint32_t nraw = a.nraw;
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + nraw * kGRawStage);
     uint64_t *fullW = fullA + nst;
     uint64_t *empty = fullW + nst;
-    uint64_t *done = empty + nst;
+    uint64_t *rawfull = empty + nst;
+    uint64_t *rawempty = rawfull + nraw;
+    uint64_t *done = rawempty + nraw;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(done + 1);
     __shared__ int s_fail;
 
@@ -231,6 +261,10 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm(const __grid_constant__ 
             mbar_init(smem_u32(fullW + s), kGDeqThreads / 32);
             mbar_init(smem_u32(empty + s), 1);
         }
+        for (uint32_t s = 0; s < nraw; ++s) {
+            mbar_init(smem_u32(rawfull + s), 1);
+            mbar_init(smem_u32(rawempty + s), kGDeqThreads / 32);
+        }
         mbar_init(smem_u32(done), 1);
         fence_mbar_init();
         s_fail = 0;
@@ -244,75 +278,106 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm(const __grid_constant__ 
     tc_fence_after();
     const uint32_t tbase = *tslot;
 
-    if (warp == 0) {
-        if (lane == 0) {
-            // ---- A loads and the MMAs, one thread ----
-            const uint32_t nA = T > 256 ? 256 : T;              // tokens per MMA (and per TMA box)
-            const uint32_t idesc = umma_idesc(nA);
-            uint32_t issued = 0, mma_done = 0;
-            auto load_a = [&](uint32_t it) {
-                const uint32_t s = it % nst;
+    const uint32_t nsb = a.k_per_split / 256, kb0 = k_lo / 256;   // super-blocks of this CTA
+    if (warp == 10) {
+        // ---- W's raw super-blocks by TMA, nraw ahead; a slot is refilled once
+        // the dequant warps are done with it (whole warp, one lane issues) ----
+        for (uint32_t j = 0; j < nsb; ++j) {
+            const uint32_t slot = j % nraw;
+            bool ok = j < nraw ||
+                      mbar_wait_bounded(smem_u32(rawempty + slot), ((j / nraw) - 1u) & 1u, a.err, a.wait_limit);
+            ok = __all_sync(0xFFFFFFFFu, ok) && !*reinterpret_cast<volatile int *>(&s_fail);
+            if (!ok) {
+                if (lane == 0) atomicExch(&s_fail, 1);
+                break;
+            }
+            if (elect_one()) {
+                const uint32_t x = ((kb0 + j) * geo.block_bytes / 2u) & ~7u;   // 16-byte aligned start
+                mbar_expect_tx(smem_u32(rawfull + slot), kGM * a.bw * 2u);
+                tma_load_2d(smem_u32(raw + slot * kGRawStage), &wmap, static_cast<int>(x), static_cast<int>(n0),
+                            smem_u32(rawfull + slot));
+            }
+            __syncwarp();
+        }
+    } else if (warp == 9) {
+        // ---- A tiles by TMA, nst ahead; a stage is refilled once its MMAs are done ----
+        const uint32_t nA = T > 256 ? 256 : T;
+        for (uint32_t it = 0; it < nk; ++it) {
+            const uint32_t s = it % nst;
+            bool ok = it < nst ||
+                      mbar_wait_bounded(smem_u32(empty + s), ((it / nst) - 1u) & 1u, a.err, a.wait_limit);
+            ok = __all_sync(0xFFFFFFFFu, ok) && !*reinterpret_cast<volatile int *>(&s_fail);
+            if (!ok) {
+                if (lane == 0) atomicExch(&s_fail, 1);
+                break;
+            }
+            if (elect_one()) {
                 uint8_t *st = sm + s * sb;
                 mbar_expect_tx(smem_u32(fullA + s), T * 128u);
                 for (uint32_t t0 = 0; t0 < T; t0 += nA)
                     tma_load_2d(smem_u32(st + kGTileW + t0 * 128u), &amap, static_cast<int>(k_lo + it * kGK),
                                 static_cast<int>(t0), smem_u32(fullA + s));
-            };
-            for (; issued < nst && issued < nk; ++issued) load_a(issued);
-            bool fail = false;
-            for (uint32_t it = 0; it < nk; ++it) {
-                const uint32_t s = it % nst, par = (it / nst) & 1u;
-                if (!mbar_wait_bounded(smem_u32(fullA + s), par, a.err, a.wait_limit) ||
-                    !mbar_wait_bounded(smem_u32(fullW + s), par, a.err, a.wait_limit)) {
-                    fail = true;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t wbase = smem_u32(sm + s * sb), abase = wbase + kGTileW;
-#pragma unroll
-                for (uint32_t j = 0; j < kGK / 16; ++j)
-                    for (uint32_t t0 = 0; t0 < T; t0 += nA)
-                        umma_f16(tbase + t0, sw128_desc(wbase + 32u * j), sw128_desc(abase + t0 * 128u + 32u * j),
-                                 idesc, (it | j) != 0 ? 1u : 0u);
-                umma_commit(smem_u32(empty + s));   // the stage is free once these MMAs are done
-                mma_done = it + 1;
-                // refill the previous iteration's stage (its MMAs were committed one
-                // iteration ago; this iteration's are queued behind them meanwhile)
-                if (it >= 1 && issued < nk) {
-                    const uint32_t sp = (it - 1) % nst, pp = ((it - 1) / nst) & 1u;
-                    if (!mbar_wait_bounded(smem_u32(empty + sp), pp, a.err, a.wait_limit)) {
-                        fail = true;
-                        break;
-                    }
-                    load_a(issued);   // issued == it - 1 + nst, stage sp
-                    ++issued;
-                }
             }
-            if (fail) atomicExch(&s_fail, 1);
-            // every MMA issued so far (possibly none) completes before the epilogue reads TMEM
-            umma_commit(smem_u32(done));
-            (void)mma_done;
+            __syncwarp();
         }
+    } else if (warp == 0) {
+        // ---- the MMAs: the whole warp waits, one elected lane issues four K-16
+        // steps per stage and the commit ----
+        const uint32_t nA = T > 256 ? 256 : T;              // tokens per MMA
+        const uint32_t idesc = umma_idesc(nA);
+        bool fail = false;
+        for (uint32_t it = 0; it < nk; ++it) {
+            const uint32_t s = it % nst, par = (it / nst) & 1u;
+            bool ok = mbar_wait_bounded(smem_u32(fullA + s), par, a.err, a.wait_limit) &&
+                      mbar_wait_bounded(smem_u32(fullW + s), par, a.err, a.wait_limit);
+            if (!__all_sync(0xFFFFFFFFu, ok)) {
+                fail = true;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t wbase = smem_u32(sm + s * sb), abase = wbase + kGTileW;
+            if (elect_one()) {
+                // MMAs into one accumulator wait for each other; consecutive K-16
+                // steps therefore rotate over nacc accumulators (columns acc * T)
+#pragma unroll
+                for (uint32_t j = 0; j < kGK / 16; ++j) {
+                    const uint32_t step = it * (kGK / 16) + j;
+                    const uint32_t acc = step % a.nacc;
+                    for (uint32_t t0 = 0; t0 < T; t0 += nA)
+                        umma_f16(tbase + acc * T + t0, sw128_desc(wbase + 32u * j),
+                                 sw128_desc(abase + t0 * 128u + 32u * j), idesc, step >= a.nacc ? 1u : 0u);
+                }
+                umma_commit(smem_u32(empty + s));   // the stage is free once these MMAs are done
+            }
+            __syncwarp();
+        }
+        if (fail && lane == 0) atomicExch(&s_fail, 1);
+        // every MMA issued so far (possibly none) completes before the epilogue reads TMEM
+        if (elect_one()) umma_commit(smem_u32(done));
         __syncwarp();
     } else {
         // ---- W dequant, 256 threads: thread = (row r, half h): 32 weights ----
+        // Row r's super-block j sits in raw slot j % nraw; each 64-K stage
+        // decodes its groups 2 sub + h.
         const uint32_t dt = tid - 32, r = dt >> 1, h = dt & 1;
-        const uint8_t *wrow = a.W + static_cast<size_t>(n0 + r) * a.row_bytes;
+        bool failed = false;
         for (uint32_t it = 0; it < nk; ++it) {
             const uint32_t s = it % nst, par = (it / nst) & 1u;
-            if (it >= nst) {   // the MMAs that read this stage's previous tile are done
-                if (!mbar_wait_bounded(smem_u32(empty + s), par ^ 1u, a.err, a.wait_limit)) {
-                    atomicExch(&s_fail, 1);
-                    break;
-                }
+            const uint32_t j = it >> 2, sub = it & 3u;          // super-block, 64-K part of it
+            failed = failed || *reinterpret_cast<volatile int *>(&s_fail) != 0;
+            if (!failed && it >= nst)   // the MMAs that read this stage's previous tile are done
+                failed = !mbar_wait_bounded(smem_u32(empty + s), par ^ 1u, a.err, a.wait_limit);
+            if (!failed)
+                failed = !mbar_wait_bounded(smem_u32(rawfull + j % nraw), (j / nraw) & 1u, a.err, a.wait_limit);
+            if (failed) {
+                atomicExch(&s_fail, 1);
+                break;
             }
-            if (*reinterpret_cast<volatile int *>(&s_fail)) break;
-            const uint32_t k = k_lo + it * kGK + h * 32;       // first weight of the group
-            const uint8_t *blk = wrow + static_cast<size_t>(k / geo.block_weights) * geo.block_bytes;
-            const int g = static_cast<int>((k % geo.block_weights) >> 5);
+            const uint32_t boff = (kb0 + j) * geo.block_bytes;
+            const uint8_t *blk = raw + (j % nraw) * kGRawStage + r * (a.bw * 2u) + (boff & 15u);
             float w[32];
-            if constexpr (QT == QT_Q4_K) group_q4k(blk, g, w);
-            else group_q6k(blk, g, w);
+            if constexpr (QT == QT_Q4_K) group_q4k(blk, static_cast<int>(2 * sub + h), w);
+            else group_q6k(blk, static_cast<int>(2 * sub + h), w);
             uint8_t *wt = sm + s * sb;
 #pragma unroll
             for (uint32_t c = 0; c < 4; ++c) {   // 16-byte chunks h*4 + c of row r
@@ -323,7 +388,10 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm(const __grid_constant__ 
             }
             fence_proxy_async_smem();   // generic stores -> visible to the tensor core's async proxy
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(fullW + s));
+            if (lane == 0) {
+                mbar_arrive(smem_u32(fullW + s));
+                if (sub == 3) mbar_arrive(smem_u32(rawempty + j % nraw));   // done with super-block j
+            }
         }
     }
 
@@ -334,9 +402,16 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm(const __grid_constant__ 
         const uint32_t q = warp & 3u;                 // TMEM lanes 32q .. 32q + 31 (warp id mod 4)
         const uint32_t n = n0 + 32 * q + lane;
         if (ok && !*reinterpret_cast<volatile int *>(&s_fail)) {
+            const uint32_t used = nk * (kGK / 16) < a.nacc ? nk * (kGK / 16) : a.nacc;   // accumulators written
             for (uint32_t c0 = 0; c0 < T; c0 += 16) {
                 float v[16];
                 tmem_ld16(tbase + ((32u * q) << 16) + c0, v);
+                for (uint32_t u = 1; u < used; ++u) {   // fixed order: accumulator 0 + 1 + ...
+                    float t[16];
+                    tmem_ld16(tbase + ((32u * q) << 16) + u * T + c0, t);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] += t[i];
+                }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     float *dst = a.C + static_cast<size_t>(c0 + i) * a.N + n;
@@ -384,8 +459,9 @@ int qg_launch(const void *W, int qtype, int N, int K, const void *A, int T, floa
     if (qtype != QT_Q4_K && qtype != QT_Q6_K) return 0;
     if (!W || !A || !C || N <= 0 || K <= 0 || N % kGM || K % 256 || T < 16 || T > 512 || T % 16) return 0;
     const uintptr_t wa = reinterpret_cast<uintptr_t>(W), aa = reinterpret_cast<uintptr_t>(A);
-    if ((aa & 15u) || (qtype == QT_Q4_K && (wa & 15u)) || (wa & 1u)) return 0;
     const Geom g = geom_of(qtype);
+    const unsigned long long rb = static_cast<unsigned long long>(K / g.block_weights) * g.block_bytes;
+    if ((aa & 15u) || (wa & 15u) || (rb & 15u)) return 0;   // TMA: 16-byte base and row stride
     EncodeTiled enc = encode_tiled();
     if (!enc) {
         fprintf(stderr, "[tb_cuda] qgemm: cuTensorMapEncodeTiled not available\n");
@@ -403,38 +479,69 @@ int qg_launch(const void *W, int qtype, int N, int K, const void *A, int T, floa
         fprintf(stderr, "[tb_cuda] qgemm: tensor map encode failed\n");
         return 0;
     }
+    // W as [N rows][row_bytes / 2] uint16, boxes of 128 rows x one block rounded out to 16 bytes
+    const uint32_t bw = qtype == QT_Q4_K ? 72u : 112u;
+    CUtensorMap wmap;
+    const cuuint64_t wdims[2] = {static_cast<cuuint64_t>(rb / 2), static_cast<cuuint64_t>(N)};
+    const cuuint64_t wstrides[1] = {static_cast<cuuint64_t>(rb)};
+    const cuuint32_t wbox[2] = {bw, static_cast<cuuint32_t>(kGM)};
+    if (enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(W), wdims, wstrides, wbox, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+        fprintf(stderr, "[tb_cuda] qgemm: weight tensor map encode failed\n");
+        return 0;
+    }
     QgArgs a{};
+    a.bw = bw;
     a.W = static_cast<const uint8_t *>(W);
     a.C = C;
     a.err = d_err;
     a.N = static_cast<uint32_t>(N);
     a.K = static_cast<uint32_t>(K);
     a.T = static_cast<uint32_t>(T);
-    a.row_bytes = static_cast<uint32_t>((K / g.block_weights) * g.block_bytes);
+    a.row_bytes = static_cast<uint32_t>(rb);
     a.wait_limit = wait_limit;
-    // split K until the grid is about one wave (each part a multiple of 256)
+    // Two CTAs per SM when their shared memory fits (two MMA issuers per SM),
+    // else one; split K until the grid is about one wave (each part a multiple
+    // of 256); a raw ring of 2-3 super-blocks, then as many MMA stages as fit.
+    uint32_t per_sm = 2, nraw = 2, nst = 8;
+    size_t cap = (kGSmemCap - 2048) / 2;
+    while (nst > 3 && qg_smem_bytes(a.T, nst, nraw) > cap) --nst;
+    if (qg_smem_bytes(a.T, nst, nraw) > cap) {
+        per_sm = 1;
+        cap = kGSmemCap;
+        nraw = 3;
+        nst = 8;
+        while (nst > 2 && qg_smem_bytes(a.T, nst, nraw) > cap) --nst;
+        if (qg_smem_bytes(a.T, nst, nraw) > cap) nraw = 2;
+        if (qg_smem_bytes(a.T, nst, nraw) > cap) return 0;
+    }
     const uint32_t tiles = static_cast<uint32_t>(N / kGM);
     uint32_t ks = 1;
-    while (tiles * ks * 2 <= static_cast<uint32_t>(num_sms) && (K / (ks * 2)) % 256 == 0 && K / (ks * 2) >= 512)
+    while (tiles * ks * 2 <= static_cast<uint32_t>(num_sms) * per_sm && (K / (ks * 2)) % 256 == 0 &&
+           K / (ks * 2) >= 512)
         ks *= 2;
     a.ksplit = ks;
     a.k_per_split = static_cast<uint32_t>(K) / ks;
-    uint32_t tc = 32;
-    while (tc < a.T) tc <<= 1;
-    a.tcols = tc;
-    uint32_t nst = 8;
-    while (nst > 2 && qg_smem_bytes(a.T, nst) > kGSmemCap) --nst;
-    if (qg_smem_bytes(a.T, nst) > kGSmemCap) return 0;
     a.nst = nst;
-    const size_t smem = qg_smem_bytes(a.T, nst);
-    void (*kern)(const CUtensorMap, const QgArgs) = qtype == QT_Q4_K ? k_qgemm<QT_Q4_K> : k_qgemm<QT_Q6_K>;
+    a.nraw = nraw;
+    // accumulators: nacc * T TMEM columns, at most 512 per SM (256 per CTA when two share it)
+    const uint32_t tmem_cap = per_sm == 2 ? 256u : 512u;
+    a.nacc = 4;
+    while (a.nacc > 1 && a.nacc * a.T > tmem_cap) a.nacc >>= 1;
+    uint32_t tc = 32;
+    while (tc < a.T * a.nacc) tc <<= 1;
+    a.tcols = tc;
+    const size_t smem = qg_smem_bytes(a.T, nst, nraw);
+    void (*kern)(const CUtensorMap, const CUtensorMap, const QgArgs) =
+        qtype == QT_Q4_K ? k_qgemm<QT_Q4_K> : k_qgemm<QT_Q6_K>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
     if (ks > 1 && cudaMemsetAsync(C, 0, sizeof(float) * static_cast<size_t>(T) * N, st) != cudaSuccess) return 0;
-    kern<<<dim3(tiles, ks), kGThreads, smem, st>>>(map, a);
+    kern<<<dim3(tiles, ks), kGThreads, smem, st>>>(map, wmap, a);
     return cudaGetLastError() == cudaSuccess ? 1 : 0;
 }
 
