@@ -241,6 +241,65 @@ def decode_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: i
             "order": "reference (RoPE before QK-norm, K rotated n_heads/n_kv_heads times)"}
 
 
+def tensor_peak():
+    """Measured dense bf16 TFLOP/s (burst: each GEMM below is timed alone)."""
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def prefill_bench(reps: int = 20):
+    """the prefill GEMM C[T][N] = A[T][K] (bf16) x dequant(W)^T on
+    the tensor cores (tb_cuda_qgemm_dev), Q4_K and Q6_K weights of 12288 x 4096 and
+    4096 x 12288, T in {16, 128, 512}; random-init weights, A ~ N(0,1).  Each shape is
+    timed alone over `reps` launches rotating four weight copies (CUDA events on the
+    launching stream).  T = 16 is memory-bound (reported in weight GB/s against the
+    HBM peak), T = 128 and 512 compute-bound (TFLOP/s against the bf16 peak)."""
+    import torch
+    from trailblaze_b200 import load
+    from trailblaze_b200.decoder import device_weights
+    k = load()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(SEED + 5)
+    st = torch.cuda.Stream()
+    hbm, _ = peaks()
+    tpk, tkind = tensor_peak()
+    rows = {}
+    for qt, qn in ((Q.Q4_K, "Q4_K"), (Q.Q6_K, "Q6_K")):
+        for N, K in ((12288, 4096), (4096, 12288)):
+            Ws = [device_weights(qt, N, K, gen) for _ in range(4)]
+            for T in (16, 128, 512):
+                A = torch.randn(T, K, device="cuda", generator=gen).to(torch.bfloat16)
+                C = torch.empty(T, N, device="cuda")
+
+                def run(n):
+                    for i in range(n):
+                        if k.tb_cuda_qgemm_dev(Ws[i % 4].data_ptr(), qt, N, K, A.data_ptr(), T, C.data_ptr(),
+                                               st.cuda_stream) != 1:
+                            raise RuntimeError("tb_cuda_qgemm_dev refused the shape")
+                with torch.cuda.stream(st):
+                    run(3)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(st):
+                    e0.record(st)
+                    run(reps)
+                    e1.record(st)
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / reps
+                tfl = 2.0 * T * N * K / (ms * 1e-3) / 1e12
+                wgb = Q.row_bytes(qt, K) * N / (ms * 1e-3) / 1e9
+                rows[f"{qn}:{N}x{K}:T{T}"] = {"us": round(ms * 1e3, 1), "TFLOPs": round(tfl, 1),
+                                              "frac_bf16_peak": round(tfl / tpk, 4),
+                                              "weight_GBps": round(wgb, 1), "frac_hbm": round(wgb / hbm, 4)}
+            del Ws
+    return {"kernel": "k_qgemm (tcgen05.mma kind::f16, bf16 x bf16 -> fp32 in TMEM; W dequantised to bf16 "
+                      "in shared memory; A by TMA)",
+            "peak_tflops": tpk, "peak_kind": tkind, "per_shape": rows}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -285,6 +344,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3-8B-shape decode tok/s leg")
     ap.add_argument("--decode-only", action="store_true",
                     help="only the decode tok/s leg (its line's value is tok/s; profiling aid)")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM leg (BASELINE config 5)")
+    ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM leg (profiling aid)")
     ap.add_argument("--decode-ctx", type=int, default=4096)
     ap.add_argument("--decode-tokens", type=int, default=64)
     args = ap.parse_args()
@@ -308,6 +369,20 @@ def main():
     from trailblaze_b200 import load
     k = load()
     assert k.tb_cuda_init() == 1
+
+    if args.prefill_only:
+        with Clocks(local) as clk:
+            pf = prefill_bench()
+        if rank == 0:
+            best = max(v["TFLOPs"] for v in pf["per_shape"].values())
+            print(json.dumps({"metric": "prefill GEMM TFLOP/s (best shape)", "value": best, "unit": "TFLOP/s",
+                              "n_gpus": world, "higher_is_better": True, "dtype": "bf16",
+                              "data": "synthetic (seeded torch generator on the device)",
+                              "config": {"workload": "prefill only (profiling aid)"}, "prefill": pf,
+                              "clocks": clk.summary()}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     if args.decode_only:
         with Clocks(local) as clk:
@@ -475,6 +550,12 @@ def main():
                                   dist=dist if world > 1 else None)
         except Exception as e:  # noqa: BLE001 - the decode leg must not sink the sweep line
             decode = {"unavailable": f"{type(e).__name__}: {e}"}
+    prefill = None
+    if world == 1 and not args.no_prefill and not args.shape:
+        try:
+            prefill = prefill_bench()
+        except Exception as e:  # noqa: BLE001 - the prefill leg must not sink the sweep line
+            prefill = {"unavailable": f"{type(e).__name__}: {e}"}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -506,6 +587,8 @@ def main():
         line["e2e"] = e2e
     if decode:
         line["decode"] = decode
+    if prefill:
+        line["prefill"] = prefill
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
