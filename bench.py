@@ -331,6 +331,23 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def quiet_init(k) -> int:
+    """tb_cuda_init prints its device banner on the C library's stdout, as the
+    reference's init does; the bench keeps stdout for its one JSON line, so the
+    banner is sent to stderr."""
+    import ctypes
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        ok = k.tb_cuda_init()
+        ctypes.CDLL(None).fflush(None)
+    finally:
+        os.dup2(saved, 1)
+        os.close(saved)
+    return ok
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -368,7 +385,7 @@ def main():
 
     from trailblaze_b200 import load
     k = load()
-    assert k.tb_cuda_init() == 1
+    assert quiet_init(k) == 1
 
     if args.prefill_only:
         with Clocks(local) as clk:

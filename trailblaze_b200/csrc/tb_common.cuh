@@ -97,24 +97,41 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f)
 }
 
 // ── shared-memory byte-stream reader ─────────────────────────────────────────
+// The matvec decoders read staged weight rows by 32-bit shared-window address
+// (ld.shared, 32-bit address arithmetic).  These loads are plain (not volatile)
+// asm so the compiler may merge the repeated word loads of neighbouring
+// unaligned reads; they cannot run ahead of the mbarrier wait that publishes a
+// stage because every address derives from shared_after(), a volatile move
+// issued after that wait.
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a)
+{
+    uint32_t v;
+    asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds_u128(uint32_t a)
+{
+    uint4 v;
+    asm("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+// An opaque copy of a shared address, ordered after the preceding volatile asm
+// (the mbarrier wait): loads whose address derives from it stay after the wait.
+__device__ __forceinline__ uint32_t shared_after(uint32_t a)
+{
+    uint32_t v;
+    asm volatile("mov.b32 %0, %1;" : "=r"(v) : "r"(a));
+    return v;
+}
+
 // Units of 210-, 110-, 84-, 34- or 18-byte blocks start at arbitrary byte
 // offsets in the staged copy, so their 32-bit words are read as a funnel shift
 // of two aligned words.  `sh` is 8*(offset & 3); a shift of 0 returns `lo`.
-__device__ __forceinline__ uint32_t lds_u32(const uint8_t *p)
-{
-    return *reinterpret_cast<const uint32_t *>(p);
-}
-
 struct UnitBytes {
-    const uint8_t *base;   // 4-byte aligned address at or below the unit start
-    uint32_t sh;           // funnel shift in bits (0, 8, 16, 24)
+    uint32_t base;   // 4-byte aligned shared address at or below the unit start
+    uint32_t sh;     // funnel shift in bits (0, 8, 16, 24)
 
-    __device__ __forceinline__ UnitBytes(const uint8_t *unit)
-    {
-        uintptr_t a = reinterpret_cast<uintptr_t>(unit);
-        base = reinterpret_cast<const uint8_t *>(a & ~uintptr_t(3));
-        sh = static_cast<uint32_t>(a & 3u) * 8u;
-    }
+    __device__ __forceinline__ UnitBytes(uint32_t unit) : base(unit & ~3u), sh((unit & 3u) * 8u) {}
     // 32-bit little-endian word at byte offset 4*i + 0 of the unit
     __device__ __forceinline__ uint32_t w(int i) const
     {
@@ -123,7 +140,7 @@ struct UnitBytes {
     // 32-bit word at an arbitrary byte offset `off` of the unit
     __device__ __forceinline__ uint32_t at(int off) const
     {
-        const uint8_t *p = base + (off & ~3);
+        const uint32_t p = base + (off & ~3);
         uint32_t s = sh + 8u * (off & 3);
         uint32_t lo = lds_u32(p), hi = lds_u32(p + 4), hi2 = lds_u32(p + 8);
         return s >= 32 ? __funnelshift_r(hi, hi2, s - 32) : __funnelshift_r(lo, hi, s);

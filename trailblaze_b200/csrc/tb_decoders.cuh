@@ -48,20 +48,17 @@ struct Pos {
     int n;          // weights of the slot's last group present (32, fewer only for floats)
 };
 
-// 32-bit words of a block whose staged copy may start at any byte.
-// A16 = the caller guarantees 16-byte alignment (plain vector loads).
+// 32-bit words of a block whose staged copy (a shared-window address) may start
+// at any byte.  A16 = the caller guarantees 16-byte alignment (vector loads).
 template <bool A16>
 struct Words {
-    const uint8_t *p;
+    uint32_t p;
     UnitBytes ub;
-    __device__ __forceinline__ explicit Words(const uint8_t *blk) : p(blk), ub(blk) {}
-    __device__ __forceinline__ uint32_t operator()(int i) const
-    {
-        return A16 ? reinterpret_cast<const uint32_t *>(p)[i] : ub.w(i);
-    }
+    __device__ __forceinline__ explicit Words(uint32_t blk) : p(blk), ub(blk) {}
+    __device__ __forceinline__ uint32_t operator()(int i) const { return A16 ? lds_u32(p + 4 * i) : ub.w(i); }
     __device__ __forceinline__ uint4 q4(int byte_off) const
     {
-        if (A16) return *reinterpret_cast<const uint4 *>(p + byte_off);
+        if (A16) return lds_u128(p + byte_off);
         const int i = byte_off >> 2;
         return make_uint4(ub.w(i), ub.w(i + 1), ub.w(i + 2), ub.w(i + 3));
     }
@@ -339,7 +336,7 @@ struct DecQ4K {
         put_planes_slot<4>(256 * sh + sl, j, rec + LY::CST);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<A16> W(row + p.off);
         const uint4 h = W.q4(0);
@@ -379,7 +376,7 @@ struct DecQ5K {
         put_planes_slot<2>(256 * sh + sl, j, rec + LY::CST);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<A16> W(row + p.off);
         const uint4 h = W.q4(0);
@@ -413,66 +410,71 @@ struct DecQ5K {
 };
 
 // ---- Q6_K — 210 B: ql @0, qh @128, int8 scales @192, d @208 (tb_gguf_dequant.cu:196-217) ----
-// w = d*sc[i>>4]*(q-32), q = ql nibble | (qh 2 bits)<<4; the high bits are
-// masked as 0x30 per byte (already x16).  The -32 enters as the initial value
-// of each 16-weight sub-block's sums (-32 * the sub-block's digit sums).
+// w = d*sc[i>>4]*(q-32), q = ql nibble | (qh 2 bits)<<4, weight i's nibble in
+// ql byte i/2 (low nibble for even i) and its 2 bits at qh byte i/4, bit 2(i%4).
+// Slot = half a block (4 groups, 8 sub-blocks of 16 weights, two scale words).
+// Each sub-block (two ql words A, B and one qh word h) is decoded in the qh
+// fields' order (PK_TWO16: byte b of word j = weight 4b + j): two byte permutes
+// gather ql bytes 2b (weights 4b, 4b+1) and 2b+1 (4b+2, 4b+3), so every byte
+// lane holds the whole 6-bit q of one weight and one dp4a pair covers four
+// weights.  The -32 is applied once per slot: -32 * sum_s sc_s * X_s, X_s the
+// sub-block's activation sum, by dp4a of the scales against X_s's byte planes.
 struct DecQ6K {
-    using LY = IntLayout<2, 2, 8>;
-    static constexpr int GPL = 2;
+    using LY = IntLayout<4, 1, 6>;
+    static constexpr int GPL = 4;
     static constexpr bool kInt = true;
     static constexpr int REC = LY::STRIDE;
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
         PackedX a, b;
-        prep_digits<LY, PK_NIB, PK_TWO16>(g, E, fin, j, rec, a, b);
+        prep_digits<LY, PK_TWO16, -1>(g, E, fin, j, rec, a, b);
         int sh, sl;
-        psums<0, 4>(b, sh, sl);   // PK_TWO16 words 0..3 = activations 0..15
-        rec[LY::CST + 4 * j + 0] = static_cast<uint32_t>(-32 * sh);
-        rec[LY::CST + 4 * j + 1] = static_cast<uint32_t>(-32 * sl);
-        psums<4, 4>(b, sh, sl);   // activations 16..31
-        rec[LY::CST + 4 * j + 2] = static_cast<uint32_t>(-32 * sh);
-        rec[LY::CST + 4 * j + 3] = static_cast<uint32_t>(-32 * sl);
+        uint32_t *c = rec + LY::CST + 3 * (j >> 1);   // planes of the scale word holding sub-blocks 2j, 2j+1
+        psums<0, 4>(a, sh, sl);   // PK_TWO16 words 0..3 = activations 0..15
+        put_planes(256 * sh + sl, (2 * j) & 3, c);
+        psums<4, 4>(a, sh, sl);   // activations 16..31
+        put_planes(256 * sh + sl, (2 * j + 1) & 3, c);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
-    __device__ static void hi16(int &ah, int &al, uint32_t hq, const uint32_t (&r)[LY::WORDS], int g, int base)
+    // One sub-block: ql words A (weights 0..7), B (8..15), qh word h; digit
+    // words base..base+3 of group g.
+    __device__ static void sub16(int &ah, int &al, uint32_t A, uint32_t B, uint32_t h,
+                                 const uint32_t (&r)[LY::WORDS], int g, int base)
     {
-        mac_u<LY>(ah, al, (hq << 4) & 0x30303030u, r, g, 1, base + 0);
-        mac_u<LY>(ah, al, (hq << 2) & 0x30303030u, r, g, 1, base + 1);
-        mac_u<LY>(ah, al, hq & 0x30303030u, r, g, 1, base + 2);
-        mac_u<LY>(ah, al, (hq >> 2) & 0x30303030u, r, g, 1, base + 3);
+        const uint32_t e = __byte_perm(A, B, 0x6420u);   // ql bytes 0,2,4,6: weights 4b (lo), 4b+1 (hi)
+        const uint32_t o = __byte_perm(A, B, 0x7531u);   // ql bytes 1,3,5,7: weights 4b+2, 4b+3
+        mac_u<LY>(ah, al, (e & 0x0F0F0F0Fu) | ((h << 4) & 0x30303030u), r, g, 0, base + 0);
+        mac_u<LY>(ah, al, ((e >> 4) & 0x0F0F0F0Fu) | ((h << 2) & 0x30303030u), r, g, 0, base + 1);
+        mac_u<LY>(ah, al, (o & 0x0F0F0F0Fu) | (h & 0x30303030u), r, g, 0, base + 2);
+        mac_u<LY>(ah, al, ((o >> 4) & 0x0F0F0F0Fu) | ((h >> 2) & 0x30303030u), r, g, 0, base + 3);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<false> W(row + p.off);
         const float d = h2f2_ref(W(52)).x;
-        const uint32_t scw = W(48 + (p.gi0 >> 1));   // the slot's 4 int8 sub-block scales
+        const uint32_t sc0 = W(48 + (p.gi0 >> 1)), sc1 = W(49 + (p.gi0 >> 1));   // 8 int8 scales
         int th = 0, tl = 0;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             const uint32_t gi = p.gi0 + g;
             const uint4 l = W.q4(16 * gi);
             const uint32_t h0 = W(32 + 2 * gi), h1 = W(33 + 2 * gi);
-            int ah = x.cst(4 * g), al = x.cst(4 * g + 1);
-            mac_u<LY>(ah, al, l.x & 0x0F0F0F0Fu, x.r, g, 0, 0);
-            mac_u<LY>(ah, al, (l.x >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 4);
-            mac_u<LY>(ah, al, l.y & 0x0F0F0F0Fu, x.r, g, 0, 1);
-            mac_u<LY>(ah, al, (l.y >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 5);
-            hi16(ah, al, h0, x.r, g, 0);
-            int s = sbyte(scw, 2 * g);
+            const uint32_t scw = g < 2 ? sc0 : sc1;
+            int ah = 0, al = 0;
+            sub16(ah, al, l.x, l.y, h0, x.r, g, 0);
+            int s = sbyte(scw, 2 * (g & 1));
             th = s * ah + th;
             tl = s * al + tl;
-            int bh = x.cst(4 * g + 2), bl = x.cst(4 * g + 3);
-            mac_u<LY>(bh, bl, l.z & 0x0F0F0F0Fu, x.r, g, 0, 2);
-            mac_u<LY>(bh, bl, (l.z >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 6);
-            mac_u<LY>(bh, bl, l.w & 0x0F0F0F0Fu, x.r, g, 0, 3);
-            mac_u<LY>(bh, bl, (l.w >> 4) & 0x0F0F0F0Fu, x.r, g, 0, 7);
-            hi16(bh, bl, h1, x.r, g, 4);
-            s = sbyte(scw, 2 * g + 1);
+            int bh = 0, bl = 0;
+            sub16(bh, bl, l.z, l.w, h1, x.r, g, 4);
+            s = sbyte(scw, 2 * (g & 1) + 1);
             th = s * bh + th;
             tl = s * bl + tl;
         }
-        return x.sx() * d * hl_value(th, tl);
+        const int off = dot_planes_s(sc0, x.cstu(0), x.cstu(1), x.cstu(2)) +
+                        dot_planes_s(sc1, x.cstu(3), x.cstu(4), x.cstu(5));
+        return x.sx() * d * fmaf(-32.f, static_cast<float>(off), hl_value(th, tl));
     }
 };
 
@@ -505,7 +507,7 @@ struct DecQ2K {
         mac_u<LY>(ah, al, (q >> 4) & 0x03030303u, r, g, 0, base + 2);
         mac_u<LY>(ah, al, (q >> 6) & 0x03030303u, r, g, 0, base + 3);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<A4> W(row + p.off);
         const float2 dd = h2f2_ref(W(20));
@@ -547,7 +549,7 @@ struct DecQ80 {
         prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec, a, b);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         float tot = 0.f;
 #pragma unroll
@@ -583,7 +585,7 @@ struct DecQ40 {
         rec[LY::CST + 2 * j + 1] = static_cast<uint32_t>(-8 * sl);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         float tot = 0.f;
 #pragma unroll
@@ -613,7 +615,7 @@ struct DecQ8K {
         prep_digits<LY, PK_BYTE, -1>(g, E, fin, j, rec, a, b);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<false> W(row + p.off);
         const float d = __uint_as_float(W(0));
@@ -683,7 +685,7 @@ struct DecQ3K {
         ev = ue | ((ue & 0x20202020u) * 6u);   // sign-extend bit 5 into bits 6..7
         od = uo | ((uo & 0x20202020u) * 6u);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<false> W(row + p.off);
         const float d = h2f2_ref(W(27)).x;
@@ -757,7 +759,7 @@ struct DecFloat {
         const uint32_t h = (i & 1) ? (w >> 16) : (w & 0xFFFFu);
         return QT == QT_F16 ? h2f_ref(h) : __uint_as_float(h << 16);
     }
-    __device__ static float row_dot(const uint8_t *row, const Pos &p, const Lane &x)
+    __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const UnitBytes ub(row + p.off);
         float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);

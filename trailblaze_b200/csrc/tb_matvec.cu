@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         const bool ok = mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit);
         if (!__all_sync(kFull, ok)) break;   // no arrival: the producer's wait runs out as well
         const uint32_t nrows = min(a.tr, r_hi - t0);
-        const uint8_t *sbase = stage + (lo & 15u);
+        const uint32_t sbase = shared_after(smem_u32(stage) + static_cast<uint32_t>(lo & 15u));
 #pragma unroll 2
         for (uint32_t i = 0; i < a.rpl; ++i) {
             const uint32_t rt = ph + i * a.phases;
