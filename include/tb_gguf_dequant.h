@@ -107,6 +107,21 @@ int   tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K,
                                const float *d_norm_w, float eps, const float *d_res,
                                int ymode, void *stream);
 
+/* Expert matvecs on a packed expert tensor (the MoE call sites of
+ * layer4/tb_infer.c:797-816, which run one tb_gguf_dequant_matvec per selected
+ * expert on a row offset of blk.N.ffn_*_exps), all selected experts in one
+ * launch.  W_dev is n_experts matrices of M x K, back to back.  For
+ * g < n_sel, expert e = d_ids[g] (device memory, read by the kernel, so a
+ * router kernel earlier in the stream may write it; d_ids NULL: e = g):
+ *   d_y[g * y_stride + m] = (dequant(W_e) @ d_x[g * x_stride ...])[m]
+ * x_stride = 0 shares one x.  ymode 1 applies SwiGLU to (gate, up) row pairs
+ * as in tb_cuda_matvec_fused_dev (M/2 outputs per expert).  An id outside
+ * [0, n_experts) skips its expert and sets the error word (2).
+ * Stream-ordered.  1 = issued. */
+int   tb_cuda_matvec_experts_dev(const void *W_dev, int qtype, int M, int K, int n_experts,
+                                 const int *d_ids, int n_sel, const float *d_x, int x_stride,
+                                 float *d_y, int y_stride, int ymode, void *stream);
+
 /* Bit-exact dequantisation of M rows of K weights into d_out[M*K] (fp32),
  * stream-ordered.  sem = 0 gives the reference CUDA-kernel semantics (the
  * parity contract); sem = 1 gives layer4/tb_gguf.c's shipped decoders, which
@@ -216,7 +231,11 @@ int    tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_ou
  * the last layer's attention block (hidden), 2 the last layer's q | k | v
  * before QK-norm and RoPE ((n_heads + 2 n_kv_heads) head_dim), 3 its attention
  * output (n_heads head_dim), 4 its SwiGLU activation (ffn_dim), 5 the logits
- * (vocab).  Blocking.  1 = ok, 0 for an unknown vector or n past its size. */
+ * (vocab); for a routed decoder 6 the last layer's router logits (n_experts),
+ * 7 its expert weights and 8 its expert ids (top_k; int32 bits in the float
+ * slots), rank order, 9 the selected experts' SwiGLU activations (top_k x
+ * ffn_dim, rank order).  Blocking.  1 = ok, 0 for an unknown vector, one
+ * this decoder does not have, or n past its size. */
 int    tb_cuda_dec_read(void *dec, int which, float *host, int n);
 
 /* Tensor parallelism over `world` GPUs (2, 4 or 8; one process per GPU), the
@@ -240,6 +259,23 @@ int    tb_cuda_dec_tp_handle(void *dec, void *handle_out);
 /* Maps the other ranks' regions; handles = world x 64 bytes in rank order (as
  * gathered from every rank's tb_cuda_dec_tp_handle).  1 = ok. */
 int    tb_cuda_dec_tp_connect(void *dec, const void *handles);
+
+/* Mixture-of-experts decoder (replaces the routed FFN of layer4/tb_infer.c:
+ * 753-850 and the router of tb_infer.c:351-374).  cfg->ffn_dim is the expert
+ * FFN width F; every layer routes rmsnorm(x2) through its router to the top_k
+ * of n_experts (<= 256) experts, weights = softmax renormalised over the
+ * selected ones, x = x2 + sum of weight * expert SwiGLU FFN.  One device. */
+void  *tb_cuda_dec_create_moe(const tb_dec_config *cfg, int n_experts, int top_k);
+/* A routed layer's FFN tensors (its attention tensors and norms come from
+ * tb_cuda_dec_set_layer, whose w_gate_up / w_down are then ignored):
+ * w_router [n_experts][hidden] (blk.N.ffn_gate_inp); w_gate_up_exps
+ * [n_experts][2F][hidden], expert e's gate and up rows interleaved (row 2i =
+ * gate row i of blk.N.ffn_gate_exps, row 2i+1 = up row i of
+ * blk.N.ffn_up_exps); w_down_exps [n_experts][hidden][F]
+ * (blk.N.ffn_down_exps).  1 = ok. */
+int    tb_cuda_dec_set_moe_layer(void *dec, int layer, const void *w_router, int router_qtype,
+                                 const void *w_gate_up_exps, int gate_up_qtype, const void *w_down_exps,
+                                 int down_qtype);
 void   tb_cuda_dec_destroy(void *dec);
 
 #ifdef __cplusplus

@@ -18,6 +18,15 @@ numpy, float64, following layer4/tb_infer.c:553-887 (tb_layer_forward) and
   final norm, head    tb_infer.c:987-1019
   greedy              layer1/tb_tensor.c:415-420 (first index of the maximum)
 
+Mixture-of-experts layers (n_experts > 0) replace gate/up/down by the routed
+FFN of tb_infer.c:753-850: router logits of the FFN-normed x2, softmax, the
+reference's top-k scan and renormalisation (tb_infer.c:351-374), each selected
+expert's SwiGLU FFN (gate/up rows interleaved as above, down), the outputs
+accumulated with their weights in selection order, then the residual
+(tb_infer.c:876).  The reference decodes the router tensor with its legacy
+4-bit "compat" decoder whatever the tensor's GGUF type (tb_infer.c:757-763);
+here it is decoded as the type it is stored in.
+
 quirks=True keeps the reference's order: RoPE before the QK-norm, and K head
 j rotated once for every query head h with h % NK == j (tb_infer.c:665).
 quirks=False is the Qwen3 order (norm, then a single rotation).
@@ -55,7 +64,11 @@ class DecodeModel:
     lm: np.ndarray = None
     lm_qt: int = 14
     layers: list = field(default_factory=list)   # dicts: wqkv, qkv_qt, wo, o_qt, wgu, gu_qt, wd, d_qt,
-                                                # attn_norm, ffn_norm, q_norm, k_norm
+                                                # attn_norm, ffn_norm, q_norm, k_norm; routed layers
+                                                # instead of wgu / wd: wr, r_qt (router [E][H]),
+                                                # wgu_e, gue_qt ([E][2F][H]), wd_e, de_qt ([E][H][F])
+    n_experts: int = 0
+    top_k: int = 0
 
 
 def rms_norm(x, w, eps):
@@ -100,6 +113,28 @@ def swiglu(g, u):
     return (g / (1.0 + np.exp(-g))) * u
 
 
+def route(logits, k):
+    """tb_route_experts (layer4/tb_infer.c:351-374) without its optional
+    boosts: softmax, then one pass over the experts that replaces the first
+    smallest of k slots (initially -1e30) whenever an expert's probability is
+    strictly larger, then the k weights divided by their sum.  Returns
+    (indices, weights) in slot order."""
+    s = np.asarray(logits, np.float64)
+    p = np.exp(s - s.max())
+    p = p / p.sum()
+    idx = [0] * k
+    wts = [-1e30] * k
+    for e in range(s.size):
+        mi = min(range(k), key=lambda i: (wts[i], i))
+        if p[e] > wts[mi]:
+            wts[mi] = p[e]
+            idx[mi] = e
+    ws = sum(wts)
+    if ws > 0:
+        wts = [w / ws for w in wts]
+    return idx, wts
+
+
 def attention(q, kc, vc, n_heads, n_kv_heads):
     """layer1/tb_tensor.c:303-409 for one token: q [NH][HD] against cached
     kc, vc [NK][T][HD] (the new position already appended); query head h uses
@@ -127,12 +162,18 @@ class DecodeOracle:
         self.lm = deq(m.lm, m.lm_qt, m.vocab, H)
         self.out_norm = m.out_norm.astype(np.float64)
         self.L = []
+        E = m.n_experts
         for w in m.layers:
+            routed = dict(
+                wr=deq(w["wr"], w["r_qt"], E, H),
+                wgu_e=deq(w["wgu_e"], w["gue_qt"], E * 2 * F, H).reshape(E, 2 * F, H),
+                wd_e=deq(w["wd_e"], w["de_qt"], E * H, F).reshape(E, H, F)) if E else dict(
+                wgu=deq(w["wgu"], w["gu_qt"], 2 * F, H),
+                wd=deq(w["wd"], w["d_qt"], H, F))
             self.L.append(dict(
                 wqkv=deq(w["wqkv"], w["qkv_qt"], (NH + 2 * NK) * HD, H),
                 wo=deq(w["wo"], w["o_qt"], H, NH * HD),
-                wgu=deq(w["wgu"], w["gu_qt"], 2 * F, H),
-                wd=deq(w["wd"], w["d_qt"], H, F),
+                **routed,
                 attn_norm=w["attn_norm"].astype(np.float64), ffn_norm=w["ffn_norm"].astype(np.float64),
                 q_norm=None if w.get("q_norm") is None else w["q_norm"].astype(np.float64),
                 k_norm=None if w.get("k_norm") is None else w["k_norm"].astype(np.float64)))
@@ -179,7 +220,21 @@ class DecodeOracle:
             self.vc[li, :, pos] = v
             att = attention(q, self.kc[li, :, :pos + 1], self.vc[li, :, :pos + 1], NH, NK)
             x2 = x + w["wo"] @ att.reshape(-1)
-            gu = w["wgu"] @ rms_norm(x2, w["ffn_norm"], eps)
+            xn2 = rms_norm(x2, w["ffn_norm"], eps)
+            if m.n_experts:
+                rl = w["wr"] @ xn2
+                idx, wts = route(rl, m.top_k)
+                ffn = np.zeros(H)
+                acts = []
+                for e, we in zip(idx, wts):
+                    gu = w["wgu_e"][e] @ xn2
+                    act = swiglu(gu[0::2], gu[1::2])
+                    acts.append(act)
+                    ffn += we * (w["wd_e"][e] @ act)
+                x = x2 + ffn
+                self.last = dict(x2=x2, qkv=qkv, att=att.reshape(-1), router=rl, ids=idx, wts=wts, acts=acts)
+                continue
+            gu = w["wgu"] @ xn2
             act = swiglu(gu[0::2], gu[1::2])   # (gate, up) rows interleaved
             x = x2 + w["wd"] @ act
             # the last layer's vectors, for tests that read the GPU's

@@ -345,6 +345,39 @@ int tb_cuda_qgemm_dev(const void *W_dev, int qtype, int N, int K, const void *A_
     return r;
 }
 
+int tb_cuda_matvec_experts_dev(const void *W_dev, int qtype, int M, int K, int n_experts, const int *d_ids,
+                               int n_sel, const float *d_x, int x_stride, float *d_y, int y_stride, int ymode,
+                               void *stream)
+{
+    int nsm;
+    int *derr;
+    uint32_t lim;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!ensure_init_locked(false)) return 0;
+        nsm = g.num_sms;
+        derr = g.d_err;
+        lim = g.wait_limit;
+    }
+    const tb::Geom gm = tb::geom_of(qtype);
+    if (!gm.block_weights || M <= 0 || K <= 0 || K % gm.block_weights || n_experts < 1 || n_sel < 1 ||
+        x_stride < 0 || y_stride < 0 || ymode < 0 || ymode > 1)
+        return 0;
+    const int out = ymode == 1 ? M / 2 : M;
+    if ((n_sel > 1 && y_stride < out) || (!d_ids && n_sel > n_experts)) return 0;
+    tb::MvFuse f;
+    f.ymode = static_cast<uint32_t>(ymode);
+    f.ng = static_cast<uint32_t>(n_sel);
+    f.n_experts = static_cast<uint32_t>(n_experts);
+    f.ids = d_ids;
+    f.w_stride = static_cast<unsigned long long>(M) * (K / gm.block_weights) * gm.block_bytes;
+    f.x_stride = static_cast<uint32_t>(x_stride);
+    f.y_stride = static_cast<uint32_t>(y_stride);
+    const int r = tb::mv_launch(W_dev, qtype, M, K, d_x, d_y, static_cast<cudaStream_t>(stream), derr, nsm, lim, &f);
+    if (r) g_launches.fetch_add(1, std::memory_order_relaxed);
+    return r;
+}
+
 int tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K, const float *d_x, float *d_y,
                              int xmode, const float *d_x2, const float *d_norm_w, float eps,
                              const float *d_res, int ymode, void *stream)

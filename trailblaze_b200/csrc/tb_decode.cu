@@ -660,6 +660,88 @@ __global__ void __launch_bounds__(kArgThreads) k_argmax_step(const float *logits
 }
 
 // ---------------------------------------------------------------------------
+// Mixture-of-experts routing and combine (layer4/tb_infer.c:351-374, 753-850)
+// ---------------------------------------------------------------------------
+static constexpr int kMoeThreads = 256;   // experts per router at most (tb_infer.c:254 caps at 256)
+
+// Router: p = softmax(logits) over the E experts (max-shifted, the sum taken
+// in expert order as the reference's loop does), the top k experts, and
+// their weights renormalised to sum 1 (tb_infer.c:351-374).  Written to
+// ids[0..k) / wts[0..k) in rank order: largest probability first, equal
+// probabilities by lower expert index.  (The reference's replace-the-minimum
+// scan selects the same set except among exactly equal probabilities, and
+// lists it in scan order; only the rounding of the weighted sum depends on
+// that order.)  A non-finite logit sets the error word and selects nothing.
+__global__ void __launch_bounds__(kMoeThreads) k_moe_topk(const float *logits, int E, int k, int *ids, float *wts,
+                                                           int *err)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __shared__ float p[kMoeThreads];
+    __shared__ float sel[kMoeThreads];
+    __shared__ float red[kMoeThreads / 32];
+    __shared__ float s_sum;
+    const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    const float v = e < E ? logits[e] : -FLT_MAX;
+    float m = v;
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < kMoeThreads / 32; ++w) m = fmaxf(m, red[w]);
+    bool fin = isfinite(m);
+    if (e < E) {
+        fin = fin && isfinite(v);
+        p[e] = expf(v - m);
+    }
+    const bool all_fin = __syncthreads_and(fin ? 1 : 0) != 0;
+    if (!all_fin) {
+        if (e == 0) atomicExch(err, ERR_RUNTIME);
+        return;
+    }
+    if (e == 0) {
+        float s = 0.f;
+        for (int j = 0; j < E; ++j) s += p[j];
+        s_sum = s;
+    }
+    __syncthreads();
+    const float q = e < E ? p[e] / s_sum : 0.f;
+    __syncthreads();
+    if (e < E) p[e] = q;
+    __syncthreads();
+    if (e < E) {
+        int rank = 0;
+        for (int j = 0; j < E; ++j) rank += (p[j] > q || (p[j] == q && j < e)) ? 1 : 0;
+        if (rank < k) {
+            ids[rank] = e;
+            sel[rank] = q;
+        }
+    }
+    __syncthreads();
+    if (e == 0) {
+        float ws = 0.f;
+        for (int i = 0; i < k; ++i) ws += sel[i];
+        s_sum = ws;
+    }
+    __syncthreads();
+    if (e < k) wts[e] = s_sum > 0.f ? sel[e] / s_sum : sel[e];
+}
+
+// x[i] = x2[i] + sum_r wts[r] * t[r][i], r in rank order (tb_infer.c:845-848,
+// 876: the experts' weighted outputs accumulated, then the residual).
+__global__ void __launch_bounds__(kMoeThreads) k_moe_combine(const float *x2, const float *t, const float *wts, int k,
+                                                              int H, float *x)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int i = blockIdx.x * kMoeThreads + threadIdx.x;
+    if (i >= H) return;
+    float acc = 0.f;
+    for (int r = 0; r < k; ++r) acc = fmaf(wts[r], t[static_cast<size_t>(r) * H + i], acc);
+    x[i] = x2[i] + acc;
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
@@ -685,6 +767,10 @@ struct DecLayer {
     const void *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
     int qkv_qt = -1, o_qt = -1, gu_qt = -1, d_qt = -1;
     const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    // mixture of experts: router [E][H]; per expert e the (gate, up) row pairs
+    // [E][2F][H] (interleaved like wgu) and down [E][H][F]
+    const void *wr = nullptr, *wgu_e = nullptr, *wd_e = nullptr;
+    int r_qt = -1, gue_qt = -1, de_qt = -1;
 };
 
 struct Decoder {
@@ -714,6 +800,11 @@ struct Decoder {
     uint8_t *peer[kMaxRanks] = {};   // every rank's region, this rank's own included
     bool peer_opened[kMaxRanks] = {};
     int *epoch = nullptr;            // steps completed (device)
+    // mixture of experts (n_exp > 0): every layer's FFN is routed to top_k of
+    // n_exp experts of cfg.ffn_dim rows each
+    int n_exp = 0, top_k = 0;
+    float *rlog = nullptr, *wts = nullptr, *hbuf = nullptr, *tbuf = nullptr;
+    int *ids = nullptr;
 
     float *slot_o(int p) const { return reinterpret_cast<float *>(peer[p]); }
     float *slot_d(int p) const { return reinterpret_cast<float *>(peer[p] + off_xd); }
@@ -733,15 +824,60 @@ struct Decoder {
     bool ready() const
     {
         if (!emb || !lm || !out_norm) return false;
-        for (int l = 0; l < cfg.n_layers; ++l)
-            if (!layers[l].wqkv || !layers[l].wo || !layers[l].wgu || !layers[l].wd || !layers[l].attn_norm ||
-                !layers[l].ffn_norm)
-                return false;
+        for (int l = 0; l < cfg.n_layers; ++l) {
+            const DecLayer &w = layers[l];
+            if (!w.wqkv || !w.wo || !w.attn_norm || !w.ffn_norm) return false;
+            if (n_exp ? (!w.wr || !w.wgu_e || !w.wd_e) : (!w.wgu || !w.wd)) return false;
+        }
         return true;
     }
     bool enqueue(cudaStream_t s);
     bool enqueue_tp(cudaStream_t s);
+    bool enqueue_moe(cudaStream_t s, const DecLayer &w);
 };
+
+// The routed FFN of one layer (tb_infer.c:753-850): router logits of
+// rmsnorm(x2), top-k and weights, the k experts' SwiGLU FFNs as two
+// expert-group matvecs (each expert on its own CTAs, its weights found from
+// the id on the device), then x = x2 + the weighted sum of their outputs.
+bool Decoder::enqueue_moe(cudaStream_t s, const DecLayer &w)
+{
+    const DecConfig &c = cfg;
+    const int H = c.hidden, F = c.ffn_dim;
+    const uint32_t lim = 1u << 22;
+    MvFuse f;
+    f.xmode = MV_X_RMSNORM;
+    f.nw = w.ffn_norm;
+    f.eps = c.norm_eps;
+    f.w_early = true;
+    if (!mv_launch(w.wr, w.r_qt, n_exp, H, x2, rlog, s, err, sms, lim, &f)) return false;
+    if (!launch_pdl(k_moe_topk, dim3(1), dim3(kMoeThreads), 0, s, static_cast<const float *>(rlog), n_exp, top_k,
+                    ids, wts, err))
+        return false;
+    const Geom gg = geom_of(w.gue_qt), gd = geom_of(w.de_qt);
+    f = MvFuse{};
+    f.xmode = MV_X_RMSNORM;
+    f.nw = w.ffn_norm;
+    f.eps = c.norm_eps;
+    f.ymode = MV_Y_SWIGLU_PAIRS;
+    f.ng = static_cast<uint32_t>(top_k);
+    f.n_experts = static_cast<uint32_t>(n_exp);
+    f.ids = ids;
+    f.w_stride = 2ull * F * (H / gg.block_weights) * gg.block_bytes;
+    f.y_stride = static_cast<uint32_t>(F);
+    if (!mv_launch(w.wgu_e, w.gue_qt, 2 * F, H, x2, hbuf, s, err, sms, lim, &f)) return false;
+    f = MvFuse{};
+    f.ng = static_cast<uint32_t>(top_k);
+    f.n_experts = static_cast<uint32_t>(n_exp);
+    f.ids = ids;
+    f.w_stride = static_cast<unsigned long long>(H) * (F / gd.block_weights) * gd.block_bytes;
+    f.x_stride = static_cast<uint32_t>(F);
+    f.y_stride = static_cast<uint32_t>(H);
+    if (!mv_launch(w.wd_e, w.de_qt, H, F, hbuf, tbuf, s, err, sms, lim, &f)) return false;
+    return launch_pdl(k_moe_combine, dim3((H + kMoeThreads - 1) / kMoeThreads), dim3(kMoeThreads), 0, s,
+                      static_cast<const float *>(x2), static_cast<const float *>(tbuf),
+                      static_cast<const float *>(wts), top_k, H, x);
+}
 
 bool Decoder::enqueue(cudaStream_t s)
 {
@@ -789,6 +925,10 @@ bool Decoder::enqueue(cudaStream_t s)
         f.res = x;
         f.w_early = true;
         if (!mv_launch(w.wo, w.o_qt, H, NH * HD, att, x2, s, err, sms, lim, &f)) return false;
+        if (n_exp) {
+            if (!enqueue_moe(s, w)) return false;
+            continue;
+        }
         // act = swiglu(gate, up), (gate | up) rows interleaved in Wgu, of rmsnorm(x2)
         f = MvFuse{};
         f.xmode = MV_X_RMSNORM;
@@ -943,8 +1083,9 @@ static void dec_free(Decoder *d)
     if (d->st) cudaStreamDestroy(d->st);
     if (d->ev0) cudaEventDestroy(d->ev0);
     if (d->ev1) cudaEventDestroy(d->ev1);
-    void *bufs[] = {d->x, d->x2, d->qkv, d->att, d->gu, d->logits, d->kc, d->vc, d->part, d->argv,
-                    d->argi, d->tok, d->pos, d->counts, d->err};
+    void *bufs[] = {d->x,    d->x2,  d->qkv, d->att, d->gu,     d->logits, d->kc,   d->vc,   d->part,
+                    d->argv, d->argi, d->tok, d->pos, d->counts, d->err,    d->rlog, d->wts, d->hbuf,
+                    d->tbuf, d->ids};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->hostio) cudaFreeHost(d->hostio);
@@ -958,8 +1099,13 @@ static void dec_free(Decoder *d)
 
 // full: the whole model's shape; rank / world: this process's share
 // (world 1 = the whole model on one device).
-Decoder *dec_create(const DecConfig &full, int rank, int world)
+Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, int top_k = 0)
 {
+    if (n_exp < 0 || n_exp > kMoeThreads || (n_exp && (top_k < 1 || top_k > n_exp || world != 1))) {
+        fprintf(stderr, "[tb_cuda] decoder: unsupported experts (%d, top %d; at most %d, one device)\n", n_exp, top_k,
+                kMoeThreads);
+        return nullptr;
+    }
     if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || full.n_heads % world ||
         full.n_kv_heads % world || full.ffn_dim % world || full.vocab % world) {
         fprintf(stderr, "[tb_cuda] decoder: rank %d of %d does not divide the heads, FFN rows and vocabulary\n",
@@ -1020,6 +1166,15 @@ Decoder *dec_create(const DecConfig &full, int rank, int world)
               dec_ok(cudaMalloc(&d->counts, sizeof(unsigned) * (NK + 1)), "tickets") &&
               dec_ok(cudaMalloc(&d->err, sizeof(int)), "err") &&
               dec_ok(cudaMallocHost(&d->hostio, sizeof(int) * 4), "host io");
+    if (ok && n_exp) {
+        d->n_exp = n_exp;
+        d->top_k = top_k;
+        ok = dec_ok(cudaMalloc(&d->rlog, sizeof(float) * n_exp), "router logits") &&
+             dec_ok(cudaMalloc(&d->wts, sizeof(float) * top_k), "expert weights") &&
+             dec_ok(cudaMalloc(&d->ids, sizeof(int) * top_k), "expert ids") &&
+             dec_ok(cudaMalloc(&d->hbuf, sizeof(float) * static_cast<size_t>(top_k) * c.ffn_dim), "expert act") &&
+             dec_ok(cudaMalloc(&d->tbuf, sizeof(float) * static_cast<size_t>(top_k) * c.hidden), "expert out");
+    }
     if (ok && world > 1) {
         // the exchange region, 256-byte aligned parts; CUDA IPC maps whole allocations
         auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
@@ -1139,6 +1294,40 @@ void *tb_cuda_dec_create_tp(const tb_dec_config *c, int rank, int world)
     return tb::dec_create(k, rank, world);
 }
 
+void *tb_cuda_dec_create_moe(const tb_dec_config *c, int n_experts, int top_k)
+{
+    if (!c || n_experts < 1) return nullptr;
+    tb::DecConfig k{c->n_layers, c->hidden, c->n_heads, c->n_kv_heads, c->head_dim, c->ffn_dim,
+                    c->vocab, c->max_ctx, c->rope_base, c->norm_eps, c->quirks};
+    return tb::dec_create(k, 0, 1, n_experts, top_k);
+}
+
+int tb_cuda_dec_set_moe_layer(void *dec, int layer, const void *w_router, int router_qtype,
+                              const void *w_gate_up_exps, int gate_up_qtype, const void *w_down_exps,
+                              int down_qtype)
+{
+    tb::Decoder *d = static_cast<tb::Decoder *>(dec);
+    if (!d || !d->n_exp || layer < 0 || layer >= d->cfg.n_layers || !w_router || !w_gate_up_exps || !w_down_exps)
+        return 0;
+    for (int qt : {router_qtype, gate_up_qtype, down_qtype})
+        if (!tb::geom_of(qt).block_weights) return 0;
+    if (d->cfg.hidden % tb::geom_of(router_qtype).block_weights || d->cfg.hidden % tb::geom_of(gate_up_qtype).block_weights ||
+        d->cfg.ffn_dim % tb::geom_of(down_qtype).block_weights)
+        return 0;
+    tb::DecLayer &l = d->layers[layer];
+    l.wr = w_router;
+    l.r_qt = router_qtype;
+    l.wgu_e = w_gate_up_exps;
+    l.gue_qt = gate_up_qtype;
+    l.wd_e = w_down_exps;
+    l.de_qt = down_qtype;
+    if (d->gexec) {
+        cudaGraphExecDestroy(d->gexec);
+        d->gexec = nullptr;
+    }
+    return 1;
+}
+
 int tb_cuda_dec_tp_handle(void *dec, void *handle_out)
 {
     tb::Decoder *d = static_cast<tb::Decoder *>(dec);
@@ -1174,8 +1363,11 @@ int tb_cuda_dec_set_layer(void *dec, int layer, const tb_dec_layer *w)
 {
     tb::Decoder *d = static_cast<tb::Decoder *>(dec);
     if (!d || !w || layer < 0 || layer >= d->cfg.n_layers) return 0;
-    for (int qt : {w->qkv_qtype, w->o_qtype, w->gate_up_qtype, w->down_qtype})
+    for (int qt : {w->qkv_qtype, w->o_qtype})
         if (!tb::geom_of(qt).block_weights) return 0;
+    if (!d->n_exp)   // a routed decoder takes its FFN from tb_cuda_dec_set_moe_layer
+        for (int qt : {w->gate_up_qtype, w->down_qtype})
+            if (!tb::geom_of(qt).block_weights) return 0;
     tb::DecLayer &l = d->layers[layer];
     l.wqkv = w->w_qkv;
     l.qkv_qt = w->qkv_qtype;
@@ -1265,6 +1457,10 @@ int tb_cuda_dec_read(void *dec, int which, float *host, int n)
     case 3: src = d->att, size = static_cast<long long>(c.n_heads) * c.head_dim; break;
     case 4: src = d->gu, size = c.ffn_dim; break;
     case 5: src = d->logits, size = c.vocab; break;
+    case 6: src = d->rlog, size = d->n_exp; break;
+    case 7: src = d->wts, size = d->top_k; break;
+    case 8: src = reinterpret_cast<const float *>(d->ids), size = d->top_k; break;
+    case 9: src = d->hbuf, size = static_cast<long long>(d->top_k) * c.ffn_dim; break;
     default: return 0;
     }
     if (n > size) return 0;

@@ -76,15 +76,17 @@ __host__ __device__ constexpr int rec_stride(int words)
     return ((words + 3) / 4) % 2 ? ((words + 3) / 4) * 4 : ((words + 3) / 4 + 1) * 4;
 }
 
-// Copies a record of W words (W a multiple of 4) into registers, 16 bytes at a time.
+// Copies a record of W words (W a multiple of 4) into registers, 16 bytes at a
+// time, by ld.shared (called once per launch, after the barrier that completes
+// the records; the laundered address keeps the loads after it).
 template <int W>
 __device__ __forceinline__ void load_rec(uint32_t (&r)[W], const uint32_t *rec)
 {
     static_assert(W % 4 == 0, "records are whole 16-byte chunks");
-    const uint4 *p = reinterpret_cast<const uint4 *>(rec);
+    const uint32_t a = shared_after(static_cast<uint32_t>(__cvta_generic_to_shared(rec)));
 #pragma unroll
     for (int i = 0; i < W / 4; ++i) {
-        const uint4 v = p[i];
+        const uint4 v = lds_u128(a + 16 * i);
         r[4 * i] = v.x;
         r[4 * i + 1] = v.y;
         r[4 * i + 2] = v.z;
@@ -734,12 +736,12 @@ struct XRegs {
 
 __device__ __forceinline__ void load_f32(XRegs &L, const uint32_t *rec)
 {
-    const float4 *p = reinterpret_cast<const float4 *>(rec);
+    const uint32_t a = shared_after(static_cast<uint32_t>(__cvta_generic_to_shared(rec)));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float4 t = p[i];
-        L.a[2 * i] = f2(t.x, t.y);
-        L.a[2 * i + 1] = f2(t.z, t.w);
+        const uint4 t = lds_u128(a + 16 * i);
+        L.a[2 * i] = f2(__uint_as_float(t.x), __uint_as_float(t.y));
+        L.a[2 * i + 1] = f2(__uint_as_float(t.z), __uint_as_float(t.w));
     }
 }
 

@@ -34,6 +34,16 @@ struct MvFuse {
     uint32_t nsl = 0, ny = 0;
     float *ys[kMaxRanks] = {};
     unsigned long long *yctr[kMaxRanks] = {};
+    // Expert groups (MoE; unused when ng is 0): ng matvecs of M rows
+    // each in one launch, group g on its own CTAs.  Group g reads the
+    // matrix W + e * w_stride bytes, e = ids[g] read on the device after the
+    // dependency wait (ids produced by the previous kernel; e = g when ids is
+    // null; e >= n_experts sets the error word and skips the group), x + g *
+    // x_stride floats (0: one shared x) and writes y + g * y_stride floats.
+    uint32_t ng = 0, n_experts = 0;
+    const int *ids = nullptr;
+    unsigned long long w_stride = 0;
+    uint32_t x_stride = 0, y_stride = 0;
 };
 
 // Launch the matvec d_y[M] = dequant(W) @ d_x[K] on `st`.  Returns 1 when the

@@ -68,6 +68,11 @@ struct MvArgs {
     uint32_t nsl, ny;
     float *ys[kMaxRanks];
     unsigned long long *yctr[kMaxRanks];
+    // expert groups (MvFuse): ng > 0 splits the grid into ng equal runs of CTAs
+    const int *ids;
+    uint32_t ng, n_experts;
+    unsigned long long w_stride;
+    uint32_t x_stride, y_stride;
 };
 
 static constexpr uint32_t kFull = 0xFFFFFFFFu;
@@ -138,10 +143,10 @@ __device__ __forceinline__ void load32_cg(const float *p, uint32_t k0, uint32_t 
 //   RMSNorm: x * nw; the scalar 1/rms of layer1/tb_tensor.c:194-199 is applied
 //            to each slot's scale once the whole sum of squares is known.
 //   SwiGLU:  silu(x) * x2, silu(g) = g / (1 + e^-g) (layer4/tb_infer.c:130-135).
-__device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t g, float (&v)[32], float &ss)
+__device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t xoff, uint32_t g, float (&v)[32], float &ss)
 {
     const uint32_t k0 = 32 * g;
-    load32(a.x, k0, a.K, v);
+    load32(a.x + xoff, k0, a.K, v);
     if (a.nsl) {   // tensor-parallel input: the residual plus the ranks' partials
         for (uint32_t r = 0; r < a.nsl; ++r) {
             float t[32];
@@ -164,7 +169,7 @@ __device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t g, float 
         }
     } else if (a.xmode == MV_X_SWIGLU) {
         float u[32];
-        load32(a.x2, k0, a.K, u);
+        load32(a.x2 + xoff, k0, a.K, u);
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = (v[i] / (1.0f + expf(-v[i]))) * u[i];
     }
@@ -189,7 +194,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
 
-    const uint32_t G = gridDim.x, c = blockIdx.x;
+    uint32_t G = gridDim.x, c = blockIdx.x, grp = 0;
+    if (a.ng > 0) {   // expert groups: ng equal runs of CTAs, each a whole matvec
+        const uint32_t cpg = G / a.ng;
+        grp = c / cpg;
+        c -= grp * cpg;
+        G = cpg;
+    }
     const uint32_t ua = a.ymode == MV_Y_SWIGLU_PAIRS ? 2u : 1u;   // rows per output unit
     const uint32_t r_lo = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * c) / G);
     const uint32_t r_hi = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * (c + 1)) / G);
@@ -208,7 +219,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     const uint64_t pol = l2_evict_first_policy();
     // Tiles advance by TR rows and TR*row_bytes bytes; stage index and barrier
     // phase are carried along, so the loops below need no division.
-    const uintptr_t w_lo = reinterpret_cast<uintptr_t>(a.W) + static_cast<uintptr_t>(r_lo) * a.row_bytes;
+    uintptr_t w_lo = reinterpret_cast<uintptr_t>(a.W) + static_cast<uintptr_t>(r_lo) * a.row_bytes;
+    if (a.ng > 0 && !a.ids) w_lo += static_cast<uintptr_t>(grp) * a.w_stride;
     const uintptr_t tile_bytes = static_cast<uintptr_t>(a.tr) * a.row_bytes;
     auto issue = [&](uint32_t s, uint32_t t0, uintptr_t lo) {   // one thread of the producer warp
         const uint32_t nrows = min(a.tr, r_hi - t0);
@@ -241,6 +253,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (a.ng > 0 && a.ids) {   // the group's expert, chosen by the previous kernel (same for the whole CTA)
+        const int e = a.ids[grp];
+        if (e < 0 || static_cast<uint32_t>(e) >= a.n_experts) {
+            if (tid == 0) atomicExch(a.err, ERR_RUNTIME);
+            return;
+        }
+        w_lo += static_cast<uintptr_t>(e) * a.w_stride;
+    }
     if (!a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     if (a.nsl) {   // the ranks' partials of x have all arrived
         if (tid == 0) {
@@ -263,7 +283,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         const bool have = g < ngp;
         float v[32];
         if (have) {
-            load_x_group(a, g, v, ss);
+            load_x_group(a, grp * a.x_stride, g, v, ss);
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -308,6 +328,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         const uint32_t rows_ahead = a.nst * a.tr;
         const float *pb = part;
         const uint32_t pstride = a.tr * a.npart;
+        float *const yg = a.y + grp * a.y_stride;
         for (uint32_t it = 0; it < n_tiles; ++it) {
             const bool ok = mbar_wait_bounded(smem_u32(empty + s), par, a.err, a.wait_limit);
             if (!__all_sync(kFull, ok)) {
@@ -324,7 +345,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
                         gs += pg[j];
                         us += pu[j];
                     }
-                    a.y[(t0 + r) / 2] = (gs / (1.0f + expf(-gs))) * us;
+                    yg[(t0 + r) / 2] = (gs / (1.0f + expf(-gs))) * us;
                 }
             } else {
                 for (uint32_t r = lane; r < nrows; r += 32) {
@@ -334,7 +355,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
                     if (a.ny) {   // tensor-parallel output: this rank's partial to every rank
                         for (uint32_t p = 0; p < a.ny; ++p) a.ys[p][t0 + r] = acc;
                     } else {
-                        a.y[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
+                        yg[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
                     }
                 }
             }
@@ -450,7 +471,7 @@ static constexpr uint32_t kMaxStages = 8;
 
 struct Plan {
     const void *kern;
-    uint32_t M, K, sms, ymode;
+    uint32_t M, K, sms, ymode, ng;
     int dev;
     uint32_t nthr, grid, cs, phases, rpl, tr, rw, npart, nst, cap, ncw;
     size_t smem;
@@ -513,7 +534,14 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
                 row_bytes);
         return false;
     }
-    p.grid = p.M < p.sms ? p.M : p.sms;
+    if (p.ng > 0) {   // equal runs of CTAs per group, each at most one per output unit
+        const uint32_t units = p.ymode == MV_Y_SWIGLU_PAIRS ? p.M / 2 : p.M;
+        uint32_t cpg = p.sms / p.ng;
+        cpg = cpg < 1 ? 1 : (cpg > units ? units : cpg);
+        p.grid = p.ng * cpg;
+    } else {
+        p.grid = p.M < p.sms ? p.M : p.sms;
+    }
     return true;
 }
 
@@ -528,7 +556,7 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
     for (int i = 0; i < t_nplans; ++i) {
         const Plan &q = t_plans[i];
         if (q.kern == kp && q.M == a.M && q.K == a.K && q.dev == dev && q.sms == static_cast<uint32_t>(num_sms) &&
-            q.ymode == a.ymode) {
+            q.ymode == a.ymode && q.ng == a.ng) {
             p = &q;
             break;
         }
@@ -542,6 +570,7 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
         np.dev = dev;
         np.sms = static_cast<uint32_t>(num_sms);
         np.ymode = a.ymode;
+        np.ng = a.ng;
         if (!make_plan<D>(np, a.row_bytes)) return 0;
         if (getenv("TB_MV_VERBOSE"))
             fprintf(stderr,
@@ -617,6 +646,19 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
             a.ys[p] = fuse->ys[p];
             a.yctr[p] = fuse->yctr[p];
         }
+        if (fuse->ng > 0) {
+            // groups: no residual, no tensor-parallel exchange; an expert id
+            // read on the device cannot be prefetched ahead of the wait
+            if (fuse->ng > 1024 || fuse->res || fuse->nsl || fuse->ny || (fuse->ids && fuse->w_early) ||
+                (fuse->ids && !fuse->n_experts) || !fuse->w_stride)
+                return 0;
+            a.ng = fuse->ng;
+            a.n_experts = fuse->n_experts;
+            a.ids = fuse->ids;
+            a.w_stride = fuse->w_stride;
+            a.x_stride = fuse->x_stride;
+            a.y_stride = fuse->y_stride;
+        }
     }
     a.W = static_cast<const uint8_t *>(W);
     a.x = d_x;
@@ -630,8 +672,8 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
     a.wait_limit = wait_limit;
 
     const uintptr_t wa = reinterpret_cast<uintptr_t>(W);
-    const bool a16 = (wa & 15u) == 0 && (a.row_bytes & 15u) == 0;
-    const bool a4 = (wa & 3u) == 0 && (a.row_bytes & 3u) == 0;
+    const bool a16 = (wa & 15u) == 0 && (a.row_bytes & 15u) == 0 && (a.w_stride & 15u) == 0;
+    const bool a4 = (wa & 3u) == 0 && (a.row_bytes & 3u) == 0 && (a.w_stride & 3u) == 0;
     switch (qtype) {
     case QT_Q4_K: return a16 ? launch_dec<DecQ4K<true>>(a, num_sms, st) : launch_dec<DecQ4K<false>>(a, num_sms, st);
     case QT_Q5_K: return a16 ? launch_dec<DecQ5K<true>>(a, num_sms, st) : launch_dec<DecQ5K<false>>(a, num_sms, st);

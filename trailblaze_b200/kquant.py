@@ -90,6 +90,13 @@ class KQuantLib:
                                                v(d_x2), v(d_norm_w), ctypes.c_float(eps), v(d_res), ymode,
                                                v(stream))
 
+    def tb_cuda_matvec_experts_dev(self, W_dev: int, qtype: int, M: int, K: int, n_experts: int, d_ids: int,
+                                   n_sel: int, d_x: int, x_stride: int, d_y: int, y_stride: int, ymode: int = 0,
+                                   stream: int = 0) -> int:
+        v = lambda p: ctypes.c_void_p(p) if p else None  # noqa: E731
+        return self.L.tb_cuda_matvec_experts_dev(ctypes.c_void_p(W_dev), qtype, M, K, n_experts, v(d_ids), n_sel,
+                                                 v(d_x), x_stride, v(d_y), y_stride, ymode, v(stream))
+
     def tb_cuda_dequant_dev(self, W_dev: int, qtype: int, M: int, K: int, d_out: int, sem: int = 0,
                             stream: int = 0) -> int:
         return self.L.tb_cuda_dequant_dev(ctypes.c_void_p(W_dev), qtype, M, K, ctypes.c_void_p(d_out),
