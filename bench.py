@@ -241,6 +241,41 @@ def decode_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: i
             "order": "reference (RoPE before QK-norm, K rotated n_heads/n_kv_heads times)"}
 
 
+def moe_bench(ctx: int, n: int, e2e_tokens: int = 16):
+    """BASELINE config 4 on one GPU: batch-1 greedy decode of a random-init
+    Qwen3-30B-A3B-shape routed model (48 layers, hidden 2048, 32 q / 4 kv heads,
+    128 experts of FFN 768, top 8; Q4_K experts, Q6_K attention and output, fp32
+    router) with an N(0,1) fp32 KV prefix of ctx positions.  Each layer: q/k/v,
+    attention, o, router logits, top-k, the 8 selected experts' gate/up and down
+    as two expert-group matvecs (expert ids read on the device), combine."""
+    from trailblaze_b200.decoder import QWEN3_30B_A3B, synthetic_model
+    shape = QWEN3_30B_A3B
+    t0 = time.perf_counter()
+    dec = synthetic_model(shape, max_ctx=ctx + n + e2e_tokens + 8, ctx=ctx)
+    log(f"[bench] MoE model built in {time.perf_counter() - t0:.1f}s")
+    try:
+        dec.generate(1, ctx, 4, want_tokens=False)
+        _, ms = dec.generate(1, ctx, n, want_tokens=False)
+        tok_s = n / (ms * 1e-3)
+        bpt = shape.bytes_per_token(ctx + n // 2)
+        tok = 1
+        t1 = time.perf_counter()
+        for i in range(e2e_tokens):
+            tok = dec.step(tok, ctx + i)
+        e2e = e2e_tokens / (time.perf_counter() - t1)
+    finally:
+        dec.close()
+    hbm, kind = peaks()
+    return {"model": "qwen3-30b-a3b shape: 48 layers, hidden 2048, 32 q / 4 kv heads, head_dim 128, 128 experts "
+                     "(FFN 768) top 8, vocab 151936; Q4_K experts, Q6_K attention and output, fp32 router; fp32 KV",
+            "ctx": ctx, "tokens": n, "tok_per_s": round(tok_s, 2), "ms_per_token": round(ms / n, 4),
+            "parallelism": "one GPU (all 128 experts resident)",
+            "bytes_per_token": bpt, "GBps": round(bpt * tok_s / 1e9, 1),
+            "frac_of_hbm": round(bpt * tok_s / 1e9 / hbm, 4), "hbm_peak_kind": kind,
+            "e2e_tok_per_s": round(e2e, 2), "e2e_api": "tb_cuda_dec_step (blocking, token read back)",
+            "launches_per_token": 1 + 8 * shape.n_layers + 2}
+
+
 def tensor_peak():
     """Measured dense bf16 TFLOP/s (burst: each GEMM below is timed alone)."""
     try:
@@ -363,6 +398,9 @@ def main():
                     help="only the decode tok/s leg (its line's value is tok/s; profiling aid)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM leg (BASELINE config 5)")
     ap.add_argument("--prefill-only", action="store_true", help="only the prefill GEMM leg (profiling aid)")
+    ap.add_argument("--no-moe", action="store_true", help="skip the routed (MoE) decode leg (BASELINE config 4)")
+    ap.add_argument("--moe-only", action="store_true", help="only the MoE decode leg (profiling aid)")
+    ap.add_argument("--moe-ctx", type=int, default=2048)
     ap.add_argument("--decode-ctx", type=int, default=4096)
     ap.add_argument("--decode-tokens", type=int, default=64)
     args = ap.parse_args()
@@ -399,6 +437,17 @@ def main():
                               "clocks": clk.summary()}), flush=True)
         if world > 1:
             dist.destroy_process_group()
+        return
+
+    if args.moe_only:
+        with Clocks(local) as clk:
+            d = moe_bench(args.moe_ctx, args.decode_tokens)
+        if rank == 0:
+            print(json.dumps({"metric": "Qwen3-30B-A3B-shape MoE decode tok/s", "value": d["tok_per_s"],
+                              "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+                              "dtype": "fp32", "data": "synthetic (seeded torch generator on the device)",
+                              "config": {"workload": "MoE decode only (profiling aid)"}, "moe": d,
+                              "clocks": clk.summary()}), flush=True)
         return
 
     if args.decode_only:
@@ -567,6 +616,12 @@ def main():
                                   dist=dist if world > 1 else None)
         except Exception as e:  # noqa: BLE001 - the decode leg must not sink the sweep line
             decode = {"unavailable": f"{type(e).__name__}: {e}"}
+    moe = None
+    if world == 1 and not args.no_moe and not args.shape:
+        try:
+            moe = moe_bench(args.moe_ctx, args.decode_tokens)
+        except Exception as e:  # noqa: BLE001 - the MoE leg must not sink the sweep line
+            moe = {"unavailable": f"{type(e).__name__}: {e}"}
     prefill = None
     if world == 1 and not args.no_prefill and not args.shape:
         try:
@@ -604,6 +659,8 @@ def main():
         line["e2e"] = e2e
     if decode:
         line["decode"] = decode
+    if moe:
+        line["moe"] = moe
     if prefill:
         line["prefill"] = prefill
     if cpu:

@@ -30,22 +30,39 @@ class ModelShape:
     vocab: int
     rope_base: float = 1e6
     norm_eps: float = 1e-6
-    w_qt: int = Q.Q4_K       # q/k/v/o/gate/up and the token embedding
-    down_qt: int = Q.Q6_K    # ffn_down
+    w_qt: int = Q.Q4_K       # q/k/v/o/gate/up (routed: the experts' gate/up/down) and the token embedding
+    down_qt: int = Q.Q6_K    # ffn_down (dense)
     out_qt: int = Q.Q6_K     # output (lm head)
+    n_experts: int = 0       # > 0: every layer's FFN is routed (ffn_dim = one expert's width)
+    top_k: int = 0
+    attn_qt: int = -1        # q/k/v/o when it differs from w_qt
+    router_qt: int = Q.F32   # ffn_gate_inp
+
+    @property
+    def a_qt(self) -> int:
+        return self.w_qt if self.attn_qt < 0 else self.attn_qt
 
     def bytes_per_token(self, ctx: int) -> int:
-        """Algorithmic HBM bytes of one decode step at context ctx (weights once,
-        K and V of every layer over ctx positions, activations negligible)."""
+        """Algorithmic HBM bytes of one decode step at context ctx (weights once, the
+        selected experts only for a routed model, K and V of every layer over ctx
+        positions, activations negligible)."""
         H, NH, NK, HD, F = self.hidden, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn_dim
-        per_layer = (Q.row_bytes(self.w_qt, H) * ((NH + 2 * NK) * HD + 2 * F) +
-                     Q.row_bytes(self.w_qt, NH * HD) * H + Q.row_bytes(self.down_qt, F) * H +
-                     2 * NK * ctx * HD * 4)
+        attn = Q.row_bytes(self.a_qt, H) * (NH + 2 * NK) * HD + Q.row_bytes(self.a_qt, NH * HD) * H
+        if self.n_experts:
+            ffn = (Q.row_bytes(self.router_qt, H) * self.n_experts +
+                   self.top_k * (Q.row_bytes(self.w_qt, H) * 2 * F + Q.row_bytes(self.w_qt, F) * H))
+        else:
+            ffn = Q.row_bytes(self.w_qt, H) * 2 * F + Q.row_bytes(self.down_qt, F) * H
+        per_layer = attn + ffn + 2 * NK * ctx * HD * 4
         return self.n_layers * per_layer + Q.row_bytes(self.out_qt, H) * self.vocab + Q.row_bytes(self.w_qt, H)
 
 
 # Qwen3-8B shape (BASELINE config 3)
 QWEN3_8B = ModelShape(36, 4096, 32, 8, 128, 12288, 151936)
+# Qwen3-30B-A3B shape (BASELINE config 4): 128 experts of FFN 768, top 8; Q4_K
+# experts, Q6_K attention and output
+QWEN3_30B_A3B = ModelShape(48, 2048, 32, 4, 128, 768, 151936, w_qt=Q.Q4_K, out_qt=Q.Q6_K, n_experts=128, top_k=8,
+                           attn_qt=Q.Q6_K)
 
 
 class Decoder:
@@ -58,7 +75,11 @@ class Decoder:
         s = shape
         self.cfg = DecConfig(s.n_layers, s.hidden, s.n_heads, s.n_kv_heads, s.head_dim, s.ffn_dim, s.vocab,
                              max_ctx, s.rope_base, s.norm_eps, 1 if quirks else 0)
-        if world > 1:
+        if s.n_experts:
+            if world != 1:
+                raise ValueError("a routed decoder runs on one device")
+            self.d = self.L.tb_cuda_dec_create_moe(ctypes.byref(self.cfg), s.n_experts, s.top_k)
+        elif world > 1:
             self.d = self.L.tb_cuda_dec_create_tp(ctypes.byref(self.cfg), rank, world)
         else:
             self.d = self.L.tb_cuda_dec_create(ctypes.byref(self.cfg))
@@ -86,6 +107,13 @@ class Decoder:
         self._keep += [wqkv, wo, wgu, wd, attn_norm, ffn_norm, q_norm, k_norm]
         if self.L.tb_cuda_dec_set_layer(self.d, li, ctypes.byref(lw)) != 1:
             raise RuntimeError(f"tb_cuda_dec_set_layer({li}) failed")
+
+    def set_moe_layer(self, li: int, wr, r_qt, wgu_e, gue_qt, wd_e, de_qt):
+        """Router [E][H], expert (gate, up) row pairs [E][2F][H], expert down [E][H][F]."""
+        self._keep += [wr, wgu_e, wd_e]
+        if self.L.tb_cuda_dec_set_moe_layer(self.d, li, wr.data_ptr(), r_qt, wgu_e.data_ptr(), gue_qt,
+                                            wd_e.data_ptr(), de_qt) != 1:
+            raise RuntimeError(f"tb_cuda_dec_set_moe_layer({li}) failed")
 
     def set_head(self, emb, emb_qt, out_norm, w_out, out_qt):
         self._keep += [emb, out_norm, w_out]
@@ -155,12 +183,21 @@ def synthetic_model(shape: ModelShape, max_ctx: int, ctx: int, seed: int = 20261
         return 1.0 + 0.1 * torch.randn(n, device="cuda", generator=shared)
 
     for li in range(s.n_layers):
-        dec.set_layer(li,
-                      device_weights(s.w_qt, (NH + 2 * NK) * HD, H, gen), s.w_qt,
-                      device_weights(s.w_qt, H, NH * HD, gen), s.w_qt,
-                      device_weights(s.w_qt, 2 * F, H, gen), s.w_qt,
-                      device_weights(s.down_qt, H, F, gen), s.down_qt,
-                      norm(H), norm(H), norm(HD), norm(HD))
+        if s.n_experts:
+            E, aq = s.n_experts, s.a_qt
+            dec.set_layer(li, device_weights(aq, (NH + 2 * NK) * HD, H, gen), aq,
+                          device_weights(aq, H, NH * HD, gen), aq, None, aq, None, aq,
+                          norm(H), norm(H), norm(HD), norm(HD))
+            router = (0.05 * torch.randn(E * H, device="cuda", generator=gen)).view(torch.uint8)
+            dec.set_moe_layer(li, router, Q.F32, device_weights(s.w_qt, E * 2 * F, H, gen), s.w_qt,
+                              device_weights(s.w_qt, E * H, F, gen), s.w_qt)
+        else:
+            dec.set_layer(li,
+                          device_weights(s.w_qt, (NH + 2 * NK) * HD, H, gen), s.w_qt,
+                          device_weights(s.w_qt, H, NH * HD, gen), s.w_qt,
+                          device_weights(s.w_qt, 2 * F, H, gen), s.w_qt,
+                          device_weights(s.down_qt, H, F, gen), s.down_qt,
+                          norm(H), norm(H), norm(HD), norm(HD))
         if ctx > 0:
             for which in (0, 1):
                 dec.load_kv(li, which, torch.randn(NK, ctx, HD, device="cuda", generator=gen))
