@@ -250,6 +250,29 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     // sooner.  With w_early stage 0 is requested before the wait, so the
     // weight stream overlaps the previous kernel's tail (W is never written by
     // a kernel of the same chain in that case).
+    // A consumer's column slot and phase (row offset within a tile): pure
+    // functions of the shape, computed while the previous kernel finishes.
+    const bool active = !producer && tid < a.phases * a.cs;
+    const uint32_t cs = active ? tid % a.cs : 0;
+    const uint32_t ph = active ? tid / a.cs : 0;
+    const bool useful = active && ph < r_hi - r_lo;
+    Pos pos;
+    {
+        const uint32_t g0 = cs * D::GPL;                 // first group of the slot
+        const uint32_t ngrp = (a.K + 31) / 32;           // groups per row
+        if (a.block_weights == 256) {
+            pos.off = (g0 >> 3) * a.block_bytes;
+            pos.gi0 = g0 & 7u;
+        } else if (a.block_weights == 32) {
+            pos.off = g0 * a.block_bytes;
+            pos.gi0 = 0;
+        } else {
+            pos.off = g0 * 32u * a.block_bytes;
+            pos.gi0 = 0;
+        }
+        pos.ng = static_cast<int>(min(static_cast<uint32_t>(D::GPL), ngrp - min(ngrp, g0)));
+        pos.n = static_cast<int>(min(32u, a.K - min(a.K, 32u * (g0 + pos.ng - 1))));
+    }
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -395,30 +418,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     }
 
     // ---- consumers ----
-    const bool active = tid < a.phases * a.cs;
-    const uint32_t cs = active ? tid % a.cs : 0;
-    const uint32_t ph = active ? tid / a.cs : 0;
-    const uint32_t g0 = cs * D::GPL;                 // first group of the slot
-    const uint32_t ngrp = (a.K + 31) / 32;           // groups per row
-    Pos pos;
-    if (a.block_weights == 256) {
-        pos.off = (g0 >> 3) * a.block_bytes;
-        pos.gi0 = g0 & 7u;
-    } else if (a.block_weights == 32) {
-        pos.off = g0 * a.block_bytes;
-        pos.gi0 = 0;
-    } else {
-        pos.off = g0 * 32u * a.block_bytes;
-        pos.gi0 = 0;
-    }
-    pos.ng = static_cast<int>(min(static_cast<uint32_t>(D::GPL), ngrp - min(ngrp, g0)));
-    pos.n = static_cast<int>(min(32u, a.K - min(a.K, 32u * (g0 + pos.ng - 1))));
+    // (slot and phase were set up before the dependency wait; a thread whose
+    // phase is past this CTA's rows never decodes, so it loads no record)
     typename D::Lane lx;
-    D::load(lx, table + cs * D::REC);
-    if (a.xmode == MV_X_RMSNORM) {   // 1/sqrt(sum(x^2)/K + eps), summed in warp order
-        float t = 0.f;
-        for (uint32_t w = 0; w < nthr / 32; ++w) t += red[w];
-        lane_scale(lx, 1.0f / sqrtf(t / static_cast<float>(a.K) + a.eps));
+    if (useful) {
+        D::load(lx, table + cs * D::REC);
+        if (a.xmode == MV_X_RMSNORM) {   // 1/sqrt(sum(x^2)/K + eps), summed in warp order
+            float t = 0.f;
+            for (uint32_t w = 0; w < nthr / 32; ++w) t += red[w];
+            lane_scale(lx, 1.0f / sqrtf(t / static_cast<float>(a.K) + a.eps));
+        }
     }
     const uint32_t row_bytes32 = static_cast<uint32_t>(a.row_bytes);   // a tile's rows fit one stage
     const bool writer = active && (cs % a.rw) == 0;
@@ -437,7 +446,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
 #pragma unroll 2
         for (uint32_t i = 0; i < a.rpl; ++i) {
             const uint32_t rt = ph + i * a.phases;
-            const bool live = active && rt < nrows;
+            const bool live = useful && rt < nrows;
             float v = 0.f;
             if (live) v = D::row_dot(sbase + rt * row_bytes32, pos, lx);
 #pragma unroll
