@@ -216,7 +216,9 @@ int    tb_cuda_dec_set_head(void *dec, const void *tok_embd, int embd_qtype, con
 float *tb_cuda_dec_kv(void *dec, int layer, int which);
 /* Copies positions [p0, p0 + n) of a layer's K (which = 0) or V (1) cache in
  * (to_device = 1, e.g. a prefix) or out (0); the other side, `host`, is
- * [n_kv_heads][n][head_dim] fp32 in host or device memory.  Blocking.  1 = ok. */
+ * [n_kv_heads][n][head_dim] fp32 in host or device memory.  Blocking; the copy
+ * runs on the decoder's own (non-blocking) stream, so device memory written
+ * by work on another stream must be complete before the call.  1 = ok. */
 int    tb_cuda_dec_kv_copy(void *dec, int layer, int which, int p0, int n, float *host, int to_device);
 /* One token at position pos: *next_token = greedy argmax; logits_host (may be
  * NULL) receives the vocab logits.  Blocking.  1 = ok. */
@@ -264,7 +266,10 @@ int    tb_cuda_dec_tp_connect(void *dec, const void *handles);
  * 753-850 and the router of tb_infer.c:351-374).  cfg->ffn_dim is the expert
  * FFN width F; every layer routes rmsnorm(x2) through its router to the top_k
  * of n_experts (<= 256) experts, weights = softmax renormalised over the
- * selected ones, x = x2 + sum of weight * expert SwiGLU FFN.  One device. */
+ * selected ones, x = x2 + sum of weight * expert SwiGLU FFN.  The experts are
+ * ranked by probability, equal probabilities by lower index (the reference's
+ * replace-the-minimum scan picks the same set except among exactly equal
+ * probabilities).  One device. */
 void  *tb_cuda_dec_create_moe(const tb_dec_config *cfg, int n_experts, int top_k);
 /* A routed layer's FFN tensors (its attention tensors and norms come from
  * tb_cuda_dec_set_layer, whose w_gate_up / w_down are then ignored):

@@ -122,8 +122,13 @@ class Decoder:
             raise RuntimeError("tb_cuda_dec_set_head failed")
 
     def load_kv(self, li: int, which: int, t) -> None:
-        """t: [n_kv_heads][n][head_dim] fp32 (host or device tensor), loaded at positions [0, n)."""
+        """t: [n_kv_heads][n][head_dim] fp32 (host or device tensor), loaded at positions [0, n).
+        The library copies on its own stream, which does not wait for torch's: a device
+        tensor's producer is synchronised first."""
+        import torch
         t = t.contiguous()
+        if t.is_cuda:
+            torch.cuda.current_stream(t.device).synchronize()
         fp = ctypes.cast(ctypes.c_void_p(t.data_ptr()), ctypes.POINTER(ctypes.c_float))
         if self.L.tb_cuda_dec_kv_copy(self.d, li, which, 0, t.shape[1], fp, 1) != 1:
             raise RuntimeError("tb_cuda_dec_kv_copy failed")
