@@ -203,10 +203,13 @@ __device__ __forceinline__ void load_probs(const float *row, float (&p)[R2])
 // grid (NK, nchunk), kAttnThreads threads, one CTA per SM; R2 = query heads
 // per KV head rounded up to a power of two (1, 2, 4 or 8).
 //
-// After the programmatic-dependency wait this token's q (and, in the chunk
-// that owns pos, k and v) and the QK-norm weights are requested first, then
-// thread 0 starts the ring, so q is rotated and normed while the cache rows
-// stream in (row pos, this step's, is never read from the cache).  Warp w
+// Before the programmatic-dependency wait thread 0 starts the ring on the
+// cached rows (written by earlier steps, and pos by the previous step's
+// argmax: the q/k/v matvec ahead of this kernel lets it start only after its
+// own dependency wait, so all of those are complete).  After the wait this
+// token's q (and, in the chunk that owns pos, k and v) is loaded, rotated and
+// normed while the rows stream in (row pos, this step's, is never read from
+// the cache).  Warp w
 // takes positions kPW w .. kPW w + kPW - 1 of every block:
 //   scores   (K loads) each lane forms the partial dot products of its four
 //            dimensions for the warp's (position, head) items; one transposed
@@ -222,7 +225,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
 {
     extern __shared__ __align__(128) uint8_t smraw[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nwarp = kAttnThreads / 32;
@@ -257,18 +259,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
     float *vcache = a.vc + static_cast<size_t>(kh) * a.max_ctx * kHD;
     const uint64_t pol = l2_evict_first_policy();
 
-    // ---- this token's q (and, in the owner chunk, k and v) and the QK-norm
-    // weights, requested first: behind the ring's copies they would arrive last ----
-    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 qv = z4, kn = z4, vn = z4, qnv = z4, knv = z4;
-    if (a.qn && tid < kHD / 4) qnv = __ldg(reinterpret_cast<const float4 *>(a.qn) + tid);
-    if (owner && a.kn && tid < kHD / 4) knv = __ldg(reinterpret_cast<const float4 *>(a.kn) + tid);
-    if (tid < rep * (kHD / 4)) qv = __ldcg(reinterpret_cast<const float4 *>(a.qkv + kh * rep * kHD) + tid);
-    if (owner && tid < kHD / 4) {
-        kn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + kh) * kHD) + tid);
-        vn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK + kh) * kHD) + tid);
-    }
-
     // ---- the ring: load j (the K rows of block j for j < nb, else the V rows
     // of block j - nb) into stage j % kNS ----
     auto issue = [&](int j, int s) {   // one thread
@@ -290,6 +280,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         }
         fence_mbar_init();
         for (int u = 0; u < min(nl, kNS); ++u) issue(u, u);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // ---- this token's q (and, in the owner chunk, k and v) and the QK-norm weights ----
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 qv = z4, kn = z4, vn = z4, qnv = z4, knv = z4;
+    if (a.qn && tid < kHD / 4) qnv = __ldg(reinterpret_cast<const float4 *>(a.qn) + tid);
+    if (owner && a.kn && tid < kHD / 4) knv = __ldg(reinterpret_cast<const float4 *>(a.kn) + tid);
+    if (tid < rep * (kHD / 4)) qv = __ldcg(reinterpret_cast<const float4 *>(a.qkv + kh * rep * kHD) + tid);
+    if (owner && tid < kHD / 4) {
+        kn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + kh) * kHD) + tid);
+        vn = __ldcg(reinterpret_cast<const float4 *>(a.qkv + (a.NH + a.NK + kh) * kHD) + tid);
     }
 
     // ---- q and k normed and rotated in shared memory ----

@@ -239,11 +239,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         }
         fence_mbar_init();
     }
-    // Programmatic dependent launch: the next kernel of the stream may be
-    // scheduled from here on (it waits in its own griddepcontrol.wait), and
-    // nothing below touches global memory before the previous kernel has
-    // finished and its writes are visible.  Both are no-ops without the launch
-    // attribute.
+    // Programmatic dependent launch: nothing below touches global memory other
+    // than W before the previous kernel has finished and its writes are
+    // visible.  Both instructions are no-ops without the launch attribute.
     // Stage 0 is requested before the prologue and the other stages after it:
     // the prologue's x loads would otherwise queue behind NST stages of weight
     // misses (up to ~200 KB per SM) and the consumers could not start any
@@ -273,9 +271,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         pos.ng = static_cast<int>(min(static_cast<uint32_t>(D::GPL), ngrp - min(ngrp, g0)));
         pos.n = static_cast<int>(min(32u, a.K - min(a.K, 32u * (g0 + pos.ng - 1))));
     }
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    // The next kernel may start once every CTA is past the wait: what the
+    // kernels before this one wrote is then complete, so the next one may read
+    // it ahead of its own wait (the decode step's attention streams its cached
+    // rows that way).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (a.ng > 0 && a.ids) {   // the group's expert, chosen by the previous kernel (same for the whole CTA)
         const int e = a.ids[grp];
         if (e < 0 || static_cast<uint32_t>(e) >= a.n_experts) {
