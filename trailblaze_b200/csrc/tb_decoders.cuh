@@ -361,51 +361,60 @@ struct DecQ4K {
 };
 
 // ---- Q5_K — 176 B: d,dmin @0, scales @4, qh @16, qs @48 (tb_gguf_dequant.cu:158-191) ----
-// q = nibble | qh_bit<<4; the high bit is masked as 0x10 per byte (already x16).
+// q = nibble | qh_bit<<4, weight i's nibble in qs byte i/2 (low nibble for
+// even i) and its high bit at qh byte i/8, bit i%8.  Slot = half a block (4
+// groups).  Each group is decoded in the qh bits' order (PK_ONE32: byte b of
+// word j = weight 8b + j): a 4x4 byte transpose of the group's four qs words
+// (six byte permutes) puts qs byte 4b + k into byte b of word k, so the nibble
+// and the high bit of one weight share a byte lane and one dp4a pair covers
+// four weights.
 template <bool A16>
 struct DecQ5K {
-    using LY = IntLayout<2, 2, 3>;
-    static constexpr int GPL = 2;
+    using LY = IntLayout<4, 1, 3>;
+    static constexpr int GPL = 4;
     static constexpr bool kInt = true;
     static constexpr int REC = LY::STRIDE;
     using Lane = LaneInt<LY>;
     __device__ static void prep(const GroupX &g, int E, bool fin, int j, uint32_t *rec)
     {
         PackedX a, b;
-        prep_digits<LY, PK_NIB, PK_ONE32>(g, E, fin, j, rec, a, b);
+        prep_digits<LY, PK_ONE32, -1>(g, E, fin, j, rec, a, b);
         int sh, sl;
         psums<0, 8>(a, sh, sl);
-        put_planes_slot<2>(256 * sh + sl, j, rec + LY::CST);
+        put_planes_slot<4>(256 * sh + sl, j, rec + LY::CST);
     }
     __device__ static void load(Lane &L, const uint32_t *rec) { load_rec(L.r, rec); }
     __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<A16> W(row + p.off);
         const uint4 h = W.q4(0);
-        const uint32_t upper = p.gi0 >> 2, q0 = p.gi0 & 3u;
+        const uint32_t upper = p.gi0 >> 2;
         const uint32_t sw = sm_half(h.y, h.w, upper, false), mw = sm_half(h.z, h.w, upper, true);
+        constexpr uint32_t N = 0x0F0F0F0Fu, B = 0x10101010u;
         int th = 0, tl = 0;
 #pragma unroll
         for (int g = 0; g < GPL; ++g) {
             const uint32_t gi = p.gi0 + g;
             const uint4 q = W.q4(48 + 16 * gi);
             const uint32_t hb = W(4 + gi);
+            const uint32_t t0 = __byte_perm(q.x, q.y, 0x5140u), t1 = __byte_perm(q.z, q.w, 0x5140u);
+            const uint32_t t2 = __byte_perm(q.x, q.y, 0x7362u), t3 = __byte_perm(q.z, q.w, 0x7362u);
+            const uint32_t c0 = __byte_perm(t0, t1, 0x5410u), c1 = __byte_perm(t0, t1, 0x7632u);
+            const uint32_t c2 = __byte_perm(t2, t3, 0x5410u), c3 = __byte_perm(t2, t3, 0x7632u);
             int ah = 0, al = 0;
-            nib4<LY>(ah, al, q, x.r, g);
-            mac_u<LY>(ah, al, (hb << 4) & 0x10101010u, x.r, g, 1, 0);
-            mac_u<LY>(ah, al, (hb << 3) & 0x10101010u, x.r, g, 1, 1);
-            mac_u<LY>(ah, al, (hb << 2) & 0x10101010u, x.r, g, 1, 2);
-            mac_u<LY>(ah, al, (hb << 1) & 0x10101010u, x.r, g, 1, 3);
-            mac_u<LY>(ah, al, hb & 0x10101010u, x.r, g, 1, 4);
-            mac_u<LY>(ah, al, (hb >> 1) & 0x10101010u, x.r, g, 1, 5);
-            mac_u<LY>(ah, al, (hb >> 2) & 0x10101010u, x.r, g, 1, 6);
-            mac_u<LY>(ah, al, (hb >> 3) & 0x10101010u, x.r, g, 1, 7);
-            const int sc = ubyte(sw, static_cast<int>(q0) + g);
+            mac_u<LY>(ah, al, (c0 & N) | ((hb << 4) & B), x.r, g, 0, 0);
+            mac_u<LY>(ah, al, ((c0 >> 4) & N) | ((hb << 3) & B), x.r, g, 0, 1);
+            mac_u<LY>(ah, al, (c1 & N) | ((hb << 2) & B), x.r, g, 0, 2);
+            mac_u<LY>(ah, al, ((c1 >> 4) & N) | ((hb << 1) & B), x.r, g, 0, 3);
+            mac_u<LY>(ah, al, (c2 & N) | (hb & B), x.r, g, 0, 4);
+            mac_u<LY>(ah, al, ((c2 >> 4) & N) | ((hb >> 1) & B), x.r, g, 0, 5);
+            mac_u<LY>(ah, al, (c3 & N) | ((hb >> 2) & B), x.r, g, 0, 6);
+            mac_u<LY>(ah, al, ((c3 >> 4) & N) | ((hb >> 3) & B), x.r, g, 0, 7);
+            const int sc = ubyte(sw, g);
             th = sc * ah + th;
             tl = sc * al + tl;
         }
-        // the slot's two mins moved to bytes 0..1; the planes are zero in bytes 2..3
-        const int mn = dot_planes(mw >> (8u * q0), x.cstu(0), x.cstu(1), x.cstu(2));
+        const int mn = dot_planes(mw, x.cstu(0), x.cstu(1), x.cstu(2));
         const float2 dd = h2f2_ref(h.x);
         return x.sx() * fmaf(dd.x, hl_value(th, tl), -dd.y * static_cast<float>(mn));
     }
