@@ -143,10 +143,11 @@ def test_decode_step_matches_oracle(kq, quirks):
         dec.close()
 
 
-@pytest.mark.parametrize("nh,nk", [(32, 8), (28, 4), (12, 4), (4, 4)])
+@pytest.mark.parametrize("nh,nk", [(32, 8), (28, 4), (32, 4), (12, 4), (4, 4)])
 def test_decode_long_context(kq, nh, nk):
     """Chunks of several streamed blocks of cached positions, query heads per
-    KV head 4, 7, 3 and 1 (padded to 4, 8, 4 and 1 in the score reduction)."""
+    KV head 4, 7, 8 (the Qwen3-30B-A3B shape), 3 and 1 (padded to 4, 8, 8, 4
+    and 1 in the score reduction)."""
     m = make_model(n_layers=1, hidden=256, nh=nh, nk=nk, ffn=256, vocab=300, max_ctx=4736, seed=nh + nk)
     dec, orc = GpuDecoder(kq, m, False), DecodeOracle(m, quirks=False)
     try:

@@ -25,6 +25,7 @@
 //     in a fixed order, writes y and refills the stage with the tile NST
 //     ahead.  The summation order never depends on timing, so results are
 //     run-to-run deterministic.  Every wait is bounded.
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 
@@ -98,15 +99,18 @@ __host__ __device__ inline MvSmem mv_smem(uint32_t nst, uint32_t cs, uint32_t re
     return s;
 }
 
-// Elements [k0, k0 + 32) of p (zeros past K): eight 16-byte loads when the
-// whole run is inside K and p is 16-byte aligned.
-__device__ __forceinline__ void load32(const float *p, uint32_t k0, uint32_t K, float (&v)[32])
+// Elements [k0, k0 + N) of p (zeros past K): N/4 16-byte loads when the whole
+// run is inside K and p is 16-byte aligned.  CG: through L2 (ld.global.cg),
+// for slots written by peers over NVLink during the launch chain, which no
+// non-coherent cached copy may serve.
+template <int N, bool CG = false>
+__device__ __forceinline__ void loadn(const float *p, uint32_t k0, uint32_t K, float (&v)[N])
 {
-    if (k0 + 32 <= K && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+    if (k0 + N <= K && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
         const float4 *q = reinterpret_cast<const float4 *>(p + k0);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 t = __ldg(q + i);
+        for (int i = 0; i < N / 4; ++i) {
+            const float4 t = CG ? __ldcg(q + i) : __ldg(q + i);
             v[4 * i] = t.x;
             v[4 * i + 1] = t.y;
             v[4 * i + 2] = t.z;
@@ -114,64 +118,44 @@ __device__ __forceinline__ void load32(const float *p, uint32_t k0, uint32_t K, 
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = k0 + i < K ? __ldg(p + k0 + i) : 0.f;
+        for (int i = 0; i < N; ++i) v[i] = k0 + i < K ? (CG ? __ldcg(p + k0 + i) : __ldg(p + k0 + i)) : 0.f;
     }
 }
 
-// load32 through L2 (ld.global.cg): the slots are written by peers over NVLink
-// during the launch chain, so no non-coherent cached copy may be used.
-__device__ __forceinline__ void load32_cg(const float *p, uint32_t k0, uint32_t K, float (&v)[32])
-{
-    if (k0 + 32 <= K && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
-        const float4 *q = reinterpret_cast<const float4 *>(p + k0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 t = __ldcg(q + i);
-            v[4 * i] = t.x;
-            v[4 * i + 1] = t.y;
-            v[4 * i + 2] = t.z;
-            v[4 * i + 3] = t.w;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = k0 + i < K ? __ldcg(p + k0 + i) : 0.f;
-    }
-}
-
-// The 32 activations of group g (zeros past K) after the fused input
-// transform, and ss += the sum of the squares of the raw x.
+// Activations [k0, k0 + N) (zeros past K) after the fused input transform,
+// and ss += the sum of the squares of the raw x.
 //   RMSNorm: x * nw; the scalar 1/rms of layer1/tb_tensor.c:194-199 is applied
 //            to each slot's scale once the whole sum of squares is known.
 //   SwiGLU:  silu(x) * x2, silu(g) = g / (1 + e^-g) (layer4/tb_infer.c:130-135).
-__device__ __forceinline__ void load_x_group(const MvArgs &a, uint32_t xoff, uint32_t g, float (&v)[32], float &ss)
+template <int N>
+__device__ __forceinline__ void load_x_part(const MvArgs &a, uint32_t xoff, uint32_t k0, float (&v)[N], float &ss)
 {
-    const uint32_t k0 = 32 * g;
-    load32(a.x + xoff, k0, a.K, v);
+    loadn<N>(a.x + xoff, k0, a.K, v);
     if (a.nsl) {   // tensor-parallel input: the residual plus the ranks' partials
         for (uint32_t r = 0; r < a.nsl; ++r) {
-            float t[32];
-            load32_cg(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, t);
+            float t[N];
+            loadn<N, true>(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, t);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += t[i];
+            for (int i = 0; i < N; ++i) v[i] += t[i];
         }
         if (a.xout && blockIdx.x == 0)
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 0; i < N; ++i)
                 if (k0 + i < a.K) a.xout[k0 + i] = v[i];
     }
     if (a.xmode == MV_X_RMSNORM) {
-        float w[32];
-        load32(a.nw, k0, a.K, w);
+        float w[N];
+        loadn<N>(a.nw, k0, a.K, w);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < N; ++i) {
             ss = fmaf(v[i], v[i], ss);
             v[i] *= w[i];
         }
     } else if (a.xmode == MV_X_SWIGLU) {
-        float u[32];
-        load32(a.x2 + xoff, k0, a.K, u);
+        float u[N];
+        loadn<N>(a.x2 + xoff, k0, a.K, u);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = (v[i] / (1.0f + expf(-v[i]))) * u[i];
+        for (int i = 0; i < N; ++i) v[i] = (v[i] / (1.0f + expf(-v[i]))) * u[i];
     }
 }
 
@@ -299,38 +283,108 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     }
 
     // ---- prologue: x -> one record per column slot ----
-    // Thread g handles group g (then g + nthr, ...).  The GPL groups of a slot
-    // are neighbouring lanes of one warp, so the slot's largest |x| is a shuffle.
     float ss = 0.f;   // RMSNorm: this thread's share of sum(x^2)
     float *red = reinterpret_cast<float *>(smem + L.red);
-    for (uint32_t base = 0; base < ngp; base += nthr) {   // same trip count in every thread
-        const uint32_t g = base + tid;
-        const bool have = g < ngp;
-        float v[32];
-        if (have) {
-            load_x_group(a, grp * a.x_stride, g, v, ss);
-        } else {
+    // Integer decoders, when the digits fit ring stages 1.. (stage 0 may be in
+    // flight; the others are requested only after the prologue): two passes.
+    // Pass 1, all threads, 8 activations each ("quarters" of a group): load,
+    // input transform, the slot's largest |x| by a shuffle over its 4*GPL
+    // neighbouring lanes, the 16-bit digits X into shared memory, the slot's
+    // exponent.  Pass 2, one thread per group: the type's record from its 32 X.
+    // Otherwise one pass, one thread per group.
+    const uint32_t xq_bytes = ngp * 64u, xe_off = xq_bytes;
+    bool split = false;
+    if constexpr (D::kInt) split = a.nst >= 2 && (a.nst - 1ull) * a.cap >= xq_bytes + 4ull * a.cs;
+    if (split) {
+        uint8_t *xq = ring + a.cap;                          // [ngp * 4][8] int16, then [cs] int32 exponents
+        int *xe = reinterpret_cast<int *>(xq + xe_off);
+        constexpr uint32_t QPS = 4u * D::GPL;                // quarters per slot (a power of two <= 32)
+        const uint32_t nq = 4 * ngp;
+        for (uint32_t base = 0; base < nq; base += nthr) {   // same trip count in every thread
+            const uint32_t q = base + tid;
+            const bool have = q < nq;
+            float v[8];
+            if (have) {
+                load_x_part<8>(a, grp * a.x_stride, 8 * q, v, ss);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-        }
-        uint32_t *rec = table + (g / D::GPL) * D::REC;
-        if constexpr (D::kInt) {
+                for (int i = 0; i < 8; ++i) v[i] = 0.f;
+            }
             // largest |x| as an integer max of the magnitude bits: an inf or NaN
             // gives bits >= 0x7F800000, which marks the slot non-finite
             uint32_t mb = 0;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+            for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
 #pragma unroll
-            for (int o = 1; o < D::GPL; o <<= 1) mb = max(mb, __shfl_xor_sync(kFull, mb, o));
+            for (uint32_t o = 1; o < QPS; o <<= 1) mb = max(mb, __shfl_xor_sync(kFull, mb, o));
             if (have) {
                 const bool sfin = mb < 0x7F800000u;
                 const int E = slot_exponent(sfin ? __uint_as_float(mb) : 0.f);
-                GroupX gx;
-                quantize_group(v, E, gx);
-                D::prep(gx, E, sfin, static_cast<int>(g % D::GPL), rec);
+                const float up = exp2i(14 - E);
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    int q0, q1;
+                    asm("{\n\t.reg .s16 t;\n\tcvt.rni.sat.s16.f32 t, %1;\n\tcvt.s32.s16 %0, t;\n\t}"
+                        : "=r"(q0) : "f"(v[2 * i] * up));
+                    asm("{\n\t.reg .s16 t;\n\tcvt.rni.sat.s16.f32 t, %1;\n\tcvt.s32.s16 %0, t;\n\t}"
+                        : "=r"(q1) : "f"(v[2 * i + 1] * up));
+                    w[i] = __byte_perm(static_cast<uint32_t>(q0), static_cast<uint32_t>(q1), 0x5410u);
+                }
+                reinterpret_cast<uint4 *>(xq)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+                if (q % QPS == 0) xe[q / QPS] = sfin ? E : INT32_MIN;
             }
-        } else {
-            if (have) prep_float(v, rec);
+        }
+        __syncthreads();
+        for (uint32_t g = tid; g < ngp; g += nthr) {
+            GroupX gx;
+            const uint4 *src = reinterpret_cast<const uint4 *>(xq) + 4 * g;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 t = src[c];
+                const uint32_t tw[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    gx.X[8 * c + 2 * i] = static_cast<int>(static_cast<int16_t>(tw[i] & 0xFFFFu));
+                    gx.X[8 * c + 2 * i + 1] = static_cast<int>(tw[i]) >> 16;
+                }
+            }
+            const int e = xe[g / D::GPL];
+            const bool sfin = e != INT32_MIN;
+            if constexpr (D::kInt)
+                D::prep(gx, sfin ? e : 0, sfin, static_cast<int>(g % D::GPL), table + (g / D::GPL) * D::REC);
+        }
+    } else {
+        // Thread g handles group g (then g + nthr, ...).  The GPL groups of a
+        // slot are neighbouring lanes of one warp, so the slot's largest |x| is
+        // a shuffle.
+        for (uint32_t base = 0; base < ngp; base += nthr) {   // same trip count in every thread
+            const uint32_t g = base + tid;
+            const bool have = g < ngp;
+            float v[32];
+            if (have) {
+                load_x_part<32>(a, grp * a.x_stride, 32 * g, v, ss);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            }
+            uint32_t *rec = table + (g / D::GPL) * D::REC;
+            if constexpr (D::kInt) {
+                uint32_t mb = 0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+#pragma unroll
+                for (int o = 1; o < D::GPL; o <<= 1) mb = max(mb, __shfl_xor_sync(kFull, mb, o));
+                if (have) {
+                    const bool sfin = mb < 0x7F800000u;
+                    const int E = slot_exponent(sfin ? __uint_as_float(mb) : 0.f);
+                    GroupX gx;
+                    quantize_group(v, E, gx);
+                    D::prep(gx, E, sfin, static_cast<int>(g % D::GPL), rec);
+                }
+            } else {
+                if (have) prep_float(v, rec);
+            }
         }
     }
     if (a.xmode == MV_X_RMSNORM) {
@@ -342,6 +396,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
 
     if (producer && lane == 0) {
         const uint32_t pre = min(a.nst, n_tiles);
+        fence_proxy_async_smem();   // stages 1.. may have held the prologue's digits (generic proxy)
         for (uint32_t it = 1; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
     }
     if (producer) {
