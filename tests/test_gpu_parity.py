@@ -265,6 +265,23 @@ def test_blocking_abi_and_upload_x(kq, oracle):
     kq.tb_cuda_free_tensor(0)
 
 
+def test_blocking_abi_large_y(kq):
+    """A large y (70000 rows) through the blocking ABI: the same bits as the
+    stream-ordered entry point, twice in a row."""
+    qt, M, K = Q.Q4_K, 70000, 256
+    W = synth.weights(qt, M, K, seed=4, tensor=qt)
+    d = kq.tb_cuda_upload_tensor(W)
+    assert d
+    try:
+        for call in range(2):
+            x = synth.activations(K, seed=5 + call)
+            out = np.full(M, np.nan, dtype=np.float32)
+            assert kq.tb_cuda_matvec_device(d, qt, M, K, x, out) == 1
+            np.testing.assert_array_equal(bits(out), bits(gpu_matvec(kq, qt, d, M, K, x)))
+    finally:
+        kq.tb_cuda_free_tensor(d)
+
+
 def test_abi_rejects_bad_arguments(kq):
     W = synth.weights(Q.Q4_K, 4, 512, seed=1)
     d = kq.tb_cuda_upload_tensor(W)
