@@ -2,8 +2,8 @@
 reference's own CUDA kernels, always through the C ABI.
 
 Tolerances (north star): dequantisation bit-exact; matvec relative L2 error
-<= 1e-3 against the fp64-accumulated oracle.  The float-path types (Q3_K,
-F32, F16, BF16) accumulate in fp32 (observed ~1e-7); the integer-path types
+<= 1e-3 against the fp64-accumulated oracle.  The float-path types (F32,
+F16, BF16) accumulate in fp32 (observed ~1e-7); the integer-path types
 round x to 2^-15 of each column slot's largest |x| and are exact after that
 (observed 2e-5 to 4e-5 over many rows of Gaussian x, up to ~1e-4 for a
 single short row, whose rounding errors do not average out).  STRICT = 3e-4
