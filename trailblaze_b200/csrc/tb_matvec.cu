@@ -504,12 +504,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
         for (uint32_t i = 0; i < a.rpl; ++i) {
             const uint32_t rt = ph + i * a.phases;
             const bool live = useful && rt < nrows;
+            if (!__any_sync(kFull, live)) continue;   // the warp has no row here (uniform)
             float v = 0.f;
             if (live) v = D::row_dot(sbase + rt * row_bytes32, pos, lx);
-#pragma unroll
-            for (uint32_t o = 1; o < 8; o <<= 1)
-                if (o < a.rw) v += __shfl_xor_sync(kFull, v, o);
-            if (writer && rt < nrows) pb[rt * a.npart + part_col] = v;
+            // the row's slot sums over rw neighbouring lanes, without branches
+            const float t1 = __shfl_xor_sync(kFull, v, 1);
+            v = a.rw > 1 ? v + t1 : v;
+            const float t2 = __shfl_xor_sync(kFull, v, 2);
+            v = a.rw > 2 ? v + t2 : v;
+            const float t4 = __shfl_xor_sync(kFull, v, 4);
+            v = a.rw > 4 ? v + t4 : v;
+            if (writer && live) pb[rt * a.npart + part_col] = v;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(empty + s));
