@@ -47,7 +47,7 @@ struct QgArgs {
     const uint8_t *W;
     float *C;
     int *err;
-    uint32_t N, K, T, ksplit, k_per_split, row_bytes, nst, nraw, tcols, bw;
+    uint32_t N, K, T, ksplit, row_bytes, nst, nraw, tcols, bw;
     uint32_t nacc;   // independent accumulators (consecutive K-16 steps rotate over them)
     uint32_t wait_limit;
 };
@@ -251,8 +251,12 @@ __global__ void __launch_bounds__(kGThreads, 2) k_qgemm(const __grid_constant__ 
 
     const uint32_t n0 = blockIdx.x * kGM;                      // first W row
     const uint32_t split = blockIdx.y;
-    const uint32_t k_lo = split * a.k_per_split;
-    const uint32_t nk = a.k_per_split / kGK;                   // stages of this CTA
+    // this CTA's super-blocks: an even share of the K / 256, the ksplit parts
+    // differing by at most one super-block
+    const uint32_t nsb_all = a.K / 256;
+    const uint32_t kb0 = (split * nsb_all) / a.ksplit, kb1 = ((split + 1) * nsb_all) / a.ksplit;
+    const uint32_t k_lo = kb0 * 256;
+    const uint32_t nk = (kb1 - kb0) * (256 / kGK);               // stages of this CTA
     constexpr Geom geo = geom_of(QT);
 
     if (tid == 0) {
@@ -278,7 +282,7 @@ __global__ void __launch_bounds__(kGThreads, 2) k_qgemm(const __grid_constant__ 
     tc_fence_after();
     const uint32_t tbase = *tslot;
 
-    const uint32_t nsb = a.k_per_split / 256, kb0 = k_lo / 256;   // super-blocks of this CTA
+    const uint32_t nsb = kb1 - kb0;                             // super-blocks of this CTA
     if (warp == 10) {
         // ---- W's raw super-blocks by TMA, nraw ahead; a slot is refilled once
         // the dequant warps are done with it (whole warp, one lane issues) ----
@@ -517,12 +521,23 @@ int qg_launch(const void *W, int qtype, int N, int K, const void *A, int T, floa
         if (qg_smem_bytes(a.T, nst, nraw) > cap) return 0;
     }
     const uint32_t tiles = static_cast<uint32_t>(N / kGM);
+    // K parts per row tile.  Few tokens (T <= 32, a weight stream): as many
+    // parts as keep the grid within one wave of CTA slots, each at least two
+    // super-blocks (parts may differ by one super-block).  More tokens: the
+    // partial sums' atomic adds grow with T, so parts only double while the
+    // grid stays within one wave (measured: the finer split was no faster at
+    // T = 128 and 12288 x 4096 T = 16 went from 55.5 to 43.6 us).
+    const uint32_t slots = static_cast<uint32_t>(num_sms) * per_sm;
+    const uint32_t nsb_all = static_cast<uint32_t>(K) / 256;
     uint32_t ks = 1;
-    while (tiles * ks * 2 <= static_cast<uint32_t>(num_sms) * per_sm && (K / (ks * 2)) % 256 == 0 &&
-           K / (ks * 2) >= 512)
-        ks *= 2;
+    if (a.T <= 32) {
+        ks = slots / tiles;
+        if (ks > nsb_all / 2) ks = nsb_all / 2;
+        if (ks < 1) ks = 1;
+    } else {
+        while (tiles * ks * 2 <= slots && (K / (ks * 2)) % 256 == 0 && K / (ks * 2) >= 512) ks *= 2;
+    }
     a.ksplit = ks;
-    a.k_per_split = static_cast<uint32_t>(K) / ks;
     a.nst = nst;
     a.nraw = nraw;
     // accumulators: nacc * T TMEM columns, at most 512 per SM (256 per CTA when two share it)
