@@ -9,10 +9,11 @@
 //     consumer thread owns one slot for the whole launch and keeps the slot's
 //     activations in registers, in the decoder's form; P = floor(consumer
 //     threads / CS) rows are decoded side by side ("phases").
-//   * Prologue: the CTA turns x into per-slot records in shared memory, one
-//     thread per 32-activation group (first the group maxima, then the digits
-//     at the slot's scale), and every consumer thread copies its slot's record
-//     into registers.  x is read from global memory twice per CTA (L1/L2 hits).
+//   * Prologue: the CTA turns x into per-slot records in shared memory (for
+//     the integer decoders in two passes: every thread loads, transforms and
+//     quantizes 8 activations at its slot's scale, then one thread per
+//     32-activation group packs its record), and every consumer thread with
+//     rows copies its slot's record into registers.
 //   * Each CTA owns a contiguous range of rows and streams it in tiles of TR
 //     rows (TR*row_bytes contiguous bytes) through a ring of NST shared-memory
 //     stages.  The producer warp fills a stage with one 1-D bulk copy
