@@ -122,6 +122,17 @@ int   tb_cuda_matvec_experts_dev(const void *W_dev, int qtype, int M, int K, int
                                  const int *d_ids, int n_sel, const float *d_x, int x_stride,
                                  float *d_y, int y_stride, int ymode, void *stream);
 
+/* Sampling of one logits vector on the device (replaces layer1/tb_tensor.c:
+ * 411-540 tb_sample_top_k / tb_sample_top_p for a caller whose logits are in
+ * device memory).  u in [0, 1) is the uniform variate the reference draws with
+ * rand() / (RAND_MAX + 1.0f).  top_k > 0: top-k at temperature (k >= vocab:
+ * nucleus with p = 0.95, as the reference); top_k = 0: nucleus sampling with
+ * top_p in (0, 1].  Writes the chosen index to *d_token; stream-ordered.
+ * top_k <= 2048 (when < vocab).  Non-finite logits set the error word (2)
+ * and write 0.  1 = issued. */
+int   tb_cuda_sample_dev(const float *d_logits, int vocab, int top_k, float top_p, float temperature,
+                         float u, int *d_token, void *stream);
+
 /* Bit-exact dequantisation of M rows of K weights into d_out[M*K] (fp32),
  * stream-ordered.  sem = 0 gives the reference CUDA-kernel semantics (the
  * parity contract); sem = 1 gives layer4/tb_gguf.c's shipped decoders, which

@@ -64,6 +64,8 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_qgemm_dev": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p]),
         "tb_cuda_matvec_experts_dev": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int,
                                                c_void_p, c_int, c_int, c_void_p]),
+        "tb_cuda_sample_dev": (c_int, [c_void_p, c_int, c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float, c_void_p,
+                                       c_void_p]),
         "tb_cuda_dec_create": (c_void_p, [ctypes.POINTER(DecConfig)]),
         "tb_cuda_dec_set_layer": (c_int, [c_void_p, c_int, ctypes.POINTER(DecLayer)]),
         "tb_cuda_dec_set_head": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int]),
@@ -94,7 +96,7 @@ def exported_symbols() -> list[str]:
         "tb_cuda_set_snap", "tb_cuda_matvec_device", "tb_cuda_sync_all", "tb_cuda_cleanup",
         "tb_cuda_matvec_dev", "tb_cuda_dequant_dev", "tb_cuda_qtype_info", "tb_cuda_last_error",
         "tb_cuda_launch_count", "tb_cuda_version", "tb_cuda_matvec_device_noalloc",
-        "tb_cuda_matvec_fused_dev", "tb_cuda_matvec_experts_dev", "tb_cuda_qgemm_dev", "tb_cuda_dec_create", "tb_cuda_dec_set_layer", "tb_cuda_dec_set_head",
+        "tb_cuda_matvec_fused_dev", "tb_cuda_matvec_experts_dev", "tb_cuda_sample_dev", "tb_cuda_qgemm_dev", "tb_cuda_dec_create", "tb_cuda_dec_set_layer", "tb_cuda_dec_set_head",
         "tb_cuda_dec_kv", "tb_cuda_dec_kv_copy", "tb_cuda_dec_read", "tb_cuda_dec_create_tp",
         "tb_cuda_dec_tp_handle", "tb_cuda_dec_tp_connect", "tb_cuda_dec_create_moe", "tb_cuda_dec_set_moe_layer",
         "tb_cuda_dec_step", "tb_cuda_dec_generate", "tb_cuda_dec_destroy",

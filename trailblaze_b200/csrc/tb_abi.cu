@@ -378,6 +378,21 @@ int tb_cuda_matvec_experts_dev(const void *W_dev, int qtype, int M, int K, int n
     return r;
 }
 
+int tb_cuda_sample_dev(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
+                       int *d_token, void *stream)
+{
+    int *derr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!ensure_init_locked(false)) return 0;
+        derr = g.d_err;
+    }
+    const int r = tb::sample_launch(d_logits, vocab, top_k, top_p, temperature, u, d_token, derr,
+                                    static_cast<cudaStream_t>(stream));
+    if (r) g_launches.fetch_add(1, std::memory_order_relaxed);
+    return r;
+}
+
 int tb_cuda_matvec_fused_dev(const void *W_dev, int qtype, int M, int K, const float *d_x, float *d_y,
                              int xmode, const float *d_x2, const float *d_norm_w, float eps,
                              const float *d_res, int ymode, void *stream)

@@ -1,0 +1,310 @@
+// tb_sample.cu — top-k and nucleus (top-p) sampling of one logits vector on
+// the device (layer1/tb_tensor.c:411-540, tb_sample_top_p / tb_sample_top_k).
+//
+// One CTA of kSmpThreads threads.  The caller supplies the uniform variate u
+// in [0, 1) that the reference draws with rand() / (RAND_MAX + 1.0f); the
+// kernel writes the chosen token index.
+//
+// top-p (tb_tensor.c:423-504): softmax of logits / t (t = temperature when
+//   > 0.01, else 1) over the whole vocabulary; candidates = the tokens whose
+//   probability is >= 1e-4 of the largest, in index order, at most 2047 of
+//   them; sorted by probability, largest first (equal probabilities keep
+//   index order, as the reference's insertion sort does); cut after the first
+//   prefix whose sum reaches p; r = u * (sum of the kept), the first kept
+//   token whose running sum reaches r.
+// top-k (tb_tensor.c:506-540): k >= vocab falls back to top-p with p = 0.95;
+//   else the k largest logits (found here by a radix select on their bits,
+//   equal values by lower index), softmax of (l - l_max) / t (t = temperature
+//   when > 0, else 1), r = u * sum, the first whose running sum reaches r.
+//
+// Sums over the vocabulary are tree sums here and sequential in the
+// reference (a rounding-level difference); the running sums over the kept
+// candidates are sequential, in the reference's order.
+#include <cfloat>
+#include <cstdint>
+
+#include "tb_common.cuh"
+#include "tb_internal.h"
+
+namespace tb {
+
+static constexpr int kSmpThreads = 1024;
+static constexpr int kNucleusMax = 2048;   // candidate slots (the reference keeps at most 2047)
+
+struct SmpArgs {
+    const float *logits;
+    int *token;
+    int *err;
+    int vocab, k;
+    float p, temp, u;
+};
+
+// fp32 bits mapped to unsigned integers of the same order (NaN excluded).
+__device__ __forceinline__ uint32_t ord_key(float f)
+{
+    const uint32_t b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float block_max(float v, float *red)
+{
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float m = red[0];
+    for (int w = 1; w < kSmpThreads / 32; ++w) m = fmaxf(m, red[w]);
+    return m;
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red)
+{
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float s = 0.f;
+    for (int w = 0; w < kSmpThreads / 32; ++w) s += red[w];
+    return s;
+}
+
+// Exclusive prefix of one count per thread, in thread order; returns the total.
+__device__ __forceinline__ int block_scan(int c, int &excl, int *red)
+{
+    int incl = c;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    __syncthreads();
+    if (lane == 31) red[warp] = incl;
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < kSmpThreads / 32; ++w) {
+        if (w < warp) before += red[w];
+        total += red[w];
+    }
+    excl = before + incl - c;
+    return total;
+}
+
+// Sorts n <= kNucleusMax (value, index) pairs: value descending, index
+// ascending among equal values (bitonic network over the next power of two).
+__device__ void sort_desc(float *val, int *idx, int n)
+{
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    for (int i = n + threadIdx.x; i < n2; i += kSmpThreads) {   // pads sort last
+        val[i] = -FLT_MAX;
+        idx[i] = 0x7FFFFFFF;
+    }
+    __syncthreads();
+    for (int size = 2; size <= n2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < n2; i += kSmpThreads) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    // "a before b": larger value, or equal value and lower index
+                    const bool ib = val[i] > val[j] || (val[i] == val[j] && idx[i] < idx[j]);
+                    const bool up = (i & size) == 0;   // this half sorted in the final order
+                    if (ib != up) {
+                        const float tv = val[i];
+                        val[i] = val[j];
+                        val[j] = tv;
+                        const int ti = idx[i];
+                        idx[i] = idx[j];
+                        idx[j] = ti;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __shared__ float cval[kNucleusMax];
+    __shared__ int cidx[kNucleusMax];
+    __shared__ float red[kSmpThreads / 32];
+    __shared__ int ired[kSmpThreads / 32];
+    __shared__ int hist[256];
+    __shared__ int s_n, s_sel;
+    const int tid = threadIdx.x, V = a.vocab;
+    // the thread's contiguous run of the vocabulary (index order = thread order)
+    const int per = (V + kSmpThreads - 1) / kSmpThreads;
+    const int lo = min(V, tid * per), hi = min(V, lo + per);
+
+    float m = -FLT_MAX;
+    bool fin = true;
+    for (int i = lo; i < hi; ++i) {
+        const float l = a.logits[i];
+        fin = fin && isfinite(l);
+        m = fmaxf(m, l);
+    }
+    if (!__syncthreads_and(fin ? 1 : 0)) {
+        if (tid == 0) {
+            atomicExch(a.err, ERR_RUNTIME);
+            *a.token = 0;
+        }
+        return;
+    }
+    m = block_max(m, red);
+
+    int n = 0;   // candidates, sorted into cval / cidx by value descending
+    const bool topk = a.k > 0 && a.k < V;
+    if (!topk) {
+        // ---- nucleus candidates: probabilities >= 1e-4 of the peak ----
+        const float p = a.k > 0 ? 0.95f : a.p;   // tb_sample_top_k's fallback for k >= vocab
+        const float t = a.temp > 0.01f ? a.temp : 1.0f;
+        float s = 0.f;
+        for (int i = lo; i < hi; ++i) s += expf((a.logits[i] - m) / t);
+        const float sum = block_sum(s, red);
+        const float inv = sum > 0.f ? 1.0f / sum : 1.0f;
+        // the peak probability is that of the largest logit: expf(0) * inv
+        const float thr = inv * 1e-4f;
+        int c = 0;
+        for (int i = lo; i < hi; ++i) c += expf((a.logits[i] - m) / t) * inv >= thr ? 1 : 0;
+        int base;
+        const int total = block_scan(c, base, ired);
+        n = min(total, kNucleusMax - 1);
+        for (int i = lo; i < hi && base < n; ++i) {
+            const float q = expf((a.logits[i] - m) / t) * inv;
+            if (q >= thr) {
+                cval[base] = q;
+                cidx[base] = i;
+                ++base;
+            }
+        }
+        __syncthreads();
+        sort_desc(cval, cidx, n);
+        if (tid == 0) {
+            float cum = 0.f;
+            int cut = n - 1;
+            for (int i = 0; i < n; ++i) {
+                cum += cval[i];
+                if (cum >= p) {
+                    cut = i;
+                    break;
+                }
+            }
+            float ns = 0.f;
+            for (int i = 0; i <= cut; ++i) ns += cval[i];
+            const float r = a.u * ns;
+            int chosen = cidx[cut];
+            float acc = 0.f;
+            for (int i = 0; i <= cut; ++i) {
+                acc += cval[i];
+                if (acc >= r) {
+                    chosen = cidx[i];
+                    break;
+                }
+            }
+            *a.token = chosen;
+        }
+        return;
+    }
+
+    // ---- top-k: radix select of the k-th largest key, 8 bits at a time ----
+    uint32_t prefix = 0, pmask = 0;
+    int need = a.k;   // how many of the keys with this prefix are still to be taken
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += kSmpThreads) hist[b] = 0;
+        __syncthreads();
+        for (int i = lo; i < hi; ++i) {
+            const uint32_t key = ord_key(a.logits[i]);
+            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int acc = 0, b = 255;
+            for (; b > 0; --b) {
+                if (acc + hist[b] >= need) break;
+                acc += hist[b];
+            }
+            s_sel = b;
+            s_n = need - acc;   // keys still needed from bin b
+        }
+        __syncthreads();
+        prefix |= static_cast<uint32_t>(s_sel) << shift;
+        pmask |= 255u << shift;
+        need = s_n;
+        __syncthreads();
+    }
+    // prefix is the k-th largest key: every key above it, and the first `need`
+    // keys equal to it in index order
+    int cg = 0, ce = 0;
+    for (int i = lo; i < hi; ++i) {
+        const uint32_t key = ord_key(a.logits[i]);
+        cg += key > prefix ? 1 : 0;
+        ce += key == prefix ? 1 : 0;
+    }
+    int bg, be;
+    const int ng = block_scan(cg, bg, ired);
+    block_scan(ce, be, ired);
+    for (int i = lo; i < hi; ++i) {
+        const uint32_t key = ord_key(a.logits[i]);
+        if (key > prefix) {
+            cval[bg] = a.logits[i];
+            cidx[bg] = i;
+            ++bg;
+        } else if (key == prefix) {
+            if (be < need) {
+                cval[ng + be] = a.logits[i];
+                cidx[ng + be] = i;
+            }
+            ++be;
+        }
+    }
+    n = a.k;
+    __syncthreads();
+    sort_desc(cval, cidx, n);
+    if (tid == 0) {
+        const float t = a.temp > 0.f ? a.temp : 1.0f;
+        const float mv = cval[0];
+        float sum = 0.f;
+        for (int i = 0; i < n; ++i) {
+            cval[i] = expf((cval[i] - mv) / t);
+            sum += cval[i];
+        }
+        const float r = a.u * sum;
+        int chosen = cidx[0];
+        float acc = 0.f;
+        for (int i = 0; i < n; ++i) {
+            acc += cval[i];
+            if (acc >= r) {
+                chosen = cidx[i];
+                break;
+            }
+        }
+        *a.token = chosen;
+    }
+}
+
+int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
+                  int *d_token, int *d_err, cudaStream_t st)
+{
+    if (!d_logits || !d_token || vocab <= 0 || top_k < 0 || (top_k > 0 && top_k < vocab && top_k > kNucleusMax) ||
+        !(u >= 0.f && u < 1.f) || (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
+        return 0;
+    SmpArgs a{d_logits, d_token, d_err, vocab, top_k, top_p, temperature, u};
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kSmpThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, k_sample, a) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return 1;
+}
+
+}  // namespace tb

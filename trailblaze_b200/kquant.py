@@ -97,6 +97,11 @@ class KQuantLib:
         return self.L.tb_cuda_matvec_experts_dev(ctypes.c_void_p(W_dev), qtype, M, K, n_experts, v(d_ids), n_sel,
                                                  v(d_x), x_stride, v(d_y), y_stride, ymode, v(stream))
 
+    def tb_cuda_sample_dev(self, d_logits: int, vocab: int, top_k: int, top_p: float, temperature: float, u: float,
+                           d_token: int, stream: int = 0) -> int:
+        v = lambda p: ctypes.c_void_p(p) if p else None  # noqa: E731
+        return self.L.tb_cuda_sample_dev(v(d_logits), vocab, top_k, top_p, temperature, u, v(d_token), v(stream))
+
     def tb_cuda_dequant_dev(self, W_dev: int, qtype: int, M: int, K: int, d_out: int, sem: int = 0,
                             stream: int = 0) -> int:
         return self.L.tb_cuda_dequant_dev(ctypes.c_void_p(W_dev), qtype, M, K, ctypes.c_void_p(d_out),
