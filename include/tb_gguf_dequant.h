@@ -239,6 +239,16 @@ int    tb_cuda_dec_step(void *dec, int token, int pos, int *next_token, float *l
  * step's logits, device_ms (may be NULL) the device time of the n steps. */
 int    tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_out, float *logits_host,
                             float *device_ms);
+/* Sampling instead of the greedy argmax (the choice of layer4/tb_infer.c:
+ * 1031-1038): temperature < 0.01 greedy (the default); else top_k > 0 the
+ * top-k sampler, top_k = 0 the nucleus of top_p (tb_cuda_sample_dev's rules,
+ * inside the step's graph).  One device (world 1).  1 = ok. */
+int    tb_cuda_dec_set_sampling(void *dec, float temperature, int top_k, float top_p);
+/* tb_cuda_dec_generate with the variates: step i samples with u[i] in [0, 1)
+ * (the reference's rand() / (RAND_MAX + 1.0f)).  Required while sampling is
+ * set (tb_cuda_dec_step / _generate then fail); u is ignored when greedy. */
+int    tb_cuda_dec_generate_u(void *dec, int token, int pos, int n, const float *u, int *tokens_out,
+                              float *logits_host, float *device_ms);
 /* Copies n floats of one of the last step's activation vectors to host:
  * which = 0 the hidden state after the last layer (hidden), 1 the state after
  * the last layer's attention block (hidden), 2 the last layer's q | k | v

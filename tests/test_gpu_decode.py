@@ -197,6 +197,95 @@ def test_decode_chain_feeds_back_argmax(kq):
         dec.close()
 
 
+def _gen_u(kq, dec, token, pos, u, vocab):
+    """tb_cuda_dec_generate_u: (tokens, last logits), or None when the call returns 0."""
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    toks = (ctypes.c_int * u.size)()
+    logits = np.zeros(vocab, dtype=np.float32)
+    fp = ctypes.POINTER(ctypes.c_float)
+    if kq.L.tb_cuda_dec_generate_u(dec.d, token, pos, u.size, u.ctypes.data_as(fp), toks,
+                                   logits.ctypes.data_as(fp), None) != 1:
+        return None
+    return list(toks), logits
+
+
+def _oracle_pick(logits, temp, k, p, u):
+    from oracle.sample_ref import sample_top_k, sample_top_p
+    return sample_top_k(logits, k, temp, u) if k > 0 else sample_top_p(logits, p, temp, u)
+
+
+# (temperature, top_k, top_p): top-k, nucleus, and top-k >= vocab (nucleus 0.95)
+SAMPLING = [(0.8, 40, 0.0), (0.7, 0, 0.9), (1.3, 0, 0.5), (0.9, 5000, 0.0)]
+
+
+@pytest.mark.parametrize("temp,k,p", SAMPLING)
+def test_decode_sampled_step_matches_sampler_oracle(kq, temp, k, p):
+    """The step's sampler (tb_infer.c:1031-1038) picks what the reference's
+    tb_sample_top_k / tb_sample_top_p pick from the step's own logits for the
+    same variate; switching from greedy leaves the logits bit-identical."""
+    m = make_model(seed=11)
+    dec, orc = GpuDecoder(kq, m, True), DecodeOracle(m, quirks=True)
+    try:
+        pos = 30
+        prefill(m, dec, orc, pos)
+        lg, _ = dec.step(9, pos)
+        assert kq.L.tb_cuda_dec_set_sampling(dec.d, temp, k, p) == 1
+        for u in (0.0, 0.13, 0.5, 0.77, 0.999):
+            r = _gen_u(kq, dec, 9, pos, [u], m.vocab)
+            assert r is not None
+            toks, logits = r
+            assert np.array_equal(logits, lg)
+            assert toks[0] == _oracle_pick(logits, temp, k, p, u), (u, toks[0])
+    finally:
+        dec.close()
+
+
+def test_decode_sampled_chain_uses_each_variate(kq):
+    """Four sampled steps back to back (one graph replay each) equal four
+    single steps fed the same tokens and variates: step i draws u[i] and
+    advances the position."""
+    m = make_model(seed=12, vocab=600)
+    dec, orc = GpuDecoder(kq, m, True), DecodeOracle(m, quirks=True)
+    try:
+        pos0 = 10
+        prefill(m, dec, orc, pos0)
+        assert kq.L.tb_cuda_dec_set_sampling(dec.d, 1.5, 0, 0.98) == 1
+        u = [0.91, 0.05, 0.42, 0.66]
+        chain, last = _gen_u(kq, dec, 4, pos0, u, m.vocab)
+        tok = 4
+        for i in range(4):
+            toks, logits = _gen_u(kq, dec, tok, pos0 + i, [u[i]], m.vocab)
+            assert toks[0] == chain[i] == _oracle_pick(logits, 1.5, 0, 0.98, u[i]), (i, toks[0], chain[i])
+            tok = toks[0]
+        assert np.array_equal(logits, last)
+    finally:
+        dec.close()
+
+
+def test_decode_sampling_settings(kq):
+    m = make_model(seed=13, n_layers=1)
+    dec = GpuDecoder(kq, m, True)
+    L = kq.L
+    try:
+        lg, greedy = dec.step(2, 0)
+        assert L.tb_cuda_dec_set_sampling(dec.d, 0.8, 0, 0.0) == 0      # nucleus needs p in (0, 1]
+        assert L.tb_cuda_dec_set_sampling(dec.d, 0.8, 0, 1.5) == 0
+        assert L.tb_cuda_dec_set_sampling(dec.d, 0.8, 999, 0.0) == 1    # top-k below the vocabulary
+        nxt = ctypes.c_int(-1)
+        assert L.tb_cuda_dec_step(dec.d, 2, 0, ctypes.byref(nxt), None) == 0   # sampling needs the variates
+        assert _gen_u(kq, dec, 2, 0, [1.0], m.vocab) is None                  # u outside [0, 1)
+        assert _gen_u(kq, dec, 2, 0, [-0.1], m.vocab) is None
+        assert _gen_u(kq, dec, 2, 0, [0.3], m.vocab) is not None
+        # temperatures below 0.01 are greedy again, as in the reference
+        assert L.tb_cuda_dec_set_sampling(dec.d, 0.005, 40, 0.9) == 1
+        lg2, g2 = dec.step(2, 0)
+        assert g2 == greedy and np.array_equal(lg2, lg)
+        toks, _ = _gen_u(kq, dec, 2, 0, [0.7], m.vocab)                       # u ignored when greedy
+        assert toks[0] == greedy
+    finally:
+        dec.close()
+
+
 def test_fused_matvec_modes(kq):
     import torch
     rng = np.random.default_rng(3)

@@ -806,6 +806,14 @@ struct Decoder {
     int n_exp = 0, top_k = 0;
     float *rlog = nullptr, *wts = nullptr, *hbuf = nullptr, *tbuf = nullptr;
     int *ids = nullptr;
+    // sampling (tb_infer.c:1031-1038): greedy while smp_temp < 0.01, else
+    // top-k when smp_k > 0, else the nucleus of smp_p; step i of a run draws
+    // the caller's variate u_buf[i] (u_idx counts the steps on the device)
+    float smp_temp = 0.f, smp_p = 0.f;
+    int smp_k = 0;
+    float *u_buf = nullptr;
+    int *u_idx = nullptr;
+    bool sampling() const { return smp_temp >= 0.01f; }
 
     float *slot_o(int p) const { return reinterpret_cast<float *>(peer[p]); }
     float *slot_d(int p) const { return reinterpret_cast<float *>(peer[p] + off_xd); }
@@ -950,6 +958,8 @@ bool Decoder::enqueue(cudaStream_t s)
     f.eps = c.norm_eps;
     f.w_early = true;
     if (!mv_launch(lm, lm_qt, c.vocab, H, x, logits, s, err, sms, lim, &f)) return false;
+    if (sampling())
+        return sample_launch(logits, c.vocab, smp_k, smp_p, smp_temp, 0.f, tok, err, s, u_buf, u_idx, pos) != 0;
     const int G = sms;
     ArgTP tp{};
     tp.world = 1;
@@ -1086,7 +1096,7 @@ static void dec_free(Decoder *d)
     if (d->ev1) cudaEventDestroy(d->ev1);
     void *bufs[] = {d->x,    d->x2,  d->qkv, d->att, d->gu,     d->logits, d->kc,   d->vc,   d->part,
                     d->argv, d->argi, d->tok, d->pos, d->counts, d->err,    d->rlog, d->wts, d->hbuf,
-                    d->tbuf, d->ids};
+                    d->tbuf, d->ids, d->u_buf, d->u_idx};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->hostio) cudaFreeHost(d->hostio);
@@ -1231,12 +1241,28 @@ static bool dec_graph(Decoder *d)
     return inst;
 }
 
-// Runs n tokens back to back from (token, pos): token_i+1 = argmax of step i.
+// Runs n tokens back to back from (token, pos): token_i+1 = the token step i
+// picks (greedy, or sampled with the variate u[i] when sampling is set).
 // tokens[i] receives each generated token when not null; ms receives the device
 // time of the n replays (CUDA events on the decoder's stream).
-int dec_run(Decoder *d, int token, int pos, int n, int *tokens, float *logits_host, float *ms)
+int dec_run(Decoder *d, int token, int pos, int n, int *tokens, float *logits_host, float *ms,
+            const float *u = nullptr)
 {
     if (!d || n <= 0 || token < 0 || token >= d->vocab_full || pos < 0 || pos + n > d->cfg.max_ctx) return 0;
+    if (d->sampling()) {
+        if (!u) {
+            fprintf(stderr, "[tb_cuda] decoder: sampling is set: pass the variates (tb_cuda_dec_generate_u)\n");
+            return 0;
+        }
+        for (int i = 0; i < n; ++i)
+            if (!(u[i] >= 0.f && u[i] < 1.f)) {
+                fprintf(stderr, "[tb_cuda] decoder: variate %d outside [0, 1)\n", i);
+                return 0;
+            }
+        if (!dec_ok(cudaMemcpyAsync(d->u_buf, u, sizeof(float) * n, cudaMemcpyHostToDevice, d->st), "variates") ||
+            !dec_ok(cudaMemsetAsync(d->u_idx, 0, sizeof(int), d->st), "variates"))
+            return 0;
+    }
     if (d->world > 1 && !d->connected()) {
         fprintf(stderr, "[tb_cuda] decoder: tensor-parallel ranks not connected (tb_cuda_dec_tp_connect)\n");
         return 0;
@@ -1437,6 +1463,41 @@ int tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_out, 
                          float *device_ms)
 {
     return tb::dec_run(static_cast<tb::Decoder *>(dec), token, pos, n, tokens_out, logits_host, device_ms);
+}
+
+int tb_cuda_dec_generate_u(void *dec, int token, int pos, int n, const float *u, int *tokens_out,
+                           float *logits_host, float *device_ms)
+{
+    return tb::dec_run(static_cast<tb::Decoder *>(dec), token, pos, n, tokens_out, logits_host, device_ms, u);
+}
+
+int tb_cuda_dec_set_sampling(void *dec, float temperature, int top_k, float top_p)
+{
+    tb::Decoder *d = static_cast<tb::Decoder *>(dec);
+    if (!d || !(temperature == temperature) || top_k < 0) return 0;
+    const bool smp = temperature >= 0.01f;
+    if (smp) {
+        if (d->world > 1) {
+            fprintf(stderr, "[tb_cuda] decoder: sampling needs the whole vocabulary on one device (world 1)\n");
+            return 0;
+        }
+        if ((top_k > 0 && top_k < d->cfg.vocab && top_k > 2048) || (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
+            return 0;
+        if (!d->u_buf &&
+            !(tb::dec_ok(cudaMalloc(&d->u_buf, sizeof(float) * d->cfg.max_ctx), "variates") &&
+              tb::dec_ok(cudaMalloc(&d->u_idx, sizeof(int)), "variates")))
+            return 0;
+    }
+    if (d->sampling() != smp || (smp && (d->smp_temp != temperature || d->smp_k != top_k || d->smp_p != top_p))) {
+        if (d->gexec) {   // the last kernel changes: capture again on the next step
+            cudaGraphExecDestroy(d->gexec);
+            d->gexec = nullptr;
+        }
+    }
+    d->smp_temp = smp ? temperature : 0.f;
+    d->smp_k = top_k;
+    d->smp_p = top_p;
+    return 1;
 }
 
 int tb_cuda_dec_step(void *dec, int token, int pos, int *next_token, float *logits_host)

@@ -60,8 +60,11 @@ int qg_launch(const void *W, int qtype, int N, int K, const void *A, int T, floa
 // Launch the top-k / nucleus sampler of one logits vector (tb_sample.cu):
 // *d_token = the chosen index for the uniform variate u in [0, 1).  top_k > 0:
 // top-k (k >= vocab: nucleus with p = 0.95); top_k = 0: nucleus with top_p.
+// With d_u (the decode graph): u = d_u[*d_u_idx], then *d_pos and *d_u_idx
+// each advance by one.
 int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
-                  int *d_token, int *d_err, cudaStream_t st);
+                  int *d_token, int *d_err, cudaStream_t st, const float *d_u = nullptr, int *d_u_idx = nullptr,
+                  int *d_pos = nullptr);
 
 // Launch the bit-exact dequantisation of M rows of K weights into d_out.
 int dq_launch(const void *W, int qtype, int M, int K, float *d_out, int sem, cudaStream_t st);

@@ -5,6 +5,10 @@
 // in [0, 1) that the reference draws with rand() / (RAND_MAX + 1.0f); the
 // kernel writes the chosen token index.
 //
+// Inside the decode graph the variate comes from device memory instead
+// (u_dev[*u_idx], the step's entry of a caller-filled array) and the kernel
+// also advances the step: pos <- pos + 1, u_idx <- u_idx + 1.
+//
 // top-p (tb_tensor.c:423-504): softmax of logits / t (t = temperature when
 //   > 0.01, else 1) over the whole vocabulary; candidates = the tokens whose
 //   probability is >= 1e-4 of the largest, in index order, at most 2047 of
@@ -37,7 +41,25 @@ struct SmpArgs {
     int *err;
     int vocab, k;
     float p, temp, u;
+    const float *u_dev;   // not null: u = u_dev[*u_idx], and the step advances
+    int *u_idx, *pos;
 };
+
+// Thread 0: the chosen token, and the decode step's advance when the variate
+// came from device memory.
+__device__ __forceinline__ void finish(const SmpArgs &a, int token)
+{
+    *a.token = token;
+    if (a.u_dev) {
+        *a.pos = *a.pos + 1;
+        *a.u_idx = *a.u_idx + 1;
+    }
+}
+
+__device__ __forceinline__ float variate(const SmpArgs &a)
+{
+    return a.u_dev ? a.u_dev[*a.u_idx] : a.u;
+}
 
 // fp32 bits mapped to unsigned integers of the same order (NaN excluded).
 __device__ __forceinline__ uint32_t ord_key(float f)
@@ -148,7 +170,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     if (!__syncthreads_and(fin ? 1 : 0)) {
         if (tid == 0) {
             atomicExch(a.err, ERR_RUNTIME);
-            *a.token = 0;
+            finish(a, 0);
         }
         return;
     }
@@ -193,7 +215,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
             }
             float ns = 0.f;
             for (int i = 0; i <= cut; ++i) ns += cval[i];
-            const float r = a.u * ns;
+            const float r = variate(a) * ns;
             int chosen = cidx[cut];
             float acc = 0.f;
             for (int i = 0; i <= cut; ++i) {
@@ -203,7 +225,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
                     break;
                 }
             }
-            *a.token = chosen;
+            finish(a, chosen);
         }
         return;
     }
@@ -214,9 +236,18 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int b = tid; b < 256; b += kSmpThreads) hist[b] = 0;
         __syncthreads();
-        for (int i = lo; i < hi; ++i) {
-            const uint32_t key = ord_key(a.logits[i]);
-            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+        // coalesced (the histogram needs no index order); the lanes that
+        // fall into one bin add their count with one shared atomic (the
+        // upper bytes of nearby logits agree, so bins are crowded)
+        for (int i0 = 0; i0 < V; i0 += kSmpThreads) {
+            const int i = i0 + tid;
+            uint32_t bin = 256u;
+            if (i < V) {
+                const uint32_t key = ord_key(a.logits[i]);
+                if ((key & pmask) == prefix) bin = (key >> shift) & 255u;
+            }
+            const uint32_t same = __match_any_sync(0xFFFFFFFFu, bin);
+            if (bin < 256u && (tid & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
         }
         __syncthreads();
         if (tid == 0) {
@@ -270,7 +301,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
             cval[i] = expf((cval[i] - mv) / t);
             sum += cval[i];
         }
-        const float r = a.u * sum;
+        const float r = variate(a) * sum;
         int chosen = cidx[0];
         float acc = 0.f;
         for (int i = 0; i < n; ++i) {
@@ -280,17 +311,18 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
                 break;
             }
         }
-        *a.token = chosen;
+        finish(a, chosen);
     }
 }
 
 int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
-                  int *d_token, int *d_err, cudaStream_t st)
+                  int *d_token, int *d_err, cudaStream_t st, const float *d_u, int *d_u_idx, int *d_pos)
 {
     if (!d_logits || !d_token || vocab <= 0 || top_k < 0 || (top_k > 0 && top_k < vocab && top_k > kNucleusMax) ||
-        !(u >= 0.f && u < 1.f) || (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
+        (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
         return 0;
-    SmpArgs a{d_logits, d_token, d_err, vocab, top_k, top_p, temperature, u};
+    if (d_u ? (!d_u_idx || !d_pos) : !(u >= 0.f && u < 1.f)) return 0;
+    SmpArgs a{d_logits, d_token, d_err, vocab, top_k, top_p, temperature, u, d_u, d_u_idx, d_pos};
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(kSmpThreads);

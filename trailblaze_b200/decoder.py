@@ -15,6 +15,8 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
+
 from . import qtypes as Q
 from ._lib import DecConfig, DecLayer, lib
 
@@ -140,6 +142,28 @@ class Decoder:
         if self.L.tb_cuda_dec_generate(self.d, token, pos, n, toks, None, ctypes.byref(ms)) != 1:
             raise RuntimeError("tb_cuda_dec_generate failed")
         return (list(toks) if want_tokens else None), ms.value
+
+    def set_sampling(self, temperature: float, top_k: int = 0, top_p: float = 0.9) -> None:
+        """Greedy below temperature 0.01; else top-k (top_k > 0) or nucleus sampling in the step's graph."""
+        if self.L.tb_cuda_dec_set_sampling(self.d, temperature, top_k, top_p) != 1:
+            raise RuntimeError("tb_cuda_dec_set_sampling refused the settings")
+
+    def generate_u(self, token: int, pos: int, u, logits=None):
+        """len(u) tokens from (token, pos), step i sampled with the variate u[i]; logits (float32 numpy,
+        vocab) receives the last step's logits when given.  Returns (tokens, device milliseconds)."""
+        u = np.ascontiguousarray(u, dtype=np.float32)
+        n = int(u.size)
+        toks = (ctypes.c_int * n)()
+        ms = ctypes.c_float(0.0)
+        fp = ctypes.POINTER(ctypes.c_float)
+        lp = None
+        if logits is not None:
+            assert logits.dtype == np.float32 and logits.flags.c_contiguous
+            lp = logits.ctypes.data_as(fp)
+        if self.L.tb_cuda_dec_generate_u(self.d, token, pos, n, u.ctypes.data_as(fp), toks, lp,
+                                         ctypes.byref(ms)) != 1:
+            raise RuntimeError("tb_cuda_dec_generate_u failed")
+        return list(toks), ms.value
 
     def step(self, token: int, pos: int) -> int:
         nxt = ctypes.c_int(-1)
