@@ -1,7 +1,9 @@
 // tb_sample.cu — top-k and nucleus (top-p) sampling of one logits vector on
 // the device (layer1/tb_tensor.c:411-540, tb_sample_top_p / tb_sample_top_k).
 //
-// One CTA of kSmpThreads threads.  The caller supplies the uniform variate u
+// One CTA of kSmpThreads threads; warp w owns a contiguous segment of the
+// vocabulary, read coalesced kChunk elements at a time (warp order = index
+// order; within a warp, ballots keep index order).  The caller supplies the uniform variate u
 // in [0, 1) that the reference draws with rand() / (RAND_MAX + 1.0f); the
 // kernel writes the chosen token index.
 //
@@ -34,6 +36,9 @@ namespace tb {
 
 static constexpr int kSmpThreads = 1024;
 static constexpr int kNucleusMax = 2048;   // candidate slots (the reference keeps at most 2047)
+static constexpr int kSmpWarps = kSmpThreads / 32;
+static constexpr int kPer = 8;                   // coalesced loads in flight per lane
+static constexpr int kChunk = 32 * kPer;         // elements a warp reads per iteration
 
 struct SmpArgs {
     const float *logits;
@@ -145,28 +150,56 @@ __device__ void sort_desc(float *val, int *idx, int n)
     }
 }
 
+__device__ __forceinline__ int warp_sum(int v)
+{
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// Visits the warp's segment [lo, hi) of the logits: each iteration loads
+// kChunk consecutive elements, kPer per lane (element b + 32 j + lane), and
+// calls f(index, value, in_range) in ascending index order, j-major; every
+// lane of the warp calls f the same number of times, so f may vote.
+template <class F>
+__device__ __forceinline__ void for_seg(const float *lg, int lo, int hi, int lane, F &&f)
+{
+    for (int b = lo; b < hi; b += kChunk) {
+        float v[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = b + j * 32 + lane;
+            v[j] = i < hi ? __ldg(lg + i) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) f(b + j * 32 + lane, v[j], b + j * 32 + lane < hi);
+    }
+}
+
 __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
 {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     __shared__ float cval[kNucleusMax];
     __shared__ int cidx[kNucleusMax];
-    __shared__ float red[kSmpThreads / 32];
-    __shared__ int ired[kSmpThreads / 32];
+    __shared__ float red[kSmpWarps];
+    __shared__ int ired[kSmpWarps];
     __shared__ int hist[256];
     __shared__ int s_n, s_sel;
-    const int tid = threadIdx.x, V = a.vocab;
-    // the thread's contiguous run of the vocabulary (index order = thread order)
-    const int per = (V + kSmpThreads - 1) / kSmpThreads;
-    const int lo = min(V, tid * per), hi = min(V, lo + per);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, V = a.vocab;
+    const float *lg = a.logits;
+    const unsigned below = (1u << lane) - 1u;   // the lanes before this one
+    // the warp's contiguous segment of the vocabulary (warp order = index order)
+    const int seg = ((V + kSmpWarps - 1) / kSmpWarps + kChunk - 1) / kChunk * kChunk;
+    const int wlo = min(V, warp * seg), whi = min(V, wlo + seg);
 
     float m = -FLT_MAX;
     bool fin = true;
-    for (int i = lo; i < hi; ++i) {
-        const float l = a.logits[i];
-        fin = fin && isfinite(l);
-        m = fmaxf(m, l);
-    }
+    for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
+        if (ok) {
+            fin = fin && isfinite(v);
+            m = fmaxf(m, v);
+        }
+    });
     if (!__syncthreads_and(fin ? 1 : 0)) {
         if (tid == 0) {
             atomicExch(a.err, ERR_RUNTIME);
@@ -183,27 +216,36 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         const float p = a.k > 0 ? 0.95f : a.p;   // tb_sample_top_k's fallback for k >= vocab
         const float t = a.temp > 0.01f ? a.temp : 1.0f;
         float s = 0.f;
-        for (int i = lo; i < hi; ++i) s += expf((a.logits[i] - m) / t);
+        for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) { s += ok ? expf((v - m) / t) : 0.f; });
         const float sum = block_sum(s, red);
         const float inv = sum > 0.f ? 1.0f / sum : 1.0f;
         // the peak probability is that of the largest logit: expf(0) * inv
         const float thr = inv * 1e-4f;
         int c = 0;
-        for (int i = lo; i < hi; ++i) c += expf((a.logits[i] - m) / t) * inv >= thr ? 1 : 0;
+        for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
+            c += ok && expf((v - m) / t) * inv >= thr ? 1 : 0;
+        });
+        c = warp_sum(c);
         int base;
-        const int total = block_scan(c, base, ired);
+        const int total = block_scan(lane == 0 ? c : 0, base, ired);
+        base = __shfl_sync(0xFFFFFFFFu, base, 0);   // candidates in the warps before this one
         n = min(total, kNucleusMax - 1);
-        for (int i = lo; i < hi && base < n; ++i) {
-            const float q = expf((a.logits[i] - m) / t) * inv;
-            if (q >= thr) {
-                cval[base] = q;
-                cidx[base] = i;
-                ++base;
+        for_seg(lg, wlo, whi, lane, [&](int i, float v, bool ok) {
+            const float q = expf((v - m) / t) * inv;
+            const bool take = ok && q >= thr;
+            const unsigned vote = __ballot_sync(0xFFFFFFFFu, take);
+            const int at = base + __popc(vote & below);
+            if (take && at < n) {
+                cval[at] = q;
+                cidx[at] = i;
             }
-        }
+            base += __popc(vote);
+        });
         __syncthreads();
         sort_desc(cval, cidx, n);
         if (tid == 0) {
+            // cut after the first prefix reaching p; its running sum is the
+            // sum of the kept candidates, added in the same order
             float cum = 0.f;
             int cut = n - 1;
             for (int i = 0; i < n; ++i) {
@@ -213,9 +255,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
                     break;
                 }
             }
-            float ns = 0.f;
-            for (int i = 0; i <= cut; ++i) ns += cval[i];
-            const float r = variate(a) * ns;
+            const float r = variate(a) * cum;
             int chosen = cidx[cut];
             float acc = 0.f;
             for (int i = 0; i <= cut; ++i) {
@@ -236,19 +276,17 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int b = tid; b < 256; b += kSmpThreads) hist[b] = 0;
         __syncthreads();
-        // coalesced (the histogram needs no index order); the lanes that
-        // fall into one bin add their count with one shared atomic (the
-        // upper bytes of nearby logits agree, so bins are crowded)
-        for (int i0 = 0; i0 < V; i0 += kSmpThreads) {
-            const int i = i0 + tid;
+        // the lanes that fall into one bin add their count with one shared
+        // atomic (the upper bytes of nearby logits agree, so bins are crowded)
+        for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
             uint32_t bin = 256u;
-            if (i < V) {
-                const uint32_t key = ord_key(a.logits[i]);
+            if (ok) {
+                const uint32_t key = ord_key(v);
                 if ((key & pmask) == prefix) bin = (key >> shift) & 255u;
             }
             const uint32_t same = __match_any_sync(0xFFFFFFFFu, bin);
-            if (bin < 256u && (tid & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
-        }
+            if (bin < 256u && lane == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
+        });
         __syncthreads();
         if (tid == 0) {
             int acc = 0, b = 255;
@@ -268,28 +306,36 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     // prefix is the k-th largest key: every key above it, and the first `need`
     // keys equal to it in index order
     int cg = 0, ce = 0;
-    for (int i = lo; i < hi; ++i) {
-        const uint32_t key = ord_key(a.logits[i]);
-        cg += key > prefix ? 1 : 0;
-        ce += key == prefix ? 1 : 0;
-    }
+    for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
+        const uint32_t key = ord_key(v);
+        cg += ok && key > prefix ? 1 : 0;
+        ce += ok && key == prefix ? 1 : 0;
+    });
+    cg = warp_sum(cg);
+    ce = warp_sum(ce);
     int bg, be;
-    const int ng = block_scan(cg, bg, ired);
-    block_scan(ce, be, ired);
-    for (int i = lo; i < hi; ++i) {
-        const uint32_t key = ord_key(a.logits[i]);
-        if (key > prefix) {
-            cval[bg] = a.logits[i];
-            cidx[bg] = i;
-            ++bg;
-        } else if (key == prefix) {
-            if (be < need) {
-                cval[ng + be] = a.logits[i];
-                cidx[ng + be] = i;
+    const int ng = block_scan(lane == 0 ? cg : 0, bg, ired);
+    block_scan(lane == 0 ? ce : 0, be, ired);
+    bg = __shfl_sync(0xFFFFFFFFu, bg, 0);
+    be = __shfl_sync(0xFFFFFFFFu, be, 0);
+    for_seg(lg, wlo, whi, lane, [&](int i, float v, bool ok) {
+        const uint32_t key = ord_key(v);
+        const bool gt = ok && key > prefix, eq = ok && key == prefix;
+        const unsigned vg = __ballot_sync(0xFFFFFFFFu, gt), ve = __ballot_sync(0xFFFFFFFFu, eq);
+        if (gt) {
+            const int at = bg + __popc(vg & below);
+            cval[at] = v;
+            cidx[at] = i;
+        } else if (eq) {
+            const int rank = be + __popc(ve & below);
+            if (rank < need) {
+                cval[ng + rank] = v;
+                cidx[ng + rank] = i;
             }
-            ++be;
         }
-    }
+        bg += __popc(vg);
+        be += __popc(ve);
+    });
     n = a.k;
     __syncthreads();
     sort_desc(cval, cidx, n);
