@@ -221,9 +221,12 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         const float inv = sum > 0.f ? 1.0f / sum : 1.0f;
         // the peak probability is that of the largest logit: expf(0) * inv
         const float thr = inv * 1e-4f;
+        // a logit more than 9.5 t below the peak has a probability below
+        // e^-9.49 < 7.6e-5 of the peak, far from the 1e-4 test: no expf needed
+        const float lcut = m - 9.5f * t;
         int c = 0;
         for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
-            c += ok && expf((v - m) / t) * inv >= thr ? 1 : 0;
+            c += ok && v >= lcut && expf((v - m) / t) * inv >= thr ? 1 : 0;
         });
         c = warp_sum(c);
         int base;
@@ -231,8 +234,12 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         base = __shfl_sync(0xFFFFFFFFu, base, 0);   // candidates in the warps before this one
         n = min(total, kNucleusMax - 1);
         for_seg(lg, wlo, whi, lane, [&](int i, float v, bool ok) {
-            const float q = expf((v - m) / t) * inv;
-            const bool take = ok && q >= thr;
+            float q = 0.f;
+            bool take = false;
+            if (ok && v >= lcut) {
+                q = expf((v - m) / t) * inv;
+                take = q >= thr;
+            }
             const unsigned vote = __ballot_sync(0xFFFFFFFFu, take);
             const int at = base + __popc(vote & below);
             if (take && at < n) {
@@ -284,8 +291,10 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
                 const uint32_t key = ord_key(v);
                 if ((key & pmask) == prefix) bin = (key >> shift) & 255u;
             }
-            const uint32_t same = __match_any_sync(0xFFFFFFFFu, bin);
-            if (bin < 256u && lane == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
+            if (__any_sync(0xFFFFFFFFu, bin < 256u)) {   // later passes: most warps match nothing
+                const uint32_t same = __match_any_sync(0xFFFFFFFFu, bin);
+                if (bin < 256u && lane == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
+            }
         });
         __syncthreads();
         if (tid == 0) {
