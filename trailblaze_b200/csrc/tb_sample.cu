@@ -348,14 +348,16 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     n = a.k;
     __syncthreads();
     sort_desc(cval, cidx, n);
+    // softmax numerators from the top logit on every thread; thread 0 then
+    // adds them in rank order, as the reference's loop does
+    const float t = a.temp > 0.f ? a.temp : 1.0f;
+    const float mv = cval[0];
+    __syncthreads();
+    for (int i = tid; i < n; i += kSmpThreads) cval[i] = expf((cval[i] - mv) / t);
+    __syncthreads();
     if (tid == 0) {
-        const float t = a.temp > 0.f ? a.temp : 1.0f;
-        const float mv = cval[0];
         float sum = 0.f;
-        for (int i = 0; i < n; ++i) {
-            cval[i] = expf((cval[i] - mv) / t);
-            sum += cval[i];
-        }
+        for (int i = 0; i < n; ++i) sum += cval[i];
         const float r = variate(a) * sum;
         int chosen = cidx[0];
         float acc = 0.f;
