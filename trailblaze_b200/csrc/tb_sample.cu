@@ -156,6 +156,31 @@ __device__ __forceinline__ int warp_sum(int v)
     return v;
 }
 
+// Running sum of v[0..n) in index order: the first index whose running sum
+// reaches target, or n - 1 when none does; cum receives the running sum at
+// that index.  Loads run 8 ahead of the dependent additions.
+__device__ __forceinline__ int first_reaching(const float *v, int n, float target, float &cum)
+{
+    float acc = 0.f;
+    for (int i0 = 0; i0 < n; i0 += 8) {
+        float w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = i0 + j < n ? v[i0 + j] : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (i0 + j < n) {
+                acc += w[j];
+                if (acc >= target) {
+                    cum = acc;
+                    return i0 + j;
+                }
+            }
+        }
+    }
+    cum = acc;
+    return n - 1;
+}
+
 // Visits the warp's segment [lo, hi) of the logits: each iteration loads
 // kChunk consecutive elements, kPer per lane (element b + 32 j + lane), and
 // calls f(index, value, in_range) in ascending index order, j-major; every
@@ -253,26 +278,11 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         if (tid == 0) {
             // cut after the first prefix reaching p; its running sum is the
             // sum of the kept candidates, added in the same order
-            float cum = 0.f;
-            int cut = n - 1;
-            for (int i = 0; i < n; ++i) {
-                cum += cval[i];
-                if (cum >= p) {
-                    cut = i;
-                    break;
-                }
-            }
+            float cum, acc;
+            const int cut = first_reaching(cval, n, p, cum);
             const float r = variate(a) * cum;
-            int chosen = cidx[cut];
-            float acc = 0.f;
-            for (int i = 0; i <= cut; ++i) {
-                acc += cval[i];
-                if (acc >= r) {
-                    chosen = cidx[i];
-                    break;
-                }
-            }
-            finish(a, chosen);
+            // the first kept candidate reaching r (the last kept when none does)
+            finish(a, cidx[first_reaching(cval, cut + 1, r, acc)]);
         }
         return;
     }
@@ -359,16 +369,9 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         float sum = 0.f;
         for (int i = 0; i < n; ++i) sum += cval[i];
         const float r = variate(a) * sum;
-        int chosen = cidx[0];
-        float acc = 0.f;
-        for (int i = 0; i < n; ++i) {
-            acc += cval[i];
-            if (acc >= r) {
-                chosen = cidx[i];
-                break;
-            }
-        }
-        finish(a, chosen);
+        float acc;
+        const int j = first_reaching(cval, n, r, acc);
+        finish(a, acc >= r ? cidx[j] : cidx[0]);   // the top candidate when no running sum reaches r
     }
 }
 
