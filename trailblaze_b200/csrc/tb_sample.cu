@@ -217,26 +217,25 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     const int seg = ((V + kSmpWarps - 1) / kSmpWarps + kChunk - 1) / kChunk * kChunk;
     const int wlo = min(V, warp * seg), whi = min(V, wlo + seg);
 
-    float m = -FLT_MAX;
-    bool fin = true;
-    for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
-        if (ok) {
-            fin = fin && isfinite(v);
-            m = fmaxf(m, v);
-        }
-    });
-    if (!__syncthreads_and(fin ? 1 : 0)) {
-        if (tid == 0) {
-            atomicExch(a.err, ERR_RUNTIME);
-            finish(a, 0);
-        }
-        return;
-    }
-    m = block_max(m, red);
-
     int n = 0;   // candidates, sorted into cval / cidx by value descending
     const bool topk = a.k > 0 && a.k < V;
+    bool fin = true;   // every logit finite (else the error word and token 0)
     if (!topk) {
+        float m = -FLT_MAX;
+        for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
+            if (ok) {
+                fin = fin && isfinite(v);
+                m = fmaxf(m, v);
+            }
+        });
+        if (!__syncthreads_and(fin ? 1 : 0)) {
+            if (tid == 0) {
+                atomicExch(a.err, ERR_RUNTIME);
+                finish(a, 0);
+            }
+            return;
+        }
+        m = block_max(m, red);
         // ---- nucleus candidates: probabilities >= 1e-4 of the peak ----
         const float p = a.k > 0 ? 0.95f : a.p;   // tb_sample_top_k's fallback for k >= vocab
         const float t = a.temp > 0.01f ? a.temp : 1.0f;
@@ -298,6 +297,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         for_seg(lg, wlo, whi, lane, [&](int, float v, bool ok) {
             uint32_t bin = 256u;
             if (ok) {
+                fin = fin && isfinite(v);
                 const uint32_t key = ord_key(v);
                 if ((key & pmask) == prefix) bin = (key >> shift) & 255u;
             }
@@ -306,7 +306,17 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
                 if (bin < 256u && lane == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
             }
         });
-        __syncthreads();
+        if (shift == 24) {   // the first pass read every logit
+            if (!__syncthreads_and(fin ? 1 : 0)) {
+                if (tid == 0) {
+                    atomicExch(a.err, ERR_RUNTIME);
+                    finish(a, 0);
+                }
+                return;
+            }
+        } else {
+            __syncthreads();
+        }
         if (tid == 0) {
             int acc = 0, b = 255;
             for (; b > 0; --b) {
