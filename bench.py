@@ -2,18 +2,21 @@
 
 Metric: K-quant matvec HBM GB/s (algorithmic bytes / time).
 
-Workload ("step") — BASELINE config 2, the per-type sweep at Qwen3-4B shapes:
+Workload — BASELINE config 2, the per-type sweep at Qwen3-4B shapes:
 q 4096x2560, k 1024x2560, v 1024x2560, gate 9728x2560, up 9728x2560,
 down 2560x9728, lm_head 151936x2560, for each of Q2_K, Q3_K, Q4_K, Q5_K, Q6_K,
 Q8_0 (Q4_K added to the config's five types so the headline type is in the
 line): 42 matvecs, 1.87 GB of weights resident in HBM, seeded synthetic data
-(trailblaze_b200.synth).  Algorithmic bytes per matvec = weights + 4K + 4M.
-One step reads every tensor once, so consecutive reads of a tensor are
-separated by ~1.9 GB of other traffic (> 126 MB L2): no L2 flush is needed.
+(trailblaze_b200.synth), fp32 activations multiplied in fp32 (the library's
+default arithmetic).  Algorithmic bytes per matvec = weights + 4K + 4M.  One
+sweep reads every tensor once, so consecutive reads of a tensor are separated
+by ~1.9 GB of other traffic (> 126 MB L2): no L2 flush is needed.  A "step"
+is R sweeps (--sweeps-per-step, default 100, ~50 ms), so that the K timed
+steps span about a second.
 
-`value`      device time of K steps replayed from one CUDA graph, CUDA events on
-             the launching stream, barrier + synchronize on both sides, max over
-             ranks; whole-job GB/s.
+`value`      device time of K steps (R replays each of one CUDA graph of the
+             sweep), CUDA events on the launching stream, barrier + synchronize
+             on both sides, max over ranks; whole-job GB/s.
 `e2e`        the same sweep through the blocking reference ABI
              tb_cuda_matvec_device(W_dev, qtype, M, K, x_host, out_host): every
              call copies x host->device and y device->host (wall clock).
@@ -23,6 +26,12 @@ separated by ~1.9 GB of other traffic (> 126 MB L2): no L2 flush is needed.
              sources: tb_dispatch_matvec AVX-512/AVX2 tier for Q4_K/Q3_K/Q8_0,
              tb_gguf_dequant_matvec for Q2_K/Q5_K/Q6_K), all host threads, on a
              bounded row sample of the same tensors.
+`reference_gpu` the reference's own CUDA kernels (layer4/tb_gguf_dequant.cu,
+             unmodified, built for sm_100a into oracle/_ref) timed per launch on
+             the same tensors and B200 at their default geometry, beside this
+             library's kernels: the GPU-vs-GPU comparison (no Q2_K kernel there).
+`int16`      the same sweep under the opt-in int16 activation arithmetic
+             (tb_cuda_set_matvec_arith), labelled as such.
 
 N > 1 (torchrun, one process per GPU, NCCL): weak scaling.  Every matrix is a
 row shard of an N-times-taller matrix (rank r owns rows [r*M, (r+1)*M), drawn
@@ -56,7 +65,7 @@ SHAPES = [("q_proj", 4096, 2560), ("k_proj", 1024, 2560), ("v_proj", 1024, 2560)
 TYPES = [Q.Q2_K, Q.Q3_K, Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q8_0]
 SEED = 20261201
 METRIC = "K-quant matvec HBM GB/s (% of 8 TB/s)"
-# reference CPU routine per type (BASELINE.md section 3): 1 = tb_dispatch_matvec AVX-512 tier,
+# reference CPU routine per type: 1 = tb_dispatch_matvec AVX-512 tier,
 # 2 = AVX2 tier, 0 = tb_gguf_dequant_matvec (the dispatch tiers do no work for these types)
 REF_PATH = {Q.Q4_K: 1, Q.Q3_K: 1, Q.Q8_0: 1, Q.Q2_K: 0, Q.Q5_K: 0, Q.Q6_K: 0}
 
@@ -112,8 +121,8 @@ class Clocks:
         except Exception:  # noqa: BLE001
             pass
         self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_dev{index}.csv") \
-            if os.path.isdir(os.path.join(REPO, "gpurun_out")) else f"/tmp/tb_clocks_{os.getpid()}.csv"
+        import tempfile
+        self.path = os.path.join(tempfile.gettempdir(), f"tb_clocks_{os.getpid()}_{index}.csv")
 
     def __enter__(self):
         try:
@@ -359,7 +368,8 @@ def run_reference(args, rank, world):
                    "types": [Q.NAMES[t] for t in TYPES], "shapes": SHAPES},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nthreads, "kind": "reference",
                          "sample": f"{info.get('rows_fraction')} of every matrix's rows per step "
-                                   f"({info.get('bytes')} B), reference routines per BASELINE.md s3, "
+                                   f"({info.get('bytes')} B), tb_dispatch_matvec AVX tier for Q4_K/Q3_K/Q8_0, "
+                                   f"tb_gguf_dequant_matvec for Q2_K/Q5_K/Q6_K, "
                                    f"{info.get('variant')} build"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -391,6 +401,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sweeps-per-step", type=int, default=100,
+                    help="sweeps of the 42 matvecs per timed step (~0.5 ms each)")
+    ap.add_argument("--no-int16", action="store_true", help="skip the opt-in int16-arithmetic sweep")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip timing the reference's own CUDA kernels on the same tensors")
     ap.add_argument("--shape", default=None,
                     help="TYPE:M:K — time this single matvec instead of the sweep (profiling aid)")
     ap.add_argument("--no-decode", action="store_true", help="skip the Qwen3-8B-shape decode tok/s leg")
@@ -474,27 +489,35 @@ def main():
     dy = [torch.empty(M, dtype=torch.float32, device="cuda") for _, _, M, _, _ in items]
     torch.cuda.synchronize()
     alg = [Q.alg_bytes(qt, M, K) for _, qt, M, K, _ in items]
-    step_bytes = sum(alg)
-
-    def step(s):
-        for i, (_, qt, M, K, _) in enumerate(items):
-            r = k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), s)
-            assert r == 1
-
+    sweep_bytes = sum(alg)
+    R = max(1, args.sweeps_per_step)
     sh = stream.cuda_stream
-    with torch.cuda.stream(stream):
-        step(sh)   # sets kernel attributes before capture
-    torch.cuda.synchronize()
-    assert k.tb_cuda_last_error() == 0
-    n0 = k.tb_cuda_launch_count()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        step(stream.cuda_stream)
-    launches_per_step = k.tb_cuda_launch_count() - n0
-    torch.cuda.synchronize()
+    assert k.tb_cuda_get_matvec_arith() == 0   # fp32 activations, fp32 products and sums
 
+    def ours(i, s):
+        _, qt, M, K, _ = items[i]
+        return k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), s)
+
+    def sweep(s):
+        for i in range(len(items)):
+            assert ours(i, s) == 1
+
+    def capture():
+        with torch.cuda.stream(stream):
+            sweep(sh)   # sets kernel attributes and plans before capture
+        torch.cuda.synchronize()
+        assert k.tb_cuda_last_error() == 0
+        n0 = k.tb_cuda_launch_count()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            sweep(stream.cuda_stream)
+        torch.cuda.synchronize()
+        return gr, k.tb_cuda_launch_count() - n0
+
+    g, launches_per_sweep = capture()
     for _ in range(args.warmup):
-        g.replay()
+        for _ in range(R):
+            g.replay()
     torch.cuda.synchronize()
     assert k.tb_cuda_last_error() == 0
 
@@ -507,7 +530,8 @@ def main():
         with torch.cuda.stream(stream):
             ev0.record(stream)
             for _ in range(args.steps):
-                g.replay()
+                for _ in range(R):
+                    g.replay()
             ev1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -516,44 +540,49 @@ def main():
     assert k.tb_cuda_last_error() == 0
     ms = shard.max_over_ranks(ms, dist if world > 1 else None, device="cuda")
     ms_step = ms / args.steps
-    value = shard.whole_job_rate(step_bytes, world, ms_step * 1e-3) / 1e9
+    value = shard.whole_job_rate(sweep_bytes * R, world, ms_step * 1e-3) / 1e9
 
-    # ---- per-launch timing: one step captured with a timing event between
+    # ---- per-launch timing: one sweep captured with a timing event between
     # consecutive launches, replayed; the events run on the launching stream
     # inside the graph, so no host launch gap enters the figures ----
-    per = np.zeros(len(items))
-    reps = max(3, min(args.steps, 10))
-    per_how = "CUDA graph of one step with an event between launches"
-    try:
-        evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(items) + 1)]
-        g2 = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g2, stream=stream):
-            evs[0].record(stream)
-            for i, (_, qt, M, K, _) in enumerate(items):
-                assert k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(),
-                                            stream.cuda_stream) == 1
-                evs[i + 1].record(stream)
-        for _ in range(reps):
-            g2.replay()
-            torch.cuda.synchronize()
-            for i in range(len(items)):
-                per[i] += evs[i].elapsed_time(evs[i + 1])
-        del g2
-    except RuntimeError as e:   # no timing events inside graphs: time single launches
-        log(f"[bench] in-graph timing unavailable ({e}); timing single launches")
-        per[:] = 0
-        per_how = "single launches between CUDA events (includes the host launch gap)"
-        evs2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
-        with torch.cuda.stream(stream):
+    def per_launch(launch, idx, reps):
+        """Average device ms of launch(i, stream) for i in idx, from a graph with an event
+        between launches (or single launches between events if graphs refuse events)."""
+        per = np.zeros(len(idx))
+        try:
+            evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(idx) + 1)]
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=stream):
+                evs[0].record(stream)
+                for j, i in enumerate(idx):
+                    assert launch(i, stream.cuda_stream) == 1
+                    evs[j + 1].record(stream)
             for _ in range(reps):
-                for i, (_, qt, M, K, _) in enumerate(items):
-                    evs2[i][0].record(stream)
-                    k.tb_cuda_matvec_dev(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), sh)
-                    evs2[i][1].record(stream)
+                g2.replay()
                 torch.cuda.synchronize()
-                for i in range(len(items)):
-                    per[i] += evs2[i][0].elapsed_time(evs2[i][1])
-    per /= reps
+                for j in range(len(idx)):
+                    per[j] += evs[j].elapsed_time(evs[j + 1])
+            del g2
+            how = "CUDA graph of one sweep with an event between launches"
+        except RuntimeError as e:   # no timing events inside graphs: time single launches
+            log(f"[bench] in-graph timing unavailable ({e}); timing single launches")
+            per[:] = 0
+            how = "single launches between CUDA events (includes the host launch gap)"
+            ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in idx]
+            with torch.cuda.stream(stream):
+                for _ in range(reps):
+                    for j, i in enumerate(idx):
+                        ev2[j][0].record(stream)
+                        assert launch(i, sh) == 1
+                        ev2[j][1].record(stream)
+                    torch.cuda.synchronize()
+                    for j in range(len(idx)):
+                        per[j] += ev2[j][0].elapsed_time(ev2[j][1])
+        return per / reps, how
+
+    all_idx = list(range(len(items)))
+    reps = max(3, min(args.steps, 10))
+    per, per_how = per_launch(ours, all_idx, reps)
     assert k.tb_cuda_last_error() == 0
     # dominant kernel: a (type) instantiation, ranked by its share of the step
     by_type = {}
@@ -570,31 +599,122 @@ def main():
             traffic = json.load(open(tf)).get(items[top_i][0])
         except ValueError:
             traffic = None
-    per_mv = {items[i][0]: {"us": round(per[i] * 1e3, 2), "GBps": round(alg[i] / (per[i] * 1e-3) / 1e9, 1),
-                            "frac_hbm": round(alg[i] / (per[i] * 1e-3) / 1e9 / hbm, 3)} for i in range(len(items))}
 
-    # ---- end to end through the blocking reference ABI ----
+    def per_table(p):
+        return {items[i][0]: {"us": round(p[j] * 1e3, 2), "GBps": round(alg[i] / (p[j] * 1e-3) / 1e9, 1),
+                              "frac_hbm": round(alg[i] / (p[j] * 1e-3) / 1e9 / hbm, 3)}
+                for j, i in enumerate(all_idx)}
+
+    def per_type(p, idx):
+        out = {}
+        for qt in TYPES:
+            js = [j for j, i in enumerate(idx) if items[i][1] == qt]
+            if js:
+                b = sum(alg[idx[j]] for j in js)
+                t = sum(p[j] for j in js) * 1e-3
+                out[Q.NAMES[qt]] = {"GBps": round(b / t / 1e9, 1), "frac_hbm": round(b / t / 1e9 / hbm, 3),
+                                    "us": round(t * 1e6, 1)}
+        return out
+
+    per_mv = per_table(per)
+
+    # ---- the opt-in int16 activation arithmetic on the same sweep (labelled) ----
+    int16 = None
+    if world == 1 and not args.shape and not args.no_int16:
+        try:
+            assert k.tb_cuda_set_matvec_arith(1) == 0
+            g16, _ = capture()
+            for _ in range(3):
+                g16.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n16 = max(20, R)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(n16):
+                    g16.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            ms16 = e0.elapsed_time(e1) / n16
+            p16, _ = per_launch(ours, all_idx, reps)
+            assert k.tb_cuda_last_error() == 0
+            int16 = {"x_arith": "int16 block-scaled (x rounded to 2^-15 of each 128-activation slot's "
+                                "largest |x|; exact dp4a products and sums); opt-in, narrower than fp32",
+                     "value": round(sweep_bytes / (ms16 * 1e-3) / 1e9, 3), "unit": "GB/s",
+                     "ms_per_sweep": round(ms16, 4), "per_type": per_type(p16, all_idx)}
+            del g16
+        except Exception as e:  # noqa: BLE001 - the int16 leg must not sink the fp32 line
+            int16 = {"unavailable": f"{type(e).__name__}: {e}"}
+        finally:
+            k.tb_cuda_set_matvec_arith(0)
+
+    # ---- the reference's own CUDA kernels on the same tensors (GPU vs GPU) ----
+    ref_gpu = None
+    if world == 1 and not args.no_ref_gpu:
+        try:
+            from oracle.oracle import ReferenceCuda
+            rc = ReferenceCuda()
+            if not hasattr(rc.L, "tbr_cuda_launch"):
+                raise RuntimeError("oracle/_ref/libtbref_cuda.so predates tbr_cuda_launch")
+            ridx = [i for i in all_idx if items[i][1] != Q.Q2_K]   # the reference has no Q2_K kernel
+
+            def theirs(i, s):
+                _, qt, M, K, _ = items[i]
+                return rc.L.tbr_cuda_launch(dW[i].data_ptr(), qt, M, K, dx[K].data_ptr(), dy[i].data_ptr(), s)
+
+            for i in ridx:   # warm-up
+                assert theirs(i, sh) == 1
+            torch.cuda.synchronize()
+            pr, _ = per_launch(theirs, ridx, 3)
+            b = sum(alg[i] for i in ridx)
+            t_ref = float(sum(pr)) * 1e-3
+            t_ours = float(sum(per[all_idx.index(i)] for i in ridx)) * 1e-3
+            po = np.array([per[all_idx.index(i)] for i in ridx])
+            ref_gpu = {"kernels": "k_*_matvec of layer4/tb_gguf_dequant.cu, unmodified, sm_100a, 128 threads x M "
+                                  "CTAs (the reference's default geometry)",
+                       "types": [Q.NAMES[t] for t in TYPES if t != Q.Q2_K],
+                       "value": round(b / t_ref / 1e9, 3), "unit": "GB/s",
+                       "ours_same_subset_GBps": round(b / t_ours / 1e9, 1),
+                       "speedup_ours_over_reference": round(t_ref / t_ours, 2),
+                       "per_type_reference": per_type(pr, ridx),
+                       "per_type_speedup": {n: round(v["us"] / per_type(po, ridx)[n]["us"], 2)
+                                            for n, v in per_type(pr, ridx).items()}}
+        except Exception as e:  # noqa: BLE001 - the comparison leg must not sink the line
+            ref_gpu = {"unavailable": f"{type(e).__name__}: {e}"}
+
+    # ---- end to end through the blocking reference ABI (about a second of sweeps) ----
     e2e = None
     if not args.no_e2e:
         outs = [np.empty(M, dtype=np.float32) for _, _, M, _, _ in items]
         xh = {K: np.ascontiguousarray(x) for K, x in xs_host.items()}
-        for _ in range(2):
+
+        def blocking_sweep():
+            ok = 0
             for i, (_, qt, M, K, _) in enumerate(items):
-                assert k.tb_cuda_matvec_device(dW[i].data_ptr(), qt, M, K, xh[K], outs[i]) == 1
-        e_steps = max(3, args.steps // 2)
+                ok += k.tb_cuda_matvec_device(dW[i].data_ptr(), qt, M, K, xh[K], outs[i]) == 1
+            return ok
+
+        t0 = time.perf_counter()
+        for _ in range(2):
+            assert blocking_sweep() == len(items)
+        est = (time.perf_counter() - t0) / 2
+        e_sweeps = int(min(400, max(3, round(1.0 / max(est, 1e-6)))))
         if world > 1:
+            e_sweeps = int(shard.max_over_ranks(float(e_sweeps), dist, device="cuda"))
             dist.barrier()
         torch.cuda.synchronize()
+        ok = 0
         t0 = time.perf_counter()
-        for _ in range(e_steps):
-            for i, (_, qt, M, K, _) in enumerate(items):
-                k.tb_cuda_matvec_device(dW[i].data_ptr(), qt, M, K, xh[K], outs[i])
+        for _ in range(e_sweeps):
+            ok += blocking_sweep()
         torch.cuda.synchronize()
         dt = shard.max_over_ranks(time.perf_counter() - t0, dist if world > 1 else None, device="cuda")
-        e2e = {"value": round(world * step_bytes * e_steps / dt / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": sum(4 * K for _, _, _, K, _ in items),
-               "d2h_bytes_per_step": sum(4 * M for _, _, M, _, _ in items),
-               "api": "tb_cuda_matvec_device (blocking, host x in / host y out)"}
+        assert ok == e_sweeps * len(items), f"{e_sweeps * len(items) - ok} blocking matvecs failed"
+        e2e = {"value": round(world * sweep_bytes * e_sweeps / dt / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": R * sum(4 * K for _, _, _, K, _ in items),
+               "d2h_bytes_per_step": R * sum(4 * M for _, _, M, _, _ in items),
+               "sweeps_timed": e_sweeps,
+               "api": "tb_cuda_matvec_device (blocking, host x in / host y out), every call's return checked"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -603,7 +723,8 @@ def main():
             rate, info = cpu_sample(hosts, float(os.environ.get("TB_CPU_SECONDS", "12")), os.cpu_count() or 1)
             cpu = {"value": round(rate, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"first {info['rows_fraction']} of every matrix's rows ({info['bytes']} B, "
-                             f"{info['seconds']} s), reference routines per BASELINE.md s3, {info['variant']} build"}
+                             f"{info['seconds']} s), tb_dispatch_matvec AVX tier for Q4_K/Q3_K/Q8_0, "
+                             f"tb_gguf_dequant_matvec for Q2_K/Q5_K/Q6_K, {info['variant']} build"}
         except Exception as e:  # noqa: BLE001 - the baseline must not sink the GPU line
             cpu = {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {type(e).__name__}: {e}"}
@@ -637,24 +758,32 @@ def main():
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "x_arith": "fp32 (fp32 activations, fp32 products and fp32 sums, as the reference's kernels)",
         "data": "synthetic (seeded; trailblaze_b200.synth)",
         "config": {"workload": (f"single matvec {args.shape} (profiling aid, not the headline)" if args.shape
                                 else "qwen3-4b-shape per-type matvec sweep (BASELINE config 2 + Q4_K)"),
                    "types": [Q.NAMES[t] for t in TYPES], "shapes": SHAPES,
-                   "bytes_per_step_per_gpu": step_bytes,
-                   "l2": (f"no flush: each step streams {step_bytes / 1e9:.2f} GB > 126 MB L2 before a tensor is re-read"
-                          if step_bytes > 2 * 126e6 else "inputs partly L2-resident between steps (profiling aid)"),
+                   "sweeps_per_step": R, "bytes_per_sweep_per_gpu": sweep_bytes,
+                   "timed_region_s": round(ms * 1e-3, 3),
+                   "l2": (f"no flush: each sweep streams {sweep_bytes / 1e9:.2f} GB > 126 MB L2 before a tensor "
+                          "is re-read" if sweep_bytes > 2 * 126e6
+                          else "inputs partly L2-resident between sweeps (profiling aid)"),
                    "parallelism": f"row-sharded x{world}, no data-path collective",
-                   "timing": "CUDA graph of one step, CUDA events, max over ranks"},
+                   "timing": "R replays per step of a CUDA graph of one sweep, CUDA events, max over ranks"},
         "frac_of_8TBps": round(value / world / 8000.0, 4),
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches_per_sweep * R * args.steps,
         "roofline": {"bound": "hbm", "kernel": f"k_matvec<{Q.NAMES[top_qt]}> on {items[top_i][0]}",
                      "achieved": round(ach, 1), "peak": hbm, "peak_kind": hbm_kind, "unit": "GB/s",
                      "frac": round(ach / hbm, 4), "traffic": traffic,
                      "alg_bytes_per_launch": alg[top_i], "timing": per_how},
         "per_matvec": per_mv,
+        "per_type": per_type(per, all_idx),
         "clocks": clocks,
     }
+    if int16:
+        line["int16"] = int16
+    if ref_gpu:
+        line["reference_gpu"] = ref_gpu
     if e2e:
         line["e2e"] = e2e
     if decode:

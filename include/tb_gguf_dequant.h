@@ -20,9 +20,11 @@
  *     raw GGUF bytes, rows contiguous.  K must be a multiple of the
  *     block size (256 for K-quants, 32 for Q4_0/Q8_0, 1 for F32/F16/BF16);
  *     other K are rejected with 0 (the reference truncates silently).
- *   - Results: y[m] = sum_k dequant(W)[m,k] * x[k] with fp32 x and fp32
- *     accumulation; dequantisation follows the reference CUDA kernels bit for
- *     bit (tb_gguf_dequant.cu:89-332), and Q2_K follows tb_gguf.c:210-225.
+ *   - Results: y[m] = sum_k dequant(W)[m,k] * x[k] with fp32 x, fp32
+ *     products and fp32 accumulation (the default; tb_cuda_set_matvec_arith
+ *     selects an opt-in narrower integer form); dequantisation follows the
+ *     reference CUDA kernels bit for bit (tb_gguf_dequant.cu:89-332), and
+ *     Q2_K follows tb_gguf.c:210-225.
  *   - The library computes on the GPU only.  There is no CPU fallback inside
  *     it: the caller's own fallback (tb_gguf.c:449-451) stays where it is.
  */
@@ -152,8 +154,30 @@ int   tb_cuda_last_error(void);
  * load (a host-side counter, for launch accounting in benchmarks). */
 unsigned long long tb_cuda_launch_count(void);
 
-/* Library build identifier, e.g. "tb_cuda_sm100 1.0 sm_100a". */
+/* Library build identifier, e.g. "tb_cuda_sm100 1.1 sm_100a". */
 const char *tb_cuda_version(void);
+
+/* Activation arithmetic of the quantized matvecs (every qtype except F32, F16
+ * and BF16, which always compute in fp32), for all later launches of the
+ * process, the decode step's included (a decoder keeps the kernels its CUDA
+ * graph was captured with):
+ *   TB_MATVEC_ARITH_FP32 (0, the default): x stays fp32 and every product and
+ *     sum is an fp32 operation, as in the reference's kernels
+ *     (tb_gguf_dequant.cu:113-114).  Scales are factored out of each
+ *     sub-block's sum, and x is prescaled by exact powers of two, so the
+ *     result differs from the reference's only by fp32 rounding order.
+ *   TB_MATVEC_ARITH_INT16 (1, opt-in): x is rounded to a 16-bit integer at a
+ *     power-of-two scale shared by 128 consecutive activations (the exponent
+ *     of their largest |x|), then products and sums are exact integer dp4a.
+ *     Narrower than the reference's fp32 x: an activation 2^15 times smaller
+ *     than the largest of its 128-slot rounds to zero.
+ * Returns the previous mode, or -1 for an unknown mode (nothing changes).
+ * Host-only: it launches nothing and needs no device. */
+#define TB_MATVEC_ARITH_FP32  0
+#define TB_MATVEC_ARITH_INT16 1
+int   tb_cuda_set_matvec_arith(int mode);
+/* The current mode (TB_MATVEC_ARITH_*). */
+int   tb_cuda_get_matvec_arith(void);
 
 /* No counterpart in the reference.  Blocking matvec like tb_cuda_matvec_device
  * (x_host must not be NULL), but it allocates nothing, not even on first use:

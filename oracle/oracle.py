@@ -28,8 +28,12 @@ _vp = ctypes.c_void_p
 
 
 def build(ref: str | None = None) -> None:
-    """Run oracle/Makefile (liboracle.so always; _ref/ when the reference tree exists)."""
+    """Run oracle/Makefile (liboracle.so always; _ref/ when the reference tree exists).
+
+    The reference checkout is `ref`, else $TB_REFERENCE_DIR, else none (the
+    prebuilt _ref/ files are used as they are)."""
     cmd = ["make", "-s", "-C", HERE]
+    ref = ref or os.environ.get("TB_REFERENCE_DIR")
     if ref:
         cmd.append(f"REF={ref}")
     subprocess.run(cmd + ["oracle"], check=True)
@@ -147,13 +151,18 @@ class Reference:
 
 
 class ReferenceCuda:
-    """The reference's unmodified CUDA kernels (tb_gguf_dequant.cu) built for sm_100a."""
+    """The reference's unmodified CUDA kernels (tb_gguf_dequant.cu) built for sm_100a,
+    plus tbr_cuda_launch (oracle/ref_cuda_launch.cu): one kernel launch on device
+    pointers at the reference's default geometry, stream-ordered, for timing."""
 
     def __init__(self):
         path = os.path.join(REF_DIR, "libtbref_cuda.so")
         if not os.path.exists(path):
             raise FileNotFoundError(path)
         L = ctypes.CDLL(path)
+        if hasattr(L, "tbr_cuda_launch"):
+            L.tbr_cuda_launch.restype = ctypes.c_int
+            L.tbr_cuda_launch.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]
         L.tb_cuda_init.restype = ctypes.c_int
         L.tb_cuda_upload_tensor.restype = _vp
         L.tb_cuda_upload_tensor.argtypes = [_vp, ctypes.c_size_t]

@@ -2,13 +2,16 @@
 reference's own CUDA kernels, always through the C ABI.
 
 Tolerances (north star): dequantisation bit-exact; matvec relative L2 error
-<= 1e-3 against the fp64-accumulated oracle.  The float-path types (F32,
-F16, BF16) accumulate in fp32 (observed ~1e-7); the integer-path types
-round x to 2^-15 of each column slot's largest |x| and are exact after that
-(observed 2e-5 to 4e-5 over many rows of Gaussian x, up to ~1e-4 for a
-single short row, whose rounding errors do not average out).  STRICT = 3e-4
-is asserted as well to catch systematic errors that the contract tolerance
-would hide.
+<= 1e-3 against the fp64-accumulated oracle.  Two activation arithmetics are
+checked:
+  fp32 (the default): fp32 x, fp32 products and sums, as the reference's
+       kernels; only rounding order differs, so FP32_TOL = 2e-5 is asserted
+       besides the contract tolerance (a single short row, whose rounding does not average out,
+       reaches ~6e-6).
+  int16 (opt-in): x rounded to 2^-15 of each 128-slot's largest |x|, exact
+       after that (observed 2e-5 to 4e-5 over many rows of Gaussian x, up to
+       ~1e-4 for a single short row); STRICT = 3e-4 is asserted besides the
+       contract tolerance.
 """
 import os
 import subprocess
@@ -24,6 +27,9 @@ pytestmark = pytest.mark.gpu
 
 TOL = 1e-3
 STRICT = 3e-4
+FP32_TOL = 2e-5
+ARITH = {"fp32": 0, "int16": 1}
+QUANT = [Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K, Q.Q8_0, Q.Q4_0, Q.Q8_K]
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -38,6 +44,20 @@ def dev_bytes(a: np.ndarray, offset: int = 0):
     buf = t.zeros(a.size + offset + 64, dtype=t.uint8, device="cuda")
     buf[offset:offset + a.size] = t.from_numpy(np.ascontiguousarray(a)).cuda()
     return buf, buf.data_ptr() + offset
+
+
+@pytest.fixture(params=["fp32", "int16"])
+def arith(request, kq):
+    """Runs the test under each activation arithmetic, restoring the default after."""
+    prev = kq.tb_cuda_set_matvec_arith(ARITH[request.param])
+    assert prev == 0
+    yield request.param
+    assert kq.tb_cuda_set_matvec_arith(prev) == ARITH[request.param]
+
+
+def bound(arith, qt):
+    """The tight bound of an arithmetic (the float types are fp32 in both)."""
+    return FP32_TOL if arith == "fp32" or qt in (Q.F32, Q.F16, Q.BF16) else STRICT
 
 
 def gpu_matvec(kq, qt, wptr, M, K, x):
@@ -125,7 +145,7 @@ MV_SHAPES = [(1, 256), (3, 512), (33, 768), (97, 2560), (130, 4096), (7, 12288),
 
 @pytest.mark.parametrize("qt", Q.ALL, ids=[Q.NAMES[t] for t in Q.ALL])
 @pytest.mark.parametrize("M,K", MV_SHAPES)
-def test_matvec_parity(kq, oracle, qt, M, K):
+def test_matvec_parity(kq, oracle, arith, qt, M, K):
     W = synth.weights(qt, M, K, seed=1000 + M + K, tensor=qt)
     x = synth.activations(K, seed=M)
     buf, p = dev_bytes(W)
@@ -134,20 +154,20 @@ def test_matvec_parity(kq, oracle, qt, M, K):
     e = rel_l2(y, ref)
     assert np.all(np.isfinite(y))
     assert e <= TOL, e
-    assert e <= STRICT, e
+    assert e <= bound(arith, qt), e
 
 
 @pytest.mark.parametrize("qt", [Q.Q4_K, Q.Q5_K, Q.Q6_K, Q.Q3_K, Q.Q2_K, Q.Q8_0, Q.Q4_0, Q.Q8_K, Q.F16, Q.F32, Q.BF16],
                          ids=lambda t: Q.NAMES[t])
 @pytest.mark.parametrize("offset", [1, 2, 3, 6, 14])
-def test_matvec_unaligned_base(kq, oracle, qt, offset):
+def test_matvec_unaligned_base(kq, oracle, arith, qt, offset):
     """W at an arbitrary byte offset (e.g. a packed tensor sliced at a row boundary)."""
     M, K = 45, 1024
     W = synth.weights(qt, M, K, seed=77 + offset, tensor=qt)
     x = synth.activations(K, seed=offset)
     buf, p = dev_bytes(W, offset)
     e = rel_l2(gpu_matvec(kq, qt, p, M, K, x), oracle.matvec_f64(qt, W, M, K, x, SEM_CUDA))
-    assert e <= STRICT, e
+    assert e <= bound(arith, qt), e
 
 
 @pytest.mark.parametrize("qt", [Q.F32, Q.F16, Q.BF16])
@@ -163,27 +183,80 @@ def test_matvec_float_ragged_k(kq, oracle, qt, K):
 
 @pytest.mark.parametrize("qt", [Q.Q8_0, Q.Q4_0])
 @pytest.mark.parametrize("K", [32, 96, 288, 2080])
-def test_matvec_block32_partial_unit(kq, oracle, qt, K):
+def test_matvec_block32_partial_unit(kq, oracle, arith, qt, K):
     M = 23
     W = synth.weights(qt, M, K, seed=K, tensor=qt)
     x = synth.activations(K, seed=K + 2)
     buf, p = dev_bytes(W)
     e = rel_l2(gpu_matvec(kq, qt, p, M, K, x), oracle.matvec_f64(qt, W, M, K, x, SEM_CUDA))
-    assert e <= STRICT, e
+    assert e <= bound(arith, qt), e
 
 
-def test_matvec_golden(kq, golden):
+def test_matvec_golden(kq, golden, arith):
     for qt in Q.ALL:
         n = Q.NAMES[qt]
         M, K = (int(v) for v in golden[f"{n}/MK"])
         buf, p = dev_bytes(golden[f"{n}/W"])
         y = gpu_matvec(kq, qt, p, M, K, golden[f"{n}/x"])
-        assert rel_l2(y, golden[f"{n}/cuda_mv64"]) <= STRICT, n
+        assert rel_l2(y, golden[f"{n}/cuda_mv64"]) <= bound(arith, qt), n
 
 
-def test_matvec_deterministic_and_scale_exact(kq):
-    """Run-to-run bitwise identical; x -> 2x gives exactly 2y (power-of-two scaling is exact
-    through the prescaled fp32 path)."""
+# ---------------------------------------------------------------- heavy-tailed activations
+def outlier_x(K, seed, big=1000.0):
+    """N(0,1) activations with one +-big outlier in every run of 128 (a seeded position and
+    sign per run), like the few huge channels of real decode activations."""
+    x = synth.activations(K, seed=seed).astype(np.float32)
+    rng = np.random.default_rng(seed)
+    base = np.arange(0, K, 128)
+    pos = base + rng.integers(0, np.minimum(128, K - base))
+    x[pos] = np.where(rng.integers(0, 2, pos.size) == 1, big, -big).astype(np.float32)
+    return x, pos
+
+
+def student_t_x(K, seed, dof=3):
+    return np.random.default_rng(seed).standard_t(dof, K).astype(np.float32)
+
+
+@pytest.mark.parametrize("qt", QUANT, ids=lambda t: Q.NAMES[t])
+@pytest.mark.parametrize("dist", ["outlier", "student_t3"])
+def test_matvec_heavy_tailed(kq, oracle, arith, qt, dist):
+    """Heavy-tailed x against the fp64 oracle at the contract tolerance, on both arithmetics;
+    the fp32 path also at its own tight bound."""
+    M, K = 256, 4096
+    W = synth.weights(qt, M, K, seed=61, tensor=qt)
+    x = outlier_x(K, 17)[0] if dist == "outlier" else student_t_x(K, 17)
+    buf, p = dev_bytes(W)
+    e = rel_l2(gpu_matvec(kq, qt, p, M, K, x), oracle.matvec_f64(qt, W, M, K, x, SEM_CUDA))
+    assert e <= TOL, e
+    if arith == "fp32":
+        assert e <= FP32_TOL, e
+
+
+@pytest.mark.parametrize("qt", QUANT, ids=lambda t: Q.NAMES[t])
+def test_small_activations_beside_outliers(kq, oracle, arith, qt):
+    """What y's relative L2 hides: the contribution of the ordinary activations in a 128-slot
+    that also holds a +-1000 outlier.  y(x) - y(outliers only), both on the GPU, against the
+    fp64 matvec of the ordinary activations alone.  The fp32 path keeps it to rounding; the
+    int16 path rounds every activation of such a slot to 1000 * 2^-15 (0.03), which leaves
+    an error of several percent in that contribution: the documented failure mode of the
+    opt-in arithmetic, asserted here so that it stays documented."""
+    M, K = 256, 4096
+    W = synth.weights(qt, M, K, seed=62, tensor=qt)
+    x, pos = outlier_x(K, 23)
+    xo = np.zeros_like(x)
+    xo[pos] = x[pos]
+    buf, p = dev_bytes(W)
+    d = gpu_matvec(kq, qt, p, M, K, x).astype(np.float64) - gpu_matvec(kq, qt, p, M, K, xo)
+    e = rel_l2(d, oracle.matvec_f64(qt, W, M, K, x - xo, SEM_CUDA))
+    if arith == "fp32":
+        assert e <= 1e-4, e
+    else:
+        assert e > TOL, e
+
+
+def test_matvec_deterministic_and_scale_exact(kq, arith):
+    """Run-to-run bitwise identical; x -> 2x gives exactly 2y (power-of-two scaling of x
+    only moves the slot exponents, in both arithmetics)."""
     for qt in (Q.Q4_K, Q.Q6_K, Q.Q2_K, Q.Q8_0):
         M, K = 1000, 4096
         W = synth.weights(qt, M, K, seed=5, tensor=qt)
@@ -204,8 +277,9 @@ def test_matvec_linearity(kq):
     buf, p = dev_bytes(W)
     y = gpu_matvec(kq, qt, p, M, K, x1 + x2)
     ys = gpu_matvec(kq, qt, p, M, K, x1).astype(np.float64) + gpu_matvec(kq, qt, p, M, K, x2)
-    # each of the three results carries its own x rounding (2^-15 of a slot's max)
-    assert rel_l2(y, ys) <= STRICT
+    # fp32: rounding only; int16: each of the three results carries its own x rounding
+    # (2^-15 of a slot's max)
+    assert rel_l2(y, ys) <= (FP32_TOL if kq.tb_cuda_get_matvec_arith() == 0 else STRICT)
 
 
 def test_expert_slice_rows(kq, oracle):

@@ -58,6 +58,8 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_last_error": (c_int, []),
         "tb_cuda_launch_count": (ctypes.c_ulonglong, []),
         "tb_cuda_version": (ctypes.c_char_p, []),
+        "tb_cuda_set_matvec_arith": (c_int, [c_int]),
+        "tb_cuda_get_matvec_arith": (c_int, []),
         "tb_cuda_matvec_device_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, fp, fp]),
         "tb_cuda_matvec_fused_dev": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
                                              c_void_p, c_void_p, ctypes.c_float, c_void_p, c_int, c_void_p]),
@@ -93,14 +95,15 @@ def lib() -> ctypes.CDLL:
 
 def exported_symbols() -> list[str]:
     """Names the header declares (checked against the .so's dynamic symbols by the tests)."""
-    return [
+    return sorted([
         "tb_cuda_init", "tb_cuda_upload_tensor", "tb_cuda_free_tensor", "tb_cuda_upload_x",
         "tb_cuda_set_snap", "tb_cuda_matvec_device", "tb_cuda_sync_all", "tb_cuda_cleanup",
         "tb_cuda_matvec_dev", "tb_cuda_dequant_dev", "tb_cuda_qtype_info", "tb_cuda_last_error",
-        "tb_cuda_launch_count", "tb_cuda_version", "tb_cuda_matvec_device_noalloc",
+        "tb_cuda_launch_count", "tb_cuda_version", "tb_cuda_set_matvec_arith", "tb_cuda_get_matvec_arith",
+        "tb_cuda_matvec_device_noalloc",
         "tb_cuda_matvec_fused_dev", "tb_cuda_matvec_experts_dev", "tb_cuda_sample_dev", "tb_cuda_qgemm_dev", "tb_cuda_dec_create", "tb_cuda_dec_set_layer", "tb_cuda_dec_set_head",
         "tb_cuda_dec_kv", "tb_cuda_dec_kv_copy", "tb_cuda_dec_read", "tb_cuda_dec_create_tp",
         "tb_cuda_dec_tp_handle", "tb_cuda_dec_tp_connect", "tb_cuda_dec_create_moe", "tb_cuda_dec_set_moe_layer",
         "tb_cuda_dec_step", "tb_cuda_dec_generate", "tb_cuda_dec_set_sampling", "tb_cuda_dec_generate_u",
         "tb_cuda_dec_destroy",
-    ]
+    ])

@@ -180,7 +180,7 @@ bool smem_attr_once(const void *kernel, int bytes)
 
 extern "C" {
 
-const char *tb_cuda_version(void) { return "tb_cuda_sm100 1.0 sm_100a"; }
+const char *tb_cuda_version(void) { return "tb_cuda_sm100 1.1 sm_100a"; }
 
 int tb_cuda_qtype_info(int qtype, int *block_weights, int *block_bytes)
 {
@@ -444,6 +444,10 @@ int tb_cuda_last_error(void)
 }
 
 unsigned long long tb_cuda_launch_count(void) { return g_launches.load(); }
+
+int tb_cuda_set_matvec_arith(int mode) { return tb::mv_set_arith(mode); }
+
+int tb_cuda_get_matvec_arith(void) { return tb::mv_get_arith(); }
 
 int tb_cuda_matvec_device_noalloc(const void *W_device, int qtype, int M, int K, const float *x_host,
                                   float *out_host)

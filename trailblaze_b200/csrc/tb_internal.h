@@ -46,6 +46,16 @@ struct MvFuse {
     uint32_t x_stride = 0, y_stride = 0;
 };
 
+// Activation arithmetic of the quantized matvec decoders.  FP32: x stays fp32
+// (exact power-of-two prescaling), fp32 products and sums, like the reference
+// (tb_gguf_dequant.cu:113-114); the default.  INT16: x rounded to 16-bit
+// integers at a per-128-weight power-of-two scale, exact integer products and
+// sums (dp4a); opt-in, narrower than the reference's fp32 arithmetic.
+enum MvArith : int { MV_ARITH_FP32 = 0, MV_ARITH_INT16 = 1 };
+// Sets the mode for later launches; returns the previous one (-1: bad mode).
+int mv_set_arith(int mode);
+int mv_get_arith();
+
 // Launch the matvec d_y[M] = dequant(W) @ d_x[K] on `st`.  Returns 1 when the
 // launch was issued, 0 for unsupported arguments or a launch error.
 int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d_y,

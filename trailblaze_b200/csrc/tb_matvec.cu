@@ -26,12 +26,14 @@
 //     in a fixed order, writes y and refills the stage with the tile NST
 //     ahead.  The summation order never depends on timing, so results are
 //     run-to-run deterministic.  Every wait is bounded.
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 
 #include "tb_common.cuh"
 #include "tb_decoders.cuh"
+#include "tb_decoders_f32.cuh"
 #include "tb_internal.h"
 
 namespace tb {
@@ -296,7 +298,36 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     const uint32_t xq_bytes = ngp * 64u, xe_off = xq_bytes;
     bool split = false;
     if constexpr (D::kInt) split = a.nst >= 2 && (a.nst - 1ull) * a.cap >= xq_bytes + 4ull * a.cs;
-    if (split) {
+    if constexpr (IsF32X<D>::value) {
+        // fp32 decoders: the record is the slot's transformed activations
+        // themselves plus the magnitude bits of its largest |x|.  All threads,
+        // 8 activations each; the QPS quarters of a slot are neighbouring lanes.
+        constexpr uint32_t QPS = 4u * D::GPL;
+        const uint32_t nq = 4 * ngp;
+        for (uint32_t base = 0; base < nq; base += nthr) {   // same trip count in every thread
+            const uint32_t q = base + tid;
+            const bool have = q < nq;
+            float v[8];
+            if (have) {
+                load_x_part<8>(a, grp * a.x_stride, 8 * q, v, ss);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = 0.f;
+            }
+            uint32_t mb = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+#pragma unroll
+            for (uint32_t o = 1; o < QPS; o <<= 1) mb = max(mb, __shfl_xor_sync(kFull, mb, o));
+            if (have) {
+                uint32_t *rec = table + (q / QPS) * D::REC;
+                float4 *dst = reinterpret_cast<float4 *>(rec + (q % QPS) * 8);
+                dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+                dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+                if (q % QPS == 0) rec[XF_N] = mb;
+            }
+        }
+    } else if (split) {
         uint8_t *xq = ring + a.cap;                          // [ngp * 4][8] int16, then [cs] int32 exponents
         int *xe = reinterpret_cast<int *>(xq + xe_off);
         constexpr uint32_t QPS = 4u * D::GPL;                // quarters per slot (a power of two <= 32)
@@ -583,9 +614,12 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
     // two stages in shared memory (the per-tile cost is paid once per rpl
     // rows); then as many stages as fit.
     p.nst = 0;
-    for (uint32_t rpl = kMaxRpl; rpl >= 1 && !p.nst; --rpl) {
+    // TB_MV_STAGE_KB / TB_MV_RPL_MAX: planner tuning knobs (stage bytes, rows per thread)
+    static const uint32_t stage_max = getenv("TB_MV_STAGE_KB") ? 1024u * atoi(getenv("TB_MV_STAGE_KB")) : kStageMax;
+    static const uint32_t rpl_max = getenv("TB_MV_RPL_MAX") ? atoi(getenv("TB_MV_RPL_MAX")) : kMaxRpl;
+    for (uint32_t rpl = rpl_max; rpl >= 1 && !p.nst; --rpl) {
         const unsigned long long bytes = static_cast<unsigned long long>(p.phases) * rpl * row_bytes;
-        if (rpl > 1 && bytes > kStageMax) continue;
+        if (rpl > 1 && bytes > stage_max) continue;
         if (p.ymode == MV_Y_SWIGLU_PAIRS && (p.phases * rpl) % 2) continue;   // tiles of whole pairs
         const uint32_t tr = p.phases * rpl;
         const uint32_t cap = static_cast<uint32_t>((bytes + 32 + 127) & ~127ull);
@@ -681,6 +715,19 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
     return cudaGetLastError() == cudaSuccess ? 1 : 0;
 }
 
+// Activation arithmetic of the quantized types: MV_ARITH_FP32 (default) or the
+// opt-in MV_ARITH_INT16.  Read at each launch; a captured graph keeps the
+// kernels it was captured with.
+static std::atomic<int> g_arith{MV_ARITH_FP32};
+
+int mv_set_arith(int mode)
+{
+    if (mode != MV_ARITH_FP32 && mode != MV_ARITH_INT16) return -1;
+    return g_arith.exchange(mode);
+}
+
+int mv_get_arith() { return g_arith.load(); }
+
 int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d_y,
               cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit, const MvFuse *fuse)
 {
@@ -746,6 +793,23 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
     const uintptr_t wa = reinterpret_cast<uintptr_t>(W);
     const bool a16 = (wa & 15u) == 0 && (a.row_bytes & 15u) == 0 && (a.w_stride & 15u) == 0;
     const bool a4 = (wa & 3u) == 0 && (a.row_bytes & 3u) == 0 && (a.w_stride & 3u) == 0;
+    if (g_arith.load(std::memory_order_relaxed) == MV_ARITH_FP32) {
+        switch (qtype) {
+        case QT_Q4_K:
+            return a16 ? launch_dec<DecQ4KF<true>>(a, num_sms, st) : launch_dec<DecQ4KF<false>>(a, num_sms, st);
+        case QT_Q5_K:
+            return a16 ? launch_dec<DecQ5KF<true>>(a, num_sms, st) : launch_dec<DecQ5KF<false>>(a, num_sms, st);
+        case QT_Q6_K: return launch_dec<DecQ6KF>(a, num_sms, st);
+        case QT_Q3_K:
+        case QT_IQ3_S: return launch_dec<DecQ3KF>(a, num_sms, st);
+        case QT_Q2_K:
+            return a4 ? launch_dec<DecQ2KF<true>>(a, num_sms, st) : launch_dec<DecQ2KF<false>>(a, num_sms, st);
+        case QT_Q8_0: return launch_dec<DecQ80F>(a, num_sms, st);
+        case QT_Q4_0: return launch_dec<DecQ40F>(a, num_sms, st);
+        case QT_Q8_K: return launch_dec<DecQ8KF>(a, num_sms, st);
+        default: break;   // F32 / F16 / BF16: the float decoders below (fp32 already)
+        }
+    }
     switch (qtype) {
     case QT_Q4_K: return a16 ? launch_dec<DecQ4K<true>>(a, num_sms, st) : launch_dec<DecQ4K<false>>(a, num_sms, st);
     case QT_Q5_K: return a16 ? launch_dec<DecQ5K<true>>(a, num_sms, st) : launch_dec<DecQ5K<false>>(a, num_sms, st);

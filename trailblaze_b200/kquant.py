@@ -122,6 +122,12 @@ class KQuantLib:
     def tb_cuda_version(self) -> str:
         return self.L.tb_cuda_version().decode()
 
+    def tb_cuda_set_matvec_arith(self, mode: int) -> int:
+        return int(self.L.tb_cuda_set_matvec_arith(mode))
+
+    def tb_cuda_get_matvec_arith(self) -> int:
+        return int(self.L.tb_cuda_get_matvec_arith())
+
     # ---- convenience ------------------------------------------------------------------
     def matvec(self, W_dev: int, qtype: int, M: int, K: int, x: np.ndarray) -> np.ndarray:
         """Blocking y = dequant(W) @ x through tb_cuda_matvec_device; raises on a 0 return."""
