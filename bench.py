@@ -202,15 +202,15 @@ def cpu_sample(items, budget_s: float, nthreads: int, repeat: int = 1):
     return tot_b / tot_t / 1e9, info
 
 
-def decode_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: int = 1, dist=None):
-    """BASELINE config 3: batch-1 greedy decode of a random-init Qwen3-8B-shape model
-    (Q4_K weights, Q6_K ffn_down and output) with an N(0,1) fp32 KV prefix of ctx
-    positions, through the library's graph-replayed decoder (tb_cuda_dec_*).  With
-    world > 1 each rank holds its tensor-parallel share (heads, FFN rows, vocabulary
-    split; the o / down partials and the greedy pairs cross NVLink by the library's
-    own peer stores); times are the slowest rank's."""
-    from trailblaze_b200.decoder import QWEN3_8B, synthetic_model
-    shape = QWEN3_8B
+def decode_leg(shape, ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: int = 1, dist=None):
+    """Batch-1 greedy decode of a random-init model of `shape` with an N(0,1) fp32 KV
+    prefix of ctx positions, through the library's graph-replayed decoder
+    (tb_cuda_dec_*).  With world > 1 each rank holds its share of the same model
+    (heads, FFN rows or experts, vocabulary), the o / FFN partials and the greedy
+    pairs crossing NVLink by the library's own peer stores; times are the slowest
+    rank's, and rank 0 also runs the whole model on its GPU to check that the
+    tokens and the last logits are those of the single-device decode."""
+    from trailblaze_b200.decoder import synthetic_model
     t0 = time.perf_counter()
     dec = synthetic_model(shape, max_ctx=ctx + n + e2e_tokens + 8, ctx=ctx, rank=rank, world=world)
     log(f"[bench] decode model built in {time.perf_counter() - t0:.1f}s")
@@ -227,6 +227,9 @@ def decode_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: i
         ms = shard.max_over_ranks(ms, dist if world > 1 else None, device="cuda")
         tok_s = n / (ms * 1e-3)
         bpt = shape.bytes_per_token(ctx + n // 2)
+        # the same n steps again (same positions, so the same cache), tokens and last logits kept
+        lg = np.zeros(shape.vocab // world, dtype=np.float32)
+        toks, _ = dec.generate(1, ctx, n, want_tokens=True, logits=lg)
         tok = 1
         if world > 1:
             dist.barrier()
@@ -238,51 +241,59 @@ def decode_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: i
         if world > 1:
             dist.barrier()   # no rank unmaps its region while a peer may still store into it
         dec.close()
+    check = {}
+    if world > 1:
+        import torch
+        parts = [torch.zeros(shape.vocab // world, device="cuda") for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(lg).cuda())
+        if rank == 0:
+            lg_tp = torch.cat(parts).cpu().numpy().astype(np.float64)
+            one = synthetic_model(shape, max_ctx=ctx + n + e2e_tokens + 8, ctx=ctx)
+            try:
+                lg1 = np.zeros(shape.vocab, dtype=np.float32)
+                toks1, _ = one.generate(1, ctx, n, want_tokens=True, logits=lg1)
+            finally:
+                one.close()
+            check = {"tokens_match_n1": toks == toks1,
+                     "tokens_equal": int(sum(a == b for a, b in zip(toks, toks1))), "tokens": n,
+                     "last_logits_rel_l2_vs_n1": float(np.linalg.norm(lg_tp - lg1) / np.linalg.norm(lg1))}
+        dist.barrier()
     hbm, kind = peaks()
-    return {"model": "qwen3-8b shape: 36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, ffn 12288, "
-                     "vocab 151936; Q4_K weights, Q6_K ffn_down and output; fp32 KV",
-            "ctx": ctx, "tokens": n, "tok_per_s": round(tok_s, 2), "ms_per_token": round(ms / n, 4),
-            "parallelism": f"tensor-parallel x{world}" if world > 1 else "one GPU",
+    return {"ctx": ctx, "tokens": n, "tok_per_s": round(tok_s, 2), "ms_per_token": round(ms / n, 4),
             "bytes_per_token": bpt, "GBps": round(bpt * tok_s / 1e9, 1),
             "frac_of_hbm": round(bpt * tok_s / 1e9 / (hbm * world), 4), "hbm_peak_kind": kind,
             "e2e_tok_per_s": round(e2e, 2), "e2e_api": "tb_cuda_dec_step (blocking, token read back)",
-            "launches_per_token": 1 + 5 * shape.n_layers + 2,
-            "order": "reference (RoPE before QK-norm, K rotated n_heads/n_kv_heads times)"}
+            "order": "reference (RoPE before QK-norm, K rotated n_heads/n_kv_heads times)", **check}
 
 
-def moe_bench(ctx: int, n: int, e2e_tokens: int = 16):
-    """BASELINE config 4 on one GPU: batch-1 greedy decode of a random-init
-    Qwen3-30B-A3B-shape routed model (48 layers, hidden 2048, 32 q / 4 kv heads,
-    128 experts of FFN 768, top 8; Q4_K experts, Q6_K attention and output, fp32
-    router) with an N(0,1) fp32 KV prefix of ctx positions.  Each layer: q/k/v,
-    attention, o, router logits, top-k, the 8 selected experts' gate/up and down
-    as two expert-group matvecs (expert ids read on the device), combine."""
-    from trailblaze_b200.decoder import QWEN3_30B_A3B, synthetic_model
-    shape = QWEN3_30B_A3B
-    t0 = time.perf_counter()
-    dec = synthetic_model(shape, max_ctx=ctx + n + e2e_tokens + 8, ctx=ctx)
-    log(f"[bench] MoE model built in {time.perf_counter() - t0:.1f}s")
-    try:
-        dec.generate(1, ctx, 4, want_tokens=False)
-        _, ms = dec.generate(1, ctx, n, want_tokens=False)
-        tok_s = n / (ms * 1e-3)
-        bpt = shape.bytes_per_token(ctx + n // 2)
-        tok = 1
-        t1 = time.perf_counter()
-        for i in range(e2e_tokens):
-            tok = dec.step(tok, ctx + i)
-        e2e = e2e_tokens / (time.perf_counter() - t1)
-    finally:
-        dec.close()
-    hbm, kind = peaks()
+def decode_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: int = 1, dist=None):
+    """BASELINE config 3: batch-1 greedy decode of a random-init Qwen3-8B-shape model
+    (Q4_K weights, Q6_K ffn_down and output), tensor-parallel at world > 1 (q/k/v by
+    heads, o and down by K columns, gate/up by FFN rows, output by vocabulary)."""
+    from trailblaze_b200.decoder import QWEN3_8B as shape
+    d = decode_leg(shape, ctx, n, e2e_tokens, rank, world, dist)
+    return {"model": "qwen3-8b shape: 36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, ffn 12288, "
+                     "vocab 151936; Q4_K weights, Q6_K ffn_down and output; fp32 KV",
+            "parallelism": f"tensor-parallel x{world}" if world > 1 else "one GPU",
+            "launches_per_token": 1 + 5 * shape.n_layers + 2, **d}
+
+
+def moe_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: int = 1, dist=None):
+    """batch-1 greedy decode of a random-init Qwen3-30B-A3B-shape
+    routed model (48 layers, hidden 2048, 32 q / 4 kv heads, 128 experts of FFN 768,
+    top 8; Q4_K experts, Q6_K attention and output, fp32 router).  Each layer: q/k/v,
+    attention, o, router logits, top-k, the selected experts' gate/up and down as two
+    expert-group matvecs (expert ids read on the device), combine.  At world > 1 the
+    experts are sharded (128 / world per rank), attention is head-sharded (a kv head
+    shared by world / 4 ranks at 8), the router replicated, and each rank's weighted
+    expert output is summed across ranks over NVLink."""
+    from trailblaze_b200.decoder import QWEN3_30B_A3B as shape
+    d = decode_leg(shape, ctx, n, e2e_tokens, rank, world, dist)
     return {"model": "qwen3-30b-a3b shape: 48 layers, hidden 2048, 32 q / 4 kv heads, head_dim 128, 128 experts "
                      "(FFN 768) top 8, vocab 151936; Q4_K experts, Q6_K attention and output, fp32 router; fp32 KV",
-            "ctx": ctx, "tokens": n, "tok_per_s": round(tok_s, 2), "ms_per_token": round(ms / n, 4),
-            "parallelism": "one GPU (all 128 experts resident)",
-            "bytes_per_token": bpt, "GBps": round(bpt * tok_s / 1e9, 1),
-            "frac_of_hbm": round(bpt * tok_s / 1e9 / hbm, 4), "hbm_peak_kind": kind,
-            "e2e_tok_per_s": round(e2e, 2), "e2e_api": "tb_cuda_dec_step (blocking, token read back)",
-            "launches_per_token": 1 + 8 * shape.n_layers + 2}
+            "parallelism": (f"expert-parallel x{world} ({shape.n_experts // world} experts per GPU), attention "
+                            f"head-sharded" if world > 1 else "one GPU (all 128 experts resident)"),
+            "launches_per_token": 1 + 8 * shape.n_layers + 2, **d}
 
 
 def tensor_peak():
@@ -456,10 +467,12 @@ def main():
 
     if args.moe_only:
         with Clocks(local) as clk:
-            d = moe_bench(args.moe_ctx, args.decode_tokens)
+            d = moe_bench(args.moe_ctx, args.decode_tokens, rank=rank, world=world, dist=dist if world > 1 else None)
+        if world > 1:
+            dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"metric": "Qwen3-30B-A3B-shape MoE decode tok/s", "value": d["tok_per_s"],
-                              "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+                              "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
                               "dtype": "fp32", "data": "synthetic (seeded torch generator on the device)",
                               "config": {"workload": "MoE decode only (profiling aid)"}, "moe": d,
                               "clocks": clk.summary()}), flush=True)
@@ -738,9 +751,10 @@ def main():
         except Exception as e:  # noqa: BLE001 - the decode leg must not sink the sweep line
             decode = {"unavailable": f"{type(e).__name__}: {e}"}
     moe = None
-    if world == 1 and not args.no_moe and not args.shape:
+    if not args.no_moe and not args.shape:
         try:
-            moe = moe_bench(args.moe_ctx, args.decode_tokens)
+            moe = moe_bench(args.moe_ctx, args.decode_tokens, rank=rank, world=world,
+                            dist=dist if world > 1 else None)
         except Exception as e:  # noqa: BLE001 - the MoE leg must not sink the sweep line
             moe = {"unavailable": f"{type(e).__name__}: {e}"}
     prefill = None

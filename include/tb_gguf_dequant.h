@@ -192,6 +192,29 @@ int   tb_cuda_get_matvec_arith(void);
 int   tb_cuda_matvec_device_noalloc(const void *W_device, int qtype, int M, int K,
                                     const float *x_host, float *out_host);
 
+/* Model upload into one device arena (replaces the per-tensor cudaMalloc and
+ * synchronous pageable copy of layer4/tb_gguf.c:469-520 tb_gguf_cuda_upload_all
+ * / tb_gguf_dequant.cu:411-416 tb_cuda_upload_tensor).  tb_cuda_arena_create
+ * makes one device allocation of `bytes` on the current device; each upload
+ * reserves the next 256-byte aligned range and copies the host bytes into it
+ * unchanged, in 32 MB chunks through two pinned staging buffers so the host
+ * copy of one chunk overlaps the DMA of the previous one.  Blocking; returns
+ * the device pointer, NULL when the arena is full or a copy fails.  Any qtype
+ * (Q2_K, F32, BF16 included): the bytes are not interpreted.
+ *   _rows: rows [r_lo, r_hi) of a tensor of row_bytes-byte rows (a
+ *          tensor-parallel rank's q/k/v heads, FFN row pairs or vocabulary);
+ *   _cols: bytes [b_lo, b_hi) of each of the M rows, packed (a K slice on
+ *          block boundaries: a rank's o / ffn_down columns), so a rank never
+ *          holds the whole tensor on its device.
+ * Thread-safe per arena; destroy frees everything the arena holds. */
+void  *tb_cuda_arena_create(size_t bytes);
+void  *tb_cuda_arena_upload(void *arena, const void *host, size_t n);
+void  *tb_cuda_arena_upload_rows(void *arena, const void *host, size_t row_bytes, int r_lo, int r_hi);
+void  *tb_cuda_arena_upload_cols(void *arena, const void *host, int M, size_t row_bytes, size_t b_lo,
+                                 size_t b_hi);
+size_t tb_cuda_arena_used(void *arena);
+void   tb_cuda_arena_destroy(void *arena);
+
 /* Prefill GEMM on the tensor cores (tcgen05, bf16 x bf16 -> fp32):
  * C_dev[T][N] = A_bf16_dev[T][K] x dequant(W_dev)[N][K]^T, row t of C being
  * the matvec of W with token t (the batched form of the reference's
@@ -266,7 +289,10 @@ int    tb_cuda_dec_generate(void *dec, int token, int pos, int n, int *tokens_ou
 /* Sampling instead of the greedy argmax (the choice of layer4/tb_infer.c:
  * 1031-1038): temperature < 0.01 greedy (the default); else top_k > 0 the
  * top-k sampler, top_k = 0 the nucleus of top_p (tb_cuda_sample_dev's rules,
- * inside the step's graph).  One device (world 1).  1 = ok. */
+ * inside the step's graph).  Under tensor or expert parallelism every rank
+ * gathers the whole vocabulary's logits from the others over NVLink and
+ * samples them with the same variate, so all ranks take the same token (each
+ * rank must pass the same variates).  1 = ok. */
 int    tb_cuda_dec_set_sampling(void *dec, float temperature, int top_k, float top_p);
 /* tb_cuda_dec_generate with the variates: step i samples with u[i] in [0, 1)
  * (the reference's rand() / (RAND_MAX + 1.0f)).  Required while sampling is
@@ -281,8 +307,10 @@ int    tb_cuda_dec_generate_u(void *dec, int token, int pos, int n, const float 
  * (vocab); for a routed decoder 6 the last layer's router logits (n_experts),
  * 7 its expert weights and 8 its expert ids (top_k; int32 bits in the float
  * slots), rank order, 9 the selected experts' SwiGLU activations (top_k x
- * ffn_dim, rank order).  Blocking.  1 = ok, 0 for an unknown vector, one
- * this decoder does not have, or n past its size. */
+ * ffn_dim, rank order; under expert parallelism this rank's selected experts,
+ * local order), 10 the number of this rank's selected experts and 11 their
+ * local indices (expert parallelism only; int32 bits).  Blocking.  1 = ok, 0
+ * for an unknown vector, one this decoder does not have, or n past its size. */
 int    tb_cuda_dec_read(void *dec, int which, float *host, int n);
 
 /* Tensor parallelism over `world` GPUs (2, 4 or 8; one process per GPU), the
@@ -323,6 +351,19 @@ void  *tb_cuda_dec_create_moe(const tb_dec_config *cfg, int n_experts, int top_k
  * gate row i of blk.N.ffn_gate_exps, row 2i+1 = up row i of
  * blk.N.ffn_up_exps); w_down_exps [n_experts][hidden][F]
  * (blk.N.ffn_down_exps).  1 = ok. */
+/* Expert parallelism over `world` GPUs (one process per GPU; n_experts a
+ * multiple of world, top_k <= 32): rank r holds experts [r E/w, (r+1) E/w),
+ * its tb_cuda_dec_set_moe_layer tensors being those experts' rows
+ * ([E/w][2F][hidden] and [E/w][hidden][F]) and the router whole.  Attention,
+ * the output and the exchange are those of tb_cuda_dec_create_tp (rank r's q
+ * heads [r NH/w, (r+1) NH/w); when world is a multiple of n_kv_heads, kv head
+ * r / (world / n_kv_heads), its K and V cache held by that many ranks).  Each
+ * layer every rank computes the same router top k, runs its own selected
+ * experts on the whole grid, and sends its weighted share of the FFN output
+ * to every rank over NVLink (peer stores, like the down partials); the next
+ * layer adds the world shares in rank order.  Connected with
+ * tb_cuda_dec_tp_handle / _tp_connect.  NULL on unsupported shapes. */
+void  *tb_cuda_dec_create_moe_tp(const tb_dec_config *cfg, int n_experts, int top_k, int rank, int world);
 int    tb_cuda_dec_set_moe_layer(void *dec, int layer, const void *w_router, int router_qtype,
                                  const void *w_gate_up_exps, int gate_up_qtype, const void *w_down_exps,
                                  int down_qtype);

@@ -151,13 +151,59 @@ def attention(q, kc, vc, n_heads, n_kv_heads):
     return out
 
 
+class LazyMat:
+    """An M x K GGUF tensor kept as raw bytes: `@ x` dequantises chunks of rows
+    (CUDA semantics) to float64 and multiplies them, `[i]` is one dequantised
+    row, `.rows(a, b)` the tensor of rows [a, b).  For model widths whose
+    float64 matrices would not fit in memory."""
+
+    def __init__(self, o, qt, W, M, K):
+        self.o, self.qt, self.W, self.M, self.K = o, qt, W, M, K
+        self.rb = o.L.tbo_row_bytes(qt, K)
+
+    def rows(self, a, b):
+        return LazyMat(self.o, self.qt, self.W[a * self.rb:b * self.rb], b - a, self.K)
+
+    def __getitem__(self, i):
+        return self.o.dequant(self.qt, self.W[i * self.rb:(i + 1) * self.rb], 1, self.K, SEM_CUDA)[0].astype(
+            np.float64)
+
+    def __matmul__(self, x):
+        x = np.asarray(x, np.float64)
+        out = np.empty(self.M)
+        step = max(1, (1 << 23) // self.K)
+        for r0 in range(0, self.M, step):
+            r1 = min(self.M, r0 + step)
+            out[r0:r1] = self.rows(r0, r1).dense() @ x
+        return out
+
+    def dense(self):
+        return self.o.dequant(self.qt, self.W, self.M, self.K, SEM_CUDA).astype(np.float64)
+
+
+class LazyExperts:
+    """E experts of R rows each, stacked in one GGUF tensor: `[e]` is expert e's LazyMat."""
+
+    def __init__(self, o, qt, W, E, R, K):
+        self.m = LazyMat(o, qt, W, E * R, K)
+        self.R = R
+
+    def __getitem__(self, e):
+        return self.m.rows(e * self.R, (e + 1) * self.R)
+
+
 class DecodeOracle:
-    def __init__(self, m: DecodeModel, quirks: bool = True):
+    def __init__(self, m: DecodeModel, quirks: bool = True, lazy: bool = False):
+        """lazy: keep the tensors as raw bytes and dequantise them chunk by chunk at every
+        product (full model widths); otherwise dequantise every tensor once."""
         self.m = m
         self.quirks = quirks
         o = Oracle()
         H, NH, NK, HD, F = m.hidden, m.n_heads, m.n_kv_heads, m.head_dim, m.ffn_dim
-        deq = lambda W, qt, M, K: o.dequant(qt, W, M, K, SEM_CUDA).astype(np.float64)  # noqa: E731
+        if lazy:
+            deq = lambda W, qt, M, K: LazyMat(o, qt, W, M, K)  # noqa: E731
+        else:
+            deq = lambda W, qt, M, K: o.dequant(qt, W, M, K, SEM_CUDA).astype(np.float64)  # noqa: E731
         self.emb = deq(m.emb, m.emb_qt, m.vocab, H)
         self.lm = deq(m.lm, m.lm_qt, m.vocab, H)
         self.out_norm = m.out_norm.astype(np.float64)
@@ -166,8 +212,10 @@ class DecodeOracle:
         for w in m.layers:
             routed = dict(
                 wr=deq(w["wr"], w["r_qt"], E, H),
-                wgu_e=deq(w["wgu_e"], w["gue_qt"], E * 2 * F, H).reshape(E, 2 * F, H),
-                wd_e=deq(w["wd_e"], w["de_qt"], E * H, F).reshape(E, H, F)) if E else dict(
+                wgu_e=(LazyExperts(o, w["gue_qt"], w["wgu_e"], E, 2 * F, H) if lazy else
+                       deq(w["wgu_e"], w["gue_qt"], E * 2 * F, H).reshape(E, 2 * F, H)),
+                wd_e=(LazyExperts(o, w["de_qt"], w["wd_e"], E, H, F) if lazy else
+                      deq(w["wd_e"], w["de_qt"], E * H, F).reshape(E, H, F))) if E else dict(
                 wgu=deq(w["wgu"], w["gu_qt"], 2 * F, H),
                 wd=deq(w["wd"], w["d_qt"], H, F))
             self.L.append(dict(

@@ -71,3 +71,36 @@ def test_sample_rejects_and_reports(kq):
     assert r == 1 and tok == 0
     assert kq.L.tb_cuda_last_error() == 2                  # reported once, then cleared
     assert kq.L.tb_cuda_last_error() == 0
+
+
+@pytest.mark.parametrize("k", [40, 2048])
+@pytest.mark.parametrize("bad", [np.nan, np.inf])
+def test_top_k_non_finite_reported_once(kq, k, bad):
+    """Top-k checks finiteness inside its first radix pass: a NaN or +Inf logit gives
+    token 0 and the error word 2, reported once."""
+    lg = np.random.default_rng(5).standard_normal(151936).astype(np.float32)
+    lg[77777] = bad
+    r, tok = _sample(kq, lg, k, 0.0, 1.0, 0.3)
+    assert r == 1 and tok == 0
+    assert kq.L.tb_cuda_last_error() == 2
+    assert kq.L.tb_cuda_last_error() == 0
+
+
+def test_sampled_decode_step_non_finite_logits(kq):
+    """A sampled decode step whose logits are not finite (an output norm of inf) reports
+    the error word through the step's 0 return, and the next call works again."""
+    import torch
+    from test_gpu_decode import GpuDecoder, make_model
+    m = make_model(n_layers=1, hidden=256, nh=2, nk=1, ffn=256, vocab=512, max_ctx=16, seed=4)
+    m.out_norm = np.full(m.hidden, np.inf, dtype=np.float32)
+    g = GpuDecoder(kq, m, quirks=True)
+    try:
+        assert kq.L.tb_cuda_dec_set_sampling(g.d, 1.0, 40, 0.0) == 1
+        u = np.array([0.25], dtype=np.float32)
+        toks = (ctypes.c_int * 1)()
+        fp = ctypes.POINTER(ctypes.c_float)
+        assert kq.L.tb_cuda_dec_generate_u(g.d, 1, 0, 1, u.ctypes.data_as(fp), toks, None, None) == 0
+        assert kq.L.tb_cuda_last_error() == 0          # the step's own error word was read and cleared
+        torch.cuda.synchronize()
+    finally:
+        kq.L.tb_cuda_dec_destroy(g.d)

@@ -58,3 +58,20 @@ def test_top_k_matches_reference(ref, case):
     libc.srand(30 + case)
     want = L.tb_sample_top_k(lg.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), V, k, t)
     assert S.sample_top_k(lg, k, t, u) == want
+
+
+def test_top_k_tie_order_differs_from_reference(ref):
+    """A recorded divergence: among equal logits at the k boundary the reference's
+    selection sort swaps elements and keeps the later index (logits [2, 2, 3], k = 2:
+    indices 2 and 1), while the oracle and the device keep the lower index (2 and 0).
+    With u below the first candidate's probability both pick index 2; above it, the
+    reference picks 1 and the oracle 0."""
+    L, libc = ref
+    lg = np.array([2.0, 2.0, 3.0], dtype=np.float32)
+    fp = ctypes.POINTER(ctypes.c_float)
+    seed = next(s for s in range(1000) if _u(libc, s) > 0.9)
+    u = _u(libc, seed)
+    libc.srand(seed)
+    want = L.tb_sample_top_k(lg.ctypes.data_as(fp), 3, 2, 1.0)
+    assert want == 1
+    assert S.sample_top_k(lg, 2, 1.0, u) == 0

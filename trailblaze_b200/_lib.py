@@ -59,6 +59,12 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_launch_count": (ctypes.c_ulonglong, []),
         "tb_cuda_version": (ctypes.c_char_p, []),
         "tb_cuda_set_matvec_arith": (c_int, [c_int]),
+        "tb_cuda_arena_create": (c_void_p, [c_size_t]),
+        "tb_cuda_arena_upload": (c_void_p, [c_void_p, c_void_p, c_size_t]),
+        "tb_cuda_arena_upload_rows": (c_void_p, [c_void_p, c_void_p, c_size_t, c_int, c_int]),
+        "tb_cuda_arena_upload_cols": (c_void_p, [c_void_p, c_void_p, c_int, c_size_t, c_size_t, c_size_t]),
+        "tb_cuda_arena_used": (c_size_t, [c_void_p]),
+        "tb_cuda_arena_destroy": (None, [c_void_p]),
         "tb_cuda_get_matvec_arith": (c_int, []),
         "tb_cuda_matvec_device_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, fp, fp]),
         "tb_cuda_matvec_fused_dev": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
@@ -78,6 +84,7 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_dec_tp_handle": (c_int, [c_void_p, c_void_p]),
         "tb_cuda_dec_tp_connect": (c_int, [c_void_p, c_void_p]),
         "tb_cuda_dec_create_moe": (c_void_p, [ctypes.POINTER(DecConfig), c_int, c_int]),
+        "tb_cuda_dec_create_moe_tp": (c_void_p, [ctypes.POINTER(DecConfig), c_int, c_int, c_int, c_int]),
         "tb_cuda_dec_set_moe_layer": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int]),
         "tb_cuda_dec_step": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_int), fp]),
         "tb_cuda_dec_generate": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_int), fp, fp]),
@@ -100,10 +107,12 @@ def exported_symbols() -> list[str]:
         "tb_cuda_set_snap", "tb_cuda_matvec_device", "tb_cuda_sync_all", "tb_cuda_cleanup",
         "tb_cuda_matvec_dev", "tb_cuda_dequant_dev", "tb_cuda_qtype_info", "tb_cuda_last_error",
         "tb_cuda_launch_count", "tb_cuda_version", "tb_cuda_set_matvec_arith", "tb_cuda_get_matvec_arith",
+        "tb_cuda_arena_create", "tb_cuda_arena_upload", "tb_cuda_arena_upload_rows", "tb_cuda_arena_upload_cols",
+        "tb_cuda_arena_used", "tb_cuda_arena_destroy",
         "tb_cuda_matvec_device_noalloc",
         "tb_cuda_matvec_fused_dev", "tb_cuda_matvec_experts_dev", "tb_cuda_sample_dev", "tb_cuda_qgemm_dev", "tb_cuda_dec_create", "tb_cuda_dec_set_layer", "tb_cuda_dec_set_head",
         "tb_cuda_dec_kv", "tb_cuda_dec_kv_copy", "tb_cuda_dec_read", "tb_cuda_dec_create_tp",
-        "tb_cuda_dec_tp_handle", "tb_cuda_dec_tp_connect", "tb_cuda_dec_create_moe", "tb_cuda_dec_set_moe_layer",
+        "tb_cuda_dec_tp_handle", "tb_cuda_dec_tp_connect", "tb_cuda_dec_create_moe", "tb_cuda_dec_create_moe_tp", "tb_cuda_dec_set_moe_layer",
         "tb_cuda_dec_step", "tb_cuda_dec_generate", "tb_cuda_dec_set_sampling", "tb_cuda_dec_generate_u",
         "tb_cuda_dec_destroy",
     ])

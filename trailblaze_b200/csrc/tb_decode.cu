@@ -673,8 +673,12 @@ static constexpr int kMoeThreads = 256;   // experts per router at most (tb_infe
 // scan selects the same set except among exactly equal probabilities, and
 // lists it in scan order; only the rounding of the weighted sum depends on
 // that order.)  A non-finite logit sets the error word and selects nothing.
+// Expert parallelism (ep_n > 0): this rank holds experts [ep_lo, ep_lo +
+// ep_n); the selected ones among them are also listed, in rank order, as local
+// indices lids[0..*nloc) with their weights lw.
 __global__ void __launch_bounds__(kMoeThreads) k_moe_topk(const float *logits, int E, int k, int *ids, float *wts,
-                                                           int *err)
+                                                           int *err, int ep_lo, int ep_n, int *lids, float *lw,
+                                                           int *nloc)
 {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -725,7 +729,22 @@ __global__ void __launch_bounds__(kMoeThreads) k_moe_topk(const float *logits, i
         s_sum = ws;
     }
     __syncthreads();
-    if (e < k) wts[e] = s_sum > 0.f ? sel[e] / s_sum : sel[e];
+    const float wk = s_sum > 0.f ? sel[e < k ? e : 0] / s_sum : sel[e < k ? e : 0];
+    if (e < k) wts[e] = wk;
+    if (ep_n > 0) {
+        // the local experts in rank order: a ballot over the k ranks (k <= 32 lanes of warp 0)
+        if (warp == 0) {
+            const int id = e < k ? ids[e] : -1;
+            const bool mine = e < k && id >= ep_lo && id < ep_lo + ep_n;
+            const unsigned bal = __ballot_sync(0xFFFFFFFFu, mine);
+            if (mine) {
+                const int j = __popc(bal & ((1u << lane) - 1u));
+                lids[j] = id - ep_lo;
+                lw[j] = wk;
+            }
+            if (e == 0) *nloc = __popc(bal);
+        }
+    }
 }
 
 // x[i] = x2[i] + sum_r wts[r] * t[r][i], r in rank order (tb_infer.c:845-848,
@@ -740,6 +759,76 @@ __global__ void __launch_bounds__(kMoeThreads) k_moe_combine(const float *x2, co
     float acc = 0.f;
     for (int r = 0; r < k; ++r) acc = fmaf(wts[r], t[static_cast<size_t>(r) * H + i], acc);
     x[i] = x2[i] + acc;
+}
+
+// The end of an exchange launch: this CTA's stores are fenced at system
+// scope before its ticket, and the CTA whose ticket completes the launch
+// counts this rank once on each of the world counters.
+__device__ __forceinline__ void exchange_arrive(unsigned long long *tk, unsigned long long *const *ctr, int world)
+{
+    __threadfence_system();
+    __syncthreads();
+    __shared__ unsigned long long s_t;
+    if (threadIdx.x == 0) s_t = atomicAdd(tk, 1ull);
+    __syncthreads();
+    if ((s_t + 1) % gridDim.x == 0) {
+        __threadfence_system();
+        if (threadIdx.x < static_cast<unsigned>(world)) atomicAdd_system(ctr[threadIdx.x], 1ull);
+    }
+}
+
+// Tensor-parallel sampling: this rank's slice of the logits (n values, its
+// vocabulary rows [base, base + n)) into every rank's whole-vocabulary buffer
+// over NVLink, then each CTA counts itself on every rank's counter; the
+// sampler waits for world x gridDim.x arrivals per step.
+struct GatherTP {
+    float *full[kMaxRanks];
+    unsigned long long *ctr[kMaxRanks];
+    unsigned long long *tk;
+    int world, base;
+};
+__global__ void __launch_bounds__(256) k_logits_gather(const float *lg, int n, const GatherTP g)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int G = gridDim.x;
+    const int i0 = static_cast<int>((static_cast<long long>(n) * blockIdx.x) / G);
+    const int i1 = static_cast<int>((static_cast<long long>(n) * (blockIdx.x + 1)) / G);
+    for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += 256) {
+        const float v = lg[i];
+        for (int p = 0; p < g.world; ++p) g.full[p][g.base + i] = v;
+    }
+    exchange_arrive(g.tk, g.ctr, g.world);
+}
+
+// Expert-parallel combine: this rank's share sum_{j < *nloc} lw[j] * t[j][i]
+// of the routed FFN's output, stored into row `rank` of every rank's exchange
+// slots over NVLink (ys[p] + rank * H), then every CTA counts itself on every
+// rank's arrival counter (system scope), as the tensor-parallel matvecs do:
+// the next layer's q/k/v matvec adds the world rows, in rank order, onto x2.
+// The grid must be the CTA count the receivers expect (min(H, SMs)).
+struct CombineEP {
+    float *ys[kMaxRanks];
+    unsigned long long *ctr[kMaxRanks];
+    unsigned long long *tk;   // this device's ticket counter
+    int world;
+};
+
+__global__ void __launch_bounds__(kMoeThreads) k_moe_combine_ep(const float *t, const float *lw, const int *nloc,
+                                                                 int k, int H, const CombineEP ex)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int n = min(max(*nloc, 0), k);
+    const int G = gridDim.x;
+    const int i0 = static_cast<int>((static_cast<long long>(H) * blockIdx.x) / G);
+    const int i1 = static_cast<int>((static_cast<long long>(H) * (blockIdx.x + 1)) / G);
+    for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += kMoeThreads) {
+        float acc = 0.f;
+        for (int j = 0; j < n; ++j) acc = fmaf(lw[j], t[static_cast<size_t>(j) * H + i], acc);
+        for (int p = 0; p < ex.world; ++p) ex.ys[p][i] = acc;
+    }
+    exchange_arrive(ex.tk, ex.ctr, ex.world);
 }
 
 // ---------------------------------------------------------------------------
@@ -795,17 +884,24 @@ struct Decoder {
     int rank = 0, world = 1, vocab_full = 0;
     // exchange region (own memory, mapped by the peers through CUDA IPC):
     // [o partials world x H][down partials world x H][argmax pairs world]
-    // [arrival counters: o, down, argmax]
+    // [arrival counters: o, down, argmax, logits][whole-vocabulary logits (sampling)]
     uint8_t *xch = nullptr;
-    size_t off_xd = 0, off_am = 0, off_ctr = 0, xch_bytes = 0;
+    size_t off_xd = 0, off_am = 0, off_ctr = 0, off_full = 0, xch_bytes = 0;
     uint8_t *peer[kMaxRanks] = {};   // every rank's region, this rank's own included
     bool peer_opened[kMaxRanks] = {};
     int *epoch = nullptr;            // steps completed (device)
+    unsigned long long *tk = nullptr;   // ticket counters: o, down / combine, logits gather (device)
     // mixture of experts (n_exp > 0): every layer's FFN is routed to top_k of
     // n_exp experts of cfg.ffn_dim rows each
     int n_exp = 0, top_k = 0;
     float *rlog = nullptr, *wts = nullptr, *hbuf = nullptr, *tbuf = nullptr;
     int *ids = nullptr;
+    // expert parallelism (routed, world > 1): this rank holds experts
+    // [rank * n_loc_exp, (rank + 1) * n_loc_exp); the selected local ones as
+    // local indices lids[0..*nloc) with weights lw (rank order)
+    int n_loc_exp = 0;
+    int *lids = nullptr, *nloc = nullptr;
+    float *lw = nullptr;
     // sampling (tb_infer.c:1031-1038): greedy while smp_temp < 0.01, else
     // top-k when smp_k > 0, else the nucleus of smp_p; step i of a run draws
     // the caller's variate u_buf[i] (u_idx counts the steps on the device)
@@ -816,6 +912,7 @@ struct Decoder {
     bool sampling() const { return smp_temp >= 0.01f; }
 
     float *slot_o(int p) const { return reinterpret_cast<float *>(peer[p]); }
+    float *full_logits(int p) const { return reinterpret_cast<float *>(peer[p] + off_full); }
     float *slot_d(int p) const { return reinterpret_cast<float *>(peer[p] + off_xd); }
     unsigned long long *am(int p) const { return reinterpret_cast<unsigned long long *>(peer[p] + off_am); }
     unsigned long long *ctr(int p, int k) const { return reinterpret_cast<unsigned long long *>(peer[p] + off_ctr) + k; }
@@ -843,6 +940,8 @@ struct Decoder {
     bool enqueue(cudaStream_t s);
     bool enqueue_tp(cudaStream_t s);
     bool enqueue_moe(cudaStream_t s, const DecLayer &w);
+    bool enqueue_moe_ep(cudaStream_t s, const DecLayer &w, int l, unsigned long long per_x,
+                        unsigned long long per_step);
 };
 
 // The routed FFN of one layer (tb_infer.c:753-850): router logits of
@@ -861,7 +960,8 @@ bool Decoder::enqueue_moe(cudaStream_t s, const DecLayer &w)
     f.w_early = true;
     if (!mv_launch(w.wr, w.r_qt, n_exp, H, x2, rlog, s, err, sms, lim, &f)) return false;
     if (!launch_pdl(k_moe_topk, dim3(1), dim3(kMoeThreads), 0, s, static_cast<const float *>(rlog), n_exp, top_k,
-                    ids, wts, err))
+                    ids, wts, err, 0, 0, static_cast<int *>(nullptr), static_cast<float *>(nullptr),
+                    static_cast<int *>(nullptr)))
         return false;
     const Geom gg = geom_of(w.gue_qt), gd = geom_of(w.de_qt);
     f = MvFuse{};
@@ -886,6 +986,69 @@ bool Decoder::enqueue_moe(cudaStream_t s, const DecLayer &w)
     return launch_pdl(k_moe_combine, dim3((H + kMoeThreads - 1) / kMoeThreads), dim3(kMoeThreads), 0, s,
                       static_cast<const float *>(x2), static_cast<const float *>(tbuf),
                       static_cast<const float *>(wts), top_k, H, x);
+}
+
+// The routed FFN of one layer under expert parallelism (world > 1): the
+// router (replicated, all n_exp experts) on rmsnorm(x2), x2 = x + the o
+// partials (gathered here, its CTA 0 writing x2); the top k; this rank's
+// selected experts' gate/up and down as expert groups whose count is read on
+// the device (the whole grid shared among them); then this rank's weighted
+// share of the FFN output to every rank (k_moe_combine_ep), which the next
+// q/k/v matvec gathers like the down partials of the dense step.
+bool Decoder::enqueue_moe_ep(cudaStream_t s, const DecLayer &w, int l, unsigned long long per_x,
+                             unsigned long long per_step)
+{
+    const DecConfig &c = cfg;
+    const int H = c.hidden, F = c.ffn_dim;
+    const uint32_t lim = 1u << 22;
+    MvFuse f;
+    f.xmode = MV_X_RMSNORM;
+    f.nw = w.ffn_norm;
+    f.eps = c.norm_eps;
+    f.w_early = true;
+    f.xs = slot_o(rank);
+    f.nsl = static_cast<uint32_t>(world);
+    f.xs_ctr = ctr(rank, 0);
+    f.xs_epoch = epoch;
+    f.xs_mul = per_step;
+    f.xs_add = static_cast<unsigned long long>(l + 1) * per_x;
+    f.xout = x2;
+    if (!mv_launch(w.wr, w.r_qt, n_exp, H, x, rlog, s, err, sms, lim, &f)) return false;
+    if (!launch_pdl(k_moe_topk, dim3(1), dim3(kMoeThreads), 0, s, static_cast<const float *>(rlog), n_exp, top_k,
+                    ids, wts, err, rank * n_loc_exp, n_loc_exp, lids, lw, nloc))
+        return false;
+    const Geom gg = geom_of(w.gue_qt), gd = geom_of(w.de_qt);
+    f = MvFuse{};
+    f.xmode = MV_X_RMSNORM;
+    f.nw = w.ffn_norm;
+    f.eps = c.norm_eps;
+    f.ymode = MV_Y_SWIGLU_PAIRS;
+    f.ng = static_cast<uint32_t>(top_k);
+    f.ng_dev = nloc;
+    f.n_experts = static_cast<uint32_t>(n_loc_exp);
+    f.ids = lids;
+    f.w_stride = 2ull * F * (H / gg.block_weights) * gg.block_bytes;
+    f.y_stride = static_cast<uint32_t>(F);
+    if (!mv_launch(w.wgu_e, w.gue_qt, 2 * F, H, x2, hbuf, s, err, sms, lim, &f)) return false;
+    f = MvFuse{};
+    f.ng = static_cast<uint32_t>(top_k);
+    f.ng_dev = nloc;
+    f.n_experts = static_cast<uint32_t>(n_loc_exp);
+    f.ids = lids;
+    f.w_stride = static_cast<unsigned long long>(H) * (F / gd.block_weights) * gd.block_bytes;
+    f.x_stride = static_cast<uint32_t>(F);
+    f.y_stride = static_cast<uint32_t>(H);
+    if (!mv_launch(w.wd_e, w.de_qt, H, F, hbuf, tbuf, s, err, sms, lim, &f)) return false;
+    CombineEP ex{};
+    ex.world = world;
+    ex.tk = tk + 1;
+    for (int p = 0; p < world; ++p) {
+        ex.ys[p] = slot_d(p) + static_cast<size_t>(rank) * H;
+        ex.ctr[p] = ctr(p, 1);
+    }
+    const int G = H < sms ? H : sms;
+    return launch_pdl(k_moe_combine_ep, dim3(G), dim3(kMoeThreads), 0, s, static_cast<const float *>(tbuf),
+                      static_cast<const float *>(lw), static_cast<const int *>(nloc), top_k, H, ex);
 }
 
 bool Decoder::enqueue(cudaStream_t s)
@@ -983,7 +1146,7 @@ bool Decoder::enqueue_tp(cudaStream_t s)
     const int H = c.hidden, NH = c.n_heads, NK = c.n_kv_heads, HD = c.head_dim, F = c.ffn_dim, L = c.n_layers;
     const int QKV = (NH + 2 * NK) * HD;
     const uint32_t lim = 1u << 22;
-    const unsigned long long per_x = static_cast<unsigned long long>(world) * static_cast<unsigned long long>(H < sms ? H : sms);
+    const unsigned long long per_x = static_cast<unsigned long long>(world);   // one arrival per rank
     const unsigned long long per_step = static_cast<unsigned long long>(L) * per_x;
     auto gather_in = [&](MvFuse &f, int kind, unsigned long long add, float *xout) {
         f.xs = kind == 0 ? slot_o(rank) : slot_d(rank);
@@ -1000,6 +1163,7 @@ bool Decoder::enqueue_tp(cudaStream_t s)
             f.ys[p] = (kind == 0 ? slot_o(p) : slot_d(p)) + static_cast<size_t>(rank) * H;
             f.yctr[p] = ctr(p, kind);
         }
+        f.ytk = tk + kind;
     };
     if (!dq_embed_launch(emb, emb_qt, vocab_full, H, tok, x, s)) return false;
     for (int l = 0; l < L; ++l) {
@@ -1040,6 +1204,10 @@ bool Decoder::enqueue_tp(cudaStream_t s)
         f.w_early = true;
         scatter_out(f, 0);
         if (!mv_launch(w.wo, w.o_qt, H, NH * HD, att, x2, s, err, sms, lim, &f)) return false;
+        if (n_exp) {
+            if (!enqueue_moe_ep(s, w, l, per_x, per_step)) return false;
+            continue;
+        }
         // act = swiglu(gate, up) of this rank's rows, of rmsnorm(x2), x2 = x + the o partials
         f = MvFuse{};
         f.xmode = MV_X_RMSNORM;
@@ -1062,6 +1230,28 @@ bool Decoder::enqueue_tp(cudaStream_t s)
     f.w_early = true;
     gather_in(f, 1, static_cast<unsigned long long>(L) * per_x, nullptr);
     if (!mv_launch(lm, lm_qt, c.vocab, H, x2, logits, s, err, sms, lim, &f)) return false;
+    if (sampling()) {
+        // every rank gathers the whole vocabulary's logits and samples them with
+        // the same variate, so all ranks take the same token
+        GatherTP g{};
+        g.world = world;
+        g.base = rank * c.vocab;
+        g.tk = tk + 2;
+        for (int p = 0; p < world; ++p) {
+            g.full[p] = full_logits(p);
+            g.ctr[p] = ctr(p, 3);
+        }
+        const int G = sms;
+        if (!launch_pdl(k_logits_gather, dim3(G), dim3(256), 0, s, static_cast<const float *>(logits), c.vocab, g))
+            return false;
+        SmpTP tp{};
+        tp.ctr = ctr(rank, 3);
+        tp.epoch = epoch;
+        tp.per_step = static_cast<unsigned long long>(world);
+        tp.wait_limit = lim;
+        return sample_launch(full_logits(rank), vocab_full, smp_k, smp_p, smp_temp, 0.f, tok, err, s, u_buf, u_idx,
+                             pos, &tp) != 0;
+    }
     ArgTP tp{};
     tp.rank = rank;
     tp.world = world;
@@ -1096,7 +1286,7 @@ static void dec_free(Decoder *d)
     if (d->ev1) cudaEventDestroy(d->ev1);
     void *bufs[] = {d->x,    d->x2,  d->qkv, d->att, d->gu,     d->logits, d->kc,   d->vc,   d->part,
                     d->argv, d->argi, d->tok, d->pos, d->counts, d->err,    d->rlog, d->wts, d->hbuf,
-                    d->tbuf, d->ids, d->u_buf, d->u_idx};
+                    d->tbuf, d->ids, d->u_buf, d->u_idx, d->lids, d->lw, d->nloc};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->hostio) cudaFreeHost(d->hostio);
@@ -1104,6 +1294,7 @@ static void dec_free(Decoder *d)
         if (d->peer_opened[p]) cudaIpcCloseMemHandle(d->peer[p]);
     if (d->xch) cudaFree(d->xch);
     if (d->epoch) cudaFree(d->epoch);
+    if (d->tk) cudaFree(d->tk);
     delete[] d->layers;
     delete d;
 }
@@ -1112,21 +1303,26 @@ static void dec_free(Decoder *d)
 // (world 1 = the whole model on one device).
 Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, int top_k = 0)
 {
-    if (n_exp < 0 || n_exp > kMoeThreads || (n_exp && (top_k < 1 || top_k > n_exp || world != 1))) {
-        fprintf(stderr, "[tb_cuda] decoder: unsupported experts (%d, top %d; at most %d, one device)\n", n_exp, top_k,
-                kMoeThreads);
+    if (n_exp < 0 || n_exp > kMoeThreads ||
+        (n_exp && (top_k < 1 || top_k > n_exp || top_k > 32 || n_exp % world))) {
+        fprintf(stderr, "[tb_cuda] decoder: unsupported experts (%d, top %d; at most %d experts and top 32, "
+                        "a whole number per rank)\n", n_exp, top_k, kMoeThreads);
         return nullptr;
     }
+    // kv heads: split over the ranks, or (world a multiple of n_kv_heads) each
+    // held by world / n_kv_heads ranks, every rank computing its q heads' share
+    const bool kv_split = full.n_kv_heads > 0 && full.n_kv_heads % world == 0;
+    const bool kv_repl = full.n_kv_heads > 0 && world % full.n_kv_heads == 0;
     if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || full.n_heads % world ||
-        full.n_kv_heads % world || full.ffn_dim % world || full.vocab % world) {
+        !(kv_split || kv_repl) || (!n_exp && full.ffn_dim % world) || full.vocab % world) {
         fprintf(stderr, "[tb_cuda] decoder: rank %d of %d does not divide the heads, FFN rows and vocabulary\n",
                 rank, world);
         return nullptr;
     }
     DecConfig c = full;
     c.n_heads /= world;
-    c.n_kv_heads /= world;
-    c.ffn_dim /= world;
+    c.n_kv_heads = kv_split ? full.n_kv_heads / world : 1;
+    if (!n_exp) c.ffn_dim /= world;   // routed: whole experts per rank, each of ffn_dim rows
     c.vocab /= world;
     if (c.n_layers <= 0 || c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim != kHD ||
         c.n_heads % c.n_kv_heads || c.n_heads / c.n_kv_heads > 8 || c.ffn_dim <= 0 || c.vocab <= 0 ||
@@ -1185,6 +1381,13 @@ Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, i
              dec_ok(cudaMalloc(&d->ids, sizeof(int) * top_k), "expert ids") &&
              dec_ok(cudaMalloc(&d->hbuf, sizeof(float) * static_cast<size_t>(top_k) * c.ffn_dim), "expert act") &&
              dec_ok(cudaMalloc(&d->tbuf, sizeof(float) * static_cast<size_t>(top_k) * c.hidden), "expert out");
+        if (ok && world > 1) {
+            d->n_loc_exp = n_exp / world;
+            ok = dec_ok(cudaMalloc(&d->lids, sizeof(int) * top_k), "local expert ids") &&
+                 dec_ok(cudaMalloc(&d->lw, sizeof(float) * top_k), "local expert weights") &&
+                 dec_ok(cudaMalloc(&d->nloc, sizeof(int)), "local expert count") &&
+                 dec_ok(cudaMemset(d->nloc, 0, sizeof(int)), "memset");
+        }
     }
     if (ok && world > 1) {
         // the exchange region, 256-byte aligned parts; CUDA IPC maps whole allocations
@@ -1193,11 +1396,14 @@ Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, i
         d->off_xd = slots;
         d->off_am = 2 * slots;
         d->off_ctr = d->off_am + up(sizeof(unsigned long long) * world);
-        d->xch_bytes = d->off_ctr + up(3 * sizeof(unsigned long long));
+        d->off_full = d->off_ctr + up(4 * sizeof(unsigned long long));
+        d->xch_bytes = d->off_full + up(sizeof(float) * static_cast<size_t>(full.vocab));
         ok = dec_ok(cudaMalloc(&d->xch, d->xch_bytes), "exchange region") &&
              dec_ok(cudaMemset(d->xch, 0, d->xch_bytes), "memset") &&
              dec_ok(cudaMalloc(&d->epoch, sizeof(int)), "epoch") &&
-             dec_ok(cudaMemset(d->epoch, 0, sizeof(int)), "memset");
+             dec_ok(cudaMemset(d->epoch, 0, sizeof(int)), "memset") &&
+             dec_ok(cudaMalloc(&d->tk, 4 * sizeof(unsigned long long)), "tickets") &&
+             dec_ok(cudaMemset(d->tk, 0, 4 * sizeof(unsigned long long)), "memset");
         d->peer[rank] = d->xch;
     }
     if (ok) {
@@ -1221,6 +1427,7 @@ Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, i
 // change, token and position are read from device memory).
 static bool dec_graph(Decoder *d)
 {
+    const NvtxRange nvtx("tb.decode.capture");
     if (d->gexec) return true;
     if (!d->ready()) {
         fprintf(stderr, "[tb_cuda] decoder: weights not complete (set every layer and the head)\n");
@@ -1248,6 +1455,7 @@ static bool dec_graph(Decoder *d)
 int dec_run(Decoder *d, int token, int pos, int n, int *tokens, float *logits_host, float *ms,
             const float *u = nullptr)
 {
+    const NvtxRange nvtx("tb.decode.steps");
     if (!d || n <= 0 || token < 0 || token >= d->vocab_full || pos < 0 || pos + n > d->cfg.max_ctx) return 0;
     if (d->sampling()) {
         if (!u) {
@@ -1327,6 +1535,14 @@ void *tb_cuda_dec_create_moe(const tb_dec_config *c, int n_experts, int top_k)
     tb::DecConfig k{c->n_layers, c->hidden, c->n_heads, c->n_kv_heads, c->head_dim, c->ffn_dim,
                     c->vocab, c->max_ctx, c->rope_base, c->norm_eps, c->quirks};
     return tb::dec_create(k, 0, 1, n_experts, top_k);
+}
+
+void *tb_cuda_dec_create_moe_tp(const tb_dec_config *c, int n_experts, int top_k, int rank, int world)
+{
+    if (!c || n_experts < 1 || world < 2) return nullptr;
+    tb::DecConfig k{c->n_layers, c->hidden, c->n_heads, c->n_kv_heads, c->head_dim, c->ffn_dim,
+                    c->vocab, c->max_ctx, c->rope_base, c->norm_eps, c->quirks};
+    return tb::dec_create(k, rank, world, n_experts, top_k);
 }
 
 int tb_cuda_dec_set_moe_layer(void *dec, int layer, const void *w_router, int router_qtype,
@@ -1477,11 +1693,7 @@ int tb_cuda_dec_set_sampling(void *dec, float temperature, int top_k, float top_
     if (!d || !(temperature == temperature) || top_k < 0) return 0;
     const bool smp = temperature >= 0.01f;
     if (smp) {
-        if (d->world > 1) {
-            fprintf(stderr, "[tb_cuda] decoder: sampling needs the whole vocabulary on one device (world 1)\n");
-            return 0;
-        }
-        if ((top_k > 0 && top_k < d->cfg.vocab && top_k > 2048) || (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
+        if ((top_k > 0 && top_k < d->vocab_full && top_k > 2048) || (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
             return 0;
         if (!d->u_buf &&
             !(tb::dec_ok(cudaMalloc(&d->u_buf, sizeof(float) * d->cfg.max_ctx), "variates") &&
@@ -1523,6 +1735,8 @@ int tb_cuda_dec_read(void *dec, int which, float *host, int n)
     case 7: src = d->wts, size = d->top_k; break;
     case 8: src = reinterpret_cast<const float *>(d->ids), size = d->top_k; break;
     case 9: src = d->hbuf, size = static_cast<long long>(d->top_k) * c.ffn_dim; break;
+    case 10: src = reinterpret_cast<const float *>(d->nloc), size = d->nloc ? 1 : 0; break;
+    case 11: src = reinterpret_cast<const float *>(d->lids), size = d->lids ? d->top_k : 0; break;
     default: return 0;
     }
     if (n > size) return 0;

@@ -204,6 +204,7 @@ static int dq_go(const void *W, int M, int K, float *out, cudaStream_t st)
 
 int dq_launch(const void *W, int qtype, int M, int K, float *d_out, int sem, cudaStream_t st)
 {
+    const NvtxRange nvtx("tb.dequant");
     const Geom g = geom_of(qtype);
     if (!g.block_weights || !W || !d_out || M <= 0 || K <= 0 || K % g.block_weights) return 0;
     if (reinterpret_cast<uintptr_t>(d_out) & 15u) return 0;

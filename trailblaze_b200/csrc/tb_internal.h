@@ -3,8 +3,19 @@
 
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 namespace tb {
+
+// An NVTX range over a scope (a kernel family's host-side launch or a blocking
+// call), named per family, e.g. "tb.matvec", "tb.decode.step"; free when no
+// profiler is attached (NVTX3 is header-only and injected by the tool).
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
 
 // Fused transforms of the matvec's input and output (see tb_cuda_matvec_fused_dev).
 enum MvXMode : uint32_t { MV_X_PLAIN = 0, MV_X_RMSNORM = 1, MV_X_SWIGLU = 2 };
@@ -25,7 +36,10 @@ struct MvFuse {
     // Input: x <- x + the nsl rows of xs ([nsl][K], summed in row order) once
     // *xs_ctr >= (*xs_epoch) * xs_mul + xs_add; CTA 0 also writes that x to
     // xout when not null.  Output: y[row] goes to ys[p][row] for the ny ranks
-    // p instead of y, then every CTA adds 1 to each yctr[p] (system scope).
+    // p instead of y; then each CTA fences its stores at system scope and takes
+    // a ticket on *ytk (this device), and the CTA that completes a launch
+    // (ticket count a multiple of the grid) adds 1 to each yctr[p] (system
+    // scope): one arrival per rank per exchange.
     const float *xs = nullptr;
     const unsigned long long *xs_ctr = nullptr;
     const int *xs_epoch = nullptr;
@@ -34,6 +48,7 @@ struct MvFuse {
     uint32_t nsl = 0, ny = 0;
     float *ys[kMaxRanks] = {};
     unsigned long long *yctr[kMaxRanks] = {};
+    unsigned long long *ytk = nullptr;
     // Expert groups (MoE; unused when ng is 0): ng matvecs of M rows
     // each in one launch, group g on its own CTAs.  Group g reads the
     // matrix W + e * w_stride bytes, e = ids[g] read on the device after the
@@ -42,6 +57,10 @@ struct MvFuse {
     // x_stride floats (0: one shared x) and writes y + g * y_stride floats.
     uint32_t ng = 0, n_experts = 0;
     const int *ids = nullptr;
+    // With ng_dev (device memory, written by the previous kernel; requires
+    // ids): only the first min(*ng_dev, ng) groups run, the grid split evenly
+    // among them.
+    const int *ng_dev = nullptr;
     unsigned long long w_stride = 0;
     uint32_t x_stride = 0, y_stride = 0;
 };
@@ -72,9 +91,19 @@ int qg_launch(const void *W, int qtype, int N, int K, const void *A, int T, floa
 // top-k (k >= vocab: nucleus with p = 0.95); top_k = 0: nucleus with top_p.
 // With d_u (the decode graph): u = d_u[*d_u_idx], then *d_pos and *d_u_idx
 // each advance by one.
+// Tensor parallelism (the decode step's sampler on a rank): before reading the
+// logits, wait (bounded) until *ctr >= (*epoch + 1) * per_step, the arrivals of
+// every rank's logits slice; after the pick, *epoch += 1 (the step count).
+struct SmpTP {
+    const unsigned long long *ctr = nullptr;
+    int *epoch = nullptr;
+    unsigned long long per_step = 0;
+    uint32_t wait_limit = 0;
+};
+
 int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
                   int *d_token, int *d_err, cudaStream_t st, const float *d_u = nullptr, int *d_u_idx = nullptr,
-                  int *d_pos = nullptr);
+                  int *d_pos = nullptr, const SmpTP *tp = nullptr);
 
 // Launch the bit-exact dequantisation of M rows of K weights into d_out.
 int dq_launch(const void *W, int qtype, int M, int K, float *d_out, int sem, cudaStream_t st);

@@ -27,6 +27,7 @@
 //     ahead.  The summation order never depends on timing, so results are
 //     run-to-run deterministic.  Every wait is bounded.
 #include <atomic>
+#include <type_traits>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -43,8 +44,9 @@ struct MvArgs {
     const float *x;
     float *y;
     int *err;
-    uint32_t M, K;
-    unsigned long long row_bytes;
+    uint32_t M, K;        // K: the columns this launch multiplies (a window of the row when k_off > 0 or
+    uint32_t k_off;       // K < the row's length); k_off: the window's first column (whole blocks)
+    unsigned long long row_bytes;   // bytes of a whole row (the row stride)
     uint32_t block_weights, block_bytes;
     uint32_t cs;       // column slots per row
     uint32_t phases;   // rows decoded side by side
@@ -72,8 +74,10 @@ struct MvArgs {
     uint32_t nsl, ny;
     float *ys[kMaxRanks];
     unsigned long long *yctr[kMaxRanks];
+    unsigned long long *ytk;   // this device's ticket counter of the exchange
     // expert groups (MvFuse): ng > 0 splits the grid into ng equal runs of CTAs
     const int *ids;
+    const int *ng_dev;   // device count of the groups present (<= ng), or null
     uint32_t ng, n_experts;
     unsigned long long w_stride;
     uint32_t x_stride, y_stride;
@@ -82,7 +86,13 @@ struct MvArgs {
 static constexpr uint32_t kFull = 0xFFFFFFFFu;
 static constexpr uint32_t kDrainLimit = 1u << 26;
 static constexpr int kMaxThreads = 512;      // 15 consumer warps + 1 producer, <= 128 registers
-static constexpr uint32_t kMaxConsumerWarps = kMaxThreads / 32 - 1;
+
+// Threads of decoder D's CTA: D::kThreads when it declares one (the fp32
+// decoders: 256 threads of up to 255 registers), else kMaxThreads.
+template <class D, class = void>
+struct ThreadsOf : std::integral_constant<int, kMaxThreads> {};
+template <class D>
+struct ThreadsOf<D, std::void_t<decltype(D::kThreads)>> : std::integral_constant<int, D::kThreads> {};
 
 // Shared-memory layout: [full NST][empty NST] [reduction scratch 64 floats]
 // [slot records] [partials NST*TR*NPART] [ring NST*CAP].
@@ -176,23 +186,31 @@ __device__ __forceinline__ void lane_scale(XRegs &L, float f)
 }
 
 template <class D>
-__global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
+__global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs a)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
 
     uint32_t G = gridDim.x, c = blockIdx.x, grp = 0;
-    if (a.ng > 0) {   // expert groups: ng equal runs of CTAs, each a whole matvec
+    if (a.ng > 0 && !a.ng_dev) {   // expert groups: ng equal runs of CTAs, each a whole matvec
         const uint32_t cpg = G / a.ng;
         grp = c / cpg;
         c -= grp * cpg;
         G = cpg;
     }
     const uint32_t ua = a.ymode == MV_Y_SWIGLU_PAIRS ? 2u : 1u;   // rows per output unit
-    const uint32_t r_lo = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * c) / G);
-    const uint32_t r_hi = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * (c + 1)) / G);
-    if (r_lo >= r_hi) return;
-    const uint32_t n_tiles = (r_hi - r_lo + a.tr - 1) / a.tr;
+    uint32_t r_lo = 0, r_hi = 0, n_tiles = 0;
+    auto span = [&]() {   // this CTA's rows of its group's matvec
+        r_lo = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * c) / G);
+        r_hi = ua * static_cast<uint32_t>((static_cast<unsigned long long>(a.M / ua) * (c + 1)) / G);
+        n_tiles = (r_hi - r_lo + a.tr - 1) / a.tr;
+    };
+    // with a device-side group count (ng_dev) the partition is known only
+    // after the dependency wait
+    if (!a.ng_dev) {
+        span();
+        if (r_lo >= r_hi) return;
+    }
     const uint32_t ngp = a.cs * D::GPL;   // groups of all slots (past K: zeros)
 
     const MvSmem L = mv_smem(a.nst, a.cs, D::REC, a.tr, a.npart, a.cap);
@@ -240,19 +258,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     const bool active = !producer && tid < a.phases * a.cs;
     const uint32_t cs = active ? tid % a.cs : 0;
     const uint32_t ph = active ? tid / a.cs : 0;
-    const bool useful = active && ph < r_hi - r_lo;
+    bool useful = active && ph < r_hi - r_lo;
     Pos pos;
     {
         const uint32_t g0 = cs * D::GPL;                 // first group of the slot
         const uint32_t ngrp = (a.K + 31) / 32;           // groups per row
         if (a.block_weights == 256) {
-            pos.off = (g0 >> 3) * a.block_bytes;
+            pos.off = ((a.k_off >> 8) + (g0 >> 3)) * a.block_bytes;
             pos.gi0 = g0 & 7u;
         } else if (a.block_weights == 32) {
-            pos.off = g0 * a.block_bytes;
+            pos.off = ((a.k_off >> 5) + g0) * a.block_bytes;
             pos.gi0 = 0;
         } else {
-            pos.off = g0 * 32u * a.block_bytes;
+            pos.off = (a.k_off + g0 * 32u) * a.block_bytes;
             pos.gi0 = 0;
         }
         pos.ng = static_cast<int>(min(static_cast<uint32_t>(D::GPL), ngrp - min(ngrp, g0)));
@@ -265,6 +283,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
     // it ahead of its own wait (the decode step's attention streams its cached
     // rows that way).
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (a.ng_dev) {   // the groups present this time (a count the previous kernel wrote): the grid is split among them
+        const uint32_t ngd = min(static_cast<uint32_t>(max(*a.ng_dev, 0)), a.ng);
+        if (ngd == 0) return;
+        const uint32_t cpg = gridDim.x / ngd;
+        grp = blockIdx.x / cpg;
+        if (grp >= ngd) return;
+        c = blockIdx.x - grp * cpg;
+        G = cpg;
+        span();
+        if (r_lo >= r_hi) return;
+        w_lo = reinterpret_cast<uintptr_t>(a.W) + static_cast<uintptr_t>(r_lo) * a.row_bytes;
+        useful = active && ph < r_hi - r_lo;
+    }
     if (a.ng > 0 && a.ids) {   // the group's expert, chosen by the previous kernel (same for the whole CTA)
         const int e = a.ids[grp];
         if (e < 0 || static_cast<uint32_t>(e) >= a.n_experts) {
@@ -309,7 +340,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             const bool have = q < nq;
             float v[8];
             if (have) {
-                load_x_part<8>(a, grp * a.x_stride, 8 * q, v, ss);
+                load_x_part<8>(a, grp * a.x_stride + a.k_off, 8 * q, v, ss);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) v[i] = 0.f;
@@ -324,7 +355,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
                 float4 *dst = reinterpret_cast<float4 *>(rec + (q % QPS) * 8);
                 dst[0] = make_float4(v[0], v[1], v[2], v[3]);
                 dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-                if (q % QPS == 0) rec[XF_N] = mb;
+                if (q % QPS == 0) rec[D::XN] = mb;
             }
         }
     } else if (split) {
@@ -337,7 +368,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             const bool have = q < nq;
             float v[8];
             if (have) {
-                load_x_part<8>(a, grp * a.x_stride, 8 * q, v, ss);
+                load_x_part<8>(a, grp * a.x_stride + a.k_off, 8 * q, v, ss);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) v[i] = 0.f;
@@ -395,7 +426,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             const bool have = g < ngp;
             float v[32];
             if (have) {
-                load_x_part<32>(a, grp * a.x_stride, 32 * g, v, ss);
+                load_x_part<32>(a, grp * a.x_stride + a.k_off, 32 * g, v, ss);
             } else {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = 0.f;
@@ -491,11 +522,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_matvec(const MvArgs a)
             }
         }
         if (a.ny && !fail) {
-            // the partials are visible system-wide before each rank counts this CTA
-            // (a failed CTA never counts, so the ranks' own waits run out)
+            // this CTA's partials are visible system-wide before its ticket; the
+            // CTA whose ticket completes the launch counts this rank once on
+            // every rank (a failed CTA never takes a ticket, so the ranks' own
+            // waits run out)
             __threadfence_system();
             __syncwarp();
-            if (lane < a.ny) atomicAdd_system(a.yctr[lane], 1ull);
+            unsigned long long t = 0;
+            if (lane == 0) t = atomicAdd(a.ytk, 1ull);
+            t = __shfl_sync(kFull, t, 0);
+            if ((t + 1) % gridDim.x == 0) {
+                __threadfence_system();
+                if (lane < a.ny) atomicAdd_system(a.yctr[lane], 1ull);
+            }
         }
         if (fail && lane == 0) {
             // A wait ran out: let every copy still in flight land before the CTA
@@ -574,6 +613,7 @@ static constexpr uint32_t kMaxStages = 8;
 
 struct Plan {
     const void *kern;
+    unsigned long long row_bytes;
     uint32_t M, K, sms, ymode, ng;
     int dev;
     uint32_t nthr, grid, cs, phases, rpl, tr, rw, npart, nst, cap, ncw;
@@ -588,6 +628,7 @@ static thread_local int t_nplans = 0, t_next = 0;
 template <class D>
 static bool make_plan(Plan &p, unsigned long long row_bytes)
 {
+    constexpr uint32_t kMaxConsumerWarps = ThreadsOf<D>::value / 32 - 1;
     const uint32_t ngrp = (p.K + 31) / 32;
     p.cs = (ngrp + D::GPL - 1) / D::GPL;
     if (p.cs > 32 * kMaxConsumerWarps) {
@@ -661,8 +702,8 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
     const Plan *p = nullptr;
     for (int i = 0; i < t_nplans; ++i) {
         const Plan &q = t_plans[i];
-        if (q.kern == kp && q.M == a.M && q.K == a.K && q.dev == dev && q.sms == static_cast<uint32_t>(num_sms) &&
-            q.ymode == a.ymode && q.ng == a.ng) {
+        if (q.kern == kp && q.M == a.M && q.K == a.K && q.row_bytes == a.row_bytes && q.dev == dev &&
+            q.sms == static_cast<uint32_t>(num_sms) && q.ymode == a.ymode && q.ng == a.ng) {
             p = &q;
             break;
         }
@@ -671,6 +712,7 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
         if (!smem_attr_once(kp, kSmemMax)) return 0;
         Plan np{};
         np.kern = kp;
+        np.row_bytes = a.row_bytes;
         np.M = a.M;
         np.K = a.K;
         np.dev = dev;
@@ -728,9 +770,13 @@ int mv_set_arith(int mode)
 
 int mv_get_arith() { return g_arith.load(); }
 
+static int mv_dispatch(MvArgs &a, int qtype, const void *W, bool fp32, cudaStream_t st, int num_sms);
+static int mv_launch_window(MvArgs a, int qtype, uint32_t k_off, uint32_t K, cudaStream_t st, int num_sms);
+
 int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d_y,
               cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit, const MvFuse *fuse)
 {
+    const NvtxRange nvtx("tb.matvec");
     const Geom g = geom_of(qtype);
     if (!g.block_weights || !W || !d_x || !d_y || M <= 0 || K <= 0 || K % g.block_weights) return 0;
     MvArgs a{};
@@ -753,6 +799,8 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
             return 0;
         for (uint32_t p = 0; p < fuse->ny; ++p)
             if (!fuse->ys[p] || !fuse->yctr[p]) return 0;
+        if (fuse->ny && !fuse->ytk) return 0;
+        a.ytk = fuse->ytk;
         a.xs = fuse->xs;
         a.xs_ctr = fuse->xs_ctr;
         a.xs_epoch = fuse->xs_epoch;
@@ -769,9 +817,10 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
             // groups: no residual, no tensor-parallel exchange; an expert id
             // read on the device cannot be prefetched ahead of the wait
             if (fuse->ng > 1024 || fuse->res || fuse->nsl || fuse->ny || (fuse->ids && fuse->w_early) ||
-                (fuse->ids && !fuse->n_experts) || !fuse->w_stride)
+                (fuse->ids && !fuse->n_experts) || !fuse->w_stride || (fuse->ng_dev && !fuse->ids))
                 return 0;
             a.ng = fuse->ng;
+            a.ng_dev = fuse->ng_dev;
             a.n_experts = fuse->n_experts;
             a.ids = fuse->ids;
             a.w_stride = fuse->w_stride;
@@ -790,23 +839,65 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
     a.row_bytes = static_cast<unsigned long long>(K / g.block_weights) * g.block_bytes;
     a.wait_limit = wait_limit;
 
+    const bool fp32 = g_arith.load(std::memory_order_relaxed) == MV_ARITH_FP32 && g.block_weights > 1;
+    {
+        // A row longer than the decoder's column slots cover (one slot per
+        // consumer thread: 64 weights for the fp32 decoders, 128 for the int16
+        // ones, 32 for F32 / F16 / BF16) runs as launches over column windows of
+        // the same rows, in order: the first writes y (+ res), each later one
+        // adds its window onto y.  Each streams whole rows, so these shapes move
+        // their weights once per window.
+        const uint32_t kCols = g.block_weights == 1 ? 32u * (kMaxThreads - 32u)
+                             : fp32 ? 64u * XF_NP * (XfGeom<XF_NP>::THREADS - 32u)
+                                    : 128u * (kMaxThreads - 32u);
+        if (a.K > kCols && a.k_off == 0) {
+            const uint32_t bw = static_cast<uint32_t>(g.block_weights);
+            const uint32_t nw = (a.K + kCols - 1) / kCols;              // windows
+            const uint32_t step = ((a.K / nw + bw - 1) / bw) * bw;      // columns per window, whole blocks
+            const bool plain = a.xmode != MV_X_RMSNORM && a.ymode == MV_Y_PLAIN && !a.nsl && !a.ny && !a.ng;
+            if (!plain || step > kCols) {
+                fprintf(stderr, "[tb_cuda] matvec: K=%u is longer than one launch covers%s\n", a.K,
+                        plain ? "" : " with this fused mode");
+                return 0;
+            }
+            const uint32_t K0 = a.K;
+            for (uint32_t k0 = 0; k0 < K0; k0 += step) {
+                if (!mv_launch_window(a, qtype, k0, K0 - k0 < step ? K0 - k0 : step, st, num_sms)) return 0;
+                a.res = d_y;   // later windows add onto the result so far
+            }
+            return 1;
+        }
+    }
+    return mv_dispatch(a, qtype, W, fp32, st, num_sms);
+}
+
+static int mv_launch_window(MvArgs a, int qtype, uint32_t k_off, uint32_t K, cudaStream_t st, int num_sms)
+{
+    a.k_off = k_off;
+    a.K = K;
+    const bool fp32 = g_arith.load(std::memory_order_relaxed) == MV_ARITH_FP32 && a.block_weights > 1;
+    return mv_dispatch(a, qtype, a.W, fp32, st, num_sms);
+}
+
+static int mv_dispatch(MvArgs &a, int qtype, const void *W, bool fp32, cudaStream_t st, int num_sms)
+{
     const uintptr_t wa = reinterpret_cast<uintptr_t>(W);
     const bool a16 = (wa & 15u) == 0 && (a.row_bytes & 15u) == 0 && (a.w_stride & 15u) == 0;
     const bool a4 = (wa & 3u) == 0 && (a.row_bytes & 3u) == 0 && (a.w_stride & 3u) == 0;
-    if (g_arith.load(std::memory_order_relaxed) == MV_ARITH_FP32) {
+    if (fp32) {
         switch (qtype) {
         case QT_Q4_K:
             return a16 ? launch_dec<DecQ4KF<true>>(a, num_sms, st) : launch_dec<DecQ4KF<false>>(a, num_sms, st);
         case QT_Q5_K:
             return a16 ? launch_dec<DecQ5KF<true>>(a, num_sms, st) : launch_dec<DecQ5KF<false>>(a, num_sms, st);
-        case QT_Q6_K: return launch_dec<DecQ6KF>(a, num_sms, st);
+        case QT_Q6_K: return launch_dec<DecQ6KF<>>(a, num_sms, st);
         case QT_Q3_K:
-        case QT_IQ3_S: return launch_dec<DecQ3KF>(a, num_sms, st);
+        case QT_IQ3_S: return launch_dec<DecQ3KF<>>(a, num_sms, st);
         case QT_Q2_K:
             return a4 ? launch_dec<DecQ2KF<true>>(a, num_sms, st) : launch_dec<DecQ2KF<false>>(a, num_sms, st);
-        case QT_Q8_0: return launch_dec<DecQ80F>(a, num_sms, st);
-        case QT_Q4_0: return launch_dec<DecQ40F>(a, num_sms, st);
-        case QT_Q8_K: return launch_dec<DecQ8KF>(a, num_sms, st);
+        case QT_Q8_0: return launch_dec<DecQ80F<>>(a, num_sms, st);
+        case QT_Q4_0: return launch_dec<DecQ40F<>>(a, num_sms, st);
+        case QT_Q8_K: return launch_dec<DecQ8KF<>>(a, num_sms, st);
         default: break;   // F32 / F16 / BF16: the float decoders below (fp32 already)
         }
     }

@@ -460,6 +460,7 @@ static constexpr size_t kGSmemCap = 232448;   // 227 KB opt-in per CTA
 int qg_launch(const void *W, int qtype, int N, int K, const void *A, int T, float *C, cudaStream_t st, int *d_err,
               int num_sms, uint32_t wait_limit)
 {
+    const NvtxRange nvtx("tb.qgemm");
     if (qtype != QT_Q4_K && qtype != QT_Q6_K) return 0;
     if (!W || !A || !C || N <= 0 || K <= 0 || N % kGM || K % 256 || T < 16 || T > 512 || T % 16) return 0;
     const uintptr_t wa = reinterpret_cast<uintptr_t>(W), aa = reinterpret_cast<uintptr_t>(A);

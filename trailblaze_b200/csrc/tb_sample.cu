@@ -48,6 +48,7 @@ struct SmpArgs {
     float p, temp, u;
     const float *u_dev;   // not null: u = u_dev[*u_idx], and the step advances
     int *u_idx, *pos;
+    SmpTP tp;             // tensor parallelism: wait for the ranks' logits, count the step
 };
 
 // Thread 0: the chosen token, and the decode step's advance when the variate
@@ -59,6 +60,7 @@ __device__ __forceinline__ void finish(const SmpArgs &a, int token)
         *a.pos = *a.pos + 1;
         *a.u_idx = *a.u_idx + 1;
     }
+    if (a.tp.epoch) *a.tp.epoch = *a.tp.epoch + 1;
 }
 
 __device__ __forceinline__ float variate(const SmpArgs &a)
@@ -193,7 +195,7 @@ __device__ __forceinline__ void for_seg(const float *lg, int lo, int hi, int lan
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
             const int i = b + j * 32 + lane;
-            v[j] = i < hi ? __ldg(lg + i) : 0.f;
+            v[j] = i < hi ? __ldcg(lg + i) : 0.f;   // through L2: peers may have written them (tensor parallel)
         }
 #pragma unroll
         for (int j = 0; j < kPer; ++j) f(b + j * 32 + lane, v[j], b + j * 32 + lane < hi);
@@ -211,6 +213,14 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     __shared__ int hist[256];
     __shared__ int s_n, s_sel;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, V = a.vocab;
+    if (a.tp.ctr) {
+        // tensor parallelism: every rank's logits slice has arrived (a bounded
+        // wait; once a wait of this device ran out the step only finishes)
+        if (tid == 0 && *reinterpret_cast<volatile int *>(a.err) == 0 &&
+            !wait_counter(a.tp.ctr, static_cast<unsigned long long>(*a.tp.epoch + 1) * a.tp.per_step, a.tp.wait_limit))
+            atomicExch(a.err, ERR_WAIT_TIMEOUT);
+        __syncthreads();
+    }
     const float *lg = a.logits;
     const unsigned below = (1u << lane) - 1u;   // the lanes before this one
     // the warp's contiguous segment of the vocabulary (warp order = index order)
@@ -386,13 +396,16 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
 }
 
 int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
-                  int *d_token, int *d_err, cudaStream_t st, const float *d_u, int *d_u_idx, int *d_pos)
+                  int *d_token, int *d_err, cudaStream_t st, const float *d_u, int *d_u_idx, int *d_pos,
+                  const SmpTP *tp)
 {
+    const NvtxRange nvtx("tb.sample");
     if (!d_logits || !d_token || vocab <= 0 || top_k < 0 || (top_k > 0 && top_k < vocab && top_k > kNucleusMax) ||
         (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
         return 0;
     if (d_u ? (!d_u_idx || !d_pos) : !(u >= 0.f && u < 1.f)) return 0;
-    SmpArgs a{d_logits, d_token, d_err, vocab, top_k, top_p, temperature, u, d_u, d_u_idx, d_pos};
+    SmpArgs a{d_logits, d_token, d_err, vocab, top_k, top_p, temperature, u, d_u, d_u_idx, d_pos, SmpTP{}};
+    if (tp) a.tp = *tp;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(kSmpThreads);

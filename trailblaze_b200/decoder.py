@@ -77,9 +77,9 @@ class Decoder:
         s = shape
         self.cfg = DecConfig(s.n_layers, s.hidden, s.n_heads, s.n_kv_heads, s.head_dim, s.ffn_dim, s.vocab,
                              max_ctx, s.rope_base, s.norm_eps, 1 if quirks else 0)
-        if s.n_experts:
-            if world != 1:
-                raise ValueError("a routed decoder runs on one device")
+        if s.n_experts and world > 1:
+            self.d = self.L.tb_cuda_dec_create_moe_tp(ctypes.byref(self.cfg), s.n_experts, s.top_k, rank, world)
+        elif s.n_experts:
             self.d = self.L.tb_cuda_dec_create_moe(ctypes.byref(self.cfg), s.n_experts, s.top_k)
         elif world > 1:
             self.d = self.L.tb_cuda_dec_create_tp(ctypes.byref(self.cfg), rank, world)
@@ -135,11 +135,16 @@ class Decoder:
         if self.L.tb_cuda_dec_kv_copy(self.d, li, which, 0, t.shape[1], fp, 1) != 1:
             raise RuntimeError("tb_cuda_dec_kv_copy failed")
 
-    def generate(self, token: int, pos: int, n: int, want_tokens: bool = True):
-        """n greedy tokens from (token, pos); returns (tokens or None, device milliseconds)."""
+    def generate(self, token: int, pos: int, n: int, want_tokens: bool = True, logits=None):
+        """n greedy tokens from (token, pos); returns (tokens or None, device milliseconds).
+        logits (float32 numpy, this rank's vocabulary rows) receives the last step's logits."""
         toks = (ctypes.c_int * n)() if want_tokens else None
         ms = ctypes.c_float(0.0)
-        if self.L.tb_cuda_dec_generate(self.d, token, pos, n, toks, None, ctypes.byref(ms)) != 1:
+        lp = None
+        if logits is not None:
+            assert logits.dtype == np.float32 and logits.flags.c_contiguous
+            lp = logits.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        if self.L.tb_cuda_dec_generate(self.d, token, pos, n, toks, lp, ctypes.byref(ms)) != 1:
             raise RuntimeError("tb_cuda_dec_generate failed")
         return (list(toks) if want_tokens else None), ms.value
 
@@ -196,41 +201,75 @@ def device_weights(qt: int, M: int, K: int, gen):
 
 def synthetic_model(shape: ModelShape, max_ctx: int, ctx: int, seed: int = 20261201, quirks: bool = True,
                     log=None, rank: int = 0, world: int = 1) -> Decoder:
-    """A Decoder loaded with random-init weights of `shape` and an N(0,1) KV prefix of ctx positions;
-    with world > 1 the shard shapes of rank `rank` (drawn from that rank's own seed stream)."""
+    """A Decoder loaded with random-init weights of `shape` and an N(0,1) KV prefix of ctx positions.
+
+    Every rank draws the whole model from one seeded generator, so the model is
+    the same at every world size, and keeps its tensor-parallel share
+    (include/tb_gguf_dequant.h part 3): the q, k and v rows of its heads (its kv
+    head shared with world / n_kv_heads - 1 other ranks when world exceeds
+    n_kv_heads), o's K columns of its q heads, its (gate, up) row pairs and
+    down's K columns of those FFN rows (routed: its experts' rows, the router
+    whole), its vocabulary rows of the output, the K and V cache of its kv
+    heads; the norms and the token embedding whole.  A decode at world N
+    therefore computes the same tokens as at world 1."""
     import torch
+    from . import shard
     s = shape
-    gen = torch.Generator(device="cuda")        # this rank's shards
-    gen.manual_seed(seed + 7919 * rank)
-    shared = torch.Generator(device="cuda")     # tensors every rank holds whole (same on every rank)
-    shared.manual_seed(seed)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
     dec = Decoder(s, max_ctx, quirks, rank, world)
-    H, HD = s.hidden, s.head_dim
-    NH, NK, F = s.n_heads // world, s.n_kv_heads // world, s.ffn_dim // world
+    H, HD, NH, NK, F, V = s.hidden, s.head_dim, s.n_heads, s.n_kv_heads, s.ffn_dim, s.vocab
+    nh, f = NH // world, F // world
+    # this rank's kv heads [k0, k0 + nk): split, or one head shared by world / NK ranks
+    nk, k0 = (NK // world, rank * (NK // world)) if NK % world == 0 else (1, rank // (world // NK))
 
     def norm(n):
-        return 1.0 + 0.1 * torch.randn(n, device="cuda", generator=shared)
+        return 1.0 + 0.1 * torch.randn(n, device="cuda", generator=gen)
+
+    def attn_shard(qkv, qt, wo, oqt):
+        if world == 1:
+            return qkv, wo
+        R = (NH + 2 * NK) * HD
+        qkv = torch.cat([shard.row_slice(qkv, qt, R, H, rank * nh * HD, (rank + 1) * nh * HD),
+                         shard.row_slice(qkv, qt, R, H, (NH + k0) * HD, (NH + k0 + nk) * HD),
+                         shard.row_slice(qkv, qt, R, H, (NH + NK + k0) * HD, (NH + NK + k0 + nk) * HD)])
+        wo = shard.k_slice(wo, oqt, H, NH * HD, rank * nh * HD, (rank + 1) * nh * HD).contiguous()
+        return qkv, wo
 
     for li in range(s.n_layers):
         if s.n_experts:
             E, aq = s.n_experts, s.a_qt
-            dec.set_layer(li, device_weights(aq, (NH + 2 * NK) * HD, H, gen), aq,
-                          device_weights(aq, H, NH * HD, gen), aq, None, aq, None, aq,
-                          norm(H), norm(H), norm(HD), norm(HD))
+            qkv, wo = attn_shard(device_weights(aq, (NH + 2 * NK) * HD, H, gen), aq,
+                                 device_weights(aq, H, NH * HD, gen), aq)
+            dec.set_layer(li, qkv, aq, wo, aq, None, aq, None, aq, norm(H), norm(H), norm(HD), norm(HD))
             router = (0.05 * torch.randn(E * H, device="cuda", generator=gen)).view(torch.uint8)
-            dec.set_moe_layer(li, router, Q.F32, device_weights(s.w_qt, E * 2 * F, H, gen), s.w_qt,
-                              device_weights(s.w_qt, E * H, F, gen), s.w_qt)
+            wgu_e = device_weights(s.w_qt, E * 2 * F, H, gen)
+            wd_e = device_weights(s.w_qt, E * H, F, gen)
+            if world > 1:   # this rank's experts [rank E/w, (rank+1) E/w): whole row ranges
+                el = E // world
+                wgu_e = shard.row_slice(wgu_e, s.w_qt, E * 2 * F, H, rank * el * 2 * F,
+                                        (rank + 1) * el * 2 * F).contiguous()
+                wd_e = shard.row_slice(wd_e, s.w_qt, E * H, F, rank * el * H, (rank + 1) * el * H).contiguous()
+            dec.set_moe_layer(li, router, Q.F32, wgu_e, s.w_qt, wd_e, s.w_qt)
         else:
-            dec.set_layer(li,
-                          device_weights(s.w_qt, (NH + 2 * NK) * HD, H, gen), s.w_qt,
-                          device_weights(s.w_qt, H, NH * HD, gen), s.w_qt,
-                          device_weights(s.w_qt, 2 * F, H, gen), s.w_qt,
-                          device_weights(s.down_qt, H, F, gen), s.down_qt,
-                          norm(H), norm(H), norm(HD), norm(HD))
+            qkv, qt = device_weights(s.w_qt, (NH + 2 * NK) * HD, H, gen), s.w_qt
+            wo = device_weights(s.w_qt, H, NH * HD, gen)
+            wgu = device_weights(s.w_qt, 2 * F, H, gen)
+            wd = device_weights(s.down_qt, H, F, gen)
+            qkv, wo = attn_shard(qkv, qt, wo, s.w_qt)
+            if world > 1:
+                wgu = shard.row_slice(wgu, s.w_qt, 2 * F, H, 2 * rank * f, 2 * (rank + 1) * f).contiguous()
+                wd = shard.k_slice(wd, s.down_qt, H, F, rank * f, (rank + 1) * f).contiguous()
+            dec.set_layer(li, qkv, qt, wo, s.w_qt, wgu, s.w_qt, wd, s.down_qt, norm(H), norm(H), norm(HD), norm(HD))
         if ctx > 0:
             for which in (0, 1):
-                dec.load_kv(li, which, torch.randn(NK, ctx, HD, device="cuda", generator=gen))
-    dec.set_head(device_weights(s.w_qt, s.vocab, H, shared), s.w_qt, norm(H),
-                 device_weights(s.out_qt, s.vocab // world, H, gen), s.out_qt)
+                kv = torch.randn(NK, ctx, HD, device="cuda", generator=gen)
+                dec.load_kv(li, which, kv[k0:k0 + nk])
+    emb = device_weights(s.w_qt, V, H, gen)
+    onorm = norm(H)
+    w_out = device_weights(s.out_qt, V, H, gen)
+    if world > 1:
+        w_out = shard.row_slice(w_out, s.out_qt, V, H, rank * (V // world), (rank + 1) * (V // world)).contiguous()
+    dec.set_head(emb, s.w_qt, onorm, w_out, s.out_qt)
     torch.cuda.synchronize()
     return dec
