@@ -278,6 +278,18 @@ float *tb_cuda_dec_kv(void *dec, int layer, int which);
  * runs on the decoder's own (non-blocking) stream, so device memory written
  * by work on another stream must be complete before the call.  1 = ok. */
 int    tb_cuda_dec_kv_copy(void *dec, int layer, int which, int p0, int n, float *host, int to_device);
+/* Batched prefill of a prompt (the reference prefills by one decode step per
+ * prompt token, layer4/tb_infer.c:1071-1074): tokens[0..n) at positions
+ * pos0 .. pos0 + n - 1 go through every layer together, in chunks of up to 512,
+ * filling the K and V cache; the projections run on the tcgen05 GEMM
+ * (tb_cuda_qgemm_dev: bf16 activations, weights dequantised exactly and
+ * rounded to bf16), attention, norms and the residual stream in fp32.  Then
+ * the last token's final norm, output matvec and greedy argmax:
+ * *next_token, logits_host (may be NULL) its vocab logits; decoding continues
+ * with tb_cuda_dec_generate(*next_token, pos0 + n, ...).  Dense single-device
+ * decoder; every projection Q4_K or Q6_K with rows a multiple of 128, K of
+ * 256 and row bytes of 16 (Q6_K: K a multiple of 2048).  Blocking.  1 = ok. */
+int    tb_cuda_dec_prefill(void *dec, const int *tokens, int n, int pos0, int *next_token, float *logits_host);
 /* One token at position pos: *next_token = greedy argmax; logits_host (may be
  * NULL) receives the vocab logits.  Blocking.  1 = ok. */
 int    tb_cuda_dec_step(void *dec, int token, int pos, int *next_token, float *logits_host);

@@ -151,6 +151,14 @@ def attention(q, kc, vc, n_heads, n_kv_heads):
     return out
 
 
+def bf16_round(x):
+    """float -> bf16 (round to nearest even) -> float64, as the prefill GEMM's
+    operands (fp32 values rounded by __float2bfloat16_rn)."""
+    u = np.ascontiguousarray(np.asarray(x, dtype=np.float32)).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF
+    return (r.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+
+
 class LazyMat:
     """An M x K GGUF tensor kept as raw bytes: `@ x` dequantises chunks of rows
     (CUDA semantics) to float64 and multiplies them, `[i]` is one dequantised
@@ -228,6 +236,68 @@ class DecodeOracle:
         # caches [layer][NK][max_ctx][HD]
         self.kc = np.zeros((m.n_layers, NK, m.max_ctx, HD))
         self.vc = np.zeros((m.n_layers, NK, m.max_ctx, HD))
+
+    def prefill(self, tokens, pos0: int):
+        """The batched prefill of the library (tb_cuda_dec_prefill) restated one
+        token at a time (causal attention makes the two the same): the dense
+        layers' projections take bf16-rounded fp32 activations (RMSNorm outputs,
+        attention output, SwiGLU activation) against bf16-rounded weights, as the
+        tensor-core GEMM does; norms, attention and the residual in float64.
+        Fills the caches; returns (last token's logits through the exact output
+        matvec, greedy next token)."""
+        m = self.m
+        H, NH, NK, HD = m.hidden, m.n_heads, m.n_kv_heads, m.head_dim
+        rep, eps = NH // NK, m.norm_eps
+        if not hasattr(self, "_bf"):
+            self._bf = [{k: bf16_round(w[k]) for k in ("wqkv", "wo", "wgu", "wd")} for w in self.L]
+        x = None
+        for i, token in enumerate(tokens):
+            pos = pos0 + i
+            x = np.asarray(self.emb[token], np.float64).copy()
+            for li, w in enumerate(self.L):
+                wb = self._bf[li]
+                xn = bf16_round(rms_norm(x, w["attn_norm"], eps))
+                qkv = wb["wqkv"] @ xn
+                q = qkv[:NH * HD].reshape(NH, HD).copy()
+                k = qkv[NH * HD:(NH + NK) * HD].reshape(NK, HD).copy()
+                v = qkv[(NH + NK) * HD:].reshape(NK, HD).copy()
+                self._rope_norm(w, q, k, pos, rep, eps)
+                self.kc[li, :, pos] = k
+                self.vc[li, :, pos] = v
+                att = attention(q, self.kc[li, :, :pos + 1], self.vc[li, :, :pos + 1], NH, NK)
+                x2 = x + wb["wo"] @ bf16_round(att.reshape(-1))
+                xn2 = bf16_round(rms_norm(x2, w["ffn_norm"], eps))
+                gu = wb["wgu"] @ xn2
+                act = bf16_round(swiglu(gu[0::2], gu[1::2]))
+                x = x2 + wb["wd"] @ act
+        logits = self.lm @ rms_norm(x, self.out_norm, eps)
+        return logits, int(np.argmax(logits))
+
+    def _rope_norm(self, w, q, k, pos, rep, eps):
+        m = self.m
+        NH, NK, HD = m.n_heads, m.n_kv_heads, m.head_dim
+
+        def rope_all():
+            for h in range(NH):
+                q[h] = rope(q[h], pos, m.rope_base, HD)
+            for j in range(NK):
+                for _ in range(rep if self.quirks else 1):
+                    k[j] = rope(k[j], pos, m.rope_base, HD)
+
+        def norm_all():
+            if w["q_norm"] is not None:
+                for h in range(NH):
+                    q[h] = rms_norm(q[h], w["q_norm"], eps)
+            if w["k_norm"] is not None:
+                for j in range(NK):
+                    k[j] = rms_norm(k[j], w["k_norm"], eps)
+
+        if self.quirks:
+            rope_all()
+            norm_all()
+        else:
+            norm_all()
+            rope_all()
 
     def step(self, token: int, pos: int):
         """One token at position pos; returns (logits, next_token).  Updates the caches."""

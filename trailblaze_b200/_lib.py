@@ -87,6 +87,7 @@ def lib() -> ctypes.CDLL:
         "tb_cuda_dec_create_moe_tp": (c_void_p, [ctypes.POINTER(DecConfig), c_int, c_int, c_int, c_int]),
         "tb_cuda_dec_set_moe_layer": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int]),
         "tb_cuda_dec_step": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(c_int), fp]),
+        "tb_cuda_dec_prefill": (c_int, [c_void_p, ctypes.POINTER(c_int), c_int, c_int, ctypes.POINTER(c_int), fp]),
         "tb_cuda_dec_generate": (c_int, [c_void_p, c_int, c_int, c_int, ctypes.POINTER(c_int), fp, fp]),
         "tb_cuda_dec_set_sampling": (c_int, [c_void_p, ctypes.c_float, c_int, ctypes.c_float]),
         "tb_cuda_dec_generate_u": (c_int, [c_void_p, c_int, c_int, c_int, fp, ctypes.POINTER(c_int), fp, fp]),
@@ -113,6 +114,6 @@ def exported_symbols() -> list[str]:
         "tb_cuda_matvec_fused_dev", "tb_cuda_matvec_experts_dev", "tb_cuda_sample_dev", "tb_cuda_qgemm_dev", "tb_cuda_dec_create", "tb_cuda_dec_set_layer", "tb_cuda_dec_set_head",
         "tb_cuda_dec_kv", "tb_cuda_dec_kv_copy", "tb_cuda_dec_read", "tb_cuda_dec_create_tp",
         "tb_cuda_dec_tp_handle", "tb_cuda_dec_tp_connect", "tb_cuda_dec_create_moe", "tb_cuda_dec_create_moe_tp", "tb_cuda_dec_set_moe_layer",
-        "tb_cuda_dec_step", "tb_cuda_dec_generate", "tb_cuda_dec_set_sampling", "tb_cuda_dec_generate_u",
+        "tb_cuda_dec_step", "tb_cuda_dec_prefill", "tb_cuda_dec_generate", "tb_cuda_dec_set_sampling", "tb_cuda_dec_generate_u",
         "tb_cuda_dec_destroy",
     ])

@@ -20,7 +20,7 @@ LIB = os.path.join(HERE, "libtb_cuda_sm100.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 
 SOURCES = ["tb_matvec.cu", "tb_dequant.cu", "tb_abi.cu", "tb_decode.cu", "tb_qgemm.cu", "tb_sample.cu",
-           "tb_loader.cu"]
+           "tb_loader.cu", "tb_prefill.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",

@@ -909,6 +909,9 @@ struct Decoder {
     int smp_k = 0;
     float *u_buf = nullptr;
     int *u_idx = nullptr;
+    // batched prefill buffers (allocated on the first tb_cuda_dec_prefill)
+    PfBufs pf{};
+    int *pf_tok = nullptr;
     bool sampling() const { return smp_temp >= 0.01f; }
 
     float *slot_o(int p) const { return reinterpret_cast<float *>(peer[p]); }
@@ -1295,6 +1298,9 @@ static void dec_free(Decoder *d)
     if (d->xch) cudaFree(d->xch);
     if (d->epoch) cudaFree(d->epoch);
     if (d->tk) cudaFree(d->tk);
+    for (void *b : {static_cast<void *>(d->pf.X), static_cast<void *>(d->pf.QKV), static_cast<void *>(d->pf.Y),
+                    static_cast<void *>(d->pf.GU), d->pf.A, d->pf.AO, d->pf.ACT, static_cast<void *>(d->pf_tok)})
+        if (b) cudaFree(b);
     delete[] d->layers;
     delete d;
 }
@@ -1709,6 +1715,95 @@ int tb_cuda_dec_set_sampling(void *dec, float temperature, int top_k, float top_
     d->smp_temp = smp ? temperature : 0.f;
     d->smp_k = top_k;
     d->smp_p = top_p;
+    return 1;
+}
+
+int tb_cuda_dec_prefill(void *dec, const int *tokens, int n, int pos0, int *next_token, float *logits_host)
+{
+    tb::Decoder *d = static_cast<tb::Decoder *>(dec);
+    if (!d || !tokens || n < 1 || pos0 < 0 || pos0 + n > d->cfg.max_ctx) return 0;
+    const tb::DecConfig &c = d->cfg;
+    if (d->world != 1 || d->n_exp || !d->ready()) {
+        fprintf(stderr, "[tb_cuda] decoder: prefill needs a dense single-device decoder with its tensors set\n");
+        return 0;
+    }
+    const int H = c.hidden, NH = c.n_heads, NK = c.n_kv_heads, F = c.ffn_dim;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const tb::DecLayer &w = d->layers[l];
+        if (!tb::pf_supported(w.qkv_qt, (NH + 2 * NK) * 128, H) || !tb::pf_supported(w.o_qt, H, NH * 128) ||
+            !tb::pf_supported(w.gu_qt, 2 * F, H) || !tb::pf_supported(w.d_qt, H, F)) {
+            fprintf(stderr, "[tb_cuda] decoder: prefill needs Q4_K / Q6_K projections the tensor-core GEMM takes "
+                            "(rows a multiple of 128, K of 256, row bytes of 16)\n");
+            return 0;
+        }
+    }
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= d->vocab_full) return 0;
+    constexpr int kT = 512;   // tokens per chunk (the GEMM's largest T)
+    tb::PfBufs &b = d->pf;
+    if (!b.X) {
+        const size_t r = kT;
+        const bool ok = tb::dec_ok(cudaMalloc(&b.X, sizeof(float) * r * H), "prefill") &&
+                        tb::dec_ok(cudaMalloc(&b.QKV, sizeof(float) * r * (NH + 2 * NK) * 128), "prefill") &&
+                        tb::dec_ok(cudaMalloc(&b.Y, sizeof(float) * r * H), "prefill") &&
+                        tb::dec_ok(cudaMalloc(&b.GU, sizeof(float) * r * 2 * F), "prefill") &&
+                        tb::dec_ok(cudaMalloc(&b.A, 2 * r * H), "prefill") &&
+                        tb::dec_ok(cudaMalloc(&b.AO, 2 * r * NH * 128), "prefill") &&
+                        tb::dec_ok(cudaMalloc(&b.ACT, 2 * r * F), "prefill") &&
+                        tb::dec_ok(cudaMalloc(&d->pf_tok, sizeof(int) * r), "prefill");
+        if (!ok) return 0;
+    }
+    const tb::NvtxRange nvtx("tb.decode.prefill");
+    tb::PfShape ps{H, NH, NK, F, c.max_ctx, c.quirks, c.norm_eps, c.rope_base};
+    cudaStream_t s = d->st;
+    int last = 0;
+    for (int c0 = 0; c0 < n; c0 += kT) {
+        const int T = n - c0 < kT ? n - c0 : kT, Tp = (T + 15) & ~15;
+        if (!tb::dec_ok(cudaMemcpyAsync(d->pf_tok, tokens + c0, sizeof(int) * T, cudaMemcpyHostToDevice, s),
+                        "prefill tokens") ||
+            !tb::dq_embed_launch(d->emb, d->emb_qt, d->vocab_full, H, d->pf_tok, b.X, s, T))
+            return 0;
+        for (int l = 0; l < c.n_layers; ++l) {
+            const tb::DecLayer &w = d->layers[l];
+            tb::PfLayer pl{w.wqkv, w.wo, w.wgu, w.wd, w.qkv_qt, w.o_qt, w.gu_qt, w.d_qt, w.attn_norm, w.ffn_norm,
+                           w.q_norm, w.k_norm, d->kc + static_cast<size_t>(l) * d->kv_layer_floats(),
+                           d->vc + static_cast<size_t>(l) * d->kv_layer_floats()};
+            if (!tb::pf_layer(pl, ps, b, pos0 + c0, T, Tp, s, d->err, d->sms)) return 0;
+        }
+        last = T - 1;
+        // the host token buffer is read by the copy above before the next chunk's copy
+        if (!tb::dec_ok(cudaStreamSynchronize(s), "prefill")) return 0;
+    }
+    // the last token's residual is the decode step's x: the final norm, the
+    // output matvec and the greedy argmax (which advances pos to pos0 + n)
+    d->hostio[1] = pos0 + n - 1;
+    if (!tb::dec_ok(cudaMemcpyAsync(d->x, b.X + static_cast<size_t>(last) * H, sizeof(float) * H,
+                                    cudaMemcpyDeviceToDevice, s), "prefill x") ||
+        !tb::dec_ok(cudaMemcpyAsync(d->pos, &d->hostio[1], sizeof(int), cudaMemcpyHostToDevice, s), "prefill pos"))
+        return 0;
+    tb::MvFuse f;
+    f.xmode = tb::MV_X_RMSNORM;
+    f.nw = d->out_norm;
+    f.eps = c.norm_eps;
+    if (!tb::mv_launch(d->lm, d->lm_qt, c.vocab, H, d->x, d->logits, s, d->err, d->sms, 1u << 22, &f)) return 0;
+    tb::ArgTP tp{};
+    tp.world = 1;
+    if (!tb::launch_pdl(tb::k_argmax_step, dim3(d->sms), dim3(tb::kArgThreads), 0, s,
+                        static_cast<const float *>(d->logits), c.vocab, d->argv, d->argi, d->counts + NK, d->tok,
+                        d->pos, tp))
+        return 0;
+    if (logits_host)
+        cudaMemcpyAsync(logits_host, d->logits, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(&d->hostio[0], d->tok, sizeof(int), cudaMemcpyDeviceToHost, s);
+    cudaMemcpyAsync(&d->hostio[2], d->err, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (!tb::dec_ok(cudaStreamSynchronize(s), "prefill")) return 0;
+    if (d->hostio[2]) {
+        fprintf(stderr, "[tb_cuda] decoder: device error %d in prefill\n", d->hostio[2]);
+        cudaMemsetAsync(d->err, 0, sizeof(int), s);
+        cudaStreamSynchronize(s);
+        return 0;
+    }
+    if (next_token) *next_token = d->hostio[0];
     return 1;
 }
 

@@ -141,7 +141,9 @@ __global__ void __launch_bounds__(256) k_embed_row(const uint8_t *__restrict__ W
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     constexpr Geom g = geom_of(QT);
-    const int t = *token;
+    // grid.y > 1: a batch of tokens (token[y] into row y of out)
+    const int t = token[blockIdx.y];
+    out += static_cast<size_t>(blockIdx.y) * K;
     const bool ok = t >= 0 && static_cast<uint32_t>(t) < vocab;
     const uint8_t *row = W + (ok ? static_cast<unsigned long long>(t) * row_bytes : 0ull);
     for (uint32_t k = blockIdx.x * 256u + threadIdx.x; k < K; k += gridDim.x * 256u)
@@ -151,12 +153,12 @@ __global__ void __launch_bounds__(256) k_embed_row(const uint8_t *__restrict__ W
 }
 
 template <int QT>
-static int embed_go(const void *W, int vocab, int K, const int *tok, float *out, cudaStream_t st)
+static int embed_go(const void *W, int vocab, int K, const int *tok, float *out, cudaStream_t st, int n = 1)
 {
     constexpr Geom g = geom_of(QT);
     const unsigned long long row_bytes = static_cast<unsigned long long>(K / g.block_weights) * g.block_bytes;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>((K + 255) / 256));
+    cfg.gridDim = dim3(static_cast<unsigned>((K + 255) / 256), static_cast<unsigned>(n));
     cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -168,23 +170,26 @@ static int embed_go(const void *W, int vocab, int K, const int *tok, float *out,
                               static_cast<uint32_t>(K), row_bytes, tok, out) == cudaSuccess ? 1 : 0;
 }
 
-int dq_embed_launch(const void *W, int qtype, int vocab, int K, const int *d_token, float *d_out, cudaStream_t st)
+int dq_embed_launch(const void *W, int qtype, int vocab, int K, const int *d_token, float *d_out, cudaStream_t st,
+                    int n)
 {
     const Geom g = geom_of(qtype);
-    if (!g.block_weights || !W || !d_token || !d_out || vocab <= 0 || K <= 0 || K % g.block_weights) return 0;
+    if (!g.block_weights || !W || !d_token || !d_out || vocab <= 0 || K <= 0 || K % g.block_weights || n < 1 ||
+        n > 65535)
+        return 0;
     switch (qtype) {
-    case QT_F32: return embed_go<QT_F32>(W, vocab, K, d_token, d_out, st);
-    case QT_F16: return embed_go<QT_F16>(W, vocab, K, d_token, d_out, st);
-    case QT_BF16: return embed_go<QT_BF16>(W, vocab, K, d_token, d_out, st);
-    case QT_Q4_0: return embed_go<QT_Q4_0>(W, vocab, K, d_token, d_out, st);
-    case QT_Q8_0: return embed_go<QT_Q8_0>(W, vocab, K, d_token, d_out, st);
-    case QT_Q8_K: return embed_go<QT_Q8_K>(W, vocab, K, d_token, d_out, st);
-    case QT_Q2_K: return embed_go<QT_Q2_K>(W, vocab, K, d_token, d_out, st);
+    case QT_F32: return embed_go<QT_F32>(W, vocab, K, d_token, d_out, st, n);
+    case QT_F16: return embed_go<QT_F16>(W, vocab, K, d_token, d_out, st, n);
+    case QT_BF16: return embed_go<QT_BF16>(W, vocab, K, d_token, d_out, st, n);
+    case QT_Q4_0: return embed_go<QT_Q4_0>(W, vocab, K, d_token, d_out, st, n);
+    case QT_Q8_0: return embed_go<QT_Q8_0>(W, vocab, K, d_token, d_out, st, n);
+    case QT_Q8_K: return embed_go<QT_Q8_K>(W, vocab, K, d_token, d_out, st, n);
+    case QT_Q2_K: return embed_go<QT_Q2_K>(W, vocab, K, d_token, d_out, st, n);
     case QT_Q3_K:
-    case QT_IQ3_S: return embed_go<QT_Q3_K>(W, vocab, K, d_token, d_out, st);
-    case QT_Q4_K: return embed_go<QT_Q4_K>(W, vocab, K, d_token, d_out, st);
-    case QT_Q5_K: return embed_go<QT_Q5_K>(W, vocab, K, d_token, d_out, st);
-    case QT_Q6_K: return embed_go<QT_Q6_K>(W, vocab, K, d_token, d_out, st);
+    case QT_IQ3_S: return embed_go<QT_Q3_K>(W, vocab, K, d_token, d_out, st, n);
+    case QT_Q4_K: return embed_go<QT_Q4_K>(W, vocab, K, d_token, d_out, st, n);
+    case QT_Q5_K: return embed_go<QT_Q5_K>(W, vocab, K, d_token, d_out, st, n);
+    case QT_Q6_K: return embed_go<QT_Q6_K>(W, vocab, K, d_token, d_out, st, n);
     default: return 0;
     }
 }

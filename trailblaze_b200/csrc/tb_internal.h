@@ -108,10 +108,34 @@ int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, floa
 // Launch the bit-exact dequantisation of M rows of K weights into d_out.
 int dq_launch(const void *W, int qtype, int M, int K, float *d_out, int sem, cudaStream_t st);
 
-// Dequantise row *d_token of a [vocab x K] table into d_out (zeros for a token
-// outside [0, vocab)); programmatic-dependent-launch aware.
+// Dequantise row d_token[i] of a [vocab x K] table into row i of d_out, for
+// i < n (zeros for a token outside [0, vocab)); programmatic-dependent-launch
+// aware.
 int dq_embed_launch(const void *W, int qtype, int vocab, int K, const int *d_token, float *d_out,
-                    cudaStream_t st);
+                    cudaStream_t st, int n = 1);
+
+// Batched prefill (tb_prefill.cu): one layer of T prompt tokens (padded to
+// Tp, a multiple of 16), the projections on the tcgen05 GEMM.
+struct PfLayer {
+    const void *wqkv, *wo, *wgu, *wd;
+    int qkv_qt, o_qt, gu_qt, d_qt;
+    const float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+    float *kc, *vc;   // the layer's K and V cache, [n_kv_heads][max_ctx][128]
+};
+struct PfShape {
+    int hidden, n_heads, n_kv_heads, ffn_dim, max_ctx, quirks;
+    float eps, rope_base;
+};
+struct PfBufs {   // [Tp] rows each
+    float *X, *QKV, *Y, *GU;
+    void *A, *AO, *ACT;   // bf16: [Tp][hidden], [Tp][n_heads * 128], [Tp][ffn_dim]
+};
+// True when the prefill GEMM takes an N x K tensor of this type.
+bool pf_supported(int qtype, int N, int K);
+// One layer over the chunk's rows of X (positions pos0 .. pos0 + T - 1);
+// stream-ordered.  1 = launched.
+int pf_layer(const PfLayer &w, const PfShape &c, const PfBufs &b, int pos0, int T, int Tp, cudaStream_t st,
+             int *err, int sms);
 
 // Shape of the decode step (tb_decode.cu); mirrors tb_dec_config.
 struct DecConfig {
