@@ -185,6 +185,57 @@ __device__ __forceinline__ void lane_scale(XRegs &L, float f)
     for (int q = 0; q < 16; ++q) L.a[q] = make_float2(L.a[q].x * f, L.a[q].y * f);
 }
 
+// The consumer warps' tile loop.  Per tile: wait for the stage, decode this
+// thread's rows (ph, ph + P, ...; a lane past the tile's rows decodes row 0 of
+// the tile again and discards it, so the warp never diverges around the
+// decode), add each row's slot sums over RW neighbouring lanes, store one
+// partial per (row, lane group), arrive on the stage's "empty" barrier.
+template <class D, int RW>
+__device__ __forceinline__ void consume(const MvArgs &a, const typename D::Lane &lx, const Pos &pos, uint64_t *full,
+                                        uint64_t *empty, float *part, const uint8_t *ring, uintptr_t w_lo,
+                                        uintptr_t tile_bytes, uint32_t r_lo, uint32_t r_hi, uint32_t n_tiles,
+                                        uint32_t cs, uint32_t ph, bool useful, bool active, uint32_t row_bytes32)
+{
+    const uint32_t lane = threadIdx.x & 31u;
+    const bool writer = active && (cs % RW) == 0;
+    const uint32_t npart = a.npart, phases = a.phases, rpl = a.rpl, tr = a.tr, nst = a.nst, cap = a.cap;
+    const uint32_t part_col = cs / RW;
+    uint32_t s = 0, par = 0, t0 = r_lo;
+    uintptr_t lo = w_lo;
+    float *pb = part;
+    const uint8_t *stage = ring;
+    const uint32_t pstride = tr * npart;
+    for (uint32_t it = 0; it < n_tiles; ++it) {
+        const bool ok = mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit);
+        if (!__all_sync(kFull, ok)) break;   // no arrival: the producer's wait runs out as well
+        const uint32_t nrows = min(tr, r_hi - t0);
+        const uint32_t sbase = shared_after(smem_u32(stage) + static_cast<uint32_t>(lo & 15u));
+#pragma unroll 2
+        for (uint32_t i = 0; i < rpl; ++i) {
+            const uint32_t rt = ph + i * phases;
+            const bool live = useful && rt < nrows;
+            if (!__any_sync(kFull, live)) break;   // rows ascend with i: none of the warp's later rows is live
+            float v = D::row_dot(sbase + (live ? rt : 0u) * row_bytes32, pos, lx);
+#pragma unroll
+            for (int o = 1; o < RW; o <<= 1) v += __shfl_xor_sync(kFull, v, o);
+            if (writer && live) pb[rt * npart + part_col] = v;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(empty + s));
+        t0 += tr;
+        lo += tile_bytes;
+        if (++s == nst) {
+            s = 0;
+            par ^= 1u;
+            pb = part;
+            stage = ring;
+        } else {
+            pb += pstride;
+            stage += cap;
+        }
+    }
+}
+
 template <class D>
 __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs a)
 {
@@ -558,48 +609,16 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
         }
     }
     const uint32_t row_bytes32 = static_cast<uint32_t>(a.row_bytes);   // a tile's rows fit one stage
-    const bool writer = active && (cs % a.rw) == 0;
-    const uint32_t part_col = cs / a.rw;
-
-    uint32_t s = 0, par = 0, t0 = r_lo;
-    uintptr_t lo = w_lo;
-    float *pb = part;
-    const uint8_t *stage = ring;
-    const uint32_t pstride = a.tr * a.npart;
-    for (uint32_t it = 0; it < n_tiles; ++it) {
-        const bool ok = mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit);
-        if (!__all_sync(kFull, ok)) break;   // no arrival: the producer's wait runs out as well
-        const uint32_t nrows = min(a.tr, r_hi - t0);
-        const uint32_t sbase = shared_after(smem_u32(stage) + static_cast<uint32_t>(lo & 15u));
-#pragma unroll 2
-        for (uint32_t i = 0; i < a.rpl; ++i) {
-            const uint32_t rt = ph + i * a.phases;
-            const bool live = useful && rt < nrows;
-            if (!__any_sync(kFull, live)) continue;   // the warp has no row here (uniform)
-            float v = 0.f;
-            if (live) v = D::row_dot(sbase + rt * row_bytes32, pos, lx);
-            // the row's slot sums over rw neighbouring lanes, without branches
-            const float t1 = __shfl_xor_sync(kFull, v, 1);
-            v = a.rw > 1 ? v + t1 : v;
-            const float t2 = __shfl_xor_sync(kFull, v, 2);
-            v = a.rw > 2 ? v + t2 : v;
-            const float t4 = __shfl_xor_sync(kFull, v, 4);
-            v = a.rw > 4 ? v + t4 : v;
-            if (writer && live) pb[rt * a.npart + part_col] = v;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(empty + s));
-        t0 += a.tr;
-        lo += tile_bytes;
-        if (++s == a.nst) {
-            s = 0;
-            par ^= 1u;
-            pb = part;
-            stage = ring;
-        } else {
-            pb += pstride;
-            stage += a.cap;
-        }
+    // the reduction width as a template argument: no runtime selects per row
+    switch (a.rw) {
+    case 8: consume<D, 8>(a, lx, pos, full, empty, part, ring, w_lo, tile_bytes, r_lo, r_hi, n_tiles, cs, ph,
+                          useful, active, row_bytes32); break;
+    case 4: consume<D, 4>(a, lx, pos, full, empty, part, ring, w_lo, tile_bytes, r_lo, r_hi, n_tiles, cs, ph,
+                          useful, active, row_bytes32); break;
+    case 2: consume<D, 2>(a, lx, pos, full, empty, part, ring, w_lo, tile_bytes, r_lo, r_hi, n_tiles, cs, ph,
+                          useful, active, row_bytes32); break;
+    default: consume<D, 1>(a, lx, pos, full, empty, part, ring, w_lo, tile_bytes, r_lo, r_hi, n_tiles, cs, ph,
+                           useful, active, row_bytes32); break;
     }
 }
 
