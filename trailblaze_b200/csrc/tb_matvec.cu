@@ -666,34 +666,39 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
         }
     }
     if (!p.ncw) return false;
-    p.nthr = 32 * (p.ncw + 1);
-    p.phases = (32 * p.ncw) / p.cs;
     p.rw = (p.cs % 8 == 0) ? 8 : (p.cs % 4 == 0) ? 4 : (p.cs % 2 == 0) ? 2 : 1;
     p.npart = p.cs / p.rw;
-    // Rows per thread per tile: as many as keep a stage within kStageMax and
-    // two stages in shared memory (the per-tile cost is paid once per rpl
-    // rows); then as many stages as fit.
-    p.nst = 0;
     // TB_MV_STAGE_KB / TB_MV_RPL_MAX: planner tuning knobs (stage bytes, rows per thread)
     static const uint32_t stage_max = getenv("TB_MV_STAGE_KB") ? 1024u * atoi(getenv("TB_MV_STAGE_KB")) : kStageMax;
     static const uint32_t rpl_max = getenv("TB_MV_RPL_MAX") ? atoi(getenv("TB_MV_RPL_MAX")) : kMaxRpl;
-    for (uint32_t rpl = rpl_max; rpl >= 1 && !p.nst; --rpl) {
-        const unsigned long long bytes = static_cast<unsigned long long>(p.phases) * rpl * row_bytes;
-        if (rpl > 1 && bytes > stage_max) continue;
-        if (p.ymode == MV_Y_SWIGLU_PAIRS && (p.phases * rpl) % 2) continue;   // tiles of whole pairs
-        const uint32_t tr = p.phases * rpl;
-        const uint32_t cap = static_cast<uint32_t>((bytes + 32 + 127) & ~127ull);
-        for (uint32_t n = kMaxStages; n >= 2; --n) {
-            const MvSmem s = mv_smem(n, p.cs, D::REC, tr, p.npart, cap);
-            if (s.total <= static_cast<size_t>(kSmemMax)) {
-                p.rpl = rpl;
-                p.tr = tr;
-                p.cap = cap;
-                p.nst = n;
-                p.smem = s.total;
-                break;
+    // Rows per thread per tile: as many as keep a stage within kStageMax and
+    // two stages in shared memory (the per-tile cost is paid once per rpl
+    // rows); then as many stages as fit.  When even one row per thread does
+    // not fit (long rows over few column slots: many phases of whole rows),
+    // fewer consumer warps make fewer phases.
+    p.nst = 0;
+    for (const uint32_t min_ncw = (p.cs + 31) / 32; !p.nst && p.ncw >= min_ncw; --p.ncw) {
+        p.nthr = 32 * (p.ncw + 1);
+        p.phases = (32 * p.ncw) / p.cs;
+        for (uint32_t rpl = rpl_max; rpl >= 1 && !p.nst; --rpl) {
+            const unsigned long long bytes = static_cast<unsigned long long>(p.phases) * rpl * row_bytes;
+            if (rpl > 1 && bytes > stage_max) continue;
+            if (p.ymode == MV_Y_SWIGLU_PAIRS && (p.phases * rpl) % 2) continue;   // tiles of whole pairs
+            const uint32_t tr = p.phases * rpl;
+            const uint32_t cap = static_cast<uint32_t>((bytes + 32 + 127) & ~127ull);
+            for (uint32_t n = kMaxStages; n >= 2; --n) {
+                const MvSmem s = mv_smem(n, p.cs, D::REC, tr, p.npart, cap);
+                if (s.total <= static_cast<size_t>(kSmemMax)) {
+                    p.rpl = rpl;
+                    p.tr = tr;
+                    p.cap = cap;
+                    p.nst = n;
+                    p.smem = s.total;
+                    break;
+                }
             }
         }
+        if (p.nst) break;
     }
     if (!p.nst) {
         fprintf(stderr, "[tb_cuda] matvec: a %u-row tile of %llu-byte rows does not fit shared memory\n", p.phases,
@@ -872,7 +877,7 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
         if (a.K > kCols && a.k_off == 0) {
             const uint32_t bw = static_cast<uint32_t>(g.block_weights);
             const uint32_t nw = (a.K + kCols - 1) / kCols;              // windows
-            const uint32_t step = ((a.K / nw + bw - 1) / bw) * bw;      // columns per window, whole blocks
+            const uint32_t step = (((a.K + nw - 1) / nw + bw - 1) / bw) * bw;   // columns per window, whole blocks
             const bool plain = a.xmode != MV_X_RMSNORM && a.ymode == MV_Y_PLAIN && !a.nsl && !a.ny && !a.ng;
             if (!plain || step > kCols) {
                 fprintf(stderr, "[tb_cuda] matvec: K=%u is longer than one launch covers%s\n", a.K,
