@@ -126,7 +126,7 @@ __device__ __forceinline__ float transpose_sum(float (&v)[V])
 // K and are cheap, so the K stages are released, and refilled with V rows,
 // while the stream is still running.
 static constexpr int kBP = 64;                                   // positions per load
-static constexpr int kNS = 3;                                    // ring stages
+static constexpr int kNS = 3;                                    // ring stages (5 and 6 measured no faster)
 static constexpr uint32_t kStageBytes = kBP * kHD * sizeof(float);   // the K or V rows of a block
 static constexpr int kPW = kBP / (kAttnThreads / 32);            // positions of a load per warp
 static_assert(kPW * 8 <= 32 && kPW * (kAttnThreads / 32) == kBP, "a warp's (position, head) items fit its lanes");

@@ -58,6 +58,7 @@ struct MvArgs {
     uint32_t cap;      // bytes per stage
     uint32_t ncw;      // consumer warps; warp ncw is the producer
     uint32_t wait_limit;
+    unsigned long long *stamp;   // TB_MV_STAMPS builds only: 8 device-clock stamps per CTA
     // fused input / output transforms (MvFuse): x is x (plain), x*rms*nw
     // (RMSNorm, rms = 1/sqrt(mean(x^2) + eps)) or silu(x)*x2 (SwiGLU); y gets
     // res added when res is not null
@@ -190,6 +191,21 @@ __device__ __forceinline__ void lane_scale(XRegs &L, float f)
 // the tile again and discards it, so the warp never diverges around the
 // decode), add each row's slot sums over RW neighbouring lanes, store one
 // partial per (row, lane group), arrive on the stage's "empty" barrier.
+#if TB_MV_STAMPS
+#define MV_STAMP(k)                                                                       \
+    do {                                                                                  \
+        if (a.stamp) {                                                                    \
+            unsigned long long t_;                                                        \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                        \
+            a.stamp[blockIdx.x * 8u + (k)] = t_;                                          \
+        }                                                                                 \
+    } while (0)
+#else
+#define MV_STAMP(k) \
+    do {            \
+    } while (0)
+#endif
+
 template <class D, int RW>
 __device__ __forceinline__ void consume(const MvArgs &a, const typename D::Lane &lx, const Pos &pos, uint64_t *full,
                                         uint64_t *empty, float *part, const uint8_t *ring, uintptr_t w_lo,
@@ -208,6 +224,7 @@ __device__ __forceinline__ void consume(const MvArgs &a, const typename D::Lane 
     for (uint32_t it = 0; it < n_tiles; ++it) {
         const bool ok = mbar_wait_bounded(smem_u32(full + s), par, a.err, a.wait_limit);
         if (!__all_sync(kFull, ok)) break;   // no arrival: the producer's wait runs out as well
+        if (it == 0 && threadIdx.x == 0) MV_STAMP(4);
         const uint32_t nrows = min(tr, r_hi - t0);
         const uint32_t sbase = shared_after(smem_u32(stage) + static_cast<uint32_t>(lo & 15u));
 #pragma unroll 2
@@ -234,6 +251,7 @@ __device__ __forceinline__ void consume(const MvArgs &a, const typename D::Lane 
             stage += cap;
         }
     }
+    if (threadIdx.x == 0) MV_STAMP(5);
 }
 
 template <class D>
@@ -241,6 +259,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
 {
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+    if (tid == 0) MV_STAMP(0);
 
     uint32_t G = gridDim.x, c = blockIdx.x, grp = 0;
     if (a.ng > 0 && !a.ng_dev) {   // expert groups: ng equal runs of CTAs, each a whole matvec
@@ -329,6 +348,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
     }
     if (a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (tid == 0) MV_STAMP(1);
     // The next kernel may start once every CTA is past the wait: what the
     // kernels before this one wrote is then complete, so the next one may read
     // it ahead of its own wait (the decode step's attention streams its cached
@@ -507,6 +527,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
         if (lane == 0) red[warp] = ss;
     }
     __syncthreads();   // records complete; barrier inits visible
+    if (tid == 0) MV_STAMP(2);
 
     if (producer && lane == 0) {
         const uint32_t pre = min(a.nst, n_tiles);
@@ -587,6 +608,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
                 if (lane < a.ny) atomicAdd_system(a.yctr[lane], 1ull);
             }
         }
+        if (lane == 0) MV_STAMP(6);
         if (fail && lane == 0) {
             // A wait ran out: let every copy still in flight land before the CTA
             // exits (fixed, generous bound: they target valid memory and complete).
@@ -608,6 +630,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
             lane_scale(lx, 1.0f / sqrtf(t / static_cast<float>(a.K) + a.eps));
         }
     }
+    if (tid == 0) MV_STAMP(3);
     const uint32_t row_bytes32 = static_cast<uint32_t>(a.row_bytes);   // a tile's rows fit one stage
     // the reduction width as a template argument: no runtime selects per row
     switch (a.rw) {
@@ -797,6 +820,33 @@ int mv_get_arith() { return g_arith.load(); }
 static int mv_dispatch(MvArgs &a, int qtype, const void *W, bool fp32, cudaStream_t st, int num_sms);
 static int mv_launch_window(MvArgs a, int qtype, uint32_t k_off, uint32_t K, cudaStream_t st, int num_sms);
 
+#if TB_MV_STAMPS
+// Instrumented builds: every launch gets its own slot of 8 stamps per CTA (a
+// captured graph keeps the slot of its capture), read back by tb_mv_stamps.
+static unsigned long long *g_stamp_buf = nullptr;
+static unsigned g_stamp_n = 0;
+static constexpr unsigned kStampSlots = 4096, kStampCtas = 160;
+}  // namespace tb
+extern "C" int tb_mv_stamps_init()
+{
+    using namespace tb;
+    const size_t n = size_t(kStampSlots) * kStampCtas * 8;
+    if (!g_stamp_buf && cudaMalloc(&g_stamp_buf, n * 8) != cudaSuccess) return 0;
+    g_stamp_n = 0;
+    return cudaMemset(g_stamp_buf, 0, n * 8) == cudaSuccess;
+}
+extern "C" int tb_mv_stamps(unsigned long long *host, int max_launches)
+{
+    using namespace tb;
+    if (!g_stamp_buf) return -1;
+    const unsigned n = g_stamp_n < unsigned(max_launches) ? g_stamp_n : unsigned(max_launches);
+    cudaDeviceSynchronize();
+    cudaMemcpy(host, g_stamp_buf, size_t(n < kStampSlots ? n : kStampSlots) * kStampCtas * 64, cudaMemcpyDeviceToHost);
+    return static_cast<int>(g_stamp_n);
+}
+namespace tb {
+#endif
+
 int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d_y,
               cudaStream_t st, int *d_err, int num_sms, uint32_t wait_limit, const MvFuse *fuse)
 {
@@ -804,6 +854,9 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
     const Geom g = geom_of(qtype);
     if (!g.block_weights || !W || !d_x || !d_y || M <= 0 || K <= 0 || K % g.block_weights) return 0;
     MvArgs a{};
+#if TB_MV_STAMPS
+    if (g_stamp_buf) a.stamp = g_stamp_buf + size_t(g_stamp_n++ % kStampSlots) * kStampCtas * 8;
+#endif
     if (fuse) {
         if (fuse->xmode > MV_X_SWIGLU || (fuse->xmode == MV_X_RMSNORM && !fuse->nw) ||
             (fuse->xmode == MV_X_SWIGLU && !fuse->x2))
