@@ -58,7 +58,7 @@ struct MvArgs {
     uint32_t cap;      // bytes per stage
     uint32_t ncw;      // consumer warps; warp ncw is the producer
     uint32_t wait_limit;
-    unsigned long long *stamp;   // TB_MV_STAMPS builds only: 8 device-clock stamps per CTA
+    unsigned long long *stamp;   // TB_MV_STAMPS builds only: 16 device-clock stamps per CTA
     // fused input / output transforms (MvFuse): x is x (plain), x*rms*nw
     // (RMSNorm, rms = 1/sqrt(mean(x^2) + eps)) or silu(x)*x2 (SwiGLU); y gets
     // res added when res is not null
@@ -197,7 +197,7 @@ __device__ __forceinline__ void lane_scale(XRegs &L, float f)
         if (a.stamp) {                                                                    \
             unsigned long long t_;                                                        \
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                        \
-            a.stamp[blockIdx.x * 8u + (k)] = t_;                                          \
+            a.stamp[blockIdx.x * 16u + (k)] = t_;                                          \
         }                                                                                 \
     } while (0)
 #else
@@ -385,6 +385,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
                 atomicExch(a.err, ERR_WAIT_TIMEOUT);
         }
         __syncthreads();
+        if (tid == 0) MV_STAMP(8);
     }
 
     // ---- prologue: x -> one record per column slot ----
@@ -593,6 +594,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
                 pb += pstride;
             }
         }
+        if (lane == 0) MV_STAMP(6);
         if (a.ny && !fail) {
             // this CTA's partials are visible system-wide before its ticket; the
             // CTA whose ticket completes the launch counts this rank once on
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
                 if (lane < a.ny) atomicAdd_system(a.yctr[lane], 1ull);
             }
         }
-        if (lane == 0) MV_STAMP(6);
+        if (lane == 0) MV_STAMP(7);
         if (fail && lane == 0) {
             // A wait ran out: let every copy still in flight land before the CTA
             // exits (fixed, generous bound: they target valid memory and complete).
@@ -821,7 +823,7 @@ static int mv_dispatch(MvArgs &a, int qtype, const void *W, bool fp32, cudaStrea
 static int mv_launch_window(MvArgs a, int qtype, uint32_t k_off, uint32_t K, cudaStream_t st, int num_sms);
 
 #if TB_MV_STAMPS
-// Instrumented builds: every launch gets its own slot of 8 stamps per CTA (a
+// Instrumented builds: every launch gets its own slot of 16 stamps per CTA (a
 // captured graph keeps the slot of its capture), read back by tb_mv_stamps.
 static unsigned long long *g_stamp_buf = nullptr;
 static unsigned g_stamp_n = 0;
@@ -830,7 +832,7 @@ static constexpr unsigned kStampSlots = 4096, kStampCtas = 160;
 extern "C" int tb_mv_stamps_init()
 {
     using namespace tb;
-    const size_t n = size_t(kStampSlots) * kStampCtas * 8;
+    const size_t n = size_t(kStampSlots) * kStampCtas * 16;
     if (!g_stamp_buf && cudaMalloc(&g_stamp_buf, n * 8) != cudaSuccess) return 0;
     g_stamp_n = 0;
     return cudaMemset(g_stamp_buf, 0, n * 8) == cudaSuccess;
@@ -841,7 +843,7 @@ extern "C" int tb_mv_stamps(unsigned long long *host, int max_launches)
     if (!g_stamp_buf) return -1;
     const unsigned n = g_stamp_n < unsigned(max_launches) ? g_stamp_n : unsigned(max_launches);
     cudaDeviceSynchronize();
-    cudaMemcpy(host, g_stamp_buf, size_t(n < kStampSlots ? n : kStampSlots) * kStampCtas * 64, cudaMemcpyDeviceToHost);
+    cudaMemcpy(host, g_stamp_buf, size_t(n < kStampSlots ? n : kStampSlots) * kStampCtas * 128, cudaMemcpyDeviceToHost);
     return static_cast<int>(g_stamp_n);
 }
 namespace tb {
@@ -855,7 +857,7 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
     if (!g.block_weights || !W || !d_x || !d_y || M <= 0 || K <= 0 || K % g.block_weights) return 0;
     MvArgs a{};
 #if TB_MV_STAMPS
-    if (g_stamp_buf) a.stamp = g_stamp_buf + size_t(g_stamp_n++ % kStampSlots) * kStampCtas * 8;
+    if (g_stamp_buf) a.stamp = g_stamp_buf + size_t(g_stamp_n++ % kStampSlots) * kStampCtas * 16;
 #endif
     if (fuse) {
         if (fuse->xmode > MV_X_SWIGLU || (fuse->xmode == MV_X_RMSNORM && !fuse->nw) ||
