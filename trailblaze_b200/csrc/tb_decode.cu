@@ -49,7 +49,23 @@ struct AttnArgs {
     int NH, NK, max_ctx, nchunk, quirks;
     float eps, rope_base, scale;
     uint32_t wait_limit;   // iterations of a bounded ring wait
+    unsigned long long *stamp;   // TB_ATTN_STAMPS builds only: 16 device-clock stamps per CTA
 };
+
+#if TB_ATTN_STAMPS
+#define ATT_STAMP(k)                                                                              \
+    do {                                                                                          \
+        if (a.stamp && threadIdx.x == 0) {                                                        \
+            unsigned long long t_;                                                                \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                \
+            a.stamp[(blockIdx.y * gridDim.x + blockIdx.x) * 16u + (k)] = t_;                      \
+        }                                                                                         \
+    } while (0)
+#else
+#define ATT_STAMP(k) \
+    do {             \
+    } while (0)
+#endif
 
 static constexpr uint32_t kAttnDrain = 1u << 26;   // bound of the drain after a failed wait
 
@@ -225,6 +241,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
 {
     extern __shared__ __align__(128) uint8_t smraw[];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    ATT_STAMP(0);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int nwarp = kAttnThreads / 32;
@@ -282,6 +299,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         for (int u = 0; u < min(nl, kNS); ++u) issue(u, u);
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    ATT_STAMP(1);
     // ---- this token's q (and, in the owner chunk, k and v) and the QK-norm weights ----
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 qv = z4, kn = z4, vn = z4, qnv = z4, knv = z4;
@@ -343,6 +361,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
     const float4 kn4 = owner ? reinterpret_cast<const float4 *>(ks)[lane] : z4;
     const float4 vn4 = owner ? reinterpret_cast<const float4 *>(vnw)[lane] : z4;
 
+    ATT_STAMP(2);
     // ---- the loads: scores from the K rows, the softmax once, p . V from the V rows ----
     constexpr int V = kPW * R2;   // (position, head) items of a warp per block
     float4 acc[R2];
@@ -355,6 +374,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         if (j == nb) {
             // every score of the chunk is in sc: maximum, probabilities and sum
             // of each head over the chunk, one warp per head
+            ATT_STAMP(3);
             __syncthreads();
             const int n = t1 - t0;
             if (warp < rep) {
@@ -375,6 +395,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
                 }
             }
             __syncthreads();
+            ATT_STAMP(4);
         }
         // a warp whose wait ran out stops consuming (and releasing) loads; the
         // others' waits then run out as well, nothing refills the ring
@@ -448,6 +469,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         if (tid < 16) red[tid] = (tid & 1) ? 0.f : -1e38f;
     }
     __syncthreads();   // every load consumed (or drained): the ring is free
+    ATT_STAMP(5);
 
     // ---- the chunk's partial: o summed over the warps, m and l per head ----
     {
@@ -481,6 +503,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         s_last = last;
     }
     __syncthreads();
+    ATT_STAMP(6);
     if (!s_last) return;
 
     // thread = (output float4 (head, quad), chunk group); each thread merges its
@@ -546,9 +569,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn_decode(const AttnArgs 
         reinterpret_cast<float4 *>(a.out + (kh * rep + h) * kHD)[q4] =
             make_float4(oc.x * il, oc.y * il, oc.z * il, oc.w * il);
     }
+    ATT_STAMP(7);
     if (tid == 0) a.count[kh] = 0u;   // ready for the next layer / token
 }
 
+
+#if TB_ATTN_STAMPS
+// Instrumented builds: every attention launch gets its own slot of 16 stamps per
+// CTA (a captured graph keeps the slot of its capture), read back by tb_attn_stamps.
+static unsigned long long *g_attn_stamps = nullptr;
+static unsigned g_attn_n = 0;
+static constexpr unsigned kAttnSlots = 1024, kAttnSlotCtas = 160;
+static unsigned long long *attn_stamp_slot()
+{
+    return g_attn_stamps ? g_attn_stamps + size_t(g_attn_n++ % kAttnSlots) * kAttnSlotCtas * 16 : nullptr;
+}
+}  // namespace tb
+extern "C" int tb_attn_stamps_init()
+{
+    using namespace tb;
+    const size_t n = size_t(kAttnSlots) * kAttnSlotCtas * 16;
+    if (!g_attn_stamps && cudaMalloc(&g_attn_stamps, n * 8) != cudaSuccess) return 0;
+    g_attn_n = 0;
+    return cudaMemset(g_attn_stamps, 0, n * 8) == cudaSuccess;
+}
+extern "C" int tb_attn_stamps(unsigned long long *host, int max_launches)
+{
+    using namespace tb;
+    if (!g_attn_stamps) return -1;
+    const unsigned n = g_attn_n < unsigned(max_launches) ? g_attn_n : unsigned(max_launches);
+    cudaDeviceSynchronize();
+    cudaMemcpy(host, g_attn_stamps, size_t(n < kAttnSlots ? n : kAttnSlots) * kAttnSlotCtas * 128, cudaMemcpyDeviceToHost);
+    return static_cast<int>(g_attn_n);
+}
+namespace tb {
+#endif
 
 static void (*attn_kernel(int rep))(const AttnArgs)
 {
@@ -1094,6 +1149,9 @@ bool Decoder::enqueue(cudaStream_t s)
         a.rope_base = c.rope_base;
         a.scale = 1.0f / sqrtf(static_cast<float>(HD));
         const size_t smem = attn_smem_bytes(NH / NK, (c.max_ctx + nchunk - 1) / nchunk);
+#if TB_ATTN_STAMPS
+        a.stamp = attn_stamp_slot();
+#endif
         if (!launch_pdl(attn_kernel(NH / NK), dim3(NK, nchunk), dim3(kAttnThreads), smem, s, a)) return false;
         // x2 = x + Wo @ att
         f = MvFuse{};
@@ -1201,6 +1259,9 @@ bool Decoder::enqueue_tp(cudaStream_t s)
         a.rope_base = c.rope_base;
         a.scale = 1.0f / sqrtf(static_cast<float>(HD));
         const size_t smem = attn_smem_bytes(NH / NK, (c.max_ctx + nchunk - 1) / nchunk);
+#if TB_ATTN_STAMPS
+        a.stamp = attn_stamp_slot();
+#endif
         if (!launch_pdl(attn_kernel(NH / NK), dim3(NK, nchunk), dim3(kAttnThreads), smem, s, a)) return false;
         // this rank's share of Wo @ att to every rank
         f = MvFuse{};

@@ -84,6 +84,9 @@ struct MvArgs {
     uint32_t x_stride, y_stride;
 };
 
+#ifndef TB_MV_TP_EARLY
+#define TB_MV_TP_EARLY 1
+#endif
 static constexpr uint32_t kFull = 0xFFFFFFFFu;
 static constexpr uint32_t kDrainLimit = 1u << 26;
 static constexpr int kMaxThreads = 512;      // 15 consumer warps + 1 producer, <= 128 registers
@@ -376,6 +379,12 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
         w_lo += static_cast<uintptr_t>(e) * a.w_stride;
     }
     if (!a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
+    // A matvec whose input waits on the other ranks' partials requests the rest
+    // of its ring as well (the fp32 prologue does not use the ring), so its
+    // weights stream while the exchange completes.
+    const bool ring_early = TB_MV_TP_EARLY && IsF32X<D>::value && a.nsl > 0;
+    if (ring_early && producer && lane == 0)
+        for (uint32_t it = 1; it < min(a.nst, n_tiles); ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
     if (a.nsl) {   // the ranks' partials of x have all arrived
         if (tid == 0) {
             // after a wait of this device ran out the chain only finishes (fast,
@@ -402,9 +411,11 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
     bool split = false;
     if constexpr (D::kInt) split = a.nst >= 2 && (a.nst - 1ull) * a.cap >= xq_bytes + 4ull * a.cs;
     if constexpr (IsF32X<D>::value) {
-        // fp32 decoders: the record is the slot's transformed activations
-        // themselves plus the magnitude bits of its largest |x|.  All threads,
-        // 8 activations each; the QPS quarters of a slot are neighbouring lanes.
+        // fp32 decoders: the record is the slot's transformed activations,
+        // prescaled and in the decoder's register order, their sub-block sums
+        // and the magnitude bits of its largest |x| (tb_decoders_f32.cuh).  All
+        // threads, 8 activations each; the QPS quarters of a slot are
+        // neighbouring lanes.
         constexpr uint32_t QPS = 4u * D::GPL;
         const uint32_t nq = 4 * ngp;
         for (uint32_t base = 0; base < nq; base += nthr) {   // same trip count in every thread
@@ -422,13 +433,9 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
             for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
 #pragma unroll
             for (uint32_t o = 1; o < QPS; o <<= 1) mb = max(mb, __shfl_xor_sync(kFull, mb, o));
-            if (have) {
-                uint32_t *rec = table + (q / QPS) * D::REC;
-                float4 *dst = reinterpret_cast<float4 *>(rec + (q % QPS) * 8);
-                dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-                dst[1] = make_float4(v[4], v[5], v[6], v[7]);
-                if (q % QPS == 0) rec[D::XN] = mb;
-            }
+            // prescaled into register order, plus the sub-block sums (shuffles: every lane)
+            if constexpr (IsF32X<D>::value)
+                xf_store_quarter<D>(table + (q / QPS) * D::REC, q % QPS, v, mb, have);
         }
     } else if (split) {
         uint8_t *xq = ring + a.cap;                          // [ngp * 4][8] int16, then [cs] int32 exponents
@@ -533,7 +540,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
     if (producer && lane == 0) {
         const uint32_t pre = min(a.nst, n_tiles);
         fence_proxy_async_smem();   // stages 1.. may have held the prologue's digits (generic proxy)
-        for (uint32_t it = 1; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
+        for (uint32_t it = ring_early ? pre : 1; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
     }
     if (producer) {
         // ---- producer: reduce each finished tile, write y, refill its stage ----
