@@ -857,15 +857,14 @@ __global__ void __launch_bounds__(256) k_logits_gather(const float *lg, int n, c
 }
 
 // Expert-parallel combine: this rank's share sum_{j < *nloc} lw[j] * t[j][i]
-// of the routed FFN's output, stored into row `rank` of every rank's exchange
-// slots over NVLink (ys[p] + rank * H), then every CTA counts itself on every
-// rank's arrival counter (system scope), as the tensor-parallel matvecs do:
-// the next layer's q/k/v matvec adds the world rows, in rank order, onto x2.
-// The grid must be the CTA count the receivers expect (min(H, SMs)).
+// of the routed FFN's output, stored tagged into row `rank` of every rank's
+// exchange slots over NVLink (ys[p] + rank * H; one 64-bit word per value, as
+// the tensor-parallel matvecs store theirs): the next layer's q/k/v matvec
+// waits for the tags and adds the world rows, in rank order, onto x2.
 struct CombineEP {
-    float *ys[kMaxRanks];
-    unsigned long long *ctr[kMaxRanks];
-    unsigned long long *tk;   // this device's ticket counter
+    unsigned long long *ys[kMaxRanks];   // every rank's tagged slot row of this rank
+    const int *epoch;                    // tag = epoch * mul + add (mod 2^32)
+    unsigned long long mul, add;
     int world;
 };
 
@@ -878,12 +877,14 @@ __global__ void __launch_bounds__(kMoeThreads) k_moe_combine_ep(const float *t, 
     const int G = gridDim.x;
     const int i0 = static_cast<int>((static_cast<long long>(H) * blockIdx.x) / G);
     const int i1 = static_cast<int>((static_cast<long long>(H) * (blockIdx.x + 1)) / G);
+    const uint32_t tag = static_cast<uint32_t>(static_cast<unsigned long long>(*ex.epoch) * ex.mul + ex.add);
     for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += kMoeThreads) {
         float acc = 0.f;
         for (int j = 0; j < n; ++j) acc = fmaf(lw[j], t[static_cast<size_t>(j) * H + i], acc);
-        for (int p = 0; p < ex.world; ++p) ex.ys[p][i] = acc;
+        const unsigned long long wv = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(acc);
+        for (int p = 0; p < ex.world; ++p)
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ex.ys[p] + i), "l"(wv) : "memory");
     }
-    exchange_arrive(ex.tk, ex.ctr, ex.world);
 }
 
 // ---------------------------------------------------------------------------
@@ -938,14 +939,15 @@ struct Decoder {
     // vocabulary divided by world); vocab_full is the embedding table's rows.
     int rank = 0, world = 1, vocab_full = 0;
     // exchange region (own memory, mapped by the peers through CUDA IPC):
-    // [o partials world x H][down partials world x H][argmax pairs world]
+    // [o partials world x H][down partials world x H] (tagged 64-bit words)
+    // [argmax pairs world]
     // [arrival counters: o, down, argmax, logits][whole-vocabulary logits (sampling)]
     uint8_t *xch = nullptr;
     size_t off_xd = 0, off_am = 0, off_ctr = 0, off_full = 0, xch_bytes = 0;
     uint8_t *peer[kMaxRanks] = {};   // every rank's region, this rank's own included
     bool peer_opened[kMaxRanks] = {};
     int *epoch = nullptr;            // steps completed (device)
-    unsigned long long *tk = nullptr;   // ticket counters: o, down / combine, logits gather (device)
+    unsigned long long *tk = nullptr;   // ticket counters (device): [2] the logits gather
     // mixture of experts (n_exp > 0): every layer's FFN is routed to top_k of
     // n_exp experts of cfg.ffn_dim rows each
     int n_exp = 0, top_k = 0;
@@ -969,9 +971,9 @@ struct Decoder {
     int *pf_tok = nullptr;
     bool sampling() const { return smp_temp >= 0.01f; }
 
-    float *slot_o(int p) const { return reinterpret_cast<float *>(peer[p]); }
+    unsigned long long *slot_o(int p) const { return reinterpret_cast<unsigned long long *>(peer[p]); }
     float *full_logits(int p) const { return reinterpret_cast<float *>(peer[p] + off_full); }
-    float *slot_d(int p) const { return reinterpret_cast<float *>(peer[p] + off_xd); }
+    unsigned long long *slot_d(int p) const { return reinterpret_cast<unsigned long long *>(peer[p] + off_xd); }
     unsigned long long *am(int p) const { return reinterpret_cast<unsigned long long *>(peer[p] + off_am); }
     unsigned long long *ctr(int p, int k) const { return reinterpret_cast<unsigned long long *>(peer[p] + off_ctr) + k; }
     bool connected() const
@@ -1066,7 +1068,6 @@ bool Decoder::enqueue_moe_ep(cudaStream_t s, const DecLayer &w, int l, unsigned 
     f.w_early = true;
     f.xs = slot_o(rank);
     f.nsl = static_cast<uint32_t>(world);
-    f.xs_ctr = ctr(rank, 0);
     f.xs_epoch = epoch;
     f.xs_mul = per_step;
     f.xs_add = static_cast<unsigned long long>(l + 1) * per_x;
@@ -1099,11 +1100,10 @@ bool Decoder::enqueue_moe_ep(cudaStream_t s, const DecLayer &w, int l, unsigned 
     if (!mv_launch(w.wd_e, w.de_qt, H, F, hbuf, tbuf, s, err, sms, lim, &f)) return false;
     CombineEP ex{};
     ex.world = world;
-    ex.tk = tk + 1;
-    for (int p = 0; p < world; ++p) {
-        ex.ys[p] = slot_d(p) + static_cast<size_t>(rank) * H;
-        ex.ctr[p] = ctr(p, 1);
-    }
+    ex.epoch = epoch;
+    ex.mul = per_step;
+    ex.add = static_cast<unsigned long long>(l + 1) * per_x;   // the next layer's q/k/v (or the output) reads it
+    for (int p = 0; p < world; ++p) ex.ys[p] = slot_d(p) + static_cast<size_t>(rank) * H;
     const int G = H < sms ? H : sms;
     return launch_pdl(k_moe_combine_ep, dim3(G), dim3(kMoeThreads), 0, s, static_cast<const float *>(tbuf),
                       static_cast<const float *>(lw), static_cast<const int *>(nloc), top_k, H, ex);
@@ -1195,36 +1195,34 @@ bool Decoder::enqueue(cudaStream_t s)
 // and FFN row pairs, attention is local; o and down hold this rank's K slice
 // and write their partial y into every rank's slots over NVLink.  The next
 // matvec sums the world partials (rank order, so every rank gets the same
-// bits) onto the residual once its arrival counter shows all of them, and its
-// CTA 0 writes the new residual.  Residual stream: x (after the down exchange)
-// and x2 (after the o exchange), alternating.  Arrival targets follow the
-// device-side step count: the down exchange of layer l in step e completes at
-// (e L + l + 1) world G_x arrivals, G_x the CTAs of the o / down launch; the o
-// exchange likewise on its own counter.
+// bits) onto the residual, each slot word waited for until it carries this
+// exchange's tag, and its CTA 0 writes the new residual.  Residual stream: x
+// (after the down exchange) and x2 (after the o exchange), alternating.  Tags
+// follow the device-side step count: the o and down exchanges of layer l in
+// step e carry (e L + l + 1) world (mod 2^32), each kind in its own slots, so
+// a word left from an earlier exchange never matches.
 bool Decoder::enqueue_tp(cudaStream_t s)
 {
     const DecConfig &c = cfg;
     const int H = c.hidden, NH = c.n_heads, NK = c.n_kv_heads, HD = c.head_dim, F = c.ffn_dim, L = c.n_layers;
     const int QKV = (NH + 2 * NK) * HD;
     const uint32_t lim = 1u << 22;
-    const unsigned long long per_x = static_cast<unsigned long long>(world);   // one arrival per rank
+    const unsigned long long per_x = static_cast<unsigned long long>(world);   // tag step of a layer
     const unsigned long long per_step = static_cast<unsigned long long>(L) * per_x;
     auto gather_in = [&](MvFuse &f, int kind, unsigned long long add, float *xout) {
         f.xs = kind == 0 ? slot_o(rank) : slot_d(rank);
         f.nsl = static_cast<uint32_t>(world);
-        f.xs_ctr = ctr(rank, kind);
         f.xs_epoch = epoch;
         f.xs_mul = per_step;
         f.xs_add = add;
         f.xout = xout;
     };
-    auto scatter_out = [&](MvFuse &f, int kind) {
+    auto scatter_out = [&](MvFuse &f, int kind, unsigned long long add) {
         f.ny = static_cast<uint32_t>(world);
-        for (int p = 0; p < world; ++p) {
-            f.ys[p] = (kind == 0 ? slot_o(p) : slot_d(p)) + static_cast<size_t>(rank) * H;
-            f.yctr[p] = ctr(p, kind);
-        }
-        f.ytk = tk + kind;
+        for (int p = 0; p < world; ++p) f.ys[p] = (kind == 0 ? slot_o(p) : slot_d(p)) + static_cast<size_t>(rank) * H;
+        f.y_epoch = epoch;
+        f.y_mul = per_step;
+        f.y_add = add;
     };
     if (!dq_embed_launch(emb, emb_qt, vocab_full, H, tok, x, s)) return false;
     for (int l = 0; l < L; ++l) {
@@ -1266,7 +1264,7 @@ bool Decoder::enqueue_tp(cudaStream_t s)
         // this rank's share of Wo @ att to every rank
         f = MvFuse{};
         f.w_early = true;
-        scatter_out(f, 0);
+        scatter_out(f, 0, static_cast<unsigned long long>(l + 1) * per_x);
         if (!mv_launch(w.wo, w.o_qt, H, NH * HD, att, x2, s, err, sms, lim, &f)) return false;
         if (n_exp) {
             if (!enqueue_moe_ep(s, w, l, per_x, per_step)) return false;
@@ -1284,7 +1282,7 @@ bool Decoder::enqueue_tp(cudaStream_t s)
         // this rank's share of Wd @ act to every rank
         f = MvFuse{};
         f.w_early = true;
-        scatter_out(f, 1);
+        scatter_out(f, 1, static_cast<unsigned long long>(l + 1) * per_x);
         if (!mv_launch(w.wd, w.d_qt, H, F, gu, x, s, err, sms, lim, &f)) return false;
     }
     MvFuse f;
@@ -1459,7 +1457,7 @@ Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, i
     if (ok && world > 1) {
         // the exchange region, 256-byte aligned parts; CUDA IPC maps whole allocations
         auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
-        const size_t slots = up(sizeof(float) * static_cast<size_t>(world) * c.hidden);
+        const size_t slots = up(sizeof(unsigned long long) * static_cast<size_t>(world) * c.hidden);   // tagged words
         d->off_xd = slots;
         d->off_am = 2 * slots;
         d->off_ctr = d->off_am + up(sizeof(unsigned long long) * world);

@@ -32,23 +32,25 @@ struct MvFuse {
     const float *res = nullptr;   // added to y when not null
     bool w_early = false;         // W is constant over the launch chain: stream it before the
                                   // programmatic-dependency wait
-    // Tensor-parallel exchange over peer memory (unused when nsl / ny are 0).
-    // Input: x <- x + the nsl rows of xs ([nsl][K], summed in row order) once
-    // *xs_ctr >= (*xs_epoch) * xs_mul + xs_add; CTA 0 also writes that x to
-    // xout when not null.  Output: y[row] goes to ys[p][row] for the ny ranks
-    // p instead of y; then each CTA fences its stores at system scope and takes
-    // a ticket on *ytk (this device), and the CTA that completes a launch
-    // (ticket count a multiple of the grid) adds 1 to each yctr[p] (system
-    // scope): one arrival per rank per exchange.
-    const float *xs = nullptr;
-    const unsigned long long *xs_ctr = nullptr;
+    // Tensor-parallel exchange over peer memory (unused when nsl / ny are 0),
+    // through tagged slots: a slot element is one 64-bit word (tag << 32 |
+    // float bits), stored and loaded whole (single-copy atomic), so a reader
+    // that sees the tag it expects also sees the value, with no fence or
+    // arrival counter in between.  Tags are (epoch * mul + add) mod 2^32 with
+    // the device-side step count epoch: unique per step and exchange.
+    // Input: x <- x + the nsl rows of xs ([nsl][K] tagged words, summed in row
+    // order), each word waited for (bounded) until it carries tag
+    // (*xs_epoch) * xs_mul + xs_add; CTA 0 also writes that x to xout when
+    // not null.  Output: y[row] goes to ys[p][row] for the ny ranks p instead
+    // of y, tagged (*y_epoch) * y_mul + y_add.
+    const unsigned long long *xs = nullptr;
     const int *xs_epoch = nullptr;
     unsigned long long xs_mul = 0, xs_add = 0;
     float *xout = nullptr;
     uint32_t nsl = 0, ny = 0;
-    float *ys[kMaxRanks] = {};
-    unsigned long long *yctr[kMaxRanks] = {};
-    unsigned long long *ytk = nullptr;
+    unsigned long long *ys[kMaxRanks] = {};
+    const int *y_epoch = nullptr;
+    unsigned long long y_mul = 0, y_add = 0;
     // Expert groups (MoE; unused when ng is 0): ng matvecs of M rows
     // each in one launch, group g on its own CTAs.  Group g reads the
     // matrix W + e * w_stride bytes, e = ids[g] read on the device after the

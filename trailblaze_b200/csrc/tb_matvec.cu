@@ -66,16 +66,15 @@ struct MvArgs {
     const float *x2, *nw, *res;
     float eps;
     uint32_t w_early;   // W is not written by the previous kernel: prefetch before griddepcontrol.wait
-    // tensor-parallel exchange (MvFuse)
-    const float *xs;
-    const unsigned long long *xs_ctr;
+    // tensor-parallel exchange through tagged slots (MvFuse)
+    const unsigned long long *xs;
     const int *xs_epoch;
     unsigned long long xs_mul, xs_add;
     float *xout;
     uint32_t nsl, ny;
-    float *ys[kMaxRanks];
-    unsigned long long *yctr[kMaxRanks];
-    unsigned long long *ytk;   // this device's ticket counter of the exchange
+    unsigned long long *ys[kMaxRanks];
+    const int *y_epoch;
+    unsigned long long y_mul, y_add;
     // expert groups (MvFuse): ng > 0 splits the grid into ng equal runs of CTAs
     const int *ids;
     const int *ng_dev;   // device count of the groups present (<= ng), or null
@@ -139,6 +138,50 @@ __device__ __forceinline__ void loadn(const float *p, uint32_t k0, uint32_t K, f
     }
 }
 
+// Elements [k0, k0 + N) of a row of tagged slot words (zeros past K): each
+// word is read whole at system scope until it carries `tag`, two per 16-byte
+// load on the first pass.  A word still missing after `limit` polls, or once
+// this device's error word is set, sets the error word and reads as what is
+// there; returns false then.
+template <int N>
+__device__ __forceinline__ bool load_tagged(const unsigned long long *p, uint32_t k0, uint32_t K, uint32_t tag,
+                                            float (&t)[N], int *err, uint32_t limit)
+{
+    unsigned long long w[N];
+    if (k0 + N <= K && (reinterpret_cast<uintptr_t>(p + k0) & 15u) == 0) {
+#pragma unroll
+        for (int i = 0; i < N; i += 2)
+            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                         : "=l"(w[i]), "=l"(w[i + 1]) : "l"(p + k0 + i) : "memory");
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            w[i] = static_cast<unsigned long long>(tag) << 32;   // past K: a ready zero
+            if (k0 + i < K) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(p + k0 + i) : "memory");
+        }
+    }
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        for (uint32_t it = 0; static_cast<uint32_t>(w[i] >> 32) != tag; ++it) {
+            if (it >= limit || *reinterpret_cast<volatile int *>(err) != 0) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(p + k0 + i) : "memory");
+        }
+        t[i] = __uint_as_float(static_cast<uint32_t>(w[i]));
+    }
+    return ok;
+}
+
+// The tag of an exchange: (epoch * mul + add) mod 2^32.
+__device__ __forceinline__ uint32_t xch_tag(const int *epoch, unsigned long long mul, unsigned long long add)
+{
+    return static_cast<uint32_t>(static_cast<unsigned long long>(*epoch) * mul + add);
+}
+
 // Activations [k0, k0 + N) (zeros past K) after the fused input transform,
 // and ss += the sum of the squares of the raw x.
 //   RMSNorm: x * nw; the scalar 1/rms of layer1/tb_tensor.c:194-199 is applied
@@ -149,12 +192,15 @@ __device__ __forceinline__ void load_x_part(const MvArgs &a, uint32_t xoff, uint
 {
     loadn<N>(a.x + xoff, k0, a.K, v);
     if (a.nsl) {   // tensor-parallel input: the residual plus the ranks' partials
+        const uint32_t tag = xch_tag(a.xs_epoch, a.xs_mul, a.xs_add);
+        bool ok = true;
         for (uint32_t r = 0; r < a.nsl; ++r) {
             float t[N];
-            loadn<N, true>(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, t);
+            ok = load_tagged<N>(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, tag, t, a.err, a.wait_limit) && ok;
 #pragma unroll
             for (int i = 0; i < N; ++i) v[i] += t[i];
         }
+        if (!ok) atomicExch(a.err, ERR_WAIT_TIMEOUT);
         if (a.xout && blockIdx.x == 0)
 #pragma unroll
             for (int i = 0; i < N; ++i)
@@ -385,17 +431,6 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
     const bool ring_early = TB_MV_TP_EARLY && IsF32X<D>::value && a.nsl > 0;
     if (ring_early && producer && lane == 0)
         for (uint32_t it = 1; it < min(a.nst, n_tiles); ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
-    if (a.nsl) {   // the ranks' partials of x have all arrived
-        if (tid == 0) {
-            // after a wait of this device ran out the chain only finishes (fast,
-            // with the error word set) instead of waiting again at every exchange
-            const unsigned long long target = static_cast<unsigned long long>(*a.xs_epoch) * a.xs_mul + a.xs_add;
-            if (*reinterpret_cast<volatile int *>(a.err) == 0 && !wait_counter(a.xs_ctr, target, a.wait_limit))
-                atomicExch(a.err, ERR_WAIT_TIMEOUT);
-        }
-        __syncthreads();
-        if (tid == 0) MV_STAMP(8);
-    }
 
     // ---- prologue: x -> one record per column slot ----
     float ss = 0.f;   // RMSNorm: this thread's share of sum(x^2)
@@ -552,6 +587,7 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
         const float *pb = part;
         const uint32_t pstride = a.tr * a.npart;
         float *const yg = a.y + grp * a.y_stride;
+        const uint32_t ytag = a.ny ? xch_tag(a.y_epoch, a.y_mul, a.y_add) : 0u;
         for (uint32_t it = 0; it < n_tiles; ++it) {
             const bool ok = mbar_wait_bounded(smem_u32(empty + s), par, a.err, a.wait_limit);
             if (!__all_sync(kFull, ok)) {
@@ -575,8 +611,10 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
                     const float *pr = pb + r * a.npart;
                     float acc = 0.f;
                     for (uint32_t j = 0; j < a.npart; ++j) acc += pr[j];
-                    if (a.ny) {   // tensor-parallel output: this rank's partial to every rank
-                        for (uint32_t p = 0; p < a.ny; ++p) a.ys[p][t0 + r] = acc;
+                    if (a.ny) {   // tensor-parallel output: this rank's partial to every rank, tagged
+                        const unsigned long long wv = (static_cast<unsigned long long>(ytag) << 32) | __float_as_uint(acc);
+                        for (uint32_t p = 0; p < a.ny; ++p)
+                            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.ys[p] + t0 + r), "l"(wv) : "memory");
                     } else {
                         yg[t0 + r] = a.res ? acc + a.res[t0 + r] : acc;
                     }
@@ -602,22 +640,6 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
             }
         }
         if (lane == 0) MV_STAMP(6);
-        if (a.ny && !fail) {
-            // this CTA's partials are visible system-wide before its ticket; the
-            // CTA whose ticket completes the launch counts this rank once on
-            // every rank (a failed CTA never takes a ticket, so the ranks' own
-            // waits run out)
-            __threadfence_system();
-            __syncwarp();
-            unsigned long long t = 0;
-            if (lane == 0) t = atomicAdd(a.ytk, 1ull);
-            t = __shfl_sync(kFull, t, 0);
-            if ((t + 1) % gridDim.x == 0) {
-                __threadfence_system();
-                if (lane < a.ny) atomicAdd_system(a.yctr[lane], 1ull);
-            }
-        }
-        if (lane == 0) MV_STAMP(7);
         if (fail && lane == 0) {
             // A wait ran out: let every copy still in flight land before the CTA
             // exits (fixed, generous bound: they target valid memory and complete).
@@ -880,25 +902,22 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
         a.res = fuse->res;
         a.w_early = fuse->w_early ? 1u : 0u;
         if (fuse->nsl > static_cast<uint32_t>(kMaxRanks) || fuse->ny > static_cast<uint32_t>(kMaxRanks) ||
-            (fuse->nsl && (!fuse->xs || !fuse->xs_ctr || !fuse->xs_epoch || fuse->xmode == MV_X_SWIGLU)) ||
-            (fuse->ny && (fuse->res || fuse->ymode != MV_Y_PLAIN)))
+            (fuse->nsl && (!fuse->xs || !fuse->xs_epoch || fuse->xmode == MV_X_SWIGLU)) ||
+            (fuse->ny && (fuse->res || fuse->ymode != MV_Y_PLAIN || !fuse->y_epoch)))
             return 0;
         for (uint32_t p = 0; p < fuse->ny; ++p)
-            if (!fuse->ys[p] || !fuse->yctr[p]) return 0;
-        if (fuse->ny && !fuse->ytk) return 0;
-        a.ytk = fuse->ytk;
+            if (!fuse->ys[p]) return 0;
         a.xs = fuse->xs;
-        a.xs_ctr = fuse->xs_ctr;
         a.xs_epoch = fuse->xs_epoch;
         a.xs_mul = fuse->xs_mul;
         a.xs_add = fuse->xs_add;
         a.xout = fuse->xout;
         a.nsl = fuse->nsl;
         a.ny = fuse->ny;
-        for (int p = 0; p < kMaxRanks; ++p) {
-            a.ys[p] = fuse->ys[p];
-            a.yctr[p] = fuse->yctr[p];
-        }
+        for (int p = 0; p < kMaxRanks; ++p) a.ys[p] = fuse->ys[p];
+        a.y_epoch = fuse->y_epoch;
+        a.y_mul = fuse->y_mul;
+        a.y_add = fuse->y_add;
         if (fuse->ng > 0) {
             // groups: no residual, no tensor-parallel exchange; an expert id
             // read on the device cannot be prefetched ahead of the wait

@@ -179,11 +179,22 @@ __device__ __forceinline__ void group_q4k(const uint8_t *b, int g, float (&w)[32
     const float Mn = __fmul_rn(dmin, static_cast<float>(m));
     const uint4 q4 = *reinterpret_cast<const uint4 *>(b + 16 + 16 * g);   // 16-byte aligned
     const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
+    // S * q - Mn per weight, two weights per paired op; q as an exact float by
+    // the 2^23 + q bit pattern minus 2^23 (no integer conversion); a - b is
+    // a + (-b) with the same rounding
+    const float2 S2 = make_float2(S, S), M2 = make_float2(-Mn, -Mn), B2 = make_float2(-8388608.f, -8388608.f);
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-        const uint32_t byte = (qw[t >> 2] >> ((t & 3) * 8)) & 0xFFu;
-        w[2 * t] = __fsub_rn(__fmul_rn(S, static_cast<float>(byte & 15u)), Mn);
-        w[2 * t + 1] = __fsub_rn(__fmul_rn(S, static_cast<float>(byte >> 4)), Mn);
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t lo = qw[c] & 0x0F0F0F0Fu, hi = (qw[c] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 q = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7650u | k)),
+                                                    __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7650u | k))),
+                                        B2);
+            const float2 v = __fadd2_rn(__fmul2_rn(S2, q), M2);
+            w[8 * c + 2 * k] = v.x;
+            w[8 * c + 2 * k + 1] = v.y;
+        }
     }
 }
 
@@ -200,11 +211,22 @@ __device__ __forceinline__ void group_q6k(const uint8_t *b, int g, float (&w)[32
     for (int j = 0; j < 4; ++j) ql[j] = ld16(b, 16 * g + 4 * j) | (ld16(b, 16 * g + 4 * j + 2) << 16);
 #pragma unroll
     for (int j = 0; j < 2; ++j) qh[j] = ld16(b, 128 + 8 * g + 4 * j) | (ld16(b, 128 + 8 * g + 4 * j + 2) << 16);
+    // (q - 32) as an exact float: the 2^23 + q bit pattern minus 2^23 + 32; two
+    // weights per paired multiply
+    const float2 B2 = make_float2(-8388640.f, -8388640.f);
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-        const uint32_t lo = (ql[e >> 3] >> (((e >> 1) & 3) * 8 + (e & 1) * 4)) & 15u;
-        const uint32_t hi = (qh[e >> 4] >> (((e >> 2) & 3) * 8 + (e & 3) * 2)) & 3u;
-        w[e] = __fmul_rn(e < 16 ? S0 : S1, static_cast<float>(static_cast<int>(lo | (hi << 4)) - 32));
+    for (int e = 0; e < 32; e += 2) {
+        const uint32_t lo0 = (ql[e >> 3] >> (((e >> 1) & 3) * 8)) & 15u;
+        const uint32_t lo1 = (ql[e >> 3] >> (((e >> 1) & 3) * 8 + 4)) & 15u;
+        const uint32_t hi0 = (qh[e >> 4] >> (((e >> 2) & 3) * 8 + (e & 3) * 2)) & 3u;
+        const uint32_t hi1 = (qh[e >> 4] >> (((e >> 2) & 3) * 8 + ((e + 1) & 3) * 2)) & 3u;
+        const float2 q = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | lo0 | (hi0 << 4)),
+                                                __uint_as_float(0x4B000000u | lo1 | (hi1 << 4))),
+                                    B2);
+        const float S = e < 16 ? S0 : S1;
+        const float2 v = __fmul2_rn(make_float2(S, S), q);
+        w[e] = v.x;
+        w[e + 1] = v.y;
     }
 }
 
