@@ -35,9 +35,7 @@
 // units of two groups or sub-blocks.  The 64 prescaled activations take 64
 // registers, so these kernels run 16 warps of up to 128 registers (NP = 2: 128
 // activations at 8 warps of up to 255); the per-row header decode (scales,
-// mins, d) is paid once per slot.  The CTA's prologue writes each slot's
-// activations already prescaled and in register order (xf_store_quarter), so a
-// consumer thread only copies its record.  Decode semantics are those of
+// mins, d) is paid once per slot.  Decode semantics are those of
 // layer4/tb_gguf_dequant.cu:89-284 (Q2_K: layer4/tb_gguf.c:210-225), the same
 // field layouts as the integer-path decoders in tb_decoders.cuh.
 #pragma once
@@ -61,9 +59,7 @@ template <int NP>
 struct XfGeom {
     static constexpr int N = 64 * NP;                    // activations per slot
     static constexpr int THREADS = NP == 1 ? 512 : 256;  // threads per CTA
-    static constexpr int SUMS = N / 16;                  // sub-block sums (16 or 32 activations each)
-    static constexpr int MB = N + SUMS;                  // word of the slot's largest |x|
-    static constexpr int REC = rec_stride(N + SUMS + 1); // record: N floats, the sums, the max word, padding
+    static constexpr int REC = rec_stride(N + 1);        // record: N floats, the max word, padding
 };
 #ifndef TB_XF_NP
 #define TB_XF_NP 1
@@ -88,54 +84,30 @@ __device__ __forceinline__ int xf_exponent(uint32_t mb)
     return e < -20 ? -20 : (e > 126 ? 126 : e);
 }
 
-// Slot records.  The prologue writes a slot's record in its final form, so a
-// consumer thread only copies it into registers:
-//   words [0, N)          the N activations of the slot, each prescaled to
-//                         x * 2^(107 - E - P) and stored at its position in the
-//                         decoder's register array (D::xdst, D::xshift);
-//   words [N, N + N/XG)   the sums of the slot's sub-blocks of XG activations,
-//                         times 2^(-E - 42) like the products;
-//   word  MB              the magnitude bits of the slot's largest |x|.
-// One prologue thread handles 8 consecutive activations (a quarter group):
-// it writes their prescaled values and adds its 8 to the sum of its
-// sub-block, which the XG/8 neighbouring lanes of that sub-block finish with
-// shuffles.
-template <class D>
-__device__ __forceinline__ void xf_store_quarter(uint32_t *rec, uint32_t qs, const float (&v)[8], uint32_t mb,
-                                                 bool have)
+// The record's N activations and the slot exponent (N / 4 + 1 shared loads).
+template <int N>
+__device__ __forceinline__ int xf_raw(const uint32_t *rec, float (&r)[N])
 {
-    constexpr int N = D::XN, XG = D::XG;
-    const int E = xf_exponent(mb);
-    float *rf = reinterpret_cast<float *>(rec);
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int i = 8 * static_cast<int>(qs) + j;
-        if (have) rf[64 * (i >> 6) + D::xdst(i & 63)] = v[j] * exp2i(107 - E - D::xshift(i & 63));
-        s += v[j];
-    }
-#pragma unroll
-    for (int o = 1; o < XG / 8; o <<= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-    if (have && qs % (XG / 8) == 0) rf[N + (8 * static_cast<int>(qs)) / XG] = (s * exp2i(-E)) * 0x1p-42f;
-    if (have && qs == 0) rec[XfGeom<N / 64>::MB] = mb;
-}
-
-// A consumer's copy of its slot's record: N / 4 + N / 64 + 1 shared loads.
-template <class D>
-__device__ __forceinline__ void xf_load(float2 *x, float2 *xs, float &sx, const uint32_t *rec)
-{
-    constexpr int N = D::XN, NS = D::XN / D::XG;
     const uint32_t a = shared_after(static_cast<uint32_t>(__cvta_generic_to_shared(rec)));
 #pragma unroll
     for (int i = 0; i < N / 4; ++i) {
         const uint4 v = lds_u128(a + 16 * i);
-        x[2 * i] = f2(__uint_as_float(v.x), __uint_as_float(v.y));
-        x[2 * i + 1] = f2(__uint_as_float(v.z), __uint_as_float(v.w));
+        r[4 * i] = __uint_as_float(v.x);
+        r[4 * i + 1] = __uint_as_float(v.y);
+        r[4 * i + 2] = __uint_as_float(v.z);
+        r[4 * i + 3] = __uint_as_float(v.w);
     }
+    return xf_exponent(lds_u32(a + 4 * N));
+}
+
+// Sum of r[i0 .. i0+n) scaled like the products: (sum * 2^-E) * 2^-42.
+template <int N, int R>
+__device__ __forceinline__ float xf_sum(const float (&r)[R], int i0, int E)
+{
+    float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < NS / 2; ++i)
-        xs[i] = f2(__uint_as_float(lds_u32(a + 4 * (N + 2 * i))), __uint_as_float(lds_u32(a + 4 * (N + 2 * i + 1))));
-    sx = exp2i(xf_exponent(lds_u32(a + 4 * XfGeom<N / 64>::MB)));
+    for (int i = 0; i < N; ++i) s += r[i0 + i];
+    return (s * exp2i(-E)) * 0x1p-42f;
 }
 
 // Both fp16 halves of w through the reference converter, times 2^42 (exact).
@@ -213,12 +185,21 @@ struct DecQ4KF {
         float2 xs[NP];
     };
     __host__ __device__ static constexpr int pos(int n) { return n < 6 ? 4 * n : 4 * n - 8; }
-    // activation i (0..63) of a 64-activation unit: its float in the register
-    // array and the bit position P its field is masked at
-    __host__ __device__ static constexpr int xdst(int i) { return 2 * (i & 31) + (i >> 5); }
-    __host__ __device__ static constexpr int xshift(int i) { return pos(i & 7); }
-    static constexpr int XG = 32;   // activations per sub-block sum
-    __device__ static void load(Lane &L, const uint32_t *rec) { xf_load<DecQ4KF>(&L.x[0][0], &L.xs[0], L.sx, rec); }
+    __device__ static void load(Lane &L, const uint32_t *rec)
+    {
+        float r[XN];
+        const int E = xf_raw(rec, r);
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+#pragma unroll
+            for (int w = 0; w < 32; ++w) {
+                const float f = exp2i(107 - E - pos(w & 7));
+                L.x[u][w] = f2(r[64 * u + w] * f, r[64 * u + 32 + w] * f);
+            }
+            L.xs[u] = f2(xf_sum<32>(r, 64 * u, E), xf_sum<32>(r, 64 * u + 32, E));
+        }
+        L.sx = exp2i(E);
+    }
     __device__ static float2 unit(const Words<A16> &W, uint32_t gi, const float2 (&x)[32])
     {
         const uint4 qa = W.q4(16 + 16 * gi), qb = W.q4(32 + 16 * gi);
@@ -270,12 +251,23 @@ struct DecQ5KF {
         float2 x[NP][32];
         float2 xs[NP];
     };
-    // activation i (0..63) of a 64-activation unit: its float in the register
-    // array and the bit position P its field is masked at
-    __host__ __device__ static constexpr int xdst(int i) { return 2 * (4 * (i & 7) + ((i & 31) >> 3)) + (i >> 5); }
-    __host__ __device__ static constexpr int xshift(int i) { return lane_pos((i & 31) >> 3); }
-    static constexpr int XG = 32;   // activations per sub-block sum
-    __device__ static void load(Lane &L, const uint32_t *rec) { xf_load<DecQ5KF>(&L.x[0][0], &L.xs[0], L.sx, rec); }
+    __device__ static void load(Lane &L, const uint32_t *rec)
+    {
+        float r[XN];
+        const int E = xf_raw(rec, r);
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const float f = exp2i(107 - E - lane_pos(b));
+                    L.x[u][4 * j + b] = f2(r[64 * u + 8 * b + j] * f, r[64 * u + 32 + 8 * b + j] * f);
+                }
+            L.xs[u] = f2(xf_sum<32>(r, 64 * u, E), xf_sum<32>(r, 64 * u + 32, E));
+        }
+        L.sx = exp2i(E);
+    }
     // the eight field words of one group
     __device__ static void fields(const Words<A16> &W, uint32_t gi, uint32_t (&F)[8])
     {
@@ -338,12 +330,24 @@ struct DecQ6KF {
         float2 x[2 * NP][16];
         float2 xs[2 * NP];
     };
-    // activation i (0..63) of a 64-activation unit: its float in the register
-    // array and the bit position P its field is masked at
-    __host__ __device__ static constexpr int xdst(int i) { return 2 * (16 * (i >> 5) + 4 * (i & 3) + ((i & 15) >> 2)) + ((i >> 4) & 1); }
-    __host__ __device__ static constexpr int xshift(int i) { return lane_pos((i & 15) >> 2); }
-    static constexpr int XG = 16;   // activations per sub-block sum
-    __device__ static void load(Lane &L, const uint32_t *rec) { xf_load<DecQ6KF>(&L.x[0][0], &L.xs[0], L.sx, rec); }
+    __device__ static void load(Lane &L, const uint32_t *rec)
+    {
+        float r[XN];
+        const int E = xf_raw(rec, r);
+#pragma unroll
+        for (int sp = 0; sp < 2 * NP; ++sp) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const float f = exp2i(107 - E - lane_pos(b));
+                    const int i = 32 * sp + 4 * b + j;
+                    L.x[sp][4 * j + b] = f2(r[i] * f, r[i + 16] * f);
+                }
+            L.xs[sp] = f2(xf_sum<16>(r, 32 * sp, E), xf_sum<16>(r, 32 * sp + 16, E));
+        }
+        L.sx = exp2i(E);
+    }
     __device__ static void fields(uint32_t A, uint32_t B, uint32_t h, uint32_t (&F)[4])
     {
         constexpr uint32_t N = 0x0F0F0F0Fu, M = 0x30303030u;
@@ -391,12 +395,24 @@ struct DecQ3KF {
         float2 x[2 * NP][16];
         float2 xs[2 * NP];
     };
-    // activation i (0..63) of a 64-activation unit: its float in the register
-    // array and the bit position P its field is masked at
-    __host__ __device__ static constexpr int xdst(int i) { return 2 * (16 * (i >> 5) + 4 * (i & 3) + ((i & 15) >> 2)) + ((i >> 4) & 1); }
-    __host__ __device__ static constexpr int xshift(int i) { return lane_pos((i & 15) >> 2); }
-    static constexpr int XG = 16;   // activations per sub-block sum
-    __device__ static void load(Lane &L, const uint32_t *rec) { xf_load<DecQ3KF>(&L.x[0][0], &L.xs[0], L.sx, rec); }
+    __device__ static void load(Lane &L, const uint32_t *rec)
+    {
+        float r[XN];
+        const int E = xf_raw(rec, r);
+#pragma unroll
+        for (int g = 0; g < 2 * NP; ++g) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const float f = exp2i(107 - E - lane_pos(b));
+                    const int i = 32 * g + 4 * b + k;
+                    L.x[g][4 * k + b] = f2(r[i] * f, r[i + 16] * f);
+                }
+            L.xs[g] = f2(xf_sum<16>(r, 32 * g, E), xf_sum<16>(r, 32 * g + 16, E));
+        }
+        L.sx = exp2i(E);
+    }
     __device__ static void fields(uint32_t q, uint32_t h, uint32_t (&F)[4])
     {
         F[0] = (q & 0x03030303u) | ((h << 2) & 0x04040404u);
@@ -445,12 +461,24 @@ struct DecQ2KF {
         float2 x[2 * NP][16];
         float2 xs[2 * NP];
     };
-    // activation i (0..63) of a 64-activation unit: its float in the register
-    // array and the bit position P its field is masked at
-    __host__ __device__ static constexpr int xdst(int i) { return 2 * (16 * (i >> 5) + (i & 15)) + ((i >> 4) & 1); }
-    __host__ __device__ static constexpr int xshift(int i) { return lane_pos((i & 15) >> 2) + 2 * (i & 3); }
-    static constexpr int XG = 16;   // activations per sub-block sum
-    __device__ static void load(Lane &L, const uint32_t *rec) { xf_load<DecQ2KF>(&L.x[0][0], &L.xs[0], L.sx, rec); }
+    __device__ static void load(Lane &L, const uint32_t *rec)
+    {
+        float r[XN];
+        const int E = xf_raw(rec, r);
+#pragma unroll
+        for (int sp = 0; sp < 2 * NP; ++sp) {
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float f = exp2i(107 - E - lane_pos(b) - 2 * k);
+                    const int i = 32 * sp + 4 * b + k;
+                    L.x[sp][4 * b + k] = f2(r[i] * f, r[i + 16] * f);
+                }
+            L.xs[sp] = f2(xf_sum<16>(r, 32 * sp, E), xf_sum<16>(r, 32 * sp + 16, E));
+        }
+        L.sx = exp2i(E);
+    }
     __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         const Words<A4> W(row + p.off);
@@ -499,12 +527,21 @@ struct DecQ80F {
         float2 x[NP][32];
         float2 xs[NP];
     };
-    // activation i (0..63) of a 64-activation unit: its float in the register
-    // array and the bit position P its field is masked at
-    __host__ __device__ static constexpr int xdst(int i) { return 2 * (i & 31) + (i >> 5); }
-    __host__ __device__ static constexpr int xshift(int i) { return lane_pos(i & 3); }
-    static constexpr int XG = 32;   // activations per sub-block sum
-    __device__ static void load(Lane &L, const uint32_t *rec) { xf_load<DecQ80F>(&L.x[0][0], &L.xs[0], L.sx, rec); }
+    __device__ static void load(Lane &L, const uint32_t *rec)
+    {
+        float r[XN];
+        const int E = xf_raw(rec, r);
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float f = exp2i(107 - E - lane_pos(i & 3));
+                L.x[u][i] = f2(r[64 * u + i] * f, r[64 * u + 32 + i] * f);
+            }
+            L.xs[u] = f2(xf_sum<32>(r, 64 * u, E), xf_sum<32>(r, 64 * u + 32, E));
+        }
+        L.sx = exp2i(E);
+    }
     __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         float tot = 0.f;
@@ -537,12 +574,21 @@ struct DecQ40F {
         float2 x[NP][32];
         float2 xs[NP];
     };
-    // activation i (0..63) of a 64-activation unit: its float in the register
-    // array and the bit position P its field is masked at
-    __host__ __device__ static constexpr int xdst(int i) { return 2 * (i & 31) + (i >> 5); }
-    __host__ __device__ static constexpr int xshift(int i) { return DecQ4KF<false, NP>::pos(i & 7); }
-    static constexpr int XG = 32;   // activations per sub-block sum
-    __device__ static void load(Lane &L, const uint32_t *rec) { xf_load<DecQ40F>(&L.x[0][0], &L.xs[0], L.sx, rec); }
+    __device__ static void load(Lane &L, const uint32_t *rec)
+    {
+        float r[XN];
+        const int E = xf_raw(rec, r);
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+#pragma unroll
+            for (int w = 0; w < 32; ++w) {
+                const float f = exp2i(107 - E - DecQ4KF<false, NP>::pos(w & 7));
+                L.x[u][w] = f2(r[64 * u + w] * f, r[64 * u + 32 + w] * f);
+            }
+            L.xs[u] = f2(xf_sum<32>(r, 64 * u, E), xf_sum<32>(r, 64 * u + 32, E));
+        }
+        L.sx = exp2i(E);
+    }
     __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {
         float tot = 0.f;
@@ -581,10 +627,7 @@ struct DecQ40F {
 template <int NP = XF_NP>
 struct DecQ8KF {
     TB_XF_TRAITS
-    using Lane = typename DecQ80F<NP>::Lane;   // same register layout and record as Q8_0
-    __host__ __device__ static constexpr int xdst(int i) { return DecQ80F<NP>::xdst(i); }
-    __host__ __device__ static constexpr int xshift(int i) { return DecQ80F<NP>::xshift(i); }
-    static constexpr int XG = DecQ80F<NP>::XG;
+    using Lane = typename DecQ80F<NP>::Lane;   // same register layout and load as Q8_0
     __device__ static void load(Lane &L, const uint32_t *rec) { DecQ80F<NP>::load(L, rec); }
     __device__ static float row_dot(uint32_t row, const Pos &p, const Lane &x)
     {

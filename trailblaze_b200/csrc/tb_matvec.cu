@@ -446,11 +446,12 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
     bool split = false;
     if constexpr (D::kInt) split = a.nst >= 2 && (a.nst - 1ull) * a.cap >= xq_bytes + 4ull * a.cs;
     if constexpr (IsF32X<D>::value) {
-        // fp32 decoders: the record is the slot's transformed activations,
-        // prescaled and in the decoder's register order, their sub-block sums
-        // and the magnitude bits of its largest |x| (tb_decoders_f32.cuh).  All
-        // threads, 8 activations each; the QPS quarters of a slot are
-        // neighbouring lanes.
+        // fp32 decoders: the record is the slot's transformed activations
+        // themselves plus the magnitude bits of its largest |x| (each consumer
+        // thread prescales its copy: writing them prescaled here, in register
+        // order, was measured slower, the scattered 4-byte stores costing the
+        // prologue more than they saved the consumers).  All threads, 8
+        // activations each; the QPS quarters of a slot are neighbouring lanes.
         constexpr uint32_t QPS = 4u * D::GPL;
         const uint32_t nq = 4 * ngp;
         for (uint32_t base = 0; base < nq; base += nthr) {   // same trip count in every thread
@@ -468,9 +469,13 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
             for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(v[i]) & 0x7FFFFFFFu);
 #pragma unroll
             for (uint32_t o = 1; o < QPS; o <<= 1) mb = max(mb, __shfl_xor_sync(kFull, mb, o));
-            // prescaled into register order, plus the sub-block sums (shuffles: every lane)
-            if constexpr (IsF32X<D>::value)
-                xf_store_quarter<D>(table + (q / QPS) * D::REC, q % QPS, v, mb, have);
+            if (have) {
+                uint32_t *rec = table + (q / QPS) * D::REC;
+                float4 *dst = reinterpret_cast<float4 *>(rec + (q % QPS) * 8);
+                dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+                dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+                if (q % QPS == 0) rec[D::XN] = mb;
+            }
         }
     } else if (split) {
         uint8_t *xq = ring + a.cap;                          // [ngp * 4][8] int16, then [cs] int32 exponents
