@@ -83,6 +83,12 @@ struct MvArgs {
     uint32_t x_stride, y_stride;
 };
 
+#ifndef TB_LL_SLEEP_NS
+#define TB_LL_SLEEP_NS 64   // back-off between polls of a tagged slot word
+#endif
+#ifndef TB_LL_QUIET
+#define TB_LL_QUIET 0
+#endif
 #ifndef TB_MV_TP_EARLY
 #define TB_MV_TP_EARLY 1
 #endif
@@ -138,41 +144,49 @@ __device__ __forceinline__ void loadn(const float *p, uint32_t k0, uint32_t K, f
     }
 }
 
-// Elements [k0, k0 + N) of a row of tagged slot words (zeros past K): each
-// word is read whole at system scope until it carries `tag`, two per 16-byte
-// load on the first pass.  A word still missing after `limit` polls, or once
-// this device's error word is set, sets the error word and reads as what is
-// there; returns false then.
+// Elements [k0, k0 + N) of a row of tagged slot words (zeros past K): all N
+// words are read whole at system scope (two per 16-byte load when aligned),
+// and read again together until every one carries `tag`, so the wait costs
+// one round trip after the last word lands, not one per word.  Still
+// incomplete after `limit` rounds, or once this device's error word is set:
+// the error word is set by the caller and the words read as what is there
+// (returns false).
 template <int N>
 __device__ __forceinline__ bool load_tagged(const unsigned long long *p, uint32_t k0, uint32_t K, uint32_t tag,
                                             float (&t)[N], int *err, uint32_t limit)
 {
     unsigned long long w[N];
-    if (k0 + N <= K && (reinterpret_cast<uintptr_t>(p + k0) & 15u) == 0) {
+    const bool vec = k0 + N <= K && (reinterpret_cast<uintptr_t>(p + k0) & 15u) == 0;
+    auto read = [&]() {
+        if (vec) {
 #pragma unroll
-        for (int i = 0; i < N; i += 2)
-            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
-                         : "=l"(w[i]), "=l"(w[i + 1]) : "l"(p + k0 + i) : "memory");
-    } else {
+            for (int i = 0; i < N; i += 2)
+                asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                             : "=l"(w[i]), "=l"(w[i + 1]) : "l"(p + k0 + i) : "memory");
+        } else {
 #pragma unroll
-        for (int i = 0; i < N; ++i) {
-            w[i] = static_cast<unsigned long long>(tag) << 32;   // past K: a ready zero
-            if (k0 + i < K) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(p + k0 + i) : "memory");
-        }
-    }
-    bool ok = true;
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-        for (uint32_t it = 0; static_cast<uint32_t>(w[i] >> 32) != tag; ++it) {
-            if (it >= limit || *reinterpret_cast<volatile int *>(err) != 0) {
-                ok = false;
-                break;
+            for (int i = 0; i < N; ++i) {
+                w[i] = static_cast<unsigned long long>(tag) << 32;   // past K: a ready zero
+                if (k0 + i < K) asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(p + k0 + i) : "memory");
             }
-            __nanosleep(64);
-            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(p + k0 + i) : "memory");
         }
-        t[i] = __uint_as_float(static_cast<uint32_t>(w[i]));
+    };
+    read();
+    bool ok = true;
+    for (uint32_t it = 0;; ++it) {
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < N; ++i) all = all && static_cast<uint32_t>(w[i] >> 32) == tag;
+        if (all) break;
+        if (it >= limit || *reinterpret_cast<volatile int *>(err) != 0) {
+            ok = false;
+            break;
+        }
+        __nanosleep(TB_LL_SLEEP_NS);
+        read();   // words already carrying the tag keep their value: a slot is rewritten only by the next exchange
     }
+#pragma unroll
+    for (int i = 0; i < N; ++i) t[i] = __uint_as_float(static_cast<uint32_t>(w[i]));
     return ok;
 }
 
@@ -395,7 +409,11 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
         pos.ng = static_cast<int>(min(static_cast<uint32_t>(D::GPL), ngrp - min(ngrp, g0)));
         pos.n = static_cast<int>(min(32u, a.K - min(a.K, 32u * (g0 + pos.ng - 1))));
     }
-    if (a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
+    // quiet: a matvec that waits for the other ranks' partials requests no
+    // weights before they are in (the peers' NVLink stores would queue behind
+    // this GPU's own weight stream in its L2)
+    const bool quiet = TB_LL_QUIET && a.nsl > 0;
+    if (a.w_early && !quiet && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (tid == 0) MV_STAMP(1);
     // The next kernel may start once every CTA is past the wait: what the
@@ -424,11 +442,11 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
         }
         w_lo += static_cast<uintptr_t>(e) * a.w_stride;
     }
-    if (!a.w_early && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
+    if (!a.w_early && !quiet && producer && lane == 0 && n_tiles) issue(0, r_lo, w_lo);
     // A matvec whose input waits on the other ranks' partials requests the rest
     // of its ring as well (the fp32 prologue does not use the ring), so its
     // weights stream while the exchange completes.
-    const bool ring_early = TB_MV_TP_EARLY && IsF32X<D>::value && a.nsl > 0;
+    const bool ring_early = TB_MV_TP_EARLY && !quiet && IsF32X<D>::value && a.nsl > 0;
     if (ring_early && producer && lane == 0)
         for (uint32_t it = 1; it < min(a.nst, n_tiles); ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
 
@@ -580,7 +598,8 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
     if (producer && lane == 0) {
         const uint32_t pre = min(a.nst, n_tiles);
         fence_proxy_async_smem();   // stages 1.. may have held the prologue's digits (generic proxy)
-        for (uint32_t it = ring_early ? pre : 1; it < pre; ++it) issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
+        for (uint32_t it = ring_early ? pre : (quiet ? 0 : 1); it < pre; ++it)
+            issue(it, r_lo + it * a.tr, w_lo + it * tile_bytes);
     }
     if (producer) {
         // ---- producer: reduce each finished tile, write y, refill its stage ----
