@@ -293,7 +293,7 @@ def moe_bench(ctx: int, n: int, e2e_tokens: int = 16, rank: int = 0, world: int 
                      "(FFN 768) top 8, vocab 151936; Q4_K experts, Q6_K attention and output, fp32 router; fp32 KV",
             "parallelism": (f"expert-parallel x{world} ({shape.n_experts // world} experts per GPU), attention "
                             f"head-sharded" if world > 1 else "one GPU (all 128 experts resident)"),
-            "launches_per_token": 1 + (8 if world > 1 else 7) * shape.n_layers + 2, **d}
+            "launches_per_token": 1 + 8 * shape.n_layers + 2, **d}
 
 
 def tensor_peak():

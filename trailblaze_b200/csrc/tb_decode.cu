@@ -30,7 +30,6 @@
 
 #include "tb_common.cuh"
 #include "tb_internal.h"
-#include "tb_moe_topk.cuh"
 
 namespace tb {
 
@@ -721,7 +720,7 @@ __global__ void __launch_bounds__(kArgThreads) k_argmax_step(const float *logits
 // ---------------------------------------------------------------------------
 // Mixture-of-experts routing and combine (layer4/tb_infer.c:351-374, 753-850)
 // ---------------------------------------------------------------------------
-static constexpr int kMoeThreads = kTopkMax;   // experts per router at most
+static constexpr int kMoeThreads = 256;   // experts per router at most (tb_infer.c:254 caps at 256)
 
 // Router: p = softmax(logits) over the E experts (max-shifted, the sum taken
 // in expert order as the reference's loop does), the top k experts, and
@@ -734,8 +733,90 @@ static constexpr int kMoeThreads = kTopkMax;   // experts per router at most
 // Expert parallelism (ep_n > 0): this rank holds experts [ep_lo, ep_lo +
 // ep_n); the selected ones among them are also listed, in rank order, as local
 // indices lids[0..*nloc) with their weights lw.
-// This runs in the router matvec's last CTA (MvFuse tk_*, tb_moe_topk.cuh).
+__global__ void __launch_bounds__(kMoeThreads) k_moe_topk(const float *logits, int E, int k, int *ids, float *wts,
+                                                           int *err, int ep_lo, int ep_n, int *lids, float *lw,
+                                                           int *nloc)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __shared__ float p[kMoeThreads];
+    __shared__ float sel[kMoeThreads];
+    __shared__ float red[kMoeThreads / 32];
+    __shared__ float s_sum;
+    const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    const float v = e < E ? logits[e] : -FLT_MAX;
+    float m = v;
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (int w = 1; w < kMoeThreads / 32; ++w) m = fmaxf(m, red[w]);
+    bool fin = isfinite(m);
+    if (e < E) {
+        fin = fin && isfinite(v);
+        p[e] = expf(v - m);
+    }
+    const bool all_fin = __syncthreads_and(fin ? 1 : 0) != 0;
+    if (!all_fin) {
+        if (e == 0) atomicExch(err, ERR_RUNTIME);
+        return;
+    }
+    if (e == 0) {
+        float s = 0.f;
+        for (int j = 0; j < E; ++j) s += p[j];
+        s_sum = s;
+    }
+    __syncthreads();
+    const float q = e < E ? p[e] / s_sum : 0.f;
+    __syncthreads();
+    if (e < E) p[e] = q;
+    __syncthreads();
+    if (e < E) {
+        int rank = 0;
+        for (int j = 0; j < E; ++j) rank += (p[j] > q || (p[j] == q && j < e)) ? 1 : 0;
+        if (rank < k) {
+            ids[rank] = e;
+            sel[rank] = q;
+        }
+    }
+    __syncthreads();
+    if (e == 0) {
+        float ws = 0.f;
+        for (int i = 0; i < k; ++i) ws += sel[i];
+        s_sum = ws;
+    }
+    __syncthreads();
+    const float wk = s_sum > 0.f ? sel[e < k ? e : 0] / s_sum : sel[e < k ? e : 0];
+    if (e < k) wts[e] = wk;
+    if (ep_n > 0) {
+        // the local experts in rank order: a ballot over the k ranks (k <= 32 lanes of warp 0)
+        if (warp == 0) {
+            const int id = e < k ? ids[e] : -1;
+            const bool mine = e < k && id >= ep_lo && id < ep_lo + ep_n;
+            const unsigned bal = __ballot_sync(0xFFFFFFFFu, mine);
+            if (mine) {
+                const int j = __popc(bal & ((1u << lane) - 1u));
+                lids[j] = id - ep_lo;
+                lw[j] = wk;
+            }
+            if (e == 0) *nloc = __popc(bal);
+        }
+    }
+}
 
+// x[i] = x2[i] + sum_r wts[r] * t[r][i], r in rank order (tb_infer.c:845-848,
+// 876: the experts' weighted outputs accumulated, then the residual).
+__global__ void __launch_bounds__(kMoeThreads) k_moe_combine(const float *x2, const float *t, const float *wts, int k,
+                                                              int H, float *x)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int i = blockIdx.x * kMoeThreads + threadIdx.x;
+    if (i >= H) return;
+    float acc = 0.f;
+    for (int r = 0; r < k; ++r) acc = fmaf(wts[r], t[static_cast<size_t>(r) * H + i], acc);
+    x[i] = x2[i] + acc;
+}
 
 // The end of an exchange launch: this CTA's stores are fenced at system
 // scope before its ticket, and the CTA whose ticket completes the launch
@@ -855,7 +936,7 @@ struct Decoder {
     float *x = nullptr, *x2 = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr, *part = nullptr, *argv = nullptr;
     int *argi = nullptr, *tok = nullptr, *pos = nullptr, *hostio = nullptr;
-    unsigned *counts = nullptr;   // [NK] attention tickets + [1] argmax ticket + [1] expert-selection ticket
+    unsigned *counts = nullptr;   // [NK] attention tickets + [1] argmax ticket
     // tensor parallelism: cfg holds this rank's shape (heads, FFN rows and
     // vocabulary divided by world); vocab_full is the embedding table's rows.
     int rank = 0, world = 1, vocab_full = 0;
@@ -922,7 +1003,6 @@ struct Decoder {
     bool enqueue(cudaStream_t s);
     bool enqueue_tp(cudaStream_t s);
     bool enqueue_moe(cudaStream_t s, const DecLayer &w);
-    void combine_in(MvFuse &f) const;
     bool enqueue_moe_ep(cudaStream_t s, const DecLayer &w, int l, unsigned long long per_x,
                         unsigned long long per_step);
 };
@@ -941,12 +1021,11 @@ bool Decoder::enqueue_moe(cudaStream_t s, const DecLayer &w)
     f.nw = w.ffn_norm;
     f.eps = c.norm_eps;
     f.w_early = true;
-    // the router's last CTA also selects the experts (softmax, top k, weights)
-    f.tk_k = top_k;
-    f.tk_ids = ids;
-    f.tk_wts = wts;
-    f.tk_ctr = counts + c.n_kv_heads + 1;
     if (!mv_launch(w.wr, w.r_qt, n_exp, H, x2, rlog, s, err, sms, lim, &f)) return false;
+    if (!launch_pdl(k_moe_topk, dim3(1), dim3(kMoeThreads), 0, s, static_cast<const float *>(rlog), n_exp, top_k,
+                    ids, wts, err, 0, 0, static_cast<int *>(nullptr), static_cast<float *>(nullptr),
+                    static_cast<int *>(nullptr)))
+        return false;
     const Geom gg = geom_of(w.gue_qt), gd = geom_of(w.de_qt);
     f = MvFuse{};
     f.xmode = MV_X_RMSNORM;
@@ -966,20 +1045,10 @@ bool Decoder::enqueue_moe(cudaStream_t s, const DecLayer &w)
     f.w_stride = static_cast<unsigned long long>(H) * (F / gd.block_weights) * gd.block_bytes;
     f.x_stride = static_cast<uint32_t>(F);
     f.y_stride = static_cast<uint32_t>(H);
-    // x = x2 + the weighted outputs: formed by the next matvec's prologue (combine_in)
-    return mv_launch(w.wd_e, w.de_qt, H, F, hbuf, tbuf, s, err, sms, lim, &f) != 0;
-}
-
-// The routed layer's combine (tb_infer.c:845-848, 876: the experts' weighted
-// outputs accumulated in rank order, then the residual) as the input transform
-// of the matvec after it (the next layer's q/k/v or the output):
-// x2 + sum_r wts[r] * tbuf[r], CTA 0 writing that residual to x.
-void Decoder::combine_in(MvFuse &f) const
-{
-    f.cmb_t = tbuf;
-    f.cmb_w = wts;
-    f.cmb_k = static_cast<uint32_t>(top_k);
-    f.xout = x;
+    if (!mv_launch(w.wd_e, w.de_qt, H, F, hbuf, tbuf, s, err, sms, lim, &f)) return false;
+    return launch_pdl(k_moe_combine, dim3((H + kMoeThreads - 1) / kMoeThreads), dim3(kMoeThreads), 0, s,
+                      static_cast<const float *>(x2), static_cast<const float *>(tbuf),
+                      static_cast<const float *>(wts), top_k, H, x);
 }
 
 // The routed FFN of one layer under expert parallelism (world > 1): the
@@ -1006,17 +1075,10 @@ bool Decoder::enqueue_moe_ep(cudaStream_t s, const DecLayer &w, int l, unsigned 
     f.xs_mul = per_step;
     f.xs_add = static_cast<unsigned long long>(l + 1) * per_x;
     f.xout = x2;
-    // the router's last CTA also selects the experts, and this rank's among them
-    f.tk_k = top_k;
-    f.tk_ids = ids;
-    f.tk_wts = wts;
-    f.tk_ctr = counts + cfg.n_kv_heads + 1;
-    f.tk_ep_lo = rank * n_loc_exp;
-    f.tk_ep_n = n_loc_exp;
-    f.tk_lids = lids;
-    f.tk_lw = lw;
-    f.tk_nloc = nloc;
     if (!mv_launch(w.wr, w.r_qt, n_exp, H, x, rlog, s, err, sms, lim, &f)) return false;
+    if (!launch_pdl(k_moe_topk, dim3(1), dim3(kMoeThreads), 0, s, static_cast<const float *>(rlog), n_exp, top_k,
+                    ids, wts, err, rank * n_loc_exp, n_loc_exp, lids, lw, nloc))
+        return false;
     const Geom gg = geom_of(w.gue_qt), gd = geom_of(w.de_qt);
     f = MvFuse{};
     f.xmode = MV_X_RMSNORM;
@@ -1061,17 +1123,13 @@ bool Decoder::enqueue(cudaStream_t s)
     for (int l = 0; l < c.n_layers; ++l) {
         const DecLayer &w = layers[l];
         MvFuse f;
-        // q | k | v = Wqkv @ rmsnorm(x); after a routed layer x = x2 + the
-        // experts' weighted outputs is formed in this matvec's prologue (CTA 0
-        // writes it back to x)
+        // q | k | v = Wqkv @ rmsnorm(x)
         f = MvFuse{};
         f.xmode = MV_X_RMSNORM;
         f.nw = w.attn_norm;
         f.w_early = true;
         f.eps = c.norm_eps;
-        const bool cmb = n_exp && l > 0;
-        if (cmb) combine_in(f);
-        if (!mv_launch(w.wqkv, w.qkv_qt, QKV, H, cmb ? x2 : x, qkv, s, err, sms, lim, &f)) return false;
+        if (!mv_launch(w.wqkv, w.qkv_qt, QKV, H, x, qkv, s, err, sms, lim, &f)) return false;
         // attention (QK-norm, RoPE, cache append, split-context softmax)
         AttnArgs a{};
         a.qkv = qkv;
@@ -1127,8 +1185,7 @@ bool Decoder::enqueue(cudaStream_t s)
     f.nw = out_norm;
     f.eps = c.norm_eps;
     f.w_early = true;
-    if (n_exp) combine_in(f);
-    if (!mv_launch(lm, lm_qt, c.vocab, H, n_exp ? x2 : x, logits, s, err, sms, lim, &f)) return false;
+    if (!mv_launch(lm, lm_qt, c.vocab, H, x, logits, s, err, sms, lim, &f)) return false;
     if (sampling())
         return sample_launch(logits, c.vocab, smp_k, smp_p, smp_temp, 0.f, tok, err, s, u_buf, u_idx, pos) != 0;
     const int G = sms;
@@ -1384,7 +1441,7 @@ Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, i
               dec_ok(cudaMalloc(&d->argv, sizeof(float) * d->sms), "argmax") &&
               dec_ok(cudaMalloc(&d->argi, sizeof(int) * d->sms), "argmax") &&
               dec_ok(cudaMalloc(&d->tok, sizeof(int)), "token") && dec_ok(cudaMalloc(&d->pos, sizeof(int)), "pos") &&
-              dec_ok(cudaMalloc(&d->counts, sizeof(unsigned) * (NK + 2)), "tickets") &&
+              dec_ok(cudaMalloc(&d->counts, sizeof(unsigned) * (NK + 1)), "tickets") &&
               dec_ok(cudaMalloc(&d->err, sizeof(int)), "err") &&
               dec_ok(cudaMallocHost(&d->hostio, sizeof(int) * 4), "host io");
     if (ok && n_exp) {
@@ -1421,7 +1478,7 @@ Decoder *dec_create(const DecConfig &full, int rank, int world, int n_exp = 0, i
         d->peer[rank] = d->xch;
     }
     if (ok) {
-        ok = dec_ok(cudaMemset(d->counts, 0, sizeof(unsigned) * (NK + 2)), "memset") &&
+        ok = dec_ok(cudaMemset(d->counts, 0, sizeof(unsigned) * (NK + 1)), "memset") &&
              dec_ok(cudaMemset(d->err, 0, sizeof(int)), "memset") &&
              dec_ok(cudaMemset(d->kc, 0, sizeof(float) * kvf), "memset") &&
              dec_ok(cudaMemset(d->vc, 0, sizeof(float) * kvf), "memset");

@@ -43,21 +43,6 @@ struct MvFuse {
     // (*xs_epoch) * xs_mul + xs_add; CTA 0 also writes that x to xout when
     // not null.  Output: y[row] goes to ys[p][row] for the ny ranks p instead
     // of y, tagged (*y_epoch) * y_mul + y_add.
-    // Routed-FFN combine input (unused when cmb_k is 0): x <- x + sum_{r < cmb_k}
-    // cmb_w[r] * cmb_t[r][.] (fmaf accumulation in r order from 0, then added
-    // to x: the combine of layer4/tb_infer.c:845-848, 876); CTA 0 also writes
-    // that x to xout when not null.  Not with nsl.
-    const float *cmb_t = nullptr, *cmb_w = nullptr;
-    uint32_t cmb_k = 0;
-    // Routed-layer expert selection after the router matvec (unused when tk_k
-    // is 0): the CTA that completes the launch (a ticket on *tk_ctr, left at 0)
-    // ranks the M logits it wrote as k_moe_topk does (tb_moe_topk.cuh) into
-    // tk_ids / tk_wts, and with tk_ep_n > 0 the local experts into tk_lids /
-    // tk_lw / *tk_nloc.  M <= 256.
-    int tk_k = 0, tk_ep_lo = 0, tk_ep_n = 0;
-    int *tk_ids = nullptr, *tk_lids = nullptr, *tk_nloc = nullptr;
-    float *tk_wts = nullptr, *tk_lw = nullptr;
-    unsigned *tk_ctr = nullptr;
     const unsigned long long *xs = nullptr;
     const int *xs_epoch = nullptr;
     unsigned long long xs_mul = 0, xs_add = 0;

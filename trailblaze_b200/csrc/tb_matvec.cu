@@ -36,7 +36,6 @@
 #include "tb_decoders.cuh"
 #include "tb_decoders_f32.cuh"
 #include "tb_internal.h"
-#include "tb_moe_topk.cuh"
 
 namespace tb {
 
@@ -72,12 +71,6 @@ struct MvArgs {
     const int *xs_epoch;
     unsigned long long xs_mul, xs_add;
     float *xout;
-    const float *cmb_t, *cmb_w;   // routed-FFN combine input (MvFuse)
-    uint32_t cmb_k;
-    int tk_k, tk_ep_lo, tk_ep_n;  // expert selection after the launch (MvFuse)
-    int *tk_ids, *tk_lids, *tk_nloc;
-    float *tk_wts, *tk_lw;
-    unsigned *tk_ctr;
     uint32_t nsl, ny;
     unsigned long long *ys[kMaxRanks];
     const int *y_epoch;
@@ -212,20 +205,6 @@ template <int N>
 __device__ __forceinline__ void load_x_part(const MvArgs &a, uint32_t xoff, uint32_t k0, float (&v)[N], float &ss)
 {
     loadn<N>(a.x + xoff, k0, a.K, v);
-    if (a.cmb_k) {   // routed FFN output: the residual plus sum_r w[r] t[r], fmaf in r order
-        float acc[N];
-#pragma unroll
-        for (int i = 0; i < N; ++i) acc[i] = 0.f;
-        for (uint32_t r = 0; r < a.cmb_k; ++r) {
-            const float wr = a.cmb_w[r];
-            float t[N];
-            loadn<N>(a.cmb_t + static_cast<size_t>(r) * a.K, k0, a.K, t);
-#pragma unroll
-            for (int i = 0; i < N; ++i) acc[i] = fmaf(wr, t[i], acc[i]);
-        }
-#pragma unroll
-        for (int i = 0; i < N; ++i) v[i] += acc[i];
-    }
     if (a.nsl) {   // tensor-parallel input: the residual plus the ranks' partials
         const uint32_t tag = xch_tag(a.xs_epoch, a.xs_mul, a.xs_add);
         bool ok = true;
@@ -236,8 +215,6 @@ __device__ __forceinline__ void load_x_part(const MvArgs &a, uint32_t xoff, uint
             for (int i = 0; i < N; ++i) v[i] += t[i];
         }
         if (!ok) atomicExch(a.err, ERR_WAIT_TIMEOUT);
-    }
-    if (a.nsl || a.cmb_k) {
         if (a.xout && blockIdx.x == 0)
 #pragma unroll
             for (int i = 0; i < N; ++i)
@@ -338,26 +315,6 @@ __device__ __forceinline__ void consume(const MvArgs &a, const typename D::Lane 
         }
     }
     if (threadIdx.x == 0) MV_STAMP(5);
-}
-
-// Router launches (tk_k > 0): after the CTA's rows are written (every thread
-// of the CTA calls this; the ring is no longer in use), the CTA whose ticket
-// completes the launch ranks the logits (tb_moe_topk.cuh) and resets the
-// ticket counter.
-__device__ __noinline__ void topk_tail(const MvArgs &a, float *sh)
-{
-    __shared__ int s_last;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = atomicAdd(a.tk_ctr, 1u) == gridDim.x - 1u;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    moe_topk_block(a.y, static_cast<int>(a.M), a.tk_k, a.tk_ids, a.tk_wts, a.err, a.tk_ep_lo, a.tk_ep_n, a.tk_lids,
-                   a.tk_lw, a.tk_nloc, sh, ERR_RUNTIME);
-    if (threadIdx.x == 0) *a.tk_ctr = 0u;
 }
 
 template <class D>
@@ -713,7 +670,6 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
             for (uint32_t it = done; it < issued; ++it)
                 mbar_wait_bounded(smem_u32(full + it % a.nst), (it / a.nst) & 1u, nullptr, kDrainLimit);
         }
-        if (a.tk_k) topk_tail(a, reinterpret_cast<float *>(ring));
         return;
     }
 
@@ -742,7 +698,6 @@ __global__ void __launch_bounds__(ThreadsOf<D>::value, 1) k_matvec(const MvArgs 
     default: consume<D, 1>(a, lx, pos, full, empty, part, ring, w_lo, tile_bytes, r_lo, r_hi, n_tiles, cs, ph,
                            useful, active, row_bytes32); break;
     }
-    if (a.tk_k) topk_tail(a, reinterpret_cast<float *>(ring));
 }
 
 // ---------------------------------------------------------------------------
@@ -885,9 +840,6 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
     a.nst = p->nst;
     a.cap = p->cap;
     a.ncw = p->ncw;
-    // the expert selection runs on one CTA of the launch: a thread per logit
-    if (a.tk_k && (p->nthr < a.M || static_cast<size_t>(p->nst) * p->cap < sizeof(float) * (2 * kTopkMax + 34)))
-        return 0;
     // launched with programmatic stream serialization, so back-to-back matvecs
     // overlap one kernel's launch with the previous one's tail
     cudaLaunchConfig_t cfg{};
@@ -984,24 +936,6 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
         a.xs_mul = fuse->xs_mul;
         a.xs_add = fuse->xs_add;
         a.xout = fuse->xout;
-        if (fuse->cmb_k && (!fuse->cmb_t || !fuse->cmb_w || fuse->nsl || fuse->xmode == MV_X_SWIGLU || fuse->ng))
-            return 0;
-        a.cmb_t = fuse->cmb_t;
-        a.cmb_w = fuse->cmb_w;
-        a.cmb_k = fuse->cmb_k;
-        if (fuse->tk_k && (M > kTopkMax || fuse->tk_k > M || fuse->tk_k > 32 || !fuse->tk_ids || !fuse->tk_wts ||
-                           !fuse->tk_ctr || fuse->ny || fuse->ng || fuse->ymode != MV_Y_PLAIN ||
-                           (fuse->tk_ep_n && (!fuse->tk_lids || !fuse->tk_lw || !fuse->tk_nloc))))
-            return 0;
-        a.tk_k = fuse->tk_k;
-        a.tk_ep_lo = fuse->tk_ep_lo;
-        a.tk_ep_n = fuse->tk_ep_n;
-        a.tk_ids = fuse->tk_ids;
-        a.tk_wts = fuse->tk_wts;
-        a.tk_lids = fuse->tk_lids;
-        a.tk_lw = fuse->tk_lw;
-        a.tk_nloc = fuse->tk_nloc;
-        a.tk_ctr = fuse->tk_ctr;
         a.nsl = fuse->nsl;
         a.ny = fuse->ny;
         for (int p = 0; p < kMaxRanks; ++p) a.ys[p] = fuse->ys[p];
@@ -1049,7 +983,7 @@ int mv_launch(const void *W, int qtype, int M, int K, const float *d_x, float *d
             const uint32_t bw = static_cast<uint32_t>(g.block_weights);
             const uint32_t nw = (a.K + kCols - 1) / kCols;              // windows
             const uint32_t step = (((a.K + nw - 1) / nw + bw - 1) / bw) * bw;   // columns per window, whole blocks
-            const bool plain = a.xmode != MV_X_RMSNORM && a.ymode == MV_Y_PLAIN && !a.nsl && !a.ny && !a.ng && !a.cmb_k;
+            const bool plain = a.xmode != MV_X_RMSNORM && a.ymode == MV_Y_PLAIN && !a.nsl && !a.ny && !a.ng;
             if (!plain || step > kCols) {
                 fprintf(stderr, "[tb_cuda] matvec: K=%u is longer than one launch covers%s\n", a.K,
                         plain ? "" : " with this fused mode");
