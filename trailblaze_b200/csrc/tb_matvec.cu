@@ -190,31 +190,6 @@ __device__ __forceinline__ bool load_tagged(const unsigned long long *p, uint32_
     return ok;
 }
 
-// Whether all words [k0, k0 + N) of a row of tagged slot words (past K: ready)
-// carry `tag`; one read of each, two per 16-byte load when aligned.
-template <int N>
-__device__ __forceinline__ bool tagged_ready(const unsigned long long *p, uint32_t k0, uint32_t K, uint32_t tag)
-{
-    bool all = true;
-    if (k0 + N <= K && (reinterpret_cast<uintptr_t>(p + k0) & 15u) == 0) {
-#pragma unroll
-        for (int i = 0; i < N; i += 2) {
-            unsigned long long w0, w1;
-            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p + k0 + i) : "memory");
-            all = all && static_cast<uint32_t>(w0 >> 32) == tag && static_cast<uint32_t>(w1 >> 32) == tag;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < N; ++i)
-            if (k0 + i < K) {
-                unsigned long long w;
-                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p + k0 + i) : "memory");
-                all = all && static_cast<uint32_t>(w >> 32) == tag;
-            }
-    }
-    return all;
-}
-
 // The tag of an exchange: (epoch * mul + add) mod 2^32.
 __device__ __forceinline__ uint32_t xch_tag(const int *epoch, unsigned long long mul, unsigned long long add)
 {
@@ -232,24 +207,10 @@ __device__ __forceinline__ void load_x_part(const MvArgs &a, uint32_t xoff, uint
     loadn<N>(a.x + xoff, k0, a.K, v);
     if (a.nsl) {   // tensor-parallel input: the residual plus the ranks' partials
         const uint32_t tag = xch_tag(a.xs_epoch, a.xs_mul, a.xs_add);
-        // every rank's words polled together until all carry the tag (one round
-        // trip after the last lands, whatever the rank count), then read again
-        // and summed in rank order (a slot changes only at its next exchange)
         bool ok = true;
-        for (uint32_t it = 0;; ++it) {
-            bool all = true;
-            for (uint32_t r = 0; r < a.nsl; ++r)
-                all = tagged_ready<N>(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, tag) && all;
-            if (all) break;
-            if (it >= a.wait_limit || *reinterpret_cast<volatile int *>(a.err) != 0) {
-                ok = false;
-                break;
-            }
-            __nanosleep(TB_LL_SLEEP_NS);
-        }
         for (uint32_t r = 0; r < a.nsl; ++r) {
             float t[N];
-            load_tagged<N>(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, tag, t, a.err, ok ? a.wait_limit : 0u);
+            ok = load_tagged<N>(a.xs + static_cast<size_t>(r) * a.K, k0, a.K, tag, t, a.err, a.wait_limit) && ok;
 #pragma unroll
             for (int i = 0; i < N; ++i) v[i] += t[i];
         }
