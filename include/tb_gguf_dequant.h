@@ -131,7 +131,10 @@ int   tb_cuda_matvec_experts_dev(const void *W_dev, int qtype, int M, int K, int
  * nucleus with p = 0.95, as the reference); top_k = 0: nucleus sampling with
  * top_p in (0, 1].  Writes the chosen index to *d_token; stream-ordered.
  * top_k <= 2048 (when < vocab).  Non-finite logits set the error word (2)
- * and write 0.  1 = issued. */
+ * and write 0.  A small top_k (at most 256, at least 8 slices of 4 k logits)
+ * runs in two launches through a candidate buffer the library allocates on
+ * the first top-k call and shares between calls: calls that overlap on the
+ * GPU (different streams) must not both use it.  1 = issued. */
 int   tb_cuda_sample_dev(const float *d_logits, int vocab, int top_k, float top_p, float temperature,
                          float u, int *d_token, void *stream);
 

@@ -38,6 +38,7 @@ struct State {
     int x_loaded = 0;                        // K of the vector tb_cuda_upload_x left in d_x
     uint32_t wait_limit = 1u << 22;
     int fault = 0;                           // 1 alloc, 2 copy, 3 launch
+    tb::SmpScratch smp;                      // two-stage top-k candidates (first sampling call)
 };
 
 State g;
@@ -304,6 +305,9 @@ void tb_cuda_cleanup(void)
     if (g.h_y) cudaFreeHost(g.h_y);
     if (g.d_err) cudaFree(g.d_err);
     if (g.h_err) cudaFreeHost(g.h_err);
+    if (g.smp.cv) cudaFree(g.smp.cv);
+    if (g.smp.ci) cudaFree(g.smp.ci);
+    if (g.smp.nonfin) cudaFree(g.smp.nonfin);
     g = State{};
 }
 
@@ -382,13 +386,27 @@ int tb_cuda_sample_dev(const float *d_logits, int vocab, int top_k, float top_p,
                        int *d_token, void *stream)
 {
     int *derr;
+    tb::SmpScratch scr;
     {
         std::lock_guard<std::mutex> lk(g_mu);
         if (!ensure_init_locked(false)) return 0;
         derr = g.d_err;
+        if (!g.smp.cv && top_k > 0) {   // the two-stage top-k's candidates; without them one CTA does it
+            if (cudaMalloc(&g.smp.cv, sizeof(float) * tb::kSmpPreCap) != cudaSuccess ||
+                cudaMalloc(&g.smp.ci, sizeof(int) * tb::kSmpPreCap) != cudaSuccess ||
+                cudaMalloc(&g.smp.nonfin, sizeof(int)) != cudaSuccess ||
+                cudaMemset(g.smp.nonfin, 0, sizeof(int)) != cudaSuccess) {
+                cudaGetLastError();
+                if (g.smp.cv) cudaFree(g.smp.cv);
+                if (g.smp.ci) cudaFree(g.smp.ci);
+                if (g.smp.nonfin) cudaFree(g.smp.nonfin);
+                g.smp = tb::SmpScratch{};
+            }
+        }
+        scr = g.smp;
     }
     const int r = tb::sample_launch(d_logits, vocab, top_k, top_p, temperature, u, d_token, derr,
-                                    static_cast<cudaStream_t>(stream));
+                                    static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, nullptr, &scr);
     if (r) g_launches.fetch_add(1, std::memory_order_relaxed);
     return r;
 }

@@ -968,6 +968,7 @@ struct Decoder {
     float smp_temp = 0.f, smp_p = 0.f;
     int smp_k = 0;
     float *u_buf = nullptr;
+    SmpScratch smp_scr;   // two-stage top-k candidates (allocated with the variates)
     int *u_idx = nullptr;
     // batched prefill buffers (allocated on the first tb_cuda_dec_prefill)
     PfBufs pf{};
@@ -1187,7 +1188,8 @@ bool Decoder::enqueue(cudaStream_t s)
     f.w_early = true;
     if (!mv_launch(lm, lm_qt, c.vocab, H, x, logits, s, err, sms, lim, &f)) return false;
     if (sampling())
-        return sample_launch(logits, c.vocab, smp_k, smp_p, smp_temp, 0.f, tok, err, s, u_buf, u_idx, pos) != 0;
+        return sample_launch(logits, c.vocab, smp_k, smp_p, smp_temp, 0.f, tok, err, s, u_buf, u_idx, pos, nullptr,
+                             &smp_scr) != 0;
     const int G = sms;
     ArgTP tp{};
     tp.world = 1;
@@ -1317,7 +1319,7 @@ bool Decoder::enqueue_tp(cudaStream_t s)
         tp.per_step = static_cast<unsigned long long>(world);
         tp.wait_limit = lim;
         return sample_launch(full_logits(rank), vocab_full, smp_k, smp_p, smp_temp, 0.f, tok, err, s, u_buf, u_idx,
-                             pos, &tp) != 0;
+                             pos, &tp, &smp_scr) != 0;
     }
     ArgTP tp{};
     tp.rank = rank;
@@ -1353,7 +1355,8 @@ static void dec_free(Decoder *d)
     if (d->ev1) cudaEventDestroy(d->ev1);
     void *bufs[] = {d->x,    d->x2,  d->qkv, d->att, d->gu,     d->logits, d->kc,   d->vc,   d->part,
                     d->argv, d->argi, d->tok, d->pos, d->counts, d->err,    d->rlog, d->wts, d->hbuf,
-                    d->tbuf, d->ids, d->u_buf, d->u_idx, d->lids, d->lw, d->nloc};
+                    d->tbuf, d->ids, d->u_buf, d->u_idx, d->lids, d->lw, d->nloc,
+                    d->smp_scr.cv, d->smp_scr.ci, d->smp_scr.nonfin};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (d->hostio) cudaFreeHost(d->hostio);
@@ -1770,6 +1773,12 @@ int tb_cuda_dec_set_sampling(void *dec, float temperature, int top_k, float top_
             !(tb::dec_ok(cudaMalloc(&d->u_buf, sizeof(float) * d->cfg.max_ctx), "variates") &&
               tb::dec_ok(cudaMalloc(&d->u_idx, sizeof(int)), "variates")))
             return 0;
+        if (!d->smp_scr.cv &&   // without it top-k runs in one CTA
+            !(tb::dec_ok(cudaMalloc(&d->smp_scr.cv, sizeof(float) * tb::kSmpPreCap), "top-k candidates") &&
+              tb::dec_ok(cudaMalloc(&d->smp_scr.ci, sizeof(int) * tb::kSmpPreCap), "top-k candidates") &&
+              tb::dec_ok(cudaMalloc(&d->smp_scr.nonfin, sizeof(int)), "top-k candidates") &&
+              tb::dec_ok(cudaMemset(d->smp_scr.nonfin, 0, sizeof(int)), "top-k candidates")))
+            d->smp_scr.cv = nullptr;
     }
     if (d->sampling() != smp || (smp && (d->smp_temp != temperature || d->smp_k != top_k || d->smp_p != top_p))) {
         if (d->gexec) {   // the last kernel changes: capture again on the next step

@@ -103,9 +103,19 @@ struct SmpTP {
     uint32_t wait_limit = 0;
 };
 
+// Device scratch of the two-stage top-k (kSmpPreCap candidates and a flag;
+// the flag starts at 0 and every call leaves it at 0).  Without it, or when
+// the top k is too large a share of the vocabulary, top-k runs in one CTA.
+static constexpr int kSmpPreCap = 160 * 256;
+struct SmpScratch {
+    float *cv = nullptr;    // [kSmpPreCap] candidate logits
+    int *ci = nullptr;      // [kSmpPreCap] their vocabulary indices
+    int *nonfin = nullptr;  // set when a slice held a non-finite logit
+};
+
 int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
                   int *d_token, int *d_err, cudaStream_t st, const float *d_u = nullptr, int *d_u_idx = nullptr,
-                  int *d_pos = nullptr, const SmpTP *tp = nullptr);
+                  int *d_pos = nullptr, const SmpTP *tp = nullptr, const SmpScratch *scr = nullptr);
 
 // Launch the bit-exact dequantisation of M rows of K weights into d_out.
 int dq_launch(const void *W, int qtype, int M, int K, float *d_out, int sem, cudaStream_t st);

@@ -49,6 +49,11 @@ struct SmpArgs {
     const float *u_dev;   // not null: u = u_dev[*u_idx], and the step advances
     int *u_idx, *pos;
     SmpTP tp;             // tensor parallelism: wait for the ranks' logits, count the step
+    // two-stage top-k: logits are the candidates of k_topk_pre, cmap their
+    // vocabulary indices; *nonfin (read and reset here) reports a non-finite
+    // logit anywhere in the vocabulary
+    const int *cmap;
+    int *nonfin;
 };
 
 // Thread 0: the chosen token, and the decode step's advance when the variate
@@ -221,6 +226,21 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
             atomicExch(a.err, ERR_WAIT_TIMEOUT);
         __syncthreads();
     }
+    if (a.nonfin) {   // two-stage top-k: a slice held a non-finite logit
+        if (tid == 0) {
+            s_sel = *a.nonfin;
+            *a.nonfin = 0;
+        }
+        __syncthreads();
+        if (s_sel) {
+            if (tid == 0) {
+                atomicExch(a.err, ERR_RUNTIME);
+                finish(a, 0);
+            }
+            return;
+        }
+        __syncthreads();
+    }
     const float *lg = a.logits;
     const unsigned below = (1u << lane) - 1u;   // the lanes before this one
     // the warp's contiguous segment of the vocabulary (warp order = index order)
@@ -364,12 +384,12 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         if (gt) {
             const int at = bg + __popc(vg & below);
             cval[at] = v;
-            cidx[at] = i;
+            cidx[at] = a.cmap ? a.cmap[i] : i;
         } else if (eq) {
             const int rank = be + __popc(ve & below);
             if (rank < need) {
                 cval[ng + rank] = v;
-                cidx[ng + rank] = i;
+                cidx[ng + rank] = a.cmap ? a.cmap[i] : i;
             }
         }
         bg += __popc(vg);
@@ -395,24 +415,169 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
     }
 }
 
+// ---- two-stage top-k, stage 1 ----
+// CTA c takes the vocabulary slice [c V / G, (c+1) V / G) (at least k and at
+// most kSliceMax logits), selects its k largest by the same order as k_sample
+// (value descending, lower index first among equal values: a radix select of
+// the k-th largest key over the slice in shared memory) and writes them, in
+// vocabulary order, to cv / ci [c k, (c+1) k).  The k largest of the whole
+// vocabulary are among the G k candidates, in the same relative order, so
+// k_sample's top-k over the candidates (cmap = ci) selects the same tokens.
+// A non-finite logit sets *nonfin instead (k_sample reports it).
+static constexpr int kPreThreads = 512;
+static constexpr int kSliceMax = 4096;
+
+struct PreArgs {
+    const float *logits;
+    int vocab, k;
+    float *cv;
+    int *ci, *nonfin, *err;
+    SmpTP tp;
+};
+
+__device__ __forceinline__ float key_val(uint32_t key)
+{
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
+__global__ void __launch_bounds__(kPreThreads) k_topk_pre(const PreArgs p)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    __shared__ uint32_t keys[kSliceMax];
+    __shared__ int hist[256];
+    __shared__ int wsum[kPreThreads / 32], wsum2[kPreThreads / 32];
+    __shared__ int s_sel, s_n;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = kPreThreads / 32;
+    if (p.tp.ctr) {   // tensor parallelism: every rank's logits slice has arrived
+        if (tid == 0 && *reinterpret_cast<volatile int *>(p.err) == 0 &&
+            !wait_counter(p.tp.ctr, static_cast<unsigned long long>(*p.tp.epoch + 1) * p.tp.per_step, p.tp.wait_limit))
+            atomicExch(p.err, ERR_WAIT_TIMEOUT);
+        __syncthreads();
+    }
+    const int G = gridDim.x, c = blockIdx.x;
+    const int lo = static_cast<int>((static_cast<long long>(p.vocab) * c) / G);
+    const int n = static_cast<int>((static_cast<long long>(p.vocab) * (c + 1)) / G) - lo;
+    bool fin = true;
+    for (int i = tid; i < n; i += kPreThreads) {
+        const float v = __ldcg(p.logits + lo + i);
+        fin = fin && isfinite(v);
+        keys[i] = ord_key(v);
+    }
+    if (!__syncthreads_and(fin ? 1 : 0)) {
+        if (tid == 0) atomicOr(p.nonfin, 1);
+        return;
+    }
+    // the k-th largest key of the slice, 8 bits at a time
+    uint32_t prefix = 0, pmask = 0;
+    int need = p.k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += kPreThreads) hist[b] = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += kPreThreads) {
+            const uint32_t key = keys[i];
+            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int acc = 0, b = 255;
+            for (; b > 0; --b) {
+                if (acc + hist[b] >= need) break;
+                acc += hist[b];
+            }
+            s_sel = b;
+            s_n = need - acc;
+        }
+        __syncthreads();
+        prefix |= static_cast<uint32_t>(s_sel) << shift;
+        pmask |= 255u << shift;
+        need = s_n;
+        __syncthreads();
+    }
+    // the keys above prefix and the first `need` equal to it, in slice order:
+    // per pass of kPreThreads elements, block-wide ordered ranks of the equal
+    // keys and of the taken ones
+    const unsigned below = (1u << lane) - 1u;
+    int eq_done = 0, out = 0;
+    for (int base = 0; base < n; base += kPreThreads) {
+        const int i = base + tid;
+        const uint32_t key = i < n ? keys[i] : 0u;
+        const bool gt = i < n && key > prefix, eq = i < n && key == prefix;
+        const unsigned ve = __ballot_sync(0xFFFFFFFFu, eq);
+        if (lane == 0) wsum[warp] = __popc(ve);
+        __syncthreads();
+        int ebefore = 0, etot = 0;
+        for (int w = 0; w < NW; ++w) {
+            ebefore += w < warp ? wsum[w] : 0;
+            etot += wsum[w];
+        }
+        const bool take = gt || (eq && eq_done + ebefore + __popc(ve & below) < need);
+        const unsigned vt = __ballot_sync(0xFFFFFFFFu, take);
+        if (lane == 0) wsum2[warp] = __popc(vt);
+        __syncthreads();
+        int tbefore = 0, ttot = 0;
+        for (int w = 0; w < NW; ++w) {
+            tbefore += w < warp ? wsum2[w] : 0;
+            ttot += wsum2[w];
+        }
+        if (take) {
+            const int at = c * p.k + out + tbefore + __popc(vt & below);
+            p.cv[at] = key_val(key);
+            p.ci[at] = lo + i;
+        }
+        eq_done += etot;
+        out += ttot;
+        __syncthreads();
+    }
+}
+
 int sample_launch(const float *d_logits, int vocab, int top_k, float top_p, float temperature, float u,
                   int *d_token, int *d_err, cudaStream_t st, const float *d_u, int *d_u_idx, int *d_pos,
-                  const SmpTP *tp)
+                  const SmpTP *tp, const SmpScratch *scr)
 {
     const NvtxRange nvtx("tb.sample");
     if (!d_logits || !d_token || vocab <= 0 || top_k < 0 || (top_k > 0 && top_k < vocab && top_k > kNucleusMax) ||
         (top_k == 0 && !(top_p > 0.f && top_p <= 1.f)))
         return 0;
     if (d_u ? (!d_u_idx || !d_pos) : !(u >= 0.f && u < 1.f)) return 0;
-    SmpArgs a{d_logits, d_token, d_err, vocab, top_k, top_p, temperature, u, d_u, d_u_idx, d_pos, SmpTP{}};
+    SmpArgs a{d_logits, d_token, d_err, vocab, top_k, top_p, temperature, u, d_u, d_u_idx, d_pos, SmpTP{},
+              nullptr, nullptr};
     if (tp) a.tp = *tp;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    // Two stages when the top k is a small share of the vocabulary: G slices of
+    // at least 4k (and at most kSliceMax) logits, G between 8 and the SM count.
+    int dev = 0, sms = 0;
+    if (scr && scr->cv && top_k > 0 && top_k < vocab && cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
+        int G = vocab / (4 * top_k);
+        if (G > sms) G = sms;
+        if (G * top_k > kSmpPreCap) G = kSmpPreCap / top_k;
+        if (G >= 8 && (vocab + G - 1) / G <= kSliceMax) {
+            PreArgs pa{d_logits, vocab, top_k, scr->cv, scr->ci, scr->nonfin, d_err, a.tp};
+            cudaLaunchConfig_t pc{};
+            pc.gridDim = dim3(G);
+            pc.blockDim = dim3(kPreThreads);
+            pc.stream = st;
+            pc.attrs = attr;
+            pc.numAttrs = 1;
+            if (cudaLaunchKernelEx(&pc, k_topk_pre, pa) != cudaSuccess) {
+                cudaGetLastError();
+                return 0;
+            }
+            a.logits = scr->cv;
+            a.vocab = G * top_k;
+            a.cmap = scr->ci;
+            a.nonfin = scr->nonfin;
+            a.tp.ctr = nullptr;   // the first stage waited; the step is still counted (epoch)
+        }
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(kSmpThreads);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (cudaLaunchKernelEx(&cfg, k_sample, a) != cudaSuccess) {
