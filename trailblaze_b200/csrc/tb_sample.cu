@@ -188,6 +188,38 @@ __device__ __forceinline__ int first_reaching(const float *v, int n, float targe
     return n - 1;
 }
 
+// One radix step's bin, by warp 0: the largest b in 255 .. 1 whose bins b ..
+// 255 hold at least `need` keys (else 0), and need minus the keys in the bins
+// above it: what a scan from bin 255 downwards finds, with lane l adding bins
+// 255 - 8l down to 248 - 8l and a shuffle prefix over the lanes.
+__device__ __forceinline__ void select_bin(const int *hist, int need, int *sel, int *rem)
+{
+    const int lane = threadIdx.x & 31, hi = 255 - 8 * lane;
+    int t = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += hist[hi - j];
+    int incl = t;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    const int excl = incl - t;   // keys in the bins above this lane's
+    const unsigned reach = __ballot_sync(0xFFFFFFFFu, incl >= need);
+    const int L = reach ? __ffs(reach) - 1 : 31;
+    if (lane == L) {
+        // lane L's lowest bin is taken untested: its bins reach need (lanes
+        // before it did not), or it is bin 0, which the downward scan takes
+        // untested as well
+        int acc = excl, b = hi;
+        for (; b > hi - 7; --b) {
+            if (acc + hist[b] >= need) break;
+            acc += hist[b];
+        }
+        *sel = b;
+        *rem = need - acc;
+    }
+}
+
 // Visits the warp's segment [lo, hi) of the logits: each iteration loads
 // kChunk consecutive elements, kPer per lane (element b + 32 j + lane), and
 // calls f(index, value, in_range) in ascending index order, j-major; every
@@ -347,15 +379,7 @@ __global__ void __launch_bounds__(kSmpThreads, 1) k_sample(const SmpArgs a)
         } else {
             __syncthreads();
         }
-        if (tid == 0) {
-            int acc = 0, b = 255;
-            for (; b > 0; --b) {
-                if (acc + hist[b] >= need) break;
-                acc += hist[b];
-            }
-            s_sel = b;
-            s_n = need - acc;   // keys still needed from bin b
-        }
+        if (warp == 0) select_bin(hist, need, &s_sel, &s_n);
         __syncthreads();
         prefix |= static_cast<uint32_t>(s_sel) << shift;
         pmask |= 255u << shift;
@@ -480,15 +504,7 @@ __global__ void __launch_bounds__(kPreThreads) k_topk_pre(const PreArgs p)
             if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
         }
         __syncthreads();
-        if (tid == 0) {
-            int acc = 0, b = 255;
-            for (; b > 0; --b) {
-                if (acc + hist[b] >= need) break;
-                acc += hist[b];
-            }
-            s_sel = b;
-            s_n = need - acc;
-        }
+        if (warp == 0) select_bin(hist, need, &s_sel, &s_n);
         __syncthreads();
         prefix |= static_cast<uint32_t>(s_sel) << shift;
         pmask |= 255u << shift;
