@@ -329,7 +329,7 @@ int    tb_cuda_dec_generate_u(void *dec, int token, int pos, int n, const float 
 int    tb_cuda_dec_read(void *dec, int which, float *host, int n);
 
 /* Tensor parallelism over `world` GPUs (2, 4 or 8; one process per GPU), the
- * sharding of SURVEY-style Megatron decode: rank r holds
+ * sharding of Megatron-style decode: rank r holds
  *   w_qkv      rows of its q heads [r NH/w, (r+1) NH/w), then of its k heads and
  *              its v heads (the same split of n_kv_heads), H columns;
  *   w_o        all H rows, the K columns of its q heads (K = NH/w * head_dim);
