@@ -55,10 +55,13 @@ struct IsF32X<D, std::void_t<decltype(D::kF32X)>> : std::integral_constant<bool,
 // NP pair units (64 activations each) per column slot; the default NP = 1
 // keeps 64 prescaled activations in registers at 16 warps per CTA, NP = 2
 // keeps 128 at 8 warps of up to 255 registers.
+#ifndef TB_XF_THREADS
+#define TB_XF_THREADS 512   // threads per CTA of the one-unit (NP = 1) decoders
+#endif
 template <int NP>
 struct XfGeom {
     static constexpr int N = 64 * NP;                    // activations per slot
-    static constexpr int THREADS = NP == 1 ? 512 : 256;  // threads per CTA
+    static constexpr int THREADS = NP == 1 ? TB_XF_THREADS : 256;  // threads per CTA
     static constexpr int REC = rec_stride(N + 1);        // record: N floats, the max word, padding
 };
 #ifndef TB_XF_NP
