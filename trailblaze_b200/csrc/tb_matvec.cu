@@ -84,7 +84,10 @@ struct MvArgs {
 };
 
 #ifndef TB_MV_MIN_TILES
-#define TB_MV_MIN_TILES 2   // tiles per CTA the planner keeps a single matvec at, when rows allow
+#define TB_MV_MIN_TILES 3         // tiles per CTA the planner keeps a single matvec at, when rows allow
+#endif
+#ifndef TB_MV_MIN_TILES_EARLY
+#define TB_MV_MIN_TILES_EARLY 2   // the same for a launch that prefetches its first tile before the wait
 #endif
 #ifndef TB_LL_SLEEP_NS
 #define TB_LL_SLEEP_NS 64   // back-off between polls of a tagged slot word
@@ -714,7 +717,7 @@ static constexpr uint32_t kMaxStages = 8;
 struct Plan {
     const void *kern;
     unsigned long long row_bytes;
-    uint32_t M, K, sms, ymode, ng;
+    uint32_t M, K, sms, ymode, ng, w_early;
     int dev;
     uint32_t nthr, grid, cs, phases, rpl, tr, rw, npart, nst, cap, ncw;
     size_t smem;
@@ -754,13 +757,18 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
     static const uint32_t rpl_max = getenv("TB_MV_RPL_MAX") ? atoi(getenv("TB_MV_RPL_MAX")) : kMaxRpl;
     // Rows per thread per tile: as many as keep a stage within kStageMax and
     // two stages in shared memory (the per-tile cost is paid once per rpl
-    // rows) and, for a single matvec, still give each CTA at least two tiles
-    // (a CTA with one tile, or one and a sliver, cannot overlap its decoding
-    // with its stream; measured 7-10 % faster on 14-28 MB projections, no
-    // change on the large ones); then as many stages as fit.  When even one
+    // rows) and, for a single matvec, still give each CTA at least three
+    // tiles (two when the first is requested before the dependency wait): a
+    // CTA with one tile, or one and a sliver, cannot overlap its decoding with
+    // its stream (measured 7-10 % faster on 14-28 MB projections, no change on
+    // the large ones; in the decode step two measured better than three);
+    // then as many stages as fit.  When even one
     // row per thread does not fit (long rows over few column slots: many
     // phases of whole rows), fewer consumer warps make fewer phases.
     const uint32_t grid1 = p.M < p.sms ? p.M : p.sms;
+    // (a launch that requests its first tile before the dependency wait keeps
+    // bigger tiles: more of its weights stream while the previous kernel ends)
+    const uint32_t min_tiles = p.w_early ? TB_MV_MIN_TILES_EARLY : TB_MV_MIN_TILES;
     const uint32_t rows_cta = p.ng > 0 || grid1 == 0 ? 0u : (p.M + grid1 - 1) / grid1;
     p.nst = 0;
     for (const uint32_t min_ncw = (p.cs + 31) / 32; !p.nst && p.ncw >= min_ncw; --p.ncw) {
@@ -771,7 +779,7 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
             if (rpl > 1 && bytes > stage_max) continue;
             if (p.ymode == MV_Y_SWIGLU_PAIRS && (p.phases * rpl) % 2) continue;   // tiles of whole pairs
             const uint32_t tr = p.phases * rpl;
-            if (rpl > 1 && rows_cta && (rows_cta + tr - 1) / tr < TB_MV_MIN_TILES) continue;   // tiles a CTA
+            if (rpl > 1 && rows_cta && (rows_cta + tr - 1) / tr < min_tiles) continue;   // tiles a CTA
             const uint32_t cap = static_cast<uint32_t>((bytes + 32 + 127) & ~127ull);
             for (uint32_t n = kMaxStages; n >= 2; --n) {
                 const MvSmem s = mv_smem(n, p.cs, D::REC, tr, p.npart, cap);
@@ -814,7 +822,8 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
     for (int i = 0; i < t_nplans; ++i) {
         const Plan &q = t_plans[i];
         if (q.kern == kp && q.M == a.M && q.K == a.K && q.row_bytes == a.row_bytes && q.dev == dev &&
-            q.sms == static_cast<uint32_t>(num_sms) && q.ymode == a.ymode && q.ng == a.ng) {
+            q.sms == static_cast<uint32_t>(num_sms) && q.ymode == a.ymode && q.ng == a.ng &&
+            q.w_early == a.w_early) {
             p = &q;
             break;
         }
@@ -830,6 +839,7 @@ static int launch_dec(MvArgs &a, int num_sms, cudaStream_t st)
         np.sms = static_cast<uint32_t>(num_sms);
         np.ymode = a.ymode;
         np.ng = a.ng;
+        np.w_early = a.w_early;
         if (!make_plan<D>(np, a.row_bytes)) return 0;
         if (getenv("TB_MV_VERBOSE"))
             fprintf(stderr,
