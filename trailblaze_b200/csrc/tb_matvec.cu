@@ -86,6 +86,9 @@ struct MvArgs {
 #ifndef TB_MV_MIN_TILES
 #define TB_MV_MIN_TILES 3         // tiles per CTA the planner keeps a single matvec at, when rows allow
 #endif
+#ifndef TB_MV_GROUP_TILES
+#define TB_MV_GROUP_TILES 0
+#endif
 #ifndef TB_MV_MIN_TILES_EARLY
 #define TB_MV_MIN_TILES_EARLY 2   // the same for a launch that prefetches its first tile before the wait
 #endif
@@ -765,11 +768,24 @@ static bool make_plan(Plan &p, unsigned long long row_bytes)
     // then as many stages as fit.  When even one
     // row per thread does not fit (long rows over few column slots: many
     // phases of whole rows), fewer consumer warps make fewer phases.
-    const uint32_t grid1 = p.M < p.sms ? p.M : p.sms;
+    // rows of one CTA: a single matvec spreads M rows over min(M, SMs) CTAs;
+    // expert groups give each group's M rows (output units of ua rows) to
+    // SMs / ng CTAs (TB_MV_GROUP_TILES: the rule for groups too)
+    uint32_t rows_cta = 0;
+    {
+        const uint32_t ua = p.ymode == MV_Y_SWIGLU_PAIRS ? 2u : 1u, units = p.M / ua;
+        if (p.ng == 0) {
+            const uint32_t g = p.M < p.sms ? p.M : p.sms;
+            rows_cta = g ? (p.M + g - 1) / g : 0u;
+        } else if (TB_MV_GROUP_TILES && units) {
+            uint32_t cpg = p.sms / p.ng;
+            cpg = cpg < 1 ? 1 : (cpg > units ? units : cpg);
+            rows_cta = ua * ((units + cpg - 1) / cpg);
+        }
+    }
     // (a launch that requests its first tile before the dependency wait keeps
     // bigger tiles: more of its weights stream while the previous kernel ends)
     const uint32_t min_tiles = p.w_early ? TB_MV_MIN_TILES_EARLY : TB_MV_MIN_TILES;
-    const uint32_t rows_cta = p.ng > 0 || grid1 == 0 ? 0u : (p.M + grid1 - 1) / grid1;
     p.nst = 0;
     for (const uint32_t min_ncw = (p.cs + 31) / 32; !p.nst && p.ncw >= min_ncw; --p.ncw) {
         p.nthr = 32 * (p.ncw + 1);
