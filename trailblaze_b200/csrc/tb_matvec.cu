@@ -87,7 +87,7 @@ struct MvArgs {
 #define TB_MV_MIN_TILES 3         // tiles per CTA the planner keeps a single matvec at, when rows allow
 #endif
 #ifndef TB_MV_GROUP_TILES
-#define TB_MV_GROUP_TILES 0
+#define TB_MV_GROUP_TILES 1
 #endif
 #ifndef TB_MV_MIN_TILES_EARLY
 #define TB_MV_MIN_TILES_EARLY 2   // the same for a launch that prefetches its first tile before the wait
